@@ -1,0 +1,60 @@
+// b3_internal.h — shared declarations of the CUDA library (not part of the ABI).
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/bark3_b200.h"
+
+namespace b3 {
+
+// ── errors: every ABI call returns 0 or a negative B3_E* code and leaves a
+// message in the calling thread's last-error slot.
+int set_error(int code, const char* fmt, ...);
+int set_cuda_error(const char* what, cudaError_t e);
+void clear_error();
+
+// Reads and clears the device error word (bounded waits that ran out).
+int check_device_error(cudaStream_t st);
+
+// ── K1 GEMM ──
+enum GemmEpi {
+    EPI_F32 = 0,       // out_f32 = acc (+ bias)
+    EPI_RESID = 1,     // out_f32 += alpha * acc
+    EPI_F16 = 2,       // out_f16 = f16(acc (+ bias))
+    EPI_SILU_F16 = 3,  // out_f16 = f16(silu(acc (+ bias)))
+    EPI_GLU_F16 = 4,   // out_f16[:, i] = f16(acc[2i] * sigmoid(acc[2i+1]))
+    EPI_QKV = 5,       // out_f16 row = [q + bias_u | q + bias_v | k | v]
+};
+
+struct GemmParams {
+    int M, N, K;
+    int ldo;                  // row stride of the output, in elements
+    float alpha;              // residual scale (EPI_RESID)
+    const float* bias;        // [N] or null
+    const float* bias_u;      // [1024] (EPI_QKV)
+    const float* bias_v;      // [1024] (EPI_QKV)
+    const uint16_t* lut;      // [N][16] f16 bits (LUT4 weights)
+    float* out_f32;
+    __half* out_f16;
+};
+
+struct GemmOp {
+    CUtensorMap map_a;
+    CUtensorMap map_b;
+    GemmParams p;
+    bool lut;
+    int bn;
+    int epi;
+};
+
+int make_map_2d(CUtensorMap* map, const void* base, bool f16, uint64_t inner, uint64_t outer,
+                uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, bool swizzle128);
+int gemm_make_a_map(CUtensorMap* map, const __half* a, int M, int K, int lda);
+int gemm_make_b_map(CUtensorMap* map, const void* w, bool lut, int N, int K, int bn);
+int gemm_validate(const GemmParams& p, bool lut, int bn);
+int gemm_launch(const GemmOp& op, cudaStream_t st);
+int gemm_take_dev_error(cudaStream_t st, unsigned int* out);
+
+}  // namespace b3

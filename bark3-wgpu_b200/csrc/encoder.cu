@@ -1,0 +1,823 @@
+// encoder.cu — context, weight store, launch sequence and the C ABI.
+//
+// The per-block launch sequence restates CpuLayer::forward
+// (src/cpu/layer.rs:157-327) / Encoder::encode_pre (src/encoder.rs:2005-2651)
+// with the element-wise passes fused into the GEMM epilogues:
+//
+//   LN1 -> ff1a[SiLU] -> ff1b[x += 0.5 acc]
+//   LN2 -> qkv[+bias_u / +bias_v split] -> rel-pos attention -> o[x += acc]
+//   LN3 -> pw1[GLU] -> dwconv+BN+SiLU -> pw2[x += acc]
+//   LN4 -> ff2a[SiLU] -> ff2b[x += 0.5 acc]
+//   norm_out (fused with the next block's LN1)
+//
+// Layout in HBM (rows = frames of all utterances, concatenated):
+//   x     [M][1024] f32   residual stream (stays f32 like the reference)
+//   a16   [M][1024] f16   GEMM input: LN output / attention output / conv output
+//   h16   [M][4096] f16   FFN hidden after SiLU
+//   qkv16 [M][4096] f16   q+bias_u | q+bias_v | k | v
+//   g16   [M][1024] f16   GLU output (depthwise conv input)
+//   sub16 [M][4096] f16   encoder input
+//   pos16 [2*Tcap-1][1024] f16 positional table, R16 [2*Tmax-1][1024] f16
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <cmath>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "b3_internal.h"
+#include "b3_kernels.h"
+
+// ───────────────────────────── errors ─────────────────────────────
+
+namespace b3 {
+namespace {
+thread_local char g_last_error[512] = "";
+}
+
+int set_error(int code, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+    va_end(ap);
+    return code;
+}
+
+int set_cuda_error(const char* what, cudaError_t e) {
+    return set_error(B3_ECUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+void clear_error() { g_last_error[0] = 0; }
+
+}  // namespace b3
+
+using namespace b3;
+
+#define B3_TRY(expr)                \
+    do {                            \
+        int _rc = (expr);           \
+        if (_rc) return _rc;        \
+    } while (0)
+
+#define B3_CUDA(expr)                                          \
+    do {                                                       \
+        cudaError_t _e = (expr);                               \
+        if (_e != cudaSuccess) return set_cuda_error(#expr, _e); \
+    } while (0)
+
+namespace {
+
+constexpr int kHidden = 1024;
+constexpr int kFfn = 4096;
+constexpr int kSubIn = 4096;
+constexpr int kProj = 640;
+
+struct DevBuf {
+    void* p = nullptr;
+    size_t bytes = 0;
+    int ensure(size_t need) {
+        if (need <= bytes) return 0;
+        if (p) cudaFree(p);
+        p = nullptr;
+        bytes = 0;
+        cudaError_t e = cudaMalloc(&p, need);
+        if (e != cudaSuccess) {
+            p = nullptr;
+            return set_error(B3_ENOMEM, "cudaMalloc(%zu bytes): %s", need, cudaGetErrorString(e));
+        }
+        bytes = need;
+        return 0;
+    }
+    void release() {
+        if (p) cudaFree(p);
+        p = nullptr;
+        bytes = 0;
+    }
+    template <class T>
+    T* as() const {
+        return static_cast<T*>(p);
+    }
+};
+
+// One linear layer's weight on the device.
+struct Linear {
+    bool present = false;
+    bool lut = false;
+    int N = 0, K = 0, bn = 128;
+    DevBuf w;      // codes [N][K/2] or f16 [N][K]
+    DevBuf lut16;  // [N][16] f16
+    CUtensorMap map_b;
+};
+
+struct Layer {
+    Linear qkv, relk, o, ff1a, ff1b, ff2a, ff2b, pw1, pw2;
+    DevBuf params;  // f32: dw_t[9][1024] | bn_a | bn_b | ln_w[5] | ln_b[5] | bu | bv
+    float* dw_t() const { return params.as<float>(); }
+    float* bn_a() const { return params.as<float>() + 9 * kHidden; }
+    float* bn_b() const { return params.as<float>() + 10 * kHidden; }
+    float* ln_w(int i) const { return params.as<float>() + (11 + i) * kHidden; }
+    float* ln_b(int i) const { return params.as<float>() + (16 + i) * kHidden; }
+    float* bu() const { return params.as<float>() + 21 * kHidden; }
+    float* bv() const { return params.as<float>() + 22 * kHidden; }
+    static constexpr size_t kParamFloats = 23 * kHidden;
+};
+
+// A tensor as pushed through the ABI, kept on the host until b3_finalize.
+struct Staged {
+    bool lowbit = false;
+    std::vector<int64_t> shape;
+    std::vector<float> f32;        // dense values, widened exactly
+    std::vector<uint16_t> f16;     // dense values rounded to f16 (RNE)
+    std::vector<uint8_t> codes;    // lowbit: [rows][cols/2]
+    std::vector<uint16_t> lut16;   // lowbit: [rows][16]
+    int rows = 0, cols = 0;
+};
+
+struct Plan {
+    std::vector<int32_t> cu;
+    int M = 0, tmax = 0, n_work = 0;
+};
+
+}  // namespace
+
+struct b3_ctx {
+    int device = 0;
+    cudaStream_t stream = nullptr;
+    std::map<std::string, Staged> staged;
+    bool finalized = false;
+    int n_layers = 0;
+    Linear sub_w, proj_w;
+    DevBuf sub_b, proj_b;
+    std::vector<Layer> layers;
+    DevBuf inv_freq;  // [512] f32
+    int tcap = 0;     // positional table capacity (frames)
+    DevBuf pos16;
+    // activation arena
+    int mcap = 0;
+    DevBuf x, a16, h16, qkv16, g16, sub16, R16;
+    DevBuf cu_d, work_d, seg_d;
+    DevBuf io_in, io_out;   // device staging for host-pointer calls
+    DevBuf scratch16;       // f16 copy of A for the single-linear entry points
+    Plan plan;
+    ~b3_ctx() {
+        auto rel = [](Linear& l) { l.w.release(); l.lut16.release(); };
+        rel(sub_w);
+        rel(proj_w);
+        for (auto& L : layers) {
+            rel(L.qkv); rel(L.relk); rel(L.o); rel(L.ff1a); rel(L.ff1b);
+            rel(L.ff2a); rel(L.ff2b); rel(L.pw1); rel(L.pw2);
+            L.params.release();
+        }
+        for (DevBuf* b : {&sub_b, &proj_b, &inv_freq, &pos16, &x, &a16, &h16, &qkv16, &g16, &sub16,
+                          &R16, &cu_d, &work_d, &seg_d, &io_in, &io_out, &scratch16})
+            b->release();
+        if (stream) cudaStreamDestroy(stream);
+    }
+};
+
+namespace {
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+uint16_t f32_to_f16_bits(float v) {
+    __half h = __float2half_rn(v);
+    return *reinterpret_cast<uint16_t*>(&h);
+}
+
+float f16_bits_to_f32(uint16_t b) {
+    __half h = *reinterpret_cast<__half*>(&b);
+    return __half2float(h);
+}
+
+float bf16_bits_to_f32(uint16_t b) {
+    uint32_t x = (static_cast<uint32_t>(b) & 0x8000u) << 16 | ((static_cast<uint32_t>(b) & 0x7FFFu) << 16);
+    float f;
+    memcpy(&f, &x, 4);
+    return f;
+}
+
+int upload(DevBuf& dst, const void* src, size_t bytes, cudaStream_t st) {
+    B3_TRY(dst.ensure(bytes));
+    B3_CUDA(cudaMemcpyAsync(dst.p, src, bytes, cudaMemcpyHostToDevice, st));
+    return 0;
+}
+
+const Staged* find(b3_ctx* c, const std::string& name) {
+    auto it = c->staged.find(name);
+    return it == c->staged.end() ? nullptr : &it->second;
+}
+
+int64_t numel(const Staged& s) {
+    int64_t n = 1;
+    for (int64_t d : s.shape) n *= d;
+    return n;
+}
+
+// Dense f32 values of a small tensor (LN, biases, BN statistics).
+int get_vec(b3_ctx* c, const std::string& name, int64_t n, std::vector<float>& out) {
+    const Staged* s = find(c, name);
+    if (!s) return set_error(B3_ENOTFOUND, "tensor %s was not loaded", name.c_str());
+    if (s->lowbit || numel(*s) != n)
+        return set_error(B3_EINVAL, "tensor %s: expected %lld dense values", name.c_str(), (long long)n);
+    out = s->f32;
+    return 0;
+}
+
+// Build a device linear from one or more staged (N_i, K) matrices stacked by
+// rows.  All parts must share the storage kind (the reference refuses a mixed
+// fused q|k|v too, src/encoder.rs:389-392).  `interleave_halves` reorders the
+// rows as (0, N/2, 1, N/2+1, ...) so a GLU pair lands in adjacent columns.
+int build_linear(b3_ctx* c, Linear& L, const std::vector<std::string>& names, int n_each, int K,
+                 bool interleave_halves, int bn) {
+    std::vector<const Staged*> parts;
+    for (auto& nm : names) {
+        const Staged* s = find(c, nm);
+        if (!s) return set_error(B3_ENOTFOUND, "tensor %s was not loaded", nm.c_str());
+        parts.push_back(s);
+    }
+    const bool lut = parts[0]->lowbit;
+    for (auto* s : parts)
+        if (s->lowbit != lut)
+            return set_error(B3_EINVAL, "%s: fused parts mix 4-bit and dense storage", names[0].c_str());
+    const int N = n_each * static_cast<int>(parts.size());
+    for (size_t i = 0; i < parts.size(); ++i) {
+        const Staged* s = parts[i];
+        const int64_t rows = lut ? s->rows : (s->shape.empty() ? 0 : s->shape[0]);
+        const int64_t cols = lut ? s->cols : (rows ? numel(*s) / rows : 0);
+        if (rows != n_each || cols != K)
+            return set_error(B3_EINVAL, "tensor %s: shape (%lld, %lld), expected (%d, %d)", names[i].c_str(),
+                             (long long)rows, (long long)cols, n_each, K);
+    }
+    auto src_row = [&](int r) -> std::pair<const Staged*, int> {
+        int rr = r;
+        if (interleave_halves) rr = (r & 1) ? N / 2 + r / 2 : r / 2;
+        return {parts[rr / n_each], rr % n_each};
+    };
+    L.present = true;
+    L.lut = lut;
+    L.N = N;
+    L.K = K;
+    L.bn = bn;
+    if (lut) {
+        std::vector<uint8_t> codes(static_cast<size_t>(N) * K / 2);
+        std::vector<uint16_t> tab(static_cast<size_t>(N) * 16);
+        for (int r = 0; r < N; ++r) {
+            auto [s, sr] = src_row(r);
+            memcpy(&codes[static_cast<size_t>(r) * K / 2], &s->codes[static_cast<size_t>(sr) * K / 2], K / 2);
+            memcpy(&tab[static_cast<size_t>(r) * 16], &s->lut16[static_cast<size_t>(sr) * 16], 32);
+        }
+        B3_TRY(upload(L.w, codes.data(), codes.size(), c->stream));
+        B3_TRY(upload(L.lut16, tab.data(), tab.size() * 2, c->stream));
+        B3_CUDA(cudaStreamSynchronize(c->stream));
+    } else {
+        std::vector<uint16_t> w(static_cast<size_t>(N) * K);
+        for (int r = 0; r < N; ++r) {
+            auto [s, sr] = src_row(r);
+            memcpy(&w[static_cast<size_t>(r) * K], &s->f16[static_cast<size_t>(sr) * K], static_cast<size_t>(K) * 2);
+        }
+        B3_TRY(upload(L.w, w.data(), w.size() * 2, c->stream));
+        B3_CUDA(cudaStreamSynchronize(c->stream));
+    }
+    return gemm_make_b_map(&L.map_b, L.w.p, lut, N, K, bn);
+}
+
+// ───────────────────────────── GEMM helper ─────────────────────────────
+
+int run_gemm(b3_ctx* c, const Linear& W, const __half* a, int M, int lda, int epi, GemmParams p) {
+    GemmOp op;
+    B3_TRY(gemm_make_a_map(&op.map_a, a, M, W.K, lda));
+    op.map_b = W.map_b;
+    p.M = M;
+    p.N = W.N;
+    p.K = W.K;
+    p.lut = W.lut ? W.lut16.as<uint16_t>() : nullptr;
+    op.p = p;
+    op.lut = W.lut;
+    op.bn = W.bn;
+    op.epi = epi;
+    return gemm_launch(op, c->stream);
+}
+
+GemmParams params_f32(float* out, int ldo, const float* bias) {
+    GemmParams p{};
+    p.out_f32 = out;
+    p.ldo = ldo;
+    p.bias = bias;
+    return p;
+}
+
+GemmParams params_resid(float* x, float alpha) {
+    GemmParams p{};
+    p.out_f32 = x;
+    p.ldo = kHidden;
+    p.alpha = alpha;
+    return p;
+}
+
+GemmParams params_f16(__half* out, int ldo) {
+    GemmParams p{};
+    p.out_f16 = out;
+    p.ldo = ldo;
+    return p;
+}
+
+// ───────────────────────────── planning ─────────────────────────────
+
+int ensure_arena(b3_ctx* c, int M) {
+    if (M <= c->mcap) return 0;
+    int mcap = ((M + 255) / 256) * 256;
+    const size_t m = static_cast<size_t>(mcap);
+    B3_TRY(c->x.ensure(m * kHidden * 4));
+    B3_TRY(c->a16.ensure(m * kHidden * 2));
+    B3_TRY(c->h16.ensure(m * kFfn * 2));
+    B3_TRY(c->qkv16.ensure(m * 4096 * 2));
+    B3_TRY(c->g16.ensure(m * kHidden * 2));
+    B3_TRY(c->sub16.ensure(m * kSubIn * 2));
+    B3_TRY(c->seg_d.ensure(m * sizeof(int2)));
+    B3_TRY(c->work_d.ensure((m / 64 + 1024) * sizeof(int2)));
+    c->mcap = mcap;
+    return 0;
+}
+
+int ensure_pos(b3_ctx* c, int tmax) {
+    if (tmax <= c->tcap) return 0;
+    int tcap = ((tmax + 511) / 512) * 512;
+    const int rows = 2 * tcap - 1;
+    B3_TRY(c->pos16.ensure(static_cast<size_t>(rows + 1) * kHidden * 2));
+    B3_TRY(c->R16.ensure(static_cast<size_t>(rows + 1) * kHidden * 2));
+    B3_TRY(launch_pos_table(c->inv_freq.as<float>(), tcap, rows, c->pos16.as<__half>(), c->stream));
+    c->tcap = tcap;
+    return 0;
+}
+
+int make_plan(b3_ctx* c, const int32_t* cu, int n_utt) {
+    if (n_utt <= 0) return set_error(B3_EINVAL, "batch needs at least one utterance");
+    if (cu[0] != 0) return set_error(B3_EINVAL, "cu_seqlens[0] must be 0");
+    int tmax = 0;
+    for (int i = 0; i < n_utt; ++i) {
+        const int t = cu[i + 1] - cu[i];
+        if (t <= 0) return set_error(B3_EINVAL, "utterance %d has %d frames", i, t);
+        if (t > tmax) tmax = t;
+    }
+    const int M = cu[n_utt];
+    std::vector<int32_t> key(cu, cu + n_utt + 1);
+    if (key == c->plan.cu && c->mcap >= M && c->tcap >= tmax) return 0;
+    B3_TRY(ensure_arena(c, M));
+    B3_TRY(ensure_pos(c, tmax));
+    const int bq = attention_block_rows();
+    std::vector<int2> work;
+    std::vector<int2> seg(M);
+    for (int i = 0; i < n_utt; ++i) {
+        for (int q = 0; q < cu[i + 1] - cu[i]; q += bq) work.push_back(make_int2(i, q));
+        for (int r = cu[i]; r < cu[i + 1]; ++r) seg[r] = make_int2(cu[i], cu[i + 1]);
+    }
+    B3_TRY(c->work_d.ensure(work.size() * sizeof(int2)));
+    B3_TRY(c->cu_d.ensure(key.size() * sizeof(int32_t)));
+    B3_CUDA(cudaMemcpyAsync(c->work_d.p, work.data(), work.size() * sizeof(int2), cudaMemcpyHostToDevice, c->stream));
+    B3_CUDA(cudaMemcpyAsync(c->seg_d.p, seg.data(), seg.size() * sizeof(int2), cudaMemcpyHostToDevice, c->stream));
+    B3_CUDA(cudaMemcpyAsync(c->cu_d.p, key.data(), key.size() * sizeof(int32_t), cudaMemcpyHostToDevice, c->stream));
+    B3_CUDA(cudaStreamSynchronize(c->stream));
+    c->plan.cu = key;
+    c->plan.M = M;
+    c->plan.tmax = tmax;
+    c->plan.n_work = static_cast<int>(work.size());
+    return 0;
+}
+
+// ───────────────────────────── forward ─────────────────────────────
+
+// Attention section of block L: x += o_proj(MHSA(LN_att(x))).
+int attention_section(b3_ctx* c, const Layer& L, int M) {
+    float* x = c->x.as<float>();
+    __half* a16 = c->a16.as<__half>();
+    __half* qkv = c->qkv16.as<__half>();
+    const int tmax = c->plan.tmax;
+    B3_TRY(launch_layernorm(x, M, L.ln_w(1), L.ln_b(1), nullptr, nullptr, nullptr, a16, c->stream));
+    GemmParams pq = params_f16(qkv, 4096);
+    pq.bias_u = L.bu();
+    pq.bias_v = L.bv();
+    B3_TRY(run_gemm(c, L.qkv, a16, M, kHidden, EPI_QKV, pq));
+    // R = pos[positions tmax-1 .. -(tmax-1)] . W_relk^T  (rounded to f16)
+    const int prow0 = c->tcap - tmax;
+    const int prows = 2 * tmax - 1;
+    const __half* pos = c->pos16.as<__half>() + static_cast<size_t>(prow0) * kHidden;
+    B3_TRY(run_gemm(c, L.relk, pos, prows, kHidden, EPI_F16, params_f16(c->R16.as<__half>(), kHidden)));
+    AttnParams ap;
+    ap.qkv = qkv;
+    ap.R = c->R16.as<__half>();
+    ap.r_center = tmax - 1;
+    ap.r_rows = prows;
+    ap.cu = c->cu_d.as<int>();
+    ap.work = c->work_d.as<int2>();
+    ap.out = a16;
+    ap.scale_log2 = 1.4426950408889634f / std::sqrt(128.0f);
+    B3_TRY(launch_attention(ap, c->plan.n_work, c->stream));
+    return run_gemm(c, L.o, a16, M, kHidden, EPI_RESID, params_resid(x, 1.0f));
+}
+
+// Conv section of block L: x += pw2(SiLU(BN(dwconv(GLU(pw1(LN_conv(x))))))).
+int conv_section(b3_ctx* c, const Layer& L, int M) {
+    float* x = c->x.as<float>();
+    __half* a16 = c->a16.as<__half>();
+    __half* g16 = c->g16.as<__half>();
+    B3_TRY(launch_layernorm(x, M, L.ln_w(2), L.ln_b(2), nullptr, nullptr, nullptr, a16, c->stream));
+    B3_TRY(run_gemm(c, L.pw1, a16, M, kHidden, EPI_GLU_F16, params_f16(g16, kHidden)));
+    B3_TRY(launch_dwconv(g16, c->seg_d.as<int2>(), M, L.dw_t(), L.bn_a(), L.bn_b(), a16, c->stream));
+    return run_gemm(c, L.pw2, a16, M, kHidden, EPI_RESID, params_resid(x, 1.0f));
+}
+
+// FFN half: x += 0.5 * W2 SiLU(W1 a16), a16 already holding LN(x).
+int ffn_half(b3_ctx* c, const Linear& w1, const Linear& w2, int M) {
+    B3_TRY(run_gemm(c, w1, c->a16.as<__half>(), M, kHidden, EPI_SILU_F16, params_f16(c->h16.as<__half>(), kFfn)));
+    return run_gemm(c, w2, c->h16.as<__half>(), M, kFfn, EPI_RESID, params_resid(c->x.as<float>(), 0.5f));
+}
+
+// sub16 holds the f16 input; runs `layers` blocks.  After the call:
+//   layers == n_layers: a16 = f16(norm_out(x)) of the last block, x = norm_out(x)
+//   otherwise:          x = pre-norm_out residual of block layers-1
+int forward_blocks(b3_ctx* c, int M, int layers) {
+    float* x = c->x.as<float>();
+    __half* a16 = c->a16.as<__half>();
+    B3_TRY(run_gemm(c, c->sub_w, c->sub16.as<__half>(), M, kSubIn, EPI_F32,
+                    params_f32(x, kHidden, c->sub_b.as<float>())));
+    const int upto = layers < c->n_layers ? layers : c->n_layers;
+    if (upto > 0) {
+        const Layer& L0 = c->layers[0];
+        B3_TRY(launch_layernorm(x, M, L0.ln_w(0), L0.ln_b(0), nullptr, nullptr, nullptr, a16, c->stream));
+    }
+    for (int i = 0; i < upto; ++i) {
+        const Layer& L = c->layers[i];
+        // a16 = LN_ff1(x) on entry
+        B3_TRY(ffn_half(c, L.ff1a, L.ff1b, M));
+        B3_TRY(attention_section(c, L, M));
+        B3_TRY(conv_section(c, L, M));
+        B3_TRY(launch_layernorm(x, M, L.ln_w(3), L.ln_b(3), nullptr, nullptr, nullptr, a16, c->stream));
+        B3_TRY(ffn_half(c, L.ff2a, L.ff2b, M));
+        const bool last = (i + 1 == upto);
+        if (!last) {
+            const Layer& N = c->layers[i + 1];
+            B3_TRY(launch_layernorm(x, M, L.ln_w(4), L.ln_b(4), x, N.ln_w(0), N.ln_b(0), a16, c->stream));
+        } else if (upto == c->n_layers) {
+            B3_TRY(launch_layernorm(x, M, L.ln_w(4), L.ln_b(4), x, nullptr, nullptr, a16, c->stream));
+        }
+    }
+    if (upto == 0 && c->n_layers == 0)
+        return set_error(B3_ESTATE, "encoder has no blocks");
+    return 0;
+}
+
+int check_finalized(b3_ctx* c) {
+    if (!c) return set_error(B3_EINVAL, "null context");
+    if (!c->finalized) return set_error(B3_ESTATE, "b3_finalize has not been called");
+    return 0;
+}
+
+int sync_and_check(b3_ctx* c) {
+    B3_CUDA(cudaStreamSynchronize(c->stream));
+    unsigned int flag = 0;
+    B3_TRY(gemm_take_dev_error(c->stream, &flag));
+    if (flag) return set_error(B3_ETIMEOUT, "device wait ran out (code 0x%x)", flag);
+    return 0;
+}
+
+// Encode rows already in device memory: sub (f32 [M][4096]) -> out.
+int encode_device(b3_ctx* c, const float* sub, int M, int layers, float* out) {
+    B3_TRY(launch_f32_to_f16(sub, c->sub16.as<__half>(), static_cast<int64_t>(M) * kSubIn, c->stream));
+    B3_TRY(forward_blocks(c, M, layers));
+    if (layers >= c->n_layers) {
+        B3_TRY(run_gemm(c, c->proj_w, c->a16.as<__half>(), M, kHidden, EPI_F32,
+                        params_f32(out, kProj, c->proj_b.as<float>())));
+    } else {
+        B3_CUDA(cudaMemcpyAsync(out, c->x.p, static_cast<size_t>(M) * kHidden * 4, cudaMemcpyDeviceToDevice, c->stream));
+    }
+    return 0;
+}
+
+int encode_any(b3_ctx* c, const float* sub, const int32_t* cu, int n_utt, int layers, float* out,
+               unsigned flags) {
+    B3_TRY(check_finalized(c));
+    if (!sub || !out || !cu) return set_error(B3_EINVAL, "null buffer");
+    DeviceGuard g(c->device);
+    B3_TRY(make_plan(c, cu, n_utt));
+    const int M = c->plan.M;
+    const int out_cols = layers >= c->n_layers ? kProj : kHidden;
+    if (flags & B3_DEVICE_PTRS) return encode_device(c, sub, M, layers, out);
+    const size_t in_bytes = static_cast<size_t>(M) * kSubIn * 4;
+    const size_t out_bytes = static_cast<size_t>(M) * out_cols * 4;
+    B3_TRY(c->io_in.ensure(in_bytes));
+    B3_TRY(c->io_out.ensure(out_bytes));
+    B3_CUDA(cudaMemcpyAsync(c->io_in.p, sub, in_bytes, cudaMemcpyHostToDevice, c->stream));
+    B3_TRY(encode_device(c, c->io_in.as<float>(), M, layers, c->io_out.as<float>()));
+    B3_CUDA(cudaMemcpyAsync(out, c->io_out.p, out_bytes, cudaMemcpyDeviceToHost, c->stream));
+    return sync_and_check(c);
+}
+
+// Single linear (configs 1 / lbtest): c = a . W^T (+ bias), W given per call.
+int linear_any(b3_ctx* c, const float* a, const void* w, const uint16_t* lut16, bool lut,
+               const float* bias, float* out, int m, int n, int k, unsigned flags) {
+    if (!c) return set_error(B3_EINVAL, "null context");
+    if (!a || !w || !out || (lut && !lut16)) return set_error(B3_EINVAL, "null buffer");
+    if (m <= 0 || n <= 0 || k <= 0 || k % 64 || n % 128)
+        return set_error(B3_EINVAL, "linear shape m=%d n=%d k=%d (need k %% 64 == 0, n %% 128 == 0)", m, n, k);
+    DeviceGuard g(c->device);
+    const bool dev = flags & B3_DEVICE_PTRS;
+    const size_t a_bytes = static_cast<size_t>(m) * k * 4;
+    const size_t w_bytes = lut ? static_cast<size_t>(n) * k / 2 : static_cast<size_t>(n) * k * 2;
+    const size_t lut_bytes = lut ? static_cast<size_t>(n) * 32 : 0;
+    const size_t bias_bytes = bias ? static_cast<size_t>(n) * 4 : 0;
+    const size_t c_bytes = static_cast<size_t>(m) * n * 4;
+    const float* da = a;
+    const void* dw = w;
+    const uint16_t* dl = lut16;
+    const float* db = bias;
+    float* dc = out;
+    if (!dev) {
+        // one staging block: a | w | lut | bias | c (each 256-byte aligned)
+        auto al = [](size_t v) { return (v + 255) & ~static_cast<size_t>(255); };
+        const size_t total = al(a_bytes) + al(w_bytes) + al(lut_bytes) + al(bias_bytes) + al(c_bytes);
+        B3_TRY(c->io_in.ensure(total));
+        char* base = c->io_in.as<char>();
+        size_t off = 0;
+        auto put = [&](const void* src, size_t bytes) -> char* {
+            char* d = base + off;
+            off += al(bytes);
+            if (src && bytes) cudaMemcpyAsync(d, src, bytes, cudaMemcpyHostToDevice, c->stream);
+            return d;
+        };
+        da = reinterpret_cast<const float*>(put(a, a_bytes));
+        dw = put(w, w_bytes);
+        dl = lut ? reinterpret_cast<const uint16_t*>(put(lut16, lut_bytes)) : nullptr;
+        db = bias ? reinterpret_cast<const float*>(put(bias, bias_bytes)) : nullptr;
+        dc = reinterpret_cast<float*>(put(nullptr, c_bytes));
+    }
+    B3_TRY(c->scratch16.ensure(static_cast<size_t>(m) * k * 2));
+    B3_TRY(launch_f32_to_f16(da, c->scratch16.as<__half>(), static_cast<int64_t>(m) * k, c->stream));
+    GemmOp op;
+    B3_TRY(gemm_make_a_map(&op.map_a, c->scratch16.as<__half>(), m, k, k));
+    B3_TRY(gemm_make_b_map(&op.map_b, dw, lut, n, k, 128));
+    op.p = params_f32(dc, n, db);
+    op.p.M = m;
+    op.p.N = n;
+    op.p.K = k;
+    op.p.lut = dl;
+    op.lut = lut;
+    op.bn = 128;
+    op.epi = EPI_F32;
+    B3_TRY(gemm_launch(op, c->stream));
+    if (dev) return 0;
+    B3_CUDA(cudaMemcpyAsync(out, dc, c_bytes, cudaMemcpyDeviceToHost, c->stream));
+    return sync_and_check(c);
+}
+
+}  // namespace
+
+// ───────────────────────────── C ABI ─────────────────────────────
+
+extern "C" {
+
+const char* b3_last_error(void) { return b3::g_last_error; }
+
+int b3_version(void) { return 100; }
+
+b3_ctx* b3_create(int device) {
+    clear_error();
+    int n = 0;
+    cudaError_t e = cudaGetDeviceCount(&n);
+    if (e != cudaSuccess || device < 0 || device >= n) {
+        set_error(B3_ECUDA, "no CUDA device %d (%s)", device, cudaGetErrorString(e));
+        return nullptr;
+    }
+    cudaDeviceProp prop;
+    if (cudaGetDeviceProperties(&prop, device) != cudaSuccess || prop.major != 10) {
+        set_error(B3_ECUDA, "device %d is not an sm_100 (Blackwell B200) GPU", device);
+        return nullptr;
+    }
+    DeviceGuard g(device);
+    b3_ctx* c = new (std::nothrow) b3_ctx();
+    if (!c) {
+        set_error(B3_ENOMEM, "out of host memory");
+        return nullptr;
+    }
+    c->device = device;
+    if (cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking) != cudaSuccess) {
+        set_error(B3_ECUDA, "cudaStreamCreate failed");
+        delete c;
+        return nullptr;
+    }
+    // inverse frequencies exactly as src/encoder.rs:231-234 computes them (f32)
+    float inv[512];
+    for (int i = 0; i < 512; ++i) inv[i] = 1.0f / powf(10000.0f, (2.0f * static_cast<float>(i)) / 1024.0f);
+    if (upload(c->inv_freq, inv, sizeof(inv), c->stream) || cudaStreamSynchronize(c->stream) != cudaSuccess) {
+        delete c;
+        return nullptr;
+    }
+    return c;
+}
+
+void b3_destroy(b3_ctx* ctx) {
+    if (!ctx) return;
+    DeviceGuard g(ctx->device);
+    cudaStreamSynchronize(ctx->stream);
+    delete ctx;
+}
+
+int b3_sync(b3_ctx* ctx) {
+    if (!ctx) return set_error(B3_EINVAL, "null context");
+    DeviceGuard g(ctx->device);
+    return sync_and_check(ctx);
+}
+
+void* b3_stream(b3_ctx* ctx) { return ctx ? static_cast<void*>(ctx->stream) : nullptr; }
+
+int b3_load_tensor(b3_ctx* ctx, const char* name, int dtype, const int64_t* shape, int ndim,
+                   const void* data) {
+    if (!ctx || !name || !data || (ndim > 0 && !shape) || ndim < 0 || ndim > 8)
+        return set_error(B3_EINVAL, "b3_load_tensor: bad arguments");
+    if (ctx->finalized) return set_error(B3_ESTATE, "weights are already finalized");
+    Staged s;
+    s.shape.assign(shape, shape + ndim);
+    int64_t n = 1;
+    for (int i = 0; i < ndim; ++i) {
+        if (shape[i] < 0) return set_error(B3_EINVAL, "%s: negative dimension", name);
+        n *= shape[i];
+    }
+    s.f32.resize(n);
+    s.f16.resize(n);
+    for (int64_t i = 0; i < n; ++i) {
+        float v;
+        switch (dtype) {
+            case B3_DTYPE_F32: v = static_cast<const float*>(data)[i]; break;
+            case B3_DTYPE_F16: v = f16_bits_to_f32(static_cast<const uint16_t*>(data)[i]); break;
+            case B3_DTYPE_BF16: v = bf16_bits_to_f32(static_cast<const uint16_t*>(data)[i]); break;
+            default: return set_error(B3_EINVAL, "%s: unknown dtype %d", name, dtype);
+        }
+        s.f32[i] = v;
+        s.f16[i] = dtype == B3_DTYPE_F16 ? static_cast<const uint16_t*>(data)[i] : f32_to_f16_bits(v);
+    }
+    ctx->staged[name] = std::move(s);
+    return 0;
+}
+
+int b3_load_lowbit(b3_ctx* ctx, const char* name, const uint8_t* codes, const uint16_t* lut16, int rows,
+                   int cols) {
+    if (!ctx || !name || !codes || !lut16 || rows <= 0 || cols <= 0 || (cols & 1))
+        return set_error(B3_EINVAL, "b3_load_lowbit: bad arguments");
+    if (ctx->finalized) return set_error(B3_ESTATE, "weights are already finalized");
+    Staged s;
+    s.lowbit = true;
+    s.rows = rows;
+    s.cols = cols;
+    s.shape = {rows, cols};
+    s.codes.assign(codes, codes + static_cast<size_t>(rows) * cols / 2);
+    s.lut16.assign(lut16, lut16 + static_cast<size_t>(rows) * 16);
+    ctx->staged[name] = std::move(s);
+    return 0;
+}
+
+int b3_load_lowbit_levels(b3_ctx* ctx, const char* name, const uint32_t* code_words, const uint16_t* levels,
+                          int k, int rows, int cols) {
+    if (!ctx || !name || !code_words || !levels || rows <= 0 || cols <= 0 || (cols & 1))
+        return set_error(B3_EINVAL, "b3_load_lowbit_levels: bad arguments");
+    if (k < 1 || k > 3) return set_error(B3_EINVAL, "%s: unsupported level count %d", name, k);
+    const int ld = (cols + 7) / 8;
+    std::vector<uint8_t> codes(static_cast<size_t>(rows) * cols / 2);
+    std::vector<uint16_t> tab(static_cast<size_t>(rows) * 16, 0);
+    for (int r = 0; r < rows; ++r) {
+        const uint8_t* wb = reinterpret_cast<const uint8_t*>(code_words + static_cast<size_t>(r) * ld);
+        memcpy(&codes[static_cast<size_t>(r) * cols / 2], wb, cols / 2);
+        const uint16_t* lev = levels + static_cast<size_t>(r) * 4;
+        for (int code = 1; code <= 2 * k; ++code) {
+            const bool neg = code > k;
+            const uint16_t mag = lev[neg ? code - k - 1 : code - 1];
+            tab[static_cast<size_t>(r) * 16 + code] = neg ? static_cast<uint16_t>(mag ^ 0x8000u) : mag;
+        }
+    }
+    return b3_load_lowbit(ctx, name, codes.data(), tab.data(), rows, cols);
+}
+
+int b3_finalize(b3_ctx* ctx, int n_layers) {
+    if (!ctx) return set_error(B3_EINVAL, "null context");
+    if (ctx->finalized) return set_error(B3_ESTATE, "already finalized");
+    if (n_layers < 1 || n_layers > 64) return set_error(B3_EINVAL, "n_layers %d out of range", n_layers);
+    DeviceGuard g(ctx->device);
+    std::vector<float> v;
+    B3_TRY(build_linear(ctx, ctx->sub_w, {"encoder.subsampling.linear.weight"}, kHidden, kSubIn, false, 128));
+    B3_TRY(get_vec(ctx, "encoder.subsampling.linear.bias", kHidden, v));
+    B3_TRY(upload(ctx->sub_b, v.data(), v.size() * 4, ctx->stream));
+    B3_TRY(build_linear(ctx, ctx->proj_w, {"encoder_projector.weight"}, kProj, kHidden, false, 128));
+    B3_TRY(get_vec(ctx, "encoder_projector.bias", kProj, v));
+    B3_TRY(upload(ctx->proj_b, v.data(), v.size() * 4, ctx->stream));
+    ctx->layers.resize(n_layers);
+    for (int l = 0; l < n_layers; ++l) {
+        Layer& L = ctx->layers[l];
+        const std::string p = "encoder.layers." + std::to_string(l) + ".";
+        B3_TRY(build_linear(ctx, L.qkv, {p + "self_attn.q_proj.weight", p + "self_attn.k_proj.weight",
+                                         p + "self_attn.v_proj.weight"}, kHidden, kHidden, false, 128));
+        B3_TRY(build_linear(ctx, L.relk, {p + "self_attn.relative_k_proj.weight"}, kHidden, kHidden, false, 128));
+        B3_TRY(build_linear(ctx, L.o, {p + "self_attn.o_proj.weight"}, kHidden, kHidden, false, 128));
+        B3_TRY(build_linear(ctx, L.ff1a, {p + "feed_forward1.linear1.weight"}, kFfn, kHidden, false, 128));
+        B3_TRY(build_linear(ctx, L.ff1b, {p + "feed_forward1.linear2.weight"}, kHidden, kFfn, false, 128));
+        B3_TRY(build_linear(ctx, L.ff2a, {p + "feed_forward2.linear1.weight"}, kFfn, kHidden, false, 128));
+        B3_TRY(build_linear(ctx, L.ff2b, {p + "feed_forward2.linear2.weight"}, kHidden, kFfn, false, 128));
+        B3_TRY(build_linear(ctx, L.pw1, {p + "conv.pointwise_conv1.weight"}, 2 * kHidden, kHidden, true, 128));
+        B3_TRY(build_linear(ctx, L.pw2, {p + "conv.pointwise_conv2.weight"}, kHidden, kHidden, false, 128));
+        std::vector<float> prm(Layer::kParamFloats, 0.f);
+        // depthwise taps rounded through f16 like every other weight
+        // (src/cpu/mod.rs:101), stored tap-major for coalesced loads
+        B3_TRY(get_vec(ctx, p + "conv.depthwise_conv.weight", kHidden * 9, v));
+        for (int c = 0; c < kHidden; ++c)
+            for (int i = 0; i < 9; ++i) prm[i * kHidden + c] = f16_bits_to_f32(f32_to_f16_bits(v[c * 9 + i]));
+        std::vector<float> gam, bet, mu, var;
+        B3_TRY(get_vec(ctx, p + "conv.norm.weight", kHidden, gam));
+        B3_TRY(get_vec(ctx, p + "conv.norm.bias", kHidden, bet));
+        B3_TRY(get_vec(ctx, p + "conv.norm.running_mean", kHidden, mu));
+        B3_TRY(get_vec(ctx, p + "conv.norm.running_var", kHidden, var));
+        for (int c = 0; c < kHidden; ++c) {  // BN fold, src/cpu/mod.rs:113-119
+            const float a = gam[c] / sqrtf(var[c] + 1e-5f);
+            prm[9 * kHidden + c] = a;
+            prm[10 * kHidden + c] = bet[c] - mu[c] * a;
+        }
+        const char* norms[5] = {"norm_feed_forward1", "norm_self_att", "norm_conv", "norm_feed_forward2", "norm_out"};
+        for (int i = 0; i < 5; ++i) {
+            B3_TRY(get_vec(ctx, p + norms[i] + ".weight", kHidden, v));
+            memcpy(&prm[(11 + i) * kHidden], v.data(), kHidden * 4);
+            B3_TRY(get_vec(ctx, p + norms[i] + ".bias", kHidden, v));
+            memcpy(&prm[(16 + i) * kHidden], v.data(), kHidden * 4);
+        }
+        B3_TRY(get_vec(ctx, p + "self_attn.bias_u", kHidden, v));
+        memcpy(&prm[21 * kHidden], v.data(), kHidden * 4);
+        B3_TRY(get_vec(ctx, p + "self_attn.bias_v", kHidden, v));
+        memcpy(&prm[22 * kHidden], v.data(), kHidden * 4);
+        B3_TRY(upload(L.params, prm.data(), prm.size() * 4, ctx->stream));
+        B3_CUDA(cudaStreamSynchronize(ctx->stream));
+    }
+    ctx->n_layers = n_layers;
+    ctx->finalized = true;
+    ctx->staged.clear();
+    return 0;
+}
+
+int b3_encode(b3_ctx* ctx, const float* sub, int t, int layers, float* out, unsigned flags) {
+    if (t <= 0) return set_error(B3_EINVAL, "t must be positive");
+    if (layers < 0) return set_error(B3_EINVAL, "layers must be >= 0");
+    int32_t cu[2] = {0, t};
+    return encode_any(ctx, sub, cu, 1, layers, out, flags);
+}
+
+int b3_encode_batch(b3_ctx* ctx, const float* sub, const int32_t* cu_seqlens, int n_utt, float* pooler,
+                    unsigned flags) {
+    if (!ctx) return set_error(B3_EINVAL, "null context");
+    return encode_any(ctx, sub, cu_seqlens, n_utt, ctx->n_layers, pooler, flags);
+}
+
+int b3_linear_lut4(b3_ctx* ctx, const float* a, const uint8_t* codes, const uint16_t* lut16, const float* bias,
+                   float* c, int m, int n, int k, unsigned flags) {
+    return linear_any(ctx, a, codes, lut16, true, bias, c, m, n, k, flags);
+}
+
+int b3_linear_f16(b3_ctx* ctx, const float* a, const uint16_t* w16, const float* bias, float* c, int m, int n,
+                  int k, unsigned flags) {
+    return linear_any(ctx, a, w16, nullptr, false, bias, c, m, n, k, flags);
+}
+
+int b3_attn_conv(b3_ctx* ctx, int layer, float* x, int t, unsigned flags) {
+    B3_TRY(check_finalized(ctx));
+    if (layer < 0 || layer >= ctx->n_layers) return set_error(B3_EINVAL, "layer %d out of range", layer);
+    if (!x || t <= 0) return set_error(B3_EINVAL, "bad input");
+    DeviceGuard g(ctx->device);
+    int32_t cu[2] = {0, t};
+    B3_TRY(make_plan(ctx, cu, 1));
+    const size_t bytes = static_cast<size_t>(t) * kHidden * 4;
+    const Layer& L = ctx->layers[layer];
+    if (flags & B3_DEVICE_PTRS) {
+        B3_CUDA(cudaMemcpyAsync(ctx->x.p, x, bytes, cudaMemcpyDeviceToDevice, ctx->stream));
+    } else {
+        B3_CUDA(cudaMemcpyAsync(ctx->x.p, x, bytes, cudaMemcpyHostToDevice, ctx->stream));
+    }
+    B3_TRY(attention_section(ctx, L, t));
+    B3_TRY(conv_section(ctx, L, t));
+    if (flags & B3_DEVICE_PTRS) {
+        B3_CUDA(cudaMemcpyAsync(x, ctx->x.p, bytes, cudaMemcpyDeviceToDevice, ctx->stream));
+        return 0;
+    }
+    B3_CUDA(cudaMemcpyAsync(x, ctx->x.p, bytes, cudaMemcpyDeviceToHost, ctx->stream));
+    return sync_and_check(ctx);
+}
+
+}  // extern "C"

@@ -1,0 +1,252 @@
+// norm_conv.cu — the memory-bound encoder kernels.
+//
+//   K4  LayerNorm over 1024 channels, one warp per frame, 16-byte loads,
+//       shuffle reductions; optionally two norms back to back (a block's
+//       norm_out followed by the next block's first pre-norm) in one pass.
+//   K3b depthwise conv over time (k = 9, zero padding 4, utterance edges
+//       treated as padding) + folded BatchNorm + SiLU.
+//   plus the f32 -> f16 conversion of encoder inputs and the sinusoidal
+//   relative-position table.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "b3_internal.h"
+#include "b3_kernels.h"
+
+namespace b3 {
+
+namespace {
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// Two-pass mean / variance over the 32 values a lane holds (1024 per warp).
+__device__ __forceinline__ void ln_stats(const float (&v)[32], float& mean, float& rstd) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) s += v[i];
+    mean = warp_sum(s) * (1.0f / 1024.0f);
+    float q = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        const float d = v[i] - mean;
+        q += d * d;
+    }
+    const float var = warp_sum(q) * (1.0f / 1024.0f);
+    rstd = rsqrtf(var + 1e-5f);
+}
+
+// lane holds channels c = 4*lane + 128*i + j  (i = 0..7, j = 0..3)
+__global__ void __launch_bounds__(256) k4_layernorm(const float* __restrict__ x, int rows,
+                                                    const float* __restrict__ w1,
+                                                    const float* __restrict__ b1,
+                                                    float* __restrict__ y32,
+                                                    const float* __restrict__ w2,
+                                                    const float* __restrict__ b2,
+                                                    __half* __restrict__ y16) {
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= rows) return;
+    const float4* xr = reinterpret_cast<const float4*>(x + static_cast<size_t>(row) * 1024);
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 t = xr[lane + 32 * i];
+        v[4 * i] = t.x;
+        v[4 * i + 1] = t.y;
+        v[4 * i + 2] = t.z;
+        v[4 * i + 3] = t.w;
+    }
+    float mean, rstd;
+    ln_stats(v, mean, rstd);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float4 w = __ldg(reinterpret_cast<const float4*>(w1) + lane + 32 * i);
+        const float4 b = __ldg(reinterpret_cast<const float4*>(b1) + lane + 32 * i);
+        v[4 * i] = (v[4 * i] - mean) * rstd * w.x + b.x;
+        v[4 * i + 1] = (v[4 * i + 1] - mean) * rstd * w.y + b.y;
+        v[4 * i + 2] = (v[4 * i + 2] - mean) * rstd * w.z + b.z;
+        v[4 * i + 3] = (v[4 * i + 3] - mean) * rstd * w.w + b.w;
+    }
+    if (y32) {
+        float4* yr = reinterpret_cast<float4*>(y32 + static_cast<size_t>(row) * 1024);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            yr[lane + 32 * i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    }
+    if (y16) {
+        if (w2) {
+            ln_stats(v, mean, rstd);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float4 w = __ldg(reinterpret_cast<const float4*>(w2) + lane + 32 * i);
+                const float4 b = __ldg(reinterpret_cast<const float4*>(b2) + lane + 32 * i);
+                v[4 * i] = (v[4 * i] - mean) * rstd * w.x + b.x;
+                v[4 * i + 1] = (v[4 * i + 1] - mean) * rstd * w.y + b.y;
+                v[4 * i + 2] = (v[4 * i + 2] - mean) * rstd * w.z + b.z;
+                v[4 * i + 3] = (v[4 * i + 3] - mean) * rstd * w.w + b.w;
+            }
+        }
+        uint2* yr = reinterpret_cast<uint2*>(y16 + static_cast<size_t>(row) * 1024);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            __half2 a = __floats2half2_rn(v[4 * i], v[4 * i + 1]);
+            __half2 b = __floats2half2_rn(v[4 * i + 2], v[4 * i + 3]);
+            yr[lane + 32 * i] = make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+        }
+    }
+}
+
+// Depthwise conv k=9 + BN(a, b) + SiLU.  Block: 128 threads x 8 channels =
+// all 1024 channels of kRows consecutive frames.  Frame t reads t-4 .. t+4
+// inside its own utterance [seg.x, seg.y); anything outside is zero.
+constexpr int kDwRows = 16;
+
+__global__ void __launch_bounds__(128) k3_dwconv_bn_silu(const __half* __restrict__ src,
+                                                         const int2* __restrict__ seg, int rows,
+                                                         const float* __restrict__ dw_t,  // [9][1024]
+                                                         const float* __restrict__ bn_a,
+                                                         const float* __restrict__ bn_b,
+                                                         __half* __restrict__ dst) {
+    const int c0 = threadIdx.x * 8;
+    const int t0 = blockIdx.x * kDwRows;
+    float w[9][8];
+#pragma unroll
+    for (int i = 0; i < 9; ++i) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(dw_t + i * 1024 + c0));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(dw_t + i * 1024 + c0 + 4));
+        w[i][0] = a.x; w[i][1] = a.y; w[i][2] = a.z; w[i][3] = a.w;
+        w[i][4] = b.x; w[i][5] = b.y; w[i][6] = b.z; w[i][7] = b.w;
+    }
+    float ba[8], bb[8];
+    {
+        const float4 a0 = __ldg(reinterpret_cast<const float4*>(bn_a + c0));
+        const float4 a1 = __ldg(reinterpret_cast<const float4*>(bn_a + c0 + 4));
+        const float4 b0 = __ldg(reinterpret_cast<const float4*>(bn_b + c0));
+        const float4 b1 = __ldg(reinterpret_cast<const float4*>(bn_b + c0 + 4));
+        ba[0] = a0.x; ba[1] = a0.y; ba[2] = a0.z; ba[3] = a0.w;
+        ba[4] = a1.x; ba[5] = a1.y; ba[6] = a1.z; ba[7] = a1.w;
+        bb[0] = b0.x; bb[1] = b0.y; bb[2] = b0.z; bb[3] = b0.w;
+        bb[4] = b1.x; bb[5] = b1.y; bb[6] = b1.z; bb[7] = b1.w;
+    }
+    // rolling window of 9 input frames (8 channels each)
+    float win[9][8];
+#pragma unroll
+    for (int i = 0; i < 9; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) win[i][j] = 0.f;
+    auto load = [&](int t, float (&dst8)[8]) {
+        if (t >= 0 && t < rows) {
+            const uint4 u = *reinterpret_cast<const uint4*>(src + static_cast<size_t>(t) * 1024 + c0);
+            const __half2* h = reinterpret_cast<const __half2*>(&u);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const float2 f = __half22float2(h[j]);
+                dst8[2 * j] = f.x;
+                dst8[2 * j + 1] = f.y;
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) dst8[j] = 0.f;
+        }
+    };
+#pragma unroll
+    for (int i = 0; i < 8; ++i) load(t0 - 4 + i, win[i + 1]);
+#pragma unroll 1
+    for (int r = 0; r < kDwRows; ++r) {
+        const int t = t0 + r;
+        if (t >= rows) break;
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) win[i][j] = win[i + 1][j];
+        load(t + 4, win[8]);
+        const int2 sg = __ldg(seg + t);
+        float acc[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+#pragma unroll
+        for (int i = 0; i < 9; ++i) {
+            const int tt = t + i - 4;
+            if (tt < sg.x || tt >= sg.y) continue;
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[j] += win[i][j] * w[i][j];
+        }
+        uint32_t o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            float y0 = acc[2 * j] * ba[2 * j] + bb[2 * j];
+            float y1 = acc[2 * j + 1] * ba[2 * j + 1] + bb[2 * j + 1];
+            y0 = y0 / (1.0f + __expf(-y0));
+            y1 = y1 / (1.0f + __expf(-y1));
+            __half2 h = __floats2half2_rn(y0, y1);
+            o[j] = *reinterpret_cast<uint32_t*>(&h);
+        }
+        *reinterpret_cast<uint4*>(dst + static_cast<size_t>(t) * 1024 + c0) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+}
+
+__global__ void k_f32_to_f16(const float4* __restrict__ src, uint2* __restrict__ dst, int64_t n4) {
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+        const float4 v = src[i];
+        __half2 a = __floats2half2_rn(v.x, v.y);
+        __half2 b = __floats2half2_rn(v.z, v.w);
+        dst[i] = make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+    }
+}
+
+// Row j is relative position (tcap - 1 - j): [sin, cos] interleaved with the
+// reference's f32 inverse frequencies (src/encoder.rs:228-246).
+__global__ void k_pos_table(const float* __restrict__ inv_freq, int tcap, int rows,
+                            __half2* __restrict__ out) {
+    const int j = blockIdx.x;
+    if (j >= rows) return;
+    const float pos = static_cast<float>(tcap - 1 - j);
+    for (int i = threadIdx.x; i < 512; i += blockDim.x) {
+        const float f = pos * inv_freq[i];
+        out[static_cast<size_t>(j) * 512 + i] = __floats2half2_rn(sinf(f), cosf(f));
+    }
+}
+
+}  // namespace
+
+int launch_layernorm(const float* x, int rows, const float* w1, const float* b1, float* y32,
+                     const float* w2, const float* b2, __half* y16, cudaStream_t st) {
+    if (rows <= 0) return 0;
+    k4_layernorm<<<(rows + 7) / 8, 256, 0, st>>>(x, rows, w1, b1, y32, w2, b2, y16);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : set_cuda_error("k4_layernorm", e);
+}
+
+int launch_dwconv(const __half* src, const int2* seg, int rows, const float* dw_t, const float* bn_a,
+                  const float* bn_b, __half* dst, cudaStream_t st) {
+    if (rows <= 0) return 0;
+    k3_dwconv_bn_silu<<<(rows + kDwRows - 1) / kDwRows, 128, 0, st>>>(src, seg, rows, dw_t, bn_a, bn_b, dst);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : set_cuda_error("k3_dwconv_bn_silu", e);
+}
+
+int launch_f32_to_f16(const float* src, __half* dst, int64_t n, cudaStream_t st) {
+    if (n <= 0) return 0;
+    if (n % 4) return set_error(B3_EINVAL, "f32->f16 length %lld not a multiple of 4", (long long)n);
+    const int64_t n4 = n / 4;
+    int blocks = static_cast<int>((n4 + 255) / 256);
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    k_f32_to_f16<<<blocks, 256, 0, st>>>(reinterpret_cast<const float4*>(src), reinterpret_cast<uint2*>(dst), n4);
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : set_cuda_error("k_f32_to_f16", e);
+}
+
+int launch_pos_table(const float* inv_freq, int tcap, int rows, __half* out, cudaStream_t st) {
+    if (rows <= 0) return 0;
+    k_pos_table<<<rows, 256, 0, st>>>(inv_freq, tcap, rows, reinterpret_cast<__half2*>(out));
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : set_cuda_error("k_pos_table", e);
+}
+
+}  // namespace b3

@@ -1,0 +1,145 @@
+/*
+ * bark3_b200.h — C ABI of the B200 (sm_100a) encoder for bark3-wgpu.
+ *
+ * This is the drop-in boundary for the reference crate's encoder seam.  A Rust
+ * (or any FFI) host binds these `extern "C"` functions in place of the wgpu
+ * encoder; everything is plain pointers, sizes and integer status codes.
+ *
+ * Conventions
+ *   - Every function returns 0 (B3_OK) or a negative B3_E* code.  The message
+ *     for the most recent failure on the calling thread is b3_last_error().
+ *     Nothing aborts or throws across this boundary (the reference panics on a
+ *     missing tensor, src/encoder.rs:419; this ABI returns B3_ENOTFOUND).
+ *   - Host buffers are borrowed for the duration of the call.  Device weights
+ *     and the activation arena belong to the context.
+ *   - One context per GPU; calls on one context must be serialised (the
+ *     reference AsrInference is effectively !Sync, src/encoder/prof.rs:22-28,
+ *     src/gpu.rs:608).  Use one host thread per context for several GPUs.
+ *   - With B3_DEVICE_PTRS the data pointers are device pointers on the
+ *     context's GPU and the call only enqueues work on the context stream;
+ *     b3_sync() waits for it.  Without the flag the pointers are host memory
+ *     and the call returns when the results are in host memory.
+ *   - Layouts: row-major, f32 unless stated.  f16 / bf16 are raw 16-bit
+ *     patterns (uint16_t).
+ */
+#ifndef BARK3_B200_H
+#define BARK3_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B3_OK 0
+#define B3_EINVAL (-1)     /* bad argument, shape or layout */
+#define B3_ENOMEM (-2)     /* host or device allocation failed */
+#define B3_ECUDA (-3)      /* CUDA runtime / driver error */
+#define B3_ETIMEOUT (-4)   /* a device-side bounded wait ran out */
+#define B3_ESTATE (-5)     /* call out of order (e.g. encode before finalize) */
+#define B3_ENOTFOUND (-6)  /* a required tensor was never loaded */
+
+#define B3_DEVICE_PTRS 1u  /* data pointers are device pointers (async) */
+
+/* Tensor element types for b3_load_tensor. */
+#define B3_DTYPE_F32 0
+#define B3_DTYPE_F16 1
+#define B3_DTYPE_BF16 2
+
+typedef struct b3_ctx b3_ctx;
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* b3_last_error(void);
+
+/* ABI version, major * 10000 + minor * 100 + patch. */
+int b3_version(void);
+
+/* Context on CUDA device `device`: stream, weight store, activation arena.
+ * Replaces Gpu::new_with + Encoder::load_with's device setup
+ * (src/gpu.rs:448, src/encoder.rs:412).  NULL on failure. */
+b3_ctx* b3_create(int device);
+void b3_destroy(b3_ctx* ctx);
+
+/* Wait for all work enqueued on the context stream; reports device-side
+ * errors (B3_ETIMEOUT) raised by the kernels since the last check. */
+int b3_sync(b3_ctx* ctx);
+
+/* The context's cudaStream_t, for callers that order their own work after
+ * B3_DEVICE_PTRS calls. */
+void* b3_stream(b3_ctx* ctx);
+
+/* ───────────────────────── weight loading ─────────────────────────
+ * Tensors are pushed by the reference checkpoint's names, the way
+ * Encoder::load_with pulls them from a WeightSource (src/weights.rs:22-36,
+ * src/encoder.rs:412-640).  A Rust host iterates its WeightSource and calls:
+ *   - b3_load_tensor for dense tensors (`WeightSource::read`, any of f32 /
+ *     f16 / bf16; matrices are rounded to f16 exactly as src/raw.rs:68-97 and
+ *     src/cpu/mod.rs:35-37 do),
+ *   - b3_load_lowbit / b3_load_lowbit_levels for 4-bit layers
+ *     (`WeightSource::read_lowbit`, src/bark.rs:33-48),
+ * then b3_finalize once. */
+int b3_load_tensor(b3_ctx* ctx, const char* name, int dtype, const int64_t* shape, int ndim,
+                   const void* data);
+
+/* 4-bit layer as codes packed two per byte (low nibble = even column; this is
+ * byte-for-byte the reference's u32 words, eight nibbles low-first,
+ * src/bark.rs:352-358) plus a per-row 16-entry f16 level table:
+ * codes [rows][cols/2], lut16 [rows][16].  cols must be even. */
+int b3_load_lowbit(b3_ctx* ctx, const char* name, const uint8_t* codes, const uint16_t* lut16,
+                   int rows, int cols);
+
+/* The reference's LowBitTensor as is (src/bark.rs:33-48): code_words
+ * [rows][ceil(cols/8)] u32, levels [rows][4] f16 with the first k (1..3) in
+ * use.  Converted at load to the 16-entry table with the sign-magnitude rule
+ * of `expand` (src/bark.rs:597-611): 0 -> 0, 1..k -> +lev, k+1..2k -> -lev,
+ * codes above 2k -> 0. */
+int b3_load_lowbit_levels(b3_ctx* ctx, const char* name, const uint32_t* code_words,
+                          const uint16_t* levels, int k, int rows, int cols);
+
+/* Build the device-resident encoder from the loaded tensors: fused q|k|v
+ * (src/encoder.rs:342-402), BatchNorm fold (src/cpu/mod.rs:103-119),
+ * GLU row interleave for pw1, transposed depthwise taps.  `n_layers` is the
+ * block count to expect (24 for the released models). */
+int b3_finalize(b3_ctx* ctx, int n_layers);
+
+/* ───────────────────────────── encoder ─────────────────────────────
+ * One utterance, the CpuEncoder::encode contract (src/cpu/mod.rs:156-188):
+ * sub [t][4096] are the conv-subsampled frames; with layers >= n_layers the
+ * result is the pooler [t][640] (projector 1024 -> 640 + bias), otherwise the
+ * pre-norm_out residual [t][1024] of block `layers - 1` (the reference's
+ * h_b{n} dump point). */
+int b3_encode(b3_ctx* ctx, const float* sub, int t, int layers, float* out, unsigned flags);
+
+/* Varlen batch: utterance i occupies rows cu_seqlens[i] .. cu_seqlens[i+1]
+ * of sub [total][4096] and pooler [total][640].  Attention and the depthwise
+ * conv stay inside each utterance; linears run over the concatenation.
+ * cu_seqlens is always host memory (n_utt + 1 entries, starting at 0). */
+int b3_encode_batch(b3_ctx* ctx, const float* sub, const int32_t* cu_seqlens, int n_utt,
+                    float* pooler, unsigned flags);
+
+/* ─────────────────────────── single kernels ───────────────────────────
+ * one 4-bit linear, c[m][n] = a[m][:] . W[n][:] + bias[n]
+ * with W from codes [n][k/2] + lut16 [n][16].  Replaces Ctx::gemm_f32 with a
+ * low-bit weight + add_bias_f32 (src/encoder.rs:1039-1100, 2078).
+ * k must be a multiple of 64 and n of 128; bias may be NULL. */
+int b3_linear_lut4(b3_ctx* ctx, const float* a, const uint8_t* codes, const uint16_t* lut16,
+                   const float* bias, float* c, int m, int n, int k, unsigned flags);
+
+/* Same with a dense f16 weight w16 [n][k] (the Pro layout after the
+ * reference's bf16 -> f16 rounding).  With the weights of b3_linear_lut4
+ * expanded through their tables this returns bit-identical results (the
+ * reference's lbtest, src/diagnostics/gemm.rs:538-652). */
+int b3_linear_f16(b3_ctx* ctx, const float* a, const uint16_t* w16, const float* bias, float* c,
+                  int m, int n, int k, unsigned flags);
+
+/* BASELINE config 4: the attention and conv sections of block `layer`
+ * (src/cpu/layer.rs:198-310) on one sequence, in place:
+ *   x += MHSA(LN_att(x));  x += Conv(LN_conv(x)).
+ * x is [t][1024]. */
+int b3_attn_conv(b3_ctx* ctx, int layer, float* x, int t, unsigned flags);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BARK3_B200_H */

@@ -1,0 +1,114 @@
+"""Encoder parity on the GPU against the CPU oracle (the reference's CpuEncoder
+restated), through the C ABI.
+
+Tolerance (north star): max relative error <= 2e-2 per layer, measured as
+max|gpu - oracle| / max|oracle| on the pre-norm residual after each block and
+on the pooler.  The GPU rounds activations to f16 at GEMM inputs and
+accumulates in f32 on tensor cores; the reference keeps f32 activations with
+the same f16 weights.
+"""
+import numpy as np
+import pytest
+
+from conftest import rel_err
+
+pytestmark = pytest.mark.gpu
+
+LAYER_TOL = 2e-2
+
+
+@pytest.fixture(scope="module")
+def lut_model(syn, oracle, gpu_encoder_factory):
+    n_layers = 3
+    w = syn.encoder_weights(seed=1, n_layers=n_layers, layout="lut4")
+    return w, gpu_encoder_factory(w, n_layers), oracle.OracleEncoder(w, n_layers), n_layers
+
+
+@pytest.mark.parametrize("t", [1, 7, 64, 130, 379])
+def test_per_layer_parity_lut4(lut_model, syn, t):
+    w, enc, ref, n_layers = lut_model
+    sub = syn.sub_features(np.random.default_rng(t), t)
+    errs = []
+    for layers in range(1, n_layers + 1):
+        got = enc.encode(sub, layers=layers)
+        want = ref.encode(sub, layers=layers)
+        assert got.shape == want.shape
+        assert np.isfinite(got).all()
+        errs.append(rel_err(got, want))
+    print(f"T={t} per-layer errors {['%.2e' % e for e in errs]}")
+    assert max(errs) <= LAYER_TOL
+
+
+def test_bf16_layout_parity(syn, oracle, gpu_encoder_factory):
+    n_layers = 2
+    w = syn.encoder_weights(seed=2, n_layers=n_layers, layout="bf16")
+    enc = gpu_encoder_factory(w, n_layers)
+    ref = oracle.OracleEncoder(w, n_layers)
+    sub = syn.sub_features(np.random.default_rng(3), 257)
+    for layers in (1, 2):
+        e = rel_err(enc.encode(sub, layers=layers), ref.encode(sub, layers=layers))
+        print(f"bf16 layers={layers} err {e:.2e}")
+        assert e <= LAYER_TOL
+
+
+def test_batch_equals_single(lut_model, syn):
+    """Varlen batching is exact: every kernel is row- or segment-local."""
+    w, enc, ref, n_layers = lut_model
+    rng = np.random.default_rng(9)
+    lens = [37, 130, 1, 64, 200]
+    subs = [syn.sub_features(rng, t) for t in lens]
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    got = enc.encode_batch(np.concatenate(subs), cu)
+    for i, s in enumerate(subs):
+        one = enc.encode(s)
+        assert np.array_equal(got[cu[i]:cu[i + 1]], one), f"utterance {i}"
+
+
+def test_levels_format(syn, oracle, pkg, gpu_encoder_factory):
+    """The .bark levels2 form (k <= 3 sign-magnitude levels, u32 code words)
+    converts to the same values as `expand` (src/bark.rs:597-611)."""
+    n_layers = 1
+    rng = np.random.default_rng(4)
+    w = syn.encoder_weights(seed=4, n_layers=n_layers, layout="lut4")
+    dense = dict(w)
+    for name in list(w):
+        if isinstance(w[name], tuple) and w[name][0] == "lut4":
+            rows, cols = w[name][2].shape[0], w[name][1].shape[1] * 2
+            k = int(rng.integers(1, 4))
+            words, levels, codes = syn.make_levels_k(rng, rows, cols, k)
+            w[name] = ("levels", words, levels, k, cols)
+            dense[name] = syn.expand_levels(codes, levels, k)
+    enc = gpu_encoder_factory(w, n_layers)
+    ref = oracle.OracleEncoder(dense, n_layers)
+    sub = syn.sub_features(rng, 90)
+    e = rel_err(enc.encode(sub), ref.encode(sub))
+    print(f"levels-format err {e:.2e}")
+    assert e <= LAYER_TOL
+
+
+def test_attn_conv_section(lut_model, syn):
+    """BASELINE config 4 shape family: attention + conv sections alone."""
+    w, enc, ref, n_layers = lut_model
+    x = np.random.default_rng(12).normal(0, 1, size=(300, 1024)).astype(np.float32)
+    got = x.copy()
+    enc.attn_conv(1, got)
+    want = ref.attn_conv(1, x)
+    e = rel_err(got - x, want - x)
+    print(f"attn+conv delta err {e:.2e}")
+    assert e <= LAYER_TOL
+
+
+def test_errors(pkg, syn):
+    enc = pkg.Encoder(0)
+    sub = np.zeros((4, 4096), dtype=np.float32)
+    with pytest.raises(pkg.B3Error) as ei:
+        enc.encode(sub, layers=1)
+    assert ei.value.code == pkg.B3_ESTATE
+    w = syn.encoder_weights(seed=0, n_layers=1, layout="lut4")
+    del w["encoder.layers.0.norm_conv.bias"]
+    enc.load(w)
+    with pytest.raises(pkg.B3Error) as ei:
+        enc.finalize(1)
+    assert ei.value.code == pkg.B3_ENOTFOUND
+    assert "norm_conv.bias" in str(ei.value)
+    enc.close()
