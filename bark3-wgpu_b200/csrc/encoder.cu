@@ -143,6 +143,25 @@ struct Plan {
     int M = 0, tmax = 0, n_work = 0;
 };
 
+// Per-kernel-class CUDA-event timing (the analogue of the reference's
+// BARK3_ENC_PROFILE timestamp queries, src/encoder/prof.rs:1-121).  Launch
+// counts are always kept; events are recorded only while enabled.
+struct ProfRec {
+    int kind;
+    int ev;
+    double flops, bytes;
+};
+
+struct Prof {
+    bool on = false;
+    std::vector<cudaEvent_t> pool;
+    int next = 0;
+    std::vector<ProfRec> recs;
+    int64_t launches[B3_K_COUNT] = {};
+    double ms[B3_K_COUNT] = {}, flops[B3_K_COUNT] = {}, bytes[B3_K_COUNT] = {};
+    int64_t timed[B3_K_COUNT] = {};
+};
+
 }  // namespace
 
 struct b3_ctx {
@@ -164,7 +183,9 @@ struct b3_ctx {
     DevBuf io_in, io_out;   // device staging for host-pointer calls
     DevBuf scratch16;       // f16 copy of A for the single-linear entry points
     Plan plan;
+    Prof prof;
     ~b3_ctx() {
+        for (cudaEvent_t e : prof.pool) cudaEventDestroy(e);
         auto rel = [](Linear& l) { l.w.release(); l.lut16.release(); };
         rel(sub_w);
         rel(proj_w);
@@ -194,6 +215,47 @@ struct DeviceGuard {
         if (prev >= 0 && cur != prev) cudaSetDevice(prev);
     }
 };
+
+// Wraps one kernel launch: counts it and, when profiling, brackets it with
+// events on the context stream.
+struct ProfScope {
+    b3_ctx* c;
+    int kind;
+    int ev = -1;
+    double flops, bytes;
+    ProfScope(b3_ctx* c_, int kind_, double flops_, double bytes_) : c(c_), kind(kind_), flops(flops_), bytes(bytes_) {
+        c->prof.launches[kind]++;
+        Prof& p = c->prof;
+        if (p.on && p.next + 2 <= static_cast<int>(p.pool.size())) {
+            ev = p.next;
+            p.next += 2;
+            cudaEventRecord(p.pool[ev], c->stream);
+        }
+    }
+    ~ProfScope() {
+        if (ev >= 0) {
+            cudaEventRecord(c->prof.pool[ev + 1], c->stream);
+            c->prof.recs.push_back({kind, ev, flops, bytes});
+        }
+    }
+};
+
+int prof_collect(b3_ctx* c) {
+    Prof& p = c->prof;
+    if (p.recs.empty()) return 0;
+    B3_CUDA(cudaStreamSynchronize(c->stream));
+    for (const ProfRec& r : p.recs) {
+        float ms = 0.f;
+        B3_CUDA(cudaEventElapsedTime(&ms, p.pool[r.ev], p.pool[r.ev + 1]));
+        p.ms[r.kind] += ms;
+        p.flops[r.kind] += r.flops;
+        p.bytes[r.kind] += r.bytes;
+        p.timed[r.kind]++;
+    }
+    p.recs.clear();
+    p.next = 0;
+    return 0;
+}
 
 uint16_t f32_to_f16_bits(float v) {
     __half h = __float2half_rn(v);
@@ -299,6 +361,39 @@ int build_linear(b3_ctx* c, Linear& L, const std::vector<std::string>& names, in
 
 // ───────────────────────────── GEMM helper ─────────────────────────────
 
+// Algorithmic DRAM bytes of one GEMM: A once, W once (codes + tables or f16),
+// the output once (read + write for the residual update).
+double gemm_bytes(int M, int N, int K, bool lut, int epi) {
+    const double a = 2.0 * M * K;
+    const double w = lut ? (0.5 * N * K + 32.0 * N) : 2.0 * N * K;
+    double o;
+    switch (epi) {
+        case EPI_F32: o = 4.0 * M * N; break;
+        case EPI_RESID: o = 8.0 * M * N; break;
+        case EPI_GLU_F16: o = 1.0 * M * N; break;
+        case EPI_QKV: o = 2.0 * M * N + 2.0 * M * 1024; break;
+        default: o = 2.0 * M * N; break;
+    }
+    return a + w + o;
+}
+
+int k_layernorm(b3_ctx* c, const float* x, int rows, const float* w1, const float* b1, float* y32,
+                const float* w2, const float* b2, __half* y16) {
+    ProfScope ps(c, B3_K_LAYERNORM, 0.0, rows * (4096.0 + (y32 ? 4096.0 : 0.0) + (y16 ? 2048.0 : 0.0)));
+    return launch_layernorm(x, rows, w1, b1, y32, w2, b2, y16, c->stream);
+}
+
+int k_dwconv(b3_ctx* c, const __half* src, int rows, const float* dw_t, const float* bn_a, const float* bn_b,
+             __half* dst) {
+    ProfScope ps(c, B3_K_DWCONV, 2.0 * 9 * 1024 * rows, rows * 4096.0);
+    return launch_dwconv(src, c->seg_d.as<int2>(), rows, dw_t, bn_a, bn_b, dst, c->stream);
+}
+
+int k_convert(b3_ctx* c, const float* src, __half* dst, int64_t n) {
+    ProfScope ps(c, B3_K_CONVERT, 0.0, 6.0 * n);
+    return launch_f32_to_f16(src, dst, n, c->stream);
+}
+
 int run_gemm(b3_ctx* c, const Linear& W, const __half* a, int M, int lda, int epi, GemmParams p) {
     GemmOp op;
     B3_TRY(gemm_make_a_map(&op.map_a, a, M, W.K, lda));
@@ -311,6 +406,8 @@ int run_gemm(b3_ctx* c, const Linear& W, const __half* a, int M, int lda, int ep
     op.lut = W.lut;
     op.bn = W.bn;
     op.epi = epi;
+    ProfScope ps(c, W.lut ? B3_K_GEMM_LUT4 : B3_K_GEMM_F16, 2.0 * M * W.N * W.K,
+                 gemm_bytes(M, W.N, W.K, W.lut, epi));
     return gemm_launch(op, c->stream);
 }
 
@@ -361,7 +458,10 @@ int ensure_pos(b3_ctx* c, int tmax) {
     const int rows = 2 * tcap - 1;
     B3_TRY(c->pos16.ensure(static_cast<size_t>(rows + 1) * kHidden * 2));
     B3_TRY(c->R16.ensure(static_cast<size_t>(rows + 1) * kHidden * 2));
-    B3_TRY(launch_pos_table(c->inv_freq.as<float>(), tcap, rows, c->pos16.as<__half>(), c->stream));
+    {
+        ProfScope ps(c, B3_K_OTHER, 0.0, rows * 2048.0);
+        B3_TRY(launch_pos_table(c->inv_freq.as<float>(), tcap, rows, c->pos16.as<__half>(), c->stream));
+    }
     c->tcap = tcap;
     return 0;
 }
@@ -408,7 +508,7 @@ int attention_section(b3_ctx* c, const Layer& L, int M) {
     __half* a16 = c->a16.as<__half>();
     __half* qkv = c->qkv16.as<__half>();
     const int tmax = c->plan.tmax;
-    B3_TRY(launch_layernorm(x, M, L.ln_w(1), L.ln_b(1), nullptr, nullptr, nullptr, a16, c->stream));
+    B3_TRY(k_layernorm(c, x, M, L.ln_w(1), L.ln_b(1), nullptr, nullptr, nullptr, a16));
     GemmParams pq = params_f16(qkv, 4096);
     pq.bias_u = L.bu();
     pq.bias_v = L.bv();
@@ -427,7 +527,16 @@ int attention_section(b3_ctx* c, const Layer& L, int M) {
     ap.work = c->work_d.as<int2>();
     ap.out = a16;
     ap.scale_log2 = 1.4426950408889634f / std::sqrt(128.0f);
-    B3_TRY(launch_attention(ap, c->plan.n_work, c->stream));
+    {
+        double fl = 0.0, by = 0.0;
+        for (size_t i = 0; i + 1 < c->plan.cu.size(); ++i) {
+            const double t = c->plan.cu[i + 1] - c->plan.cu[i];
+            fl += 6144.0 * t * t;                       // 8 heads x (QK + band + PV), 2*128 each
+            by += t * 1024 * 2 * 5 + (2 * t - 1) * 2048; // qu qv k v in, out; R band
+        }
+        ProfScope ps(c, B3_K_ATTENTION, fl, by);
+        B3_TRY(launch_attention(ap, c->plan.n_work, c->stream));
+    }
     return run_gemm(c, L.o, a16, M, kHidden, EPI_RESID, params_resid(x, 1.0f));
 }
 
@@ -436,9 +545,9 @@ int conv_section(b3_ctx* c, const Layer& L, int M) {
     float* x = c->x.as<float>();
     __half* a16 = c->a16.as<__half>();
     __half* g16 = c->g16.as<__half>();
-    B3_TRY(launch_layernorm(x, M, L.ln_w(2), L.ln_b(2), nullptr, nullptr, nullptr, a16, c->stream));
+    B3_TRY(k_layernorm(c, x, M, L.ln_w(2), L.ln_b(2), nullptr, nullptr, nullptr, a16));
     B3_TRY(run_gemm(c, L.pw1, a16, M, kHidden, EPI_GLU_F16, params_f16(g16, kHidden)));
-    B3_TRY(launch_dwconv(g16, c->seg_d.as<int2>(), M, L.dw_t(), L.bn_a(), L.bn_b(), a16, c->stream));
+    B3_TRY(k_dwconv(c, g16, M, L.dw_t(), L.bn_a(), L.bn_b(), a16));
     return run_gemm(c, L.pw2, a16, M, kHidden, EPI_RESID, params_resid(x, 1.0f));
 }
 
@@ -459,7 +568,7 @@ int forward_blocks(b3_ctx* c, int M, int layers) {
     const int upto = layers < c->n_layers ? layers : c->n_layers;
     if (upto > 0) {
         const Layer& L0 = c->layers[0];
-        B3_TRY(launch_layernorm(x, M, L0.ln_w(0), L0.ln_b(0), nullptr, nullptr, nullptr, a16, c->stream));
+        B3_TRY(k_layernorm(c, x, M, L0.ln_w(0), L0.ln_b(0), nullptr, nullptr, nullptr, a16));
     }
     for (int i = 0; i < upto; ++i) {
         const Layer& L = c->layers[i];
@@ -467,14 +576,14 @@ int forward_blocks(b3_ctx* c, int M, int layers) {
         B3_TRY(ffn_half(c, L.ff1a, L.ff1b, M));
         B3_TRY(attention_section(c, L, M));
         B3_TRY(conv_section(c, L, M));
-        B3_TRY(launch_layernorm(x, M, L.ln_w(3), L.ln_b(3), nullptr, nullptr, nullptr, a16, c->stream));
+        B3_TRY(k_layernorm(c, x, M, L.ln_w(3), L.ln_b(3), nullptr, nullptr, nullptr, a16));
         B3_TRY(ffn_half(c, L.ff2a, L.ff2b, M));
         const bool last = (i + 1 == upto);
         if (!last) {
             const Layer& N = c->layers[i + 1];
-            B3_TRY(launch_layernorm(x, M, L.ln_w(4), L.ln_b(4), x, N.ln_w(0), N.ln_b(0), a16, c->stream));
+            B3_TRY(k_layernorm(c, x, M, L.ln_w(4), L.ln_b(4), x, N.ln_w(0), N.ln_b(0), a16));
         } else if (upto == c->n_layers) {
-            B3_TRY(launch_layernorm(x, M, L.ln_w(4), L.ln_b(4), x, nullptr, nullptr, a16, c->stream));
+            B3_TRY(k_layernorm(c, x, M, L.ln_w(4), L.ln_b(4), x, nullptr, nullptr, a16));
         }
     }
     if (upto == 0 && c->n_layers == 0)
@@ -498,7 +607,7 @@ int sync_and_check(b3_ctx* c) {
 
 // Encode rows already in device memory: sub (f32 [M][4096]) -> out.
 int encode_device(b3_ctx* c, const float* sub, int M, int layers, float* out) {
-    B3_TRY(launch_f32_to_f16(sub, c->sub16.as<__half>(), static_cast<int64_t>(M) * kSubIn, c->stream));
+    B3_TRY(k_convert(c, sub, c->sub16.as<__half>(), static_cast<int64_t>(M) * kSubIn));
     B3_TRY(forward_blocks(c, M, layers));
     if (layers >= c->n_layers) {
         B3_TRY(run_gemm(c, c->proj_w, c->a16.as<__half>(), M, kHidden, EPI_F32,
@@ -567,7 +676,7 @@ int linear_any(b3_ctx* c, const float* a, const void* w, const uint16_t* lut16, 
         dc = reinterpret_cast<float*>(put(nullptr, c_bytes));
     }
     B3_TRY(c->scratch16.ensure(static_cast<size_t>(m) * k * 2));
-    B3_TRY(launch_f32_to_f16(da, c->scratch16.as<__half>(), static_cast<int64_t>(m) * k, c->stream));
+    B3_TRY(k_convert(c, da, c->scratch16.as<__half>(), static_cast<int64_t>(m) * k));
     GemmOp op;
     B3_TRY(gemm_make_a_map(&op.map_a, c->scratch16.as<__half>(), m, k, k));
     B3_TRY(gemm_make_b_map(&op.map_b, dw, lut, n, k, 128));
@@ -579,7 +688,10 @@ int linear_any(b3_ctx* c, const float* a, const void* w, const uint16_t* lut16, 
     op.lut = lut;
     op.bn = 128;
     op.epi = EPI_F32;
-    B3_TRY(gemm_launch(op, c->stream));
+    {
+        ProfScope ps(c, lut ? B3_K_GEMM_LUT4 : B3_K_GEMM_F16, 2.0 * m * n * k, gemm_bytes(m, n, k, lut, EPI_F32));
+        B3_TRY(gemm_launch(op, c->stream));
+    }
     if (dev) return 0;
     B3_CUDA(cudaMemcpyAsync(out, dc, c_bytes, cudaMemcpyDeviceToHost, c->stream));
     return sync_and_check(c);
@@ -770,6 +882,37 @@ int b3_finalize(b3_ctx* ctx, int n_layers) {
     ctx->n_layers = n_layers;
     ctx->finalized = true;
     ctx->staged.clear();
+    return 0;
+}
+
+int b3_profile(b3_ctx* ctx, int enable) {
+    if (!ctx) return set_error(B3_EINVAL, "null context");
+    DeviceGuard g(ctx->device);
+    Prof& p = ctx->prof;
+    B3_CUDA(cudaStreamSynchronize(ctx->stream));
+    if (enable && p.pool.empty()) {
+        p.pool.resize(2 * 16384);
+        for (auto& e : p.pool) B3_CUDA(cudaEventCreate(&e));
+    }
+    p.on = enable != 0;
+    p.recs.clear();
+    p.next = 0;
+    for (int k = 0; k < B3_K_COUNT; ++k) {
+        p.launches[k] = p.timed[k] = 0;
+        p.ms[k] = p.flops[k] = p.bytes[k] = 0.0;
+    }
+    return 0;
+}
+
+int b3_profile_read(b3_ctx* ctx, int kind, double* ms, double* flops, double* bytes, int64_t* launches) {
+    if (!ctx || kind < 0 || kind >= B3_K_COUNT) return set_error(B3_EINVAL, "bad profile query");
+    DeviceGuard g(ctx->device);
+    B3_TRY(prof_collect(ctx));
+    const Prof& p = ctx->prof;
+    if (ms) *ms = p.ms[kind];
+    if (flops) *flops = p.flops[kind];
+    if (bytes) *bytes = p.bytes[kind];
+    if (launches) *launches = p.launches[kind];
     return 0;
 }
 

@@ -1,0 +1,359 @@
+#!/usr/bin/env python3
+"""Benchmark of the B200 encoder hot path (bark3-wgpu's Conformer encoder).
+
+Default workload (BASELINE config 5's batch, encoder stage): per rank a batch
+of 256 seeded utterances with lengths uniform in 10-60 s, encoded by the
+24-block 4-bit (LUT) Conformer encoder: sub linear -> 24 blocks -> projector.
+The encoder input is the conv-subsampled feature matrix (T_i, 4096) per
+utterance, synthetic (seeded ReLU'd normals; the mel / subsampling front end
+and the TDT decoder are outside this hot path).  One step = one encode of the
+whole batch.  Metric: RTFx = audio seconds encoded per second.
+
+  value  device-resident inputs (HBM), CUDA events on the library's stream,
+         max over ranks; the batch (1.8 GB of f32 input) is far larger than
+         L2, so no flush is needed between steps.
+  e2e    the same through the host-pointer C ABI call: pinned host input
+         copied in and the pooler copied out inside every timed step.
+
+--impl reference times the reference's CPU encoder (the C restatement of
+src/cpu/*, all host cores) on utterances of the same batch.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from __graft_entry__ import load_oracle, load_package  # noqa: E402
+
+N_LAYERS = 24
+METRIC = "RTFx (audio-s/s), 4-bit Conformer encoder"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
+    ap.add_argument("--utterances", type=int, default=256)
+    ap.add_argument("--strong", action="store_true",
+                    help="shard one batch of --utterances across ranks (LPT) instead of one batch per rank")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the CPU-baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--seed", type=int, default=5)
+    return ap.parse_args()
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def lpt_shards(frames, n_ranks):
+    """Longest-processing-time assignment of utterances to ranks by the
+    estimated encoder cost c(T) = 52.4M T + 6144 T^2 (FLOPs per block)."""
+    cost = [52.4e6 * t + 6144.0 * t * t for t in frames]
+    order = sorted(range(len(frames)), key=lambda i: -cost[i])
+    load = [0.0] * n_ranks
+    shards = [[] for _ in range(n_ranks)]
+    for i in order:
+        r = min(range(n_ranks), key=lambda j: load[j])
+        shards[r].append(i)
+        load[r] += cost[i]
+    return [sorted(s) for s in shards]
+
+
+def batch_for_rank(args, rank, world, pkg, syn):
+    """(seconds per utterance, frames per utterance) of this rank's batch."""
+    if args.strong:
+        secs = syn.batch_lengths(args.seed, args.utterances)
+        frames = [pkg.frames_for_seconds(s) for s in secs]
+        mine = lpt_shards(frames, world)[rank]
+        return [float(secs[i]) for i in mine], [frames[i] for i in mine]
+    secs = syn.batch_lengths(args.seed + 1000 * rank, args.utterances)
+    return [float(s) for s in secs], [pkg.frames_for_seconds(s) for s in secs]
+
+
+class ClockSampler:
+    """nvidia-smi samples of the SM clock and throttle reasons while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        self.f.flush()
+        rows = []
+        for line in pathlib.Path(self.f.name).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
+            except ValueError:
+                continue
+        os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        loaded = [r for r in rows if r[2] > 300.0] or rows
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in loaded for i, v in enumerate(r[3]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(loaded)}
+
+
+def cpu_baseline_sample(oracle, syn, weights, secs, frames, budget_s, seed):
+    """The oracle (restated reference CPU encoder, all host cores) on the first
+    utterances of the batch, in turn, until the time budget is spent."""
+    enc = oracle.OracleEncoder(weights, N_LAYERS)
+    rng = np.random.default_rng(seed)
+    done_audio, used, n = 0.0, 0.0, 0
+    for s, t in zip(secs, frames):
+        sub = syn.sub_features(rng, t)
+        t0 = time.perf_counter()
+        enc.encode(sub)
+        used += time.perf_counter() - t0
+        done_audio += s
+        n += 1
+        if used >= budget_s:
+            break
+    return done_audio / used, n, done_audio, used
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference's CPU encoder path (restated in C) on
+    the host cores, one utterance of the batch per step."""
+    if rank != 0:
+        return
+    pkg = load_package()
+    import bark3_b200.synthetic as syn
+    oracle = load_oracle()
+    secs, frames = batch_for_rank(args, 0, 1, pkg, syn)
+    weights = syn.encoder_weights(seed=args.seed, n_layers=N_LAYERS, layout="lut4")
+    enc = oracle.OracleEncoder(weights, N_LAYERS)
+    rng = np.random.default_rng(args.seed)
+    subs = [syn.sub_features(rng, t) for t in frames[: max(1, min(len(frames), 4))]]
+    for w in range(args.warmup):
+        enc.encode(subs[w % len(subs)])
+    audio, wall = 0.0, 0.0
+    for k in range(args.steps):
+        i = k % len(subs)
+        t0 = time.perf_counter()
+        enc.encode(subs[i])
+        wall += time.perf_counter() - t0
+        audio += secs[i]
+    v = audio / wall
+    cores = oracle.threads()
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "audio-s/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * wall / args.steps, 3),
+        "higher_is_better": True, "scaling": "weak" if not args.strong else "strong", "vs_baseline": None,
+        "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "reference CPU encoder (src/cpu/*, restated in C, AVX2/F16C FMA), "
+                   "one utterance of the config-5 batch per step", "utterances_sampled": len(subs),
+                   "frames": frames[: len(subs)], "layers": N_LAYERS, "weights": "random-init 4-bit LUT"},
+        "cpu_baseline": {"value": round(v, 3), "unit": "audio-s/s", "cores": cores, "kind": "port",
+                         "sample": f"{args.steps} encodes of utterances {frames[:len(subs)]} frames"},
+        "e2e": {"value": round(v, 3), "unit": "audio-s/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+
+    pkg = load_package()
+    import bark3_b200.synthetic as syn
+
+    secs, frames = batch_for_rank(args, rank, world, pkg, syn)
+    M = int(sum(frames))
+    cu = np.concatenate([[0], np.cumsum(frames)]).astype(np.int32)
+    audio = float(sum(secs))
+
+    weights = syn.encoder_weights(seed=args.seed, n_layers=N_LAYERS, layout="lut4")
+    enc = pkg.Encoder(local)
+    enc.load(weights)
+    enc.finalize(N_LAYERS)
+
+    # inputs: pinned host copy (e2e) and device-resident copy (value)
+    rng = np.random.default_rng(args.seed + 17 * rank)
+    host_in = torch.empty((M, 4096), dtype=torch.float32, pin_memory=True)
+    hv = host_in.numpy()
+    for i in range(len(frames)):
+        hv[cu[i]:cu[i + 1]] = syn.sub_features(rng, frames[i])
+    host_out = torch.empty((M, 640), dtype=torch.float32, pin_memory=True)
+    dev_in = host_in.cuda()
+    dev_out = torch.empty((M, 640), dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    stream = torch.cuda.ExternalStream(enc.stream)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ── value: device-resident inputs ──
+    for _ in range(args.warmup):
+        enc.encode_batch(dev_in, cu, out=dev_out)
+    enc.sync()
+    L = pkg.lib()
+    L.b3_profile(enc.ctx, 1)
+    barrier()
+    torch.cuda.synchronize()
+    enc.sync()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        ev0.record(stream)
+        for _ in range(args.steps):
+            enc.encode_batch(dev_in, cu, out=dev_out)
+        ev1.record(stream)
+        enc.sync()
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    clocks = clk.summary()
+    prof = {}
+    import ctypes
+    for kind, name in enumerate(["gemm_lut4", "gemm_f16", "attention", "layernorm", "dwconv", "convert", "other"]):
+        a, f, b, n = ctypes.c_double(), ctypes.c_double(), ctypes.c_double(), ctypes.c_int64()
+        pkg.check(L.b3_profile_read(enc.ctx, kind, ctypes.byref(a), ctypes.byref(f), ctypes.byref(b), ctypes.byref(n)))
+        prof[name] = {"ms": a.value, "flops": f.value, "bytes": b.value, "launches": n.value}
+    L.b3_profile(enc.ctx, 0)
+    launches = int(sum(p["launches"] for p in prof.values()))
+    ms_max = max_over_ranks(ms)
+    value = world * audio * args.steps / (ms_max / 1000.0) if not args.strong else None
+    if args.strong:
+        tot = torch.tensor([audio], dtype=torch.float64, device="cuda")
+        if world > 1:
+            dist.all_reduce(tot)
+        value = float(tot.item()) * args.steps / (ms_max / 1000.0)
+
+    # ── e2e: host buffers through the host-pointer ABI call ──
+    barrier()
+    hin, hout = host_in.numpy(), host_out.numpy()
+    enc.encode_batch(hin, cu, out=hout)  # warm the staging buffers
+    barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        enc.encode_batch(hin, cu, out=hout)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1))
+    if args.strong:
+        e2e_value = value * ms_max / e2e_ms
+    else:
+        e2e_value = world * audio * args.steps / (e2e_ms / 1000.0)
+
+    pk, pk_kind = peaks()
+    g = prof["gemm_lut4"]
+    achieved = g["flops"] / (g["ms"] / 1000.0) / 1e12 if g["ms"] > 0 else None
+    peak = pk.get("bf16_tflops_sustained") or pk.get("bf16_tflops")
+    traffic_file = ROOT / "profiles" / "k1_gemm_lut4_traffic.json"
+    traffic = json.loads(traffic_file.read_text()).get("bytes_per_launch") if traffic_file.exists() else None
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        oracle = load_oracle()
+        v, n, a_s, used = cpu_baseline_sample(oracle, syn, weights, secs, frames, args.cpu_seconds, args.seed)
+        cpu = {"value": round(v, 3), "unit": "audio-s/s", "cores": oracle.threads(), "kind": "port",
+               "sample": f"first {n} utterances of the batch ({a_s:.1f} audio-s, {used:.1f} s wall), 24 blocks, in turn"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "audio-s/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3),
+            "higher_is_better": True, "scaling": "strong" if args.strong else "weak", "vs_baseline": None,
+            "dtype": "f16", "data": "synthetic",
+            "config": {"workload": "config-5 batch through the 24-block 4-bit LUT encoder (encoder stage)",
+                       "utterances_per_rank": len(frames), "audio_s_per_rank": round(audio, 1),
+                       "frames_per_rank": M, "lengths_s": "U(10,60) seeded", "layers": N_LAYERS,
+                       "d_model": 1024, "heads": 8, "ffn": 4096, "conv_kernel": 9,
+                       "weights": "random-init 4-bit codes + 16-entry f16 LUT per row",
+                       "input": "synthetic (T,4096) subsampled features, f32",
+                       "l2": "inputs (%.2f GB) > L2, no flush" % (M * 4096 * 4 / 1e9),
+                       "parallelism": f"utterance-sharded x{world}, no collective"},
+            "roofline": {"kernel": "k1_gemm (LUT4, tcgen05)", "bound": "tensor",
+                         "achieved": round(achieved, 1) if achieved else None,
+                         "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(achieved / peak, 4) if achieved else None,
+                         "peak_source": f"bf16_tflops_sustained of {pk_kind}",
+                         "traffic": traffic,
+                         "launches": g["launches"], "gemm_ms_share": round(g["ms"] / ms, 4) if ms else None},
+            "kernels": {k: {"ms_per_step": round(v["ms"] / args.steps, 3),
+                            "TFLOP/s": round(v["flops"] / v["ms"] / 1e9, 1) if v["ms"] and v["flops"] else None,
+                            "GB/s": round(v["bytes"] / v["ms"] / 1e6, 1) if v["ms"] else None,
+                            "launches": v["launches"]} for k, v in prof.items() if v["launches"]},
+            "gpu_launches": launches,
+            "clocks": clocks,
+            "e2e": {"value": round(e2e_value, 2), "unit": "audio-s/s",
+                    "h2d_bytes_per_step": int(M * 4096 * 4), "d2h_bytes_per_step": int(M * 640 * 4)},
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(line), flush=True)
+    enc.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

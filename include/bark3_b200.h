@@ -138,6 +138,26 @@ int b3_linear_f16(b3_ctx* ctx, const float* a, const uint16_t* w16, const float*
  * x is [t][1024]. */
 int b3_attn_conv(b3_ctx* ctx, int layer, float* x, int t, unsigned flags);
 
+/* ───────────────────────────── profiling ─────────────────────────────
+ * Per-kernel-class device timing with CUDA events on the context stream, the
+ * counterpart of the reference's BARK3_ENC_PROFILE timestamp queries
+ * (src/encoder/prof.rs:1-121).  b3_profile(ctx, 1) resets the counters and
+ * starts recording; b3_profile_read waits for the stream and returns, for one
+ * kernel class, the summed device milliseconds, algorithmic FLOPs and DRAM
+ * bytes of the timed launches and the number of launches issued since the
+ * last reset (launches are counted even while recording is off). */
+#define B3_K_GEMM_LUT4 0
+#define B3_K_GEMM_F16 1
+#define B3_K_ATTENTION 2
+#define B3_K_LAYERNORM 3
+#define B3_K_DWCONV 4
+#define B3_K_CONVERT 5
+#define B3_K_OTHER 6
+#define B3_K_COUNT 7
+
+int b3_profile(b3_ctx* ctx, int enable);
+int b3_profile_read(b3_ctx* ctx, int kind, double* ms, double* flops, double* bytes, int64_t* launches);
+
 #ifdef __cplusplus
 }
 #endif

@@ -182,6 +182,7 @@ static void packw_rows(PackW* p, const float* w, int n, int k, int half, int rou
     size_t sz = (size_t)panels * k * PANEL;
     if (half) p->d16 = (uint16_t*)calloc(sz, 2);
     else p->d32 = (float*)calloc(sz, 4);
+#pragma omp parallel for schedule(static) num_threads(g_threads) if (panels >= 16)
     for (int pi = 0; pi < panels; pi++) {
         size_t base = (size_t)pi * k * PANEL;
         for (int j = 0; j < PANEL; j++) {
