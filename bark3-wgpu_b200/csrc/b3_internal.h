@@ -45,15 +45,14 @@ struct GemmOp {
     CUtensorMap map_b;
     GemmParams p;
     bool lut;
-    int bn;
     int epi;
 };
 
 int make_map_2d(CUtensorMap* map, const void* base, bool f16, uint64_t inner, uint64_t outer,
                 uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, bool swizzle128);
 int gemm_make_a_map(CUtensorMap* map, const __half* a, int M, int K, int lda);
-int gemm_make_b_map(CUtensorMap* map, const void* w, bool lut, int N, int K, int bn);
-int gemm_validate(const GemmParams& p, bool lut, int bn);
+int gemm_make_b_map(CUtensorMap* map, const void* w, bool lut, int N, int K);
+int gemm_validate(const GemmParams& p, bool lut);
 int gemm_launch(const GemmOp& op, cudaStream_t st);
 int gemm_take_dev_error(cudaStream_t st, unsigned int* out);
 

@@ -108,7 +108,7 @@ struct DevBuf {
 struct Linear {
     bool present = false;
     bool lut = false;
-    int N = 0, K = 0, bn = 128;
+    int N = 0, K = 0;
     DevBuf w;      // codes [N][K/2] or f16 [N][K]
     DevBuf lut16;  // [N][16] f16
     CUtensorMap map_b;
@@ -306,7 +306,7 @@ int get_vec(b3_ctx* c, const std::string& name, int64_t n, std::vector<float>& o
 // fused q|k|v too, src/encoder.rs:389-392).  `interleave_halves` reorders the
 // rows as (0, N/2, 1, N/2+1, ...) so a GLU pair lands in adjacent columns.
 int build_linear(b3_ctx* c, Linear& L, const std::vector<std::string>& names, int n_each, int K,
-                 bool interleave_halves, int bn) {
+                 bool interleave_halves) {
     std::vector<const Staged*> parts;
     for (auto& nm : names) {
         const Staged* s = find(c, nm);
@@ -335,7 +335,6 @@ int build_linear(b3_ctx* c, Linear& L, const std::vector<std::string>& names, in
     L.lut = lut;
     L.N = N;
     L.K = K;
-    L.bn = bn;
     if (lut) {
         std::vector<uint8_t> codes(static_cast<size_t>(N) * K / 2);
         std::vector<uint16_t> tab(static_cast<size_t>(N) * 16);
@@ -356,7 +355,7 @@ int build_linear(b3_ctx* c, Linear& L, const std::vector<std::string>& names, in
         B3_TRY(upload(L.w, w.data(), w.size() * 2, c->stream));
         B3_CUDA(cudaStreamSynchronize(c->stream));
     }
-    return gemm_make_b_map(&L.map_b, L.w.p, lut, N, K, bn);
+    return gemm_make_b_map(&L.map_b, L.w.p, lut, N, K);
 }
 
 // ───────────────────────────── GEMM helper ─────────────────────────────
@@ -404,7 +403,6 @@ int run_gemm(b3_ctx* c, const Linear& W, const __half* a, int M, int lda, int ep
     p.lut = W.lut ? W.lut16.as<uint16_t>() : nullptr;
     op.p = p;
     op.lut = W.lut;
-    op.bn = W.bn;
     op.epi = epi;
     ProfScope ps(c, W.lut ? B3_K_GEMM_LUT4 : B3_K_GEMM_F16, 2.0 * M * W.N * W.K,
                  gemm_bytes(M, W.N, W.K, W.lut, epi));
@@ -679,14 +677,13 @@ int linear_any(b3_ctx* c, const float* a, const void* w, const uint16_t* lut16, 
     B3_TRY(k_convert(c, da, c->scratch16.as<__half>(), static_cast<int64_t>(m) * k));
     GemmOp op;
     B3_TRY(gemm_make_a_map(&op.map_a, c->scratch16.as<__half>(), m, k, k));
-    B3_TRY(gemm_make_b_map(&op.map_b, dw, lut, n, k, 128));
+    B3_TRY(gemm_make_b_map(&op.map_b, dw, lut, n, k));
     op.p = params_f32(dc, n, db);
     op.p.M = m;
     op.p.N = n;
     op.p.K = k;
     op.p.lut = dl;
     op.lut = lut;
-    op.bn = 128;
     op.epi = EPI_F32;
     {
         ProfScope ps(c, lut ? B3_K_GEMM_LUT4 : B3_K_GEMM_F16, 2.0 * m * n * k, gemm_bytes(m, n, k, lut, EPI_F32));
@@ -829,10 +826,10 @@ int b3_finalize(b3_ctx* ctx, int n_layers) {
     if (n_layers < 1 || n_layers > 64) return set_error(B3_EINVAL, "n_layers %d out of range", n_layers);
     DeviceGuard g(ctx->device);
     std::vector<float> v;
-    B3_TRY(build_linear(ctx, ctx->sub_w, {"encoder.subsampling.linear.weight"}, kHidden, kSubIn, false, 128));
+    B3_TRY(build_linear(ctx, ctx->sub_w, {"encoder.subsampling.linear.weight"}, kHidden, kSubIn, false));
     B3_TRY(get_vec(ctx, "encoder.subsampling.linear.bias", kHidden, v));
     B3_TRY(upload(ctx->sub_b, v.data(), v.size() * 4, ctx->stream));
-    B3_TRY(build_linear(ctx, ctx->proj_w, {"encoder_projector.weight"}, kProj, kHidden, false, 128));
+    B3_TRY(build_linear(ctx, ctx->proj_w, {"encoder_projector.weight"}, kProj, kHidden, false));
     B3_TRY(get_vec(ctx, "encoder_projector.bias", kProj, v));
     B3_TRY(upload(ctx->proj_b, v.data(), v.size() * 4, ctx->stream));
     ctx->layers.resize(n_layers);
@@ -840,15 +837,15 @@ int b3_finalize(b3_ctx* ctx, int n_layers) {
         Layer& L = ctx->layers[l];
         const std::string p = "encoder.layers." + std::to_string(l) + ".";
         B3_TRY(build_linear(ctx, L.qkv, {p + "self_attn.q_proj.weight", p + "self_attn.k_proj.weight",
-                                         p + "self_attn.v_proj.weight"}, kHidden, kHidden, false, 128));
-        B3_TRY(build_linear(ctx, L.relk, {p + "self_attn.relative_k_proj.weight"}, kHidden, kHidden, false, 128));
-        B3_TRY(build_linear(ctx, L.o, {p + "self_attn.o_proj.weight"}, kHidden, kHidden, false, 128));
-        B3_TRY(build_linear(ctx, L.ff1a, {p + "feed_forward1.linear1.weight"}, kFfn, kHidden, false, 128));
-        B3_TRY(build_linear(ctx, L.ff1b, {p + "feed_forward1.linear2.weight"}, kHidden, kFfn, false, 128));
-        B3_TRY(build_linear(ctx, L.ff2a, {p + "feed_forward2.linear1.weight"}, kFfn, kHidden, false, 128));
-        B3_TRY(build_linear(ctx, L.ff2b, {p + "feed_forward2.linear2.weight"}, kHidden, kFfn, false, 128));
-        B3_TRY(build_linear(ctx, L.pw1, {p + "conv.pointwise_conv1.weight"}, 2 * kHidden, kHidden, true, 128));
-        B3_TRY(build_linear(ctx, L.pw2, {p + "conv.pointwise_conv2.weight"}, kHidden, kHidden, false, 128));
+                                         p + "self_attn.v_proj.weight"}, kHidden, kHidden, false));
+        B3_TRY(build_linear(ctx, L.relk, {p + "self_attn.relative_k_proj.weight"}, kHidden, kHidden, false));
+        B3_TRY(build_linear(ctx, L.o, {p + "self_attn.o_proj.weight"}, kHidden, kHidden, false));
+        B3_TRY(build_linear(ctx, L.ff1a, {p + "feed_forward1.linear1.weight"}, kFfn, kHidden, false));
+        B3_TRY(build_linear(ctx, L.ff1b, {p + "feed_forward1.linear2.weight"}, kHidden, kFfn, false));
+        B3_TRY(build_linear(ctx, L.ff2a, {p + "feed_forward2.linear1.weight"}, kFfn, kHidden, false));
+        B3_TRY(build_linear(ctx, L.ff2b, {p + "feed_forward2.linear2.weight"}, kHidden, kFfn, false));
+        B3_TRY(build_linear(ctx, L.pw1, {p + "conv.pointwise_conv1.weight"}, 2 * kHidden, kHidden, true));
+        B3_TRY(build_linear(ctx, L.pw2, {p + "conv.pointwise_conv2.weight"}, kHidden, kHidden, false));
         std::vector<float> prm(Layer::kParamFloats, 0.f);
         // depthwise taps rounded through f16 like every other weight
         // (src/cpu/mod.rs:101), stored tap-major for coalesced loads

@@ -14,17 +14,21 @@
 // (encoder/gemm.rs:247-493) and CPU path (cpu/mod.rs:35, bark.rs:379-392) use
 // exactly these f16 weights with f32 accumulation.
 //
-// Structure (one 128 x BN output tile per CTA, 192 threads):
-//   warp 0      TMA producer: A tile (128 x 64 f16, 128-byte swizzle) and the
-//               code tile (BN x 32 bytes) or the f16 B tile, into a
-//               STAGES-deep ring guarded by mbarriers;
-//   warp 1      allocates TMEM, one thread issues tcgen05.mma (M=128, N=BN,
-//               K=16, f32 accumulator in TMEM) and commits stages back;
-//   warps 2..5  LUT4: expand each code tile through the per-row table, kept
-//               in registers as byte planes and indexed with PRMT, into the
-//               128-byte-swizzled K-major f16 B tile the MMA reads; then all
-//               four run the epilogue: tcgen05.ld -> bias / SiLU / GLU /
-//               residual / q-k-v split -> global.
+// Persistent, warp-specialised kernel (one CTA per SM, 448 threads).  A tile
+// is SUB*128 rows x BN columns; tiles are walked m-major so the CTAs working at
+// the same time share A rows in L2 while the (small) 4-bit B stays L2-resident.
+//   warp 0       TMA producer: SUB A boxes (128 x 64 f16, 128-byte swizzle)
+//                and the code tile (BN x 32 B) or the f16 B tile per stage,
+//                into a STAGES-deep ring guarded by mbarriers;
+//   warp 1       TMEM owner; one thread issues tcgen05.mma (M=128, N=BN, K=16,
+//                f32 accumulators in TMEM), SUB MMAs per k-step share one B;
+//   warps 2..9   LUT4 expanders: the per-row table lives in registers as
+//                low/high byte planes; PRMT looks up four codes at a time and
+//                the f16 rows are written straight into the 128-byte-swizzled
+//                K-major B tile the MMA reads;
+//   warps 10..13 epilogue: tcgen05.ld -> bias / SiLU / GLU / residual /
+//                q-k-v split -> global.  TMEM holds two accumulator sets, so
+//                the epilogue of one tile overlaps the mainloop of the next.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -37,21 +41,29 @@ namespace b3 {
 
 namespace {
 
-constexpr int kBM = 128;
-constexpr int kBK = 64;
-constexpr int kThreads = 192;
+constexpr int kBM = 128;      // rows per MMA / per A box
+constexpr int kBK = 64;       // k per stage (one 128-byte swizzle row of f16)
+constexpr int kBoxN = 64;     // rows per B / code TMA box
+constexpr int kThreads = 448;
+constexpr int kExpThreads = 256;  // warps 2..9
+constexpr int kEpiWarp0 = 10;
 
-template <int BN, bool LUT>
+template <int BN, int SUB, bool LUT>
 struct GemmCfg {
-    static constexpr uint32_t kABytes = kBM * kBK * 2;
+    static constexpr uint32_t kABytes = kBM * kBK * 2;          // one A box
     static constexpr uint32_t kBBytes = BN * kBK * 2;
     static constexpr uint32_t kCBytes = LUT ? BN * kBK / 2 : 0;
-    static constexpr uint32_t kStageBytes = kABytes + kBBytes + kCBytes;
-    static constexpr int kStages = (BN == 128) ? (LUT ? 5 : 6) : (LUT ? 3 : 4);
-    static constexpr uint32_t kTmemCols = BN;  // power of two >= 32
-    static constexpr uint32_t kBarBytes = 256;
+    static constexpr uint32_t kStageBytes = SUB * kABytes + kBBytes + kCBytes;
+    static constexpr int kStages = (220 * 1024) / kStageBytes > 8 ? 8 : (220 * 1024) / kStageBytes;
+    static constexpr uint32_t kAccCols = SUB * BN;               // one accumulator set
+    static constexpr uint32_t kTmemCols = 2 * kAccCols <= 32 ? 32 : 2 * kAccCols;
+    static constexpr uint32_t kBarBytes = 512;
     static constexpr uint32_t kSmemBytes = kStages * kStageBytes + kBarBytes + 1024;
+    static constexpr int kTPR = kExpThreads / BN;               // expander threads per B row
+    static constexpr int kWPT = 8 / kTPR;                       // 16-byte chunks per thread per stage
     static_assert(kSmemBytes <= 232448, "shared memory budget");
+    static_assert(kTmemCols <= 512, "TMEM budget");
+    static_assert(kStages >= 2, "pipeline depth");
 };
 
 __device__ __forceinline__ float silu_f(float v) { return v / (1.0f + __expf(-v)); }
@@ -79,40 +91,123 @@ __device__ __forceinline__ void lut_expand8(uint32_t w, const uint32_t (&lo)[4],
     }
 }
 
-template <int BN, bool LUT, int EPI>
+// Epilogue of 32 accumulator columns [n, n+32) of output row gm.
+template <int EPI>
+__device__ __forceinline__ void epilogue32(const GemmParams& p, int gm, int n, float (&v)[32]) {
+    if (EPI == EPI_F32 || EPI == EPI_F16 || EPI == EPI_SILU_F16) {
+        if (p.bias) {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) v[i] += __ldg(p.bias + n + i);
+        }
+    }
+    if (EPI == EPI_F32) {
+        float4* dst = reinterpret_cast<float4*>(p.out_f32 + static_cast<size_t>(gm) * p.ldo + n);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+    } else if (EPI == EPI_RESID) {
+        float4* dst = reinterpret_cast<float4*>(p.out_f32 + static_cast<size_t>(gm) * p.ldo + n);
+        float4 x[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x[i] = dst[i];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            x[i].x += p.alpha * v[4 * i];
+            x[i].y += p.alpha * v[4 * i + 1];
+            x[i].z += p.alpha * v[4 * i + 2];
+            x[i].w += p.alpha * v[4 * i + 3];
+            dst[i] = x[i];
+        }
+    } else if (EPI == EPI_F16 || EPI == EPI_SILU_F16) {
+        uint4* dst = reinterpret_cast<uint4*>(p.out_f16 + static_cast<size_t>(gm) * p.ldo + n);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float t[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) t[j] = (EPI == EPI_SILU_F16) ? silu_f(v[8 * i + j]) : v[8 * i + j];
+            dst[i] = make_uint4(pack_h2(t[0], t[1]), pack_h2(t[2], t[3]), pack_h2(t[4], t[5]), pack_h2(t[6], t[7]));
+        }
+    } else if (EPI == EPI_GLU_F16) {
+        // W rows interleaved (value, gate) at load: column 2i is GLU input a_i,
+        // column 2i+1 its gate b_i.
+        float g[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+            float a = v[2 * i], b = v[2 * i + 1];
+            if (p.bias) {
+                a += __ldg(p.bias + n + 2 * i);
+                b += __ldg(p.bias + n + 2 * i + 1);
+            }
+            g[i] = a * sigmoid_f(b);
+        }
+        uint4* dst = reinterpret_cast<uint4*>(p.out_f16 + static_cast<size_t>(gm) * p.ldo + n / 2);
+        dst[0] = make_uint4(pack_h2(g[0], g[1]), pack_h2(g[2], g[3]), pack_h2(g[4], g[5]), pack_h2(g[6], g[7]));
+        dst[1] = make_uint4(pack_h2(g[8], g[9]), pack_h2(g[10], g[11]), pack_h2(g[12], g[13]), pack_h2(g[14], g[15]));
+    } else if (EPI == EPI_QKV) {
+        // output row = [q + bias_u | q + bias_v | k | v], 1024 f16 each
+        __half* orow = p.out_f16 + static_cast<size_t>(gm) * p.ldo;
+        if (n < 1024) {
+            uint4* du = reinterpret_cast<uint4*>(orow + n);
+            uint4* dv = reinterpret_cast<uint4*>(orow + 1024 + n);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                float a[8], b[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    a[j] = v[8 * i + j] + __ldg(p.bias_u + n + 8 * i + j);
+                    b[j] = v[8 * i + j] + __ldg(p.bias_v + n + 8 * i + j);
+                }
+                du[i] = make_uint4(pack_h2(a[0], a[1]), pack_h2(a[2], a[3]), pack_h2(a[4], a[5]), pack_h2(a[6], a[7]));
+                dv[i] = make_uint4(pack_h2(b[0], b[1]), pack_h2(b[2], b[3]), pack_h2(b[4], b[5]), pack_h2(b[6], b[7]));
+            }
+        } else {
+            uint4* dk = reinterpret_cast<uint4*>(orow + n + 1024);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+                dk[i] = make_uint4(pack_h2(v[8 * i], v[8 * i + 1]), pack_h2(v[8 * i + 2], v[8 * i + 3]),
+                                   pack_h2(v[8 * i + 4], v[8 * i + 5]), pack_h2(v[8 * i + 6], v[8 * i + 7]));
+        }
+    }
+}
+
+template <int BN, int SUB, bool LUT, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     k1_gemm(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
             const GemmParams p) {
-    using Cfg = GemmCfg<BN, LUT>;
+    using Cfg = GemmCfg<BN, SUB, LUT>;
     constexpr int S = Cfg::kStages;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
-    uint8_t* sA = smem;
-    uint8_t* sB = smem + S * Cfg::kABytes;
-    uint8_t* sC = sB + S * Cfg::kBBytes;
+    uint8_t* sA = smem;                              // [S][SUB][128 x 64 f16]
+    uint8_t* sB = smem + S * SUB * Cfg::kABytes;     // [S][BN x 64 f16]
+    uint8_t* sC = sB + S * Cfg::kBBytes;             // [S][BN x 32 B]
     uint64_t* bars = reinterpret_cast<uint64_t*>(sC + S * Cfg::kCBytes);
     uint64_t* full = bars;
     uint64_t* bready = bars + S;
     uint64_t* empty = bars + 2 * S;
-    uint64_t* accf = bars + 3 * S;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 1);
+    uint64_t* tfull = bars + 3 * S;       // [2]
+    uint64_t* tempty = bars + 3 * S + 2;  // [2]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 4);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * BN;
-    const int m0 = blockIdx.y * kBM;
     const int num_k = p.K / kBK;
+    const int n_tiles = p.N / BN;
+    const int m_tiles = (p.M + SUB * kBM - 1) / (SUB * kBM);
+    const int num_tiles = n_tiles * m_tiles;
 
     if (threadIdx.x == 0) {
         tma_prefetch_desc(&tm_a);
         tma_prefetch_desc(&tm_b);
         for (int s = 0; s < S; ++s) {
             mbar_init(smem_u32(&full[s]), 1);
-            mbar_init(smem_u32(&bready[s]), 128);
+            mbar_init(smem_u32(&bready[s]), kExpThreads);
             mbar_init(smem_u32(&empty[s]), 1);
         }
-        mbar_init(smem_u32(accf), 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(smem_u32(&tfull[b]), 1);
+            mbar_init(smem_u32(&tempty[b]), 128);
+        }
         fence_mbar_init();
     }
     if (warp == 1) {
@@ -125,190 +220,151 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t tmem = *tmem_slot;
 
     if (warp == 0) {
+        // ── TMA producer ──
         if (lane == 0) {
-            for (int it = 0; it < num_k; ++it) {
-                const int s = it % S;
-                const uint32_t ph = (it / S) & 1;
-                if (it >= S && !mbar_wait(smem_u32(&empty[s]), ph ^ 1, 0x01)) break;
-                const uint32_t fb = smem_u32(&full[s]);
-                mbar_arrive_expect_tx(fb, Cfg::kABytes + (LUT ? Cfg::kCBytes : Cfg::kBBytes));
-                tma_load_2d(smem_u32(sA + s * Cfg::kABytes), &tm_a, fb, it * kBK, m0);
-                if (LUT)
-                    tma_load_2d(smem_u32(sC + s * Cfg::kCBytes), &tm_b, fb, it * (kBK / 2), n0);
-                else
-                    tma_load_2d(smem_u32(sB + s * Cfg::kBBytes), &tm_b, fb, it * kBK, n0);
+            int it = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+                const int m0 = (tile / n_tiles) * SUB * kBM;
+                const int n0 = (tile % n_tiles) * BN;
+                for (int kb = 0; kb < num_k; ++kb, ++it) {
+                    const int s = it % S;
+                    const uint32_t ph = (it / S) & 1;
+                    if (it >= S && !(ok = mbar_wait(smem_u32(&empty[s]), ph ^ 1, 0x01))) break;
+                    const uint32_t fb = smem_u32(&full[s]);
+                    mbar_arrive_expect_tx(fb, SUB * Cfg::kABytes + (LUT ? Cfg::kCBytes : Cfg::kBBytes));
+#pragma unroll
+                    for (int sub = 0; sub < SUB; ++sub)
+                        tma_load_2d(smem_u32(sA + (s * SUB + sub) * Cfg::kABytes), &tm_a, fb, kb * kBK,
+                                    m0 + sub * kBM);
+#pragma unroll
+                    for (int r = 0; r < BN / kBoxN; ++r) {
+                        if (LUT)
+                            tma_load_2d(smem_u32(sC + s * Cfg::kCBytes + r * kBoxN * (kBK / 2)), &tm_b, fb,
+                                        kb * (kBK / 2), n0 + r * kBoxN);
+                        else
+                            tma_load_2d(smem_u32(sB + s * Cfg::kBBytes + r * kBoxN * kBK * 2), &tm_b, fb,
+                                        kb * kBK, n0 + r * kBoxN);
+                    }
+                }
             }
         }
     } else if (warp == 1) {
+        // ── MMA issuer ──
         if (lane == 0) {
             constexpr uint32_t idesc = idesc_f16_f32<kBM, BN>();
+            int it = 0, lt = 0;
             bool ok = true;
-            for (int it = 0; it < num_k && ok; ++it) {
-                const int s = it % S;
-                const uint32_t ph = (it / S) & 1;
-                ok = mbar_wait(smem_u32(&full[s]), ph, 0x02);
-                if (ok && LUT) ok = mbar_wait(smem_u32(&bready[s]), ph, 0x03);
-                if (!ok) break;
+            for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++lt) {
+                const int b = lt & 1;
+                const int use = lt >> 1;
+                if (use > 0 && !(ok = mbar_wait(smem_u32(&tempty[b]), (use - 1) & 1, 0x06))) break;
                 tc_fence_after();
-                const uint32_t a0 = smem_u32(sA + s * Cfg::kABytes);
-                const uint32_t b0 = smem_u32(sB + s * Cfg::kBBytes);
+                const uint32_t acc = tmem + b * Cfg::kAccCols;
+                for (int kb = 0; kb < num_k; ++kb, ++it) {
+                    const int s = it % S;
+                    const uint32_t ph = (it / S) & 1;
+                    ok = mbar_wait(smem_u32(&full[s]), ph, 0x02);
+                    if (ok && LUT) ok = mbar_wait(smem_u32(&bready[s]), ph, 0x03);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t b0 = smem_u32(sB + s * Cfg::kBBytes);
 #pragma unroll
-                for (int kk = 0; kk < kBK / 16; ++kk) {
-                    mma_f16_ss(tmem, smem_desc_sw128(a0 + kk * 32), smem_desc_sw128(b0 + kk * 32),
-                               idesc, (it | kk) != 0);
+                    for (int kk = 0; kk < kBK / 16; ++kk) {
+                        const uint64_t bd = smem_desc_sw128(b0 + kk * 32);
+#pragma unroll
+                        for (int sub = 0; sub < SUB; ++sub) {
+                            const uint32_t a0 = smem_u32(sA + (s * SUB + sub) * Cfg::kABytes);
+                            mma_f16_ss(acc + sub * BN, smem_desc_sw128(a0 + kk * 32), bd, idesc, (kb | kk) != 0);
+                        }
+                    }
+                    mma_commit(smem_u32(&empty[s]));
                 }
-                mma_commit(smem_u32(&empty[s]));
+                if (ok) mma_commit(smem_u32(&tfull[b]));
             }
-            if (ok) mma_commit(smem_u32(accf));
+        }
+    } else if (warp < kEpiWarp0) {
+        // ── LUT expanders ──
+        if (LUT) {
+            constexpr int TPR = Cfg::kTPR, WPT = Cfg::kWPT;
+            const int e = threadIdx.x - 64;
+            const int row = e / TPR;           // B row within the tile
+            const int w0 = (e % TPR) * WPT;    // first 16-byte chunk of this thread
+            int it = 0;
+            for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+                const int n0 = (tile % n_tiles) * BN;
+                uint32_t lo[4], hi[4];
+                {
+                    const uint4* src = reinterpret_cast<const uint4*>(p.lut + static_cast<size_t>(n0 + row) * 16);
+                    const uint4 u0 = __ldg(src), u1 = __ldg(src + 1);
+                    // entries (2i, 2i+1) in word i -> byte planes of 4 entries
+                    lo[0] = prmt(u0.x, u0.y, 0x6420u);
+                    hi[0] = prmt(u0.x, u0.y, 0x7531u);
+                    lo[1] = prmt(u0.z, u0.w, 0x6420u);
+                    hi[1] = prmt(u0.z, u0.w, 0x7531u);
+                    lo[2] = prmt(u1.x, u1.y, 0x6420u);
+                    hi[2] = prmt(u1.x, u1.y, 0x7531u);
+                    lo[3] = prmt(u1.z, u1.w, 0x6420u);
+                    hi[3] = prmt(u1.z, u1.w, 0x7531u);
+                }
+                bool ok = true;
+                for (int kb = 0; kb < num_k; ++kb, ++it) {
+                    const int s = it % S;
+                    const uint32_t ph = (it / S) & 1;
+                    if (!(ok = mbar_wait(smem_u32(&full[s]), ph, 0x04))) break;
+                    const uint8_t* codes = sC + s * Cfg::kCBytes + row * 32 + w0 * 4;
+                    uint32_t wds[WPT];
+                    if (WPT == 4) {
+                        const uint4 c = *reinterpret_cast<const uint4*>(codes);
+                        wds[0] = c.x; wds[1] = c.y; wds[2 % WPT] = c.z; wds[3 % WPT] = c.w;
+                    } else if (WPT == 2) {
+                        const uint2 c = *reinterpret_cast<const uint2*>(codes);
+                        wds[0] = c.x; wds[1 % WPT] = c.y;
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < WPT; ++j) wds[j] = reinterpret_cast<const uint32_t*>(codes)[j];
+                    }
+                    uint8_t* brow = sB + s * Cfg::kBBytes + (row >> 3) * 1024 + (row & 7) * 128;
+#pragma unroll
+                    for (int j = 0; j < WPT; ++j) {
+                        uint32_t o[4];
+                        lut_expand8(wds[j], lo, hi, o);
+                        *reinterpret_cast<uint4*>(brow + (((w0 + j) ^ (row & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+                    }
+                    fence_async_shared();
+                    mbar_arrive(smem_u32(&bready[s]));
+                }
+                if (!ok) break;
+            }
         }
     } else {
-        // warps 2..5: 128 threads
-        const int e = threadIdx.x - 64;
-        bool ok = true;
-        if (LUT) {
-            constexpr int RPT = BN / 128;  // rows of B per thread
-            uint32_t lo[RPT][4], hi[RPT][4];
-#pragma unroll
-            for (int r = 0; r < RPT; ++r) {
-                const int n = n0 + e + 128 * r;
-                const uint4* src = reinterpret_cast<const uint4*>(p.lut + static_cast<size_t>(n) * 16);
-                const uint4 u0 = __ldg(src), u1 = __ldg(src + 1);
-                // entries (2i, 2i+1) in word i; byte planes of 4 entries each
-                lo[r][0] = prmt(u0.x, u0.y, 0x6420u);
-                hi[r][0] = prmt(u0.x, u0.y, 0x7531u);
-                lo[r][1] = prmt(u0.z, u0.w, 0x6420u);
-                hi[r][1] = prmt(u0.z, u0.w, 0x7531u);
-                lo[r][2] = prmt(u1.x, u1.y, 0x6420u);
-                hi[r][2] = prmt(u1.x, u1.y, 0x7531u);
-                lo[r][3] = prmt(u1.z, u1.w, 0x6420u);
-                hi[r][3] = prmt(u1.z, u1.w, 0x7531u);
-            }
-            for (int it = 0; it < num_k; ++it) {
-                const int s = it % S;
-                const uint32_t ph = (it / S) & 1;
-                if (!mbar_wait(smem_u32(&full[s]), ph, 0x04)) {
-                    ok = false;
-                    break;
-                }
-                const uint8_t* codes = sC + s * Cfg::kCBytes;
-                uint8_t* bt = sB + s * Cfg::kBBytes;
-#pragma unroll
-                for (int r = 0; r < RPT; ++r) {
-                    const int n = e + 128 * r;
-                    const uint4 c0 = *reinterpret_cast<const uint4*>(codes + n * 32);
-                    const uint4 c1 = *reinterpret_cast<const uint4*>(codes + n * 32 + 16);
-                    const uint32_t wds[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-                    uint8_t* row = bt + (n >> 3) * 1024 + (n & 7) * 128;
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        uint32_t o[4];
-                        lut_expand8(wds[j], lo[r], hi[r], o);
-                        *reinterpret_cast<uint4*>(row + ((j ^ (n & 7)) << 4)) =
-                            make_uint4(o[0], o[1], o[2], o[3]);
-                    }
-                }
-                fence_async_shared();
-                mbar_arrive(smem_u32(&bready[s]));
-            }
-        }
-        // ── epilogue ──
-        if (ok) ok = mbar_wait(smem_u32(accf), 0, 0x05);
-        if (ok) {
+        // ── epilogue (4 warps, one TMEM lane quarter each) ──
+        const int q = warp & 3;
+        int lt = 0;
+        for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++lt) {
+            const int m0 = (tile / n_tiles) * SUB * kBM;
+            const int n0 = (tile % n_tiles) * BN;
+            const int b = lt & 1;
+            if (!mbar_wait(smem_u32(&tfull[b]), (lt >> 1) & 1, 0x05)) break;
             tc_fence_after();
-            const int q = warp & 3;
-            const int row = q * 32 + lane;
-            const int gm = m0 + row;
-            const bool live = gm < p.M;
 #pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(q * 32) << 16) + c * 32, r);
-                tmem_wait_ld();
-                if (!live) continue;
-                const int n = n0 + c * 32;
-                float v[32];
+            for (int sub = 0; sub < SUB; ++sub) {
+                const int gm = m0 + sub * kBM + q * 32 + lane;
+                const bool live = gm < p.M;
+#pragma unroll 1
+                for (int c = 0; c < BN / 32; ++c) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(q * 32) << 16) + b * Cfg::kAccCols + sub * BN + c * 32, r);
+                    tmem_wait_ld();
+                    if (!live) continue;
+                    float v[32];
 #pragma unroll
-                for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-                if (EPI == EPI_F32 || EPI == EPI_F16 || EPI == EPI_SILU_F16) {
-                    if (p.bias) {
-#pragma unroll
-                        for (int i = 0; i < 32; ++i) v[i] += __ldg(p.bias + n + i);
-                    }
-                }
-                if (EPI == EPI_F32) {
-                    float4* dst = reinterpret_cast<float4*>(p.out_f32 + static_cast<size_t>(gm) * p.ldo + n);
-#pragma unroll
-                    for (int i = 0; i < 8; ++i)
-                        dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-                } else if (EPI == EPI_RESID) {
-                    float4* dst = reinterpret_cast<float4*>(p.out_f32 + static_cast<size_t>(gm) * p.ldo + n);
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        float4 x = dst[i];
-                        x.x += p.alpha * v[4 * i];
-                        x.y += p.alpha * v[4 * i + 1];
-                        x.z += p.alpha * v[4 * i + 2];
-                        x.w += p.alpha * v[4 * i + 3];
-                        dst[i] = x;
-                    }
-                } else if (EPI == EPI_F16 || EPI == EPI_SILU_F16) {
-                    uint4* dst = reinterpret_cast<uint4*>(p.out_f16 + static_cast<size_t>(gm) * p.ldo + n);
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        float t[8];
-#pragma unroll
-                        for (int j = 0; j < 8; ++j)
-                            t[j] = (EPI == EPI_SILU_F16) ? silu_f(v[8 * i + j]) : v[8 * i + j];
-                        dst[i] = make_uint4(pack_h2(t[0], t[1]), pack_h2(t[2], t[3]),
-                                            pack_h2(t[4], t[5]), pack_h2(t[6], t[7]));
-                    }
-                } else if (EPI == EPI_GLU_F16) {
-                    // rows of W interleaved (value, gate) at load: column 2i is
-                    // GLU input a_i, column 2i+1 is its gate b_i.
-                    float g[16];
-#pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        float a = v[2 * i], b = v[2 * i + 1];
-                        if (p.bias) {
-                            a += __ldg(p.bias + n + 2 * i);
-                            b += __ldg(p.bias + n + 2 * i + 1);
-                        }
-                        g[i] = a * sigmoid_f(b);
-                    }
-                    uint4* dst = reinterpret_cast<uint4*>(p.out_f16 + static_cast<size_t>(gm) * p.ldo + n / 2);
-                    dst[0] = make_uint4(pack_h2(g[0], g[1]), pack_h2(g[2], g[3]), pack_h2(g[4], g[5]),
-                                        pack_h2(g[6], g[7]));
-                    dst[1] = make_uint4(pack_h2(g[8], g[9]), pack_h2(g[10], g[11]),
-                                        pack_h2(g[12], g[13]), pack_h2(g[14], g[15]));
-                } else if (EPI == EPI_QKV) {
-                    // out row layout [qu | qv | k | v], 1024 f16 each.
-                    __half* orow = p.out_f16 + static_cast<size_t>(gm) * p.ldo;
-                    if (n < 1024) {
-                        uint4* du = reinterpret_cast<uint4*>(orow + n);
-                        uint4* dv = reinterpret_cast<uint4*>(orow + 1024 + n);
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            float a[8], b[8];
-#pragma unroll
-                            for (int j = 0; j < 8; ++j) {
-                                a[j] = v[8 * i + j] + __ldg(p.bias_u + n + 8 * i + j);
-                                b[j] = v[8 * i + j] + __ldg(p.bias_v + n + 8 * i + j);
-                            }
-                            du[i] = make_uint4(pack_h2(a[0], a[1]), pack_h2(a[2], a[3]),
-                                               pack_h2(a[4], a[5]), pack_h2(a[6], a[7]));
-                            dv[i] = make_uint4(pack_h2(b[0], b[1]), pack_h2(b[2], b[3]),
-                                               pack_h2(b[4], b[5]), pack_h2(b[6], b[7]));
-                        }
-                    } else {
-                        uint4* dk = reinterpret_cast<uint4*>(orow + n + 1024);
-#pragma unroll
-                        for (int i = 0; i < 4; ++i)
-                            dk[i] = make_uint4(pack_h2(v[8 * i], v[8 * i + 1]), pack_h2(v[8 * i + 2], v[8 * i + 3]),
-                                               pack_h2(v[8 * i + 4], v[8 * i + 5]),
-                                               pack_h2(v[8 * i + 6], v[8 * i + 7]));
-                    }
+                    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+                    epilogue32<EPI>(p, gm, n0 + c * 32, v);
                 }
             }
+            tc_fence_before();
+            mbar_arrive(smem_u32(&tempty[b]));
         }
     }
 
@@ -320,10 +376,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
-template <int BN, bool LUT, int EPI>
+int g_num_sms = 0;
+
+template <int BN, int SUB, bool LUT, int EPI>
 int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t st) {
-    using Cfg = GemmCfg<BN, LUT>;
-    auto kern = k1_gemm<BN, LUT, EPI>;
+    using Cfg = GemmCfg<BN, SUB, LUT>;
+    auto kern = k1_gemm<BN, SUB, LUT, EPI>;
     static bool attr_done = false;  // per template instance
     if (!attr_done) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -331,23 +389,29 @@ int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p
         if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(k1_gemm)", e);
         attr_done = true;
     }
-    dim3 grid(p.N / BN, (p.M + kBM - 1) / kBM);
+    if (!g_num_sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+        if (g_num_sms <= 0) g_num_sms = 148;
+    }
+    const int tiles = (p.N / BN) * ((p.M + SUB * kBM - 1) / (SUB * kBM));
+    const int grid = tiles < g_num_sms ? tiles : g_num_sms;
     kern<<<grid, kThreads, Cfg::kSmemBytes, st>>>(ta, tb, p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_cuda_error("k1_gemm launch", e);
     return 0;
 }
 
-template <int BN, bool LUT>
-int launch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p,
-               cudaStream_t st) {
+template <int BN, int SUB, bool LUT>
+int launch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t st) {
     switch (epi) {
-        case EPI_F32: return launch_one<BN, LUT, EPI_F32>(ta, tb, p, st);
-        case EPI_RESID: return launch_one<BN, LUT, EPI_RESID>(ta, tb, p, st);
-        case EPI_F16: return launch_one<BN, LUT, EPI_F16>(ta, tb, p, st);
-        case EPI_SILU_F16: return launch_one<BN, LUT, EPI_SILU_F16>(ta, tb, p, st);
-        case EPI_GLU_F16: return launch_one<BN, LUT, EPI_GLU_F16>(ta, tb, p, st);
-        case EPI_QKV: return launch_one<BN, LUT, EPI_QKV>(ta, tb, p, st);
+        case EPI_F32: return launch_one<BN, SUB, LUT, EPI_F32>(ta, tb, p, st);
+        case EPI_RESID: return launch_one<BN, SUB, LUT, EPI_RESID>(ta, tb, p, st);
+        case EPI_F16: return launch_one<BN, SUB, LUT, EPI_F16>(ta, tb, p, st);
+        case EPI_SILU_F16: return launch_one<BN, SUB, LUT, EPI_SILU_F16>(ta, tb, p, st);
+        case EPI_GLU_F16: return launch_one<BN, SUB, LUT, EPI_GLU_F16>(ta, tb, p, st);
+        case EPI_QKV: return launch_one<BN, SUB, LUT, EPI_QKV>(ta, tb, p, st);
         default: return set_error(B3_EINVAL, "unknown GEMM epilogue %d", epi);
     }
 }
@@ -366,27 +430,29 @@ int gemm_take_dev_error(cudaStream_t st, unsigned int* out) {
     return e == cudaSuccess ? 0 : set_cuda_error("reading the device error word", e);
 }
 
-int gemm_validate(const GemmParams& p, bool lut, int bn) {
-    if (p.M <= 0 || p.N <= 0 || p.K <= 0) return set_error(B3_EINVAL, "GEMM sizes must be positive (M=%d N=%d K=%d)", p.M, p.N, p.K);
+int gemm_validate(const GemmParams& p, bool lut) {
+    if (p.M <= 0 || p.N <= 0 || p.K <= 0)
+        return set_error(B3_EINVAL, "GEMM sizes must be positive (M=%d N=%d K=%d)", p.M, p.N, p.K);
     if (p.K % kBK) return set_error(B3_EINVAL, "GEMM K=%d must be a multiple of %d", p.K, kBK);
-    if (p.N % bn) return set_error(B3_EINVAL, "GEMM N=%d must be a multiple of %d", p.N, bn);
+    if (p.N % 128) return set_error(B3_EINVAL, "GEMM N=%d must be a multiple of 128", p.N);
     if (lut && !p.lut) return set_error(B3_EINVAL, "LUT4 GEMM needs a level table");
     return 0;
 }
 
+// Tile shape by problem size: large M takes 256 x 128 tiles (two MMAs share
+// each expanded B tile); small M takes 128 x 64 tiles to spread over the SMs.
 int gemm_launch(const GemmOp& op, cudaStream_t st) {
     const GemmParams& p = op.p;
-    const int bn = op.bn;
-    int rc = gemm_validate(p, op.lut, bn);
+    int rc = gemm_validate(p, op.lut);
     if (rc) return rc;
+    const long big_tiles = static_cast<long>(p.N / 128) * ((p.M + 255) / 256);
+    const bool big = big_tiles >= 2 * 148 || p.M >= 2048;
     if (op.lut) {
-        if (bn == 128) return launch_epi<128, true>(op.epi, op.map_a, op.map_b, p, st);
-        if (bn == 256) return launch_epi<256, true>(op.epi, op.map_a, op.map_b, p, st);
-    } else {
-        if (bn == 128) return launch_epi<128, false>(op.epi, op.map_a, op.map_b, p, st);
-        if (bn == 256) return launch_epi<256, false>(op.epi, op.map_a, op.map_b, p, st);
+        if (big) return launch_epi<128, 2, true>(op.epi, op.map_a, op.map_b, p, st);
+        return launch_epi<64, 1, true>(op.epi, op.map_a, op.map_b, p, st);
     }
-    return set_error(B3_EINVAL, "unsupported GEMM tile N=%d", bn);
+    if (big) return launch_epi<128, 2, false>(op.epi, op.map_a, op.map_b, p, st);
+    return launch_epi<64, 1, false>(op.epi, op.map_a, op.map_b, p, st);
 }
 
 // ───────────────────────────── tensor maps ─────────────────────────────
@@ -402,8 +468,7 @@ EncodeTiledFn encode_fn() {
     if (!fn) {
         void* ptr = nullptr;
         cudaDriverEntryPointQueryResult q;
-        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
-                cudaSuccess &&
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
             q == cudaDriverEntryPointSuccess)
             fn = reinterpret_cast<EncodeTiledFn>(ptr);
     }
@@ -434,12 +499,14 @@ int gemm_make_a_map(CUtensorMap* map, const __half* a, int M, int K, int lda) {
                        static_cast<uint64_t>(lda) * 2, kBK, kBM, true);
 }
 
-int gemm_make_b_map(CUtensorMap* map, const void* w, bool lut, int N, int K, int bn) {
+// B boxes are 64 rows tall whatever the tile width; the producer issues
+// BN / 64 of them per stage.
+int gemm_make_b_map(CUtensorMap* map, const void* w, bool lut, int N, int K) {
     if (lut)
         return make_map_2d(map, w, false, static_cast<uint64_t>(K / 2), static_cast<uint64_t>(N),
-                           static_cast<uint64_t>(K / 2), kBK / 2, bn, false);
+                           static_cast<uint64_t>(K / 2), kBK / 2, kBoxN, false);
     return make_map_2d(map, w, true, static_cast<uint64_t>(K), static_cast<uint64_t>(N),
-                       static_cast<uint64_t>(K) * 2, kBK, bn, true);
+                       static_cast<uint64_t>(K) * 2, kBK, kBoxN, true);
 }
 
 }  // namespace b3
