@@ -53,7 +53,63 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=5)
+    ap.add_argument("--workload", default="batch", choices=["batch", "linear"],
+                    help="batch: the encoder over the config-5 batch; linear: K1 GEMM shape sweep (config 1)")
     return ap.parse_args()
+
+
+def run_linear_sweep(args):
+    """BASELINE config 1 (M=1875, K=1024, N=4096, f32 activations, bias) and the
+    M >= 2048 sweep of the north-star GEMM target, through b3_linear_lut4 with
+    device pointers.  One JSON line per shape; the GEMM kernel is timed alone
+    (the f32 -> f16 conversion of A is a separate, separately timed kernel)."""
+    import ctypes
+
+    import torch
+
+    pkg = load_package()
+    import bark3_b200.synthetic as syn
+
+    enc = pkg.Encoder(0)
+    L = pkg.lib()
+    pk, pk_kind = peaks()
+    rng = np.random.default_rng(args.seed)
+    shapes = [(1875, 4096, 1024), (2048, 4096, 1024), (4096, 4096, 1024), (8192, 4096, 1024),
+              (16384, 4096, 1024), (8192, 1024, 4096), (8192, 3072, 1024), (110894, 4096, 1024)]
+    for m, n, k in shapes:
+        codes, lut16 = syn.make_lut4(rng, n, k)
+        a = torch.randn(m, k, device="cuda")
+        bias = torch.randn(n, device="cuda") * 0.01
+        tc = torch.from_numpy(codes).cuda()
+        tl = torch.from_numpy(lut16.view(np.int16)).cuda()
+        out = torch.empty(m, n, device="cuda")
+        torch.cuda.synchronize()
+        for _ in range(args.warmup):
+            enc.linear_lut4(a, tc, tl, bias, out=out)
+        enc.sync()
+        L.b3_profile(enc.ctx, 1)
+        for _ in range(args.steps):
+            enc.linear_lut4(a, tc, tl, bias, out=out)
+        vals = {}
+        for kind in (pkg_kind("gemm_lut4"), pkg_kind("convert")):
+            t, f, b, nl = ctypes.c_double(), ctypes.c_double(), ctypes.c_double(), ctypes.c_int64()
+            pkg.check(L.b3_profile_read(enc.ctx, kind, ctypes.byref(t), ctypes.byref(f), ctypes.byref(b), ctypes.byref(nl)))
+            vals[kind] = (t.value, f.value, b.value, nl.value)
+        L.b3_profile(enc.ctx, 0)
+        t, f, b, nl = vals[pkg_kind("gemm_lut4")]
+        tflops = f / (t / 1000.0) / 1e12
+        peak = pk.get("bf16_tflops")
+        print(json.dumps({"workload": "k1 LUT4 linear", "m": m, "n": n, "k": k, "us_per_launch": round(1000 * t / nl, 2),
+                          "TFLOP/s": round(tflops, 1), "frac_of_burst_peak": round(tflops / peak, 4),
+                          "peak": f"bf16_tflops (burst) of {pk_kind}", "alg_GB/s": round(b / t / 1e6, 1),
+                          "convert_us": round(1000 * vals[pkg_kind('convert')][0] / max(1, vals[pkg_kind('convert')][3]), 2)}),
+              flush=True)
+        del a, out, tc, tl
+    enc.close()
+
+
+def pkg_kind(name):
+    return ["gemm_lut4", "gemm_f16", "attention", "layernorm", "dwconv", "convert", "other"].index(name)
 
 
 def peaks():
@@ -203,6 +259,10 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         run_reference(args, rank, world)
+        return
+    if args.workload == "linear":
+        if rank == 0:
+            run_linear_sweep(args)
         return
 
     import torch
