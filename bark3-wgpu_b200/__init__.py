@@ -84,6 +84,9 @@ def lib() -> ctypes.CDLL:
         "b3_linear_lut4": (c_i, [c_p, c_p, c_p, c_p, c_p, c_p, c_i, c_i, c_i, c_u]),
         "b3_linear_f16": (c_i, [c_p, c_p, c_p, c_p, c_p, c_i, c_i, c_i, c_u]),
         "b3_attn_conv": (c_i, [c_p, c_i, c_p, c_i, c_u]),
+        "b3_linear_lut4_noalloc": (c_i, [c_p, c_p, c_p, c_p, c_p, c_i, c_i, c_i, c_p]),
+        "b3_profile": (c_i, [c_p, c_i]),
+        "b3_profile_read": (c_i, [c_p, c_i, c_p, c_p, c_p, c_p]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
