@@ -132,6 +132,20 @@ int b3_linear_lut4(b3_ctx* ctx, const float* a, const uint8_t* codes, const uint
 int b3_linear_f16(b3_ctx* ctx, const float* a, const uint16_t* w16, const float* bias, float* c,
                   int m, int n, int k, unsigned flags);
 
+/* Allocation-free twin of b3_linear_lut4 for callers that must not allocate
+ * device memory: latency-critical threads (cudaMalloc / cudaFree can
+ * synchronise the device) and hosts that account for all GPU memory in their
+ * own pool.  No counterpart in the reference.  All pointers are device
+ * pointers; the work is enqueued on `stream` (a cudaStream_t, NULL = legacy
+ * default stream) of the current device, and nothing is allocated.  The f16
+ * copy of `a` is staged in a fixed 8 MiB scratch array inside the library
+ * (held by every GPU that loads it until exit), so m * k <= 4194304; larger
+ * calls fail with B3_EINVAL.  The first call on a device looks the scratch
+ * address up (cudaGetSymbolAddress); make it before any stream capture.
+ * Calls whose work overlaps on one GPU race on the shared scratch. */
+int b3_linear_lut4_noalloc(const float* a, const uint8_t* codes, const uint16_t* lut16,
+                           const float* bias, float* c, int m, int n, int k, void* stream);
+
 /* BASELINE config 4: the attention and conv sections of block `layer`
  * (src/cpu/layer.rs:198-310) on one sequence, in place:
  *   x += MHSA(LN_att(x));  x += Conv(LN_conv(x)).
