@@ -87,6 +87,7 @@ def lib() -> ctypes.CDLL:
         "b3_linear_lut4_noalloc": (c_i, [c_p, c_p, c_p, c_p, c_p, c_i, c_i, c_i, c_p]),
         "b3_profile": (c_i, [c_p, c_i]),
         "b3_profile_read": (c_i, [c_p, c_i, c_p, c_p, c_p, c_p]),
+        "b3_shard_lpt": (c_i, [c_p, c_i, c_i, c_p]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -249,6 +250,15 @@ def _empty_like_kind(ref, shape):
     import torch
 
     return torch.empty(shape, dtype=torch.float32, device=ref.device)
+
+
+def shard_lpt(frames, n_ranks: int) -> np.ndarray:
+    """rank_of[i] for each utterance (b3_shard_lpt: longest processing time
+    first by the estimated encoder cost)."""
+    fr = np.ascontiguousarray(frames, dtype=np.int32)
+    out = np.empty(len(fr), dtype=np.int32)
+    check(lib().b3_shard_lpt(_ptr(fr), len(fr), n_ranks, _ptr(out)))
+    return out
 
 
 def frames_for_seconds(seconds: float) -> int:

@@ -29,6 +29,7 @@
 #include <map>
 #include <string>
 #include <vector>
+#include <algorithm>
 
 #include "b3_internal.h"
 #include "b3_kernels.h"
@@ -879,6 +880,28 @@ int b3_finalize(b3_ctx* ctx, int n_layers) {
     ctx->n_layers = n_layers;
     ctx->finalized = true;
     ctx->staged.clear();
+    return 0;
+}
+
+int b3_shard_lpt(const int32_t* frames, int n_utt, int n_ranks, int32_t* rank_of) {
+    if (!frames || !rank_of || n_utt < 0 || n_ranks <= 0) return set_error(B3_EINVAL, "b3_shard_lpt: bad arguments");
+    std::vector<int> order(n_utt);
+    std::vector<double> cost(n_utt);
+    for (int i = 0; i < n_utt; ++i) {
+        if (frames[i] <= 0) return set_error(B3_EINVAL, "utterance %d has %d frames", i, frames[i]);
+        const double t = frames[i];
+        cost[i] = 52.4e6 * t + 6144.0 * t * t;
+        order[i] = i;
+    }
+    std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return cost[a] > cost[b]; });
+    std::vector<double> load(n_ranks, 0.0);
+    for (int i : order) {
+        int best = 0;
+        for (int r = 1; r < n_ranks; ++r)
+            if (load[r] < load[best]) best = r;
+        rank_of[i] = best;
+        load[best] += cost[i];
+    }
     return 0;
 }
 

@@ -120,26 +120,13 @@ def peaks():
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
-def lpt_shards(frames, n_ranks):
-    """Longest-processing-time assignment of utterances to ranks by the
-    estimated encoder cost c(T) = 52.4M T + 6144 T^2 (FLOPs per block)."""
-    cost = [52.4e6 * t + 6144.0 * t * t for t in frames]
-    order = sorted(range(len(frames)), key=lambda i: -cost[i])
-    load = [0.0] * n_ranks
-    shards = [[] for _ in range(n_ranks)]
-    for i in order:
-        r = min(range(n_ranks), key=lambda j: load[j])
-        shards[r].append(i)
-        load[r] += cost[i]
-    return [sorted(s) for s in shards]
-
-
 def batch_for_rank(args, rank, world, pkg, syn):
     """(seconds per utterance, frames per utterance) of this rank's batch."""
     if args.strong:
         secs = syn.batch_lengths(args.seed, args.utterances)
         frames = [pkg.frames_for_seconds(s) for s in secs]
-        mine = lpt_shards(frames, world)[rank]
+        rank_of = pkg.shard_lpt(frames, world)
+        mine = [i for i in range(len(frames)) if rank_of[i] == rank]
         return [float(secs[i]) for i in mine], [frames[i] for i in mine]
     secs = syn.batch_lengths(args.seed + 1000 * rank, args.utterances)
     return [float(s) for s in secs], [pkg.frames_for_seconds(s) for s in secs]

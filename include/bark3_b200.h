@@ -152,6 +152,15 @@ int b3_linear_lut4_noalloc(const float* a, const uint8_t* codes, const uint16_t*
  * x is [t][1024]. */
 int b3_attn_conv(b3_ctx* ctx, int layer, float* x, int t, unsigned flags);
 
+/* ──────────────────────────── multi-GPU ────────────────────────────
+ * Utterance sharding for one process (or host thread) per GPU.  The reference
+ * is single-device; utterances are independent, so a batch is split across
+ * GPUs with no collective.  rank_of[i] receives the rank (0..n_ranks-1) that
+ * encodes utterance i, chosen longest-processing-time first by the estimated
+ * encoder cost c(T) = 52.4e6 T + 6144 T^2 (FLOPs per block; ties go to the
+ * lower rank).  Pure host code. */
+int b3_shard_lpt(const int32_t* frames, int n_utt, int n_ranks, int32_t* rank_of);
+
 /* ───────────────────────────── profiling ─────────────────────────────
  * Per-kernel-class device timing with CUDA events on the context stream, the
  * counterpart of the reference's BARK3_ENC_PROFILE timestamp queries

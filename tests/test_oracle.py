@@ -1,0 +1,276 @@
+"""The CPU oracle against the reference's own known-answer tests (restated) and
+against independent float64 restatements.  CPU only.
+
+Reference tests restated here (crate-relative paths):
+  src/cpu/gemm.rs:788  matches_naive_for_odd_shapes          (1e-4 vs naive)
+  src/cpu/gemm.rs:806  half_pack_matches_f32_pack            (bit-exact)
+  src/cpu/gemm.rs:834  matches_naive_for_unaligned_column_counts (1e-4)
+  src/raw.rs:150       bf16_f16_f32_sources_agree            (exact)
+  src/diagnostics/gemm.rs:538  lbtest construction (low-bit == f16, bit-exact)
+  src/bark.rs:597      expand (sign-magnitude level codes)
+"""
+import numpy as np
+import pytest
+
+
+def naive(a, w):
+    """The reference test's naive loop: acc += a*w in f32, k ascending."""
+    m, k = a.shape
+    n = w.shape[0]
+    c = np.zeros((m, n), dtype=np.float32)
+    for kk in range(k):
+        c += a[:, kk : kk + 1] * w[:, kk][None, :]
+    return c
+
+
+@pytest.mark.parametrize("m,n,k", [(1, 16, 5), (7, 40, 33), (13, 128, 64), (191, 64, 17)])
+def test_gemm_matches_naive_for_odd_shapes(oracle, m, n, k):
+    i = np.arange(m * k)
+    a = ((i % 17).astype(np.float32) * np.float32(0.01) - np.float32(0.05)).reshape(m, k)
+    j = np.arange(n * k)
+    w = ((j % 13).astype(np.float32) * np.float32(0.02) - np.float32(0.1)).reshape(n, k)
+    c = oracle.gemm(a, w, half=False)
+    assert np.max(np.abs(c - naive(a, w))) < 1e-4
+
+
+def test_gemm_matches_naive_for_unaligned_column_counts(oracle):
+    for ncols in range(60, 200):
+        m, k = ncols, 9
+        i = np.arange(m * k)
+        a = ((i % 19).astype(np.float32) * np.float32(0.03) - np.float32(0.2)).reshape(m, k)
+        j = np.arange(ncols * k)
+        w = ((j % 23).astype(np.float32) * np.float32(0.02) - np.float32(0.15)).reshape(ncols, k)
+        c = oracle.gemm(a, w, half=False)
+        assert np.max(np.abs(c - naive(a, w))) < 1e-4, ncols
+
+
+@pytest.mark.parametrize("m,n,k", [(6, 16, 16), (13, 40, 33), (24, 128, 64), (7, 96, 40)])
+def test_half_pack_matches_f32_pack(oracle, m, n, k):
+    i = np.arange(m * k)
+    a = ((i % 19).astype(np.float32) * np.float32(0.013) - np.float32(0.11)).reshape(m, k)
+    j = np.arange(n * k)
+    w = oracle.round_f16(((j % 23).astype(np.float32) * np.float32(0.017) - np.float32(0.2)).reshape(n, k))
+    c32 = oracle.gemm(a, w, half=False)
+    c16 = oracle.gemm(a, w, half=True)
+    assert np.array_equal(c32.view(np.uint32), c16.view(np.uint32))
+
+
+def test_gemm_is_one_fma_chain(oracle):
+    """Every output is fma(a_k, w_k, acc) for k ascending from +0: checked
+    against an explicit float32 FMA chain (via float64 products rounded once)."""
+    rng = np.random.default_rng(3)
+    a = rng.normal(size=(5, 37)).astype(np.float32)
+    w = oracle.round_f16(rng.normal(size=(20, 37)).astype(np.float32))
+    c = oracle.gemm(a, w)
+    ref = np.zeros((5, 20), dtype=np.float32)
+    for kk in range(37):
+        # fma in f32: exact product + acc, rounded once (exact in f64 here)
+        ref = (a[:, kk : kk + 1].astype(np.float64) * w[:, kk][None, :].astype(np.float64)
+               + ref.astype(np.float64)).astype(np.float32)
+    assert np.array_equal(c, ref)
+
+
+def test_bf16_f16_f32_sources_agree(oracle, syn):
+    values = np.array([0.0, 1.0, -2.5, 0.125, 1024.0, -0.0625], dtype=np.float32)
+    bf16 = (values.view(np.uint32) >> 16).astype(np.uint16)
+    f16 = values.astype(np.float16).view(np.uint16)
+    L = oracle.lib()
+    from_bf16 = np.array([L.or_bf16_bits_to_f32(int(b)) for b in bf16], dtype=np.float32)
+    from_f16 = np.array([L.or_f16_bits_to_f32(int(b)) for b in f16], dtype=np.float32)
+    assert np.array_equal(from_bf16, values)
+    assert np.array_equal(from_f16, values)
+    assert np.array_equal(syn.bf16_bits_to_f32(bf16), values)
+    words = np.array([L.or_f32_to_f16_bits(float(v)) for v in values], dtype=np.uint16)
+    assert np.array_equal(words, f16)
+
+
+def test_f16_rounding_matches_ieee(oracle):
+    """f32 -> f16 round-to-nearest-even (half::f16::from_f32) incl. subnormals,
+    overflow and ties, against numpy's IEEE conversion."""
+    rng = np.random.default_rng(0)
+    x = np.concatenate([
+        rng.normal(0, 1, 20000), rng.normal(0, 1e-5, 5000), rng.normal(0, 3e4, 5000),
+        [6.1035156e-05, 5.9604645e-08, 2.9802322e-08, 65504.0, 65520.0, 65519.99, 1e9, -1e9,
+         1.0009765625, 1.00048828125, 1.00146484375, -0.0, 0.0],
+    ]).astype(np.float32)
+    got = np.array([oracle.lib().or_f32_to_f16_bits(float(v)) for v in x], dtype=np.uint16)
+    assert np.array_equal(got, x.astype(np.float16).view(np.uint16))
+
+
+@pytest.mark.parametrize("k", [1, 2, 3])
+def test_expand_rule(oracle, syn, k):
+    levels = np.array([0.5, 0.25, 0.125, 0.0], dtype=np.float16).view(np.uint16)
+    for code in range(16):
+        want = 0.0
+        if 1 <= code <= k:
+            want = float(levels.view(np.float16)[code - 1])
+        elif k < code <= 2 * k:
+            want = -float(levels.view(np.float16)[code - k - 1])
+        assert oracle.expand_code(code, k, levels) == want
+    codes = np.arange(16, dtype=np.uint32)[None, :].repeat(3, 0)
+    lv = np.tile(levels, (3, 1))
+    vals = syn.expand_levels(codes, lv, k)
+    assert all(vals[0, c] == oracle.expand_code(c, k, levels) for c in range(16))
+
+
+def test_lbtest_lowbit_equals_f16(oracle, syn):
+    """lbtest (src/diagnostics/gemm.rs:538-652): two levels per row, codes
+    (i*13 + i/k) % 5 -> 0, +l0, +l1, -l0, -l1.  The values the low-bit path
+    multiplies equal the f16-rounded f32 weights, so both GEMMs agree bit for bit."""
+    m, n, k = 64, 128, 1024
+    i = np.arange(m * k)
+    a = (((i % 89).astype(np.float32) - np.float32(44.0)) * np.float32(0.002)).reshape(m, k)
+    j = np.arange(n * k)
+    codes = ((j * 13 + j // k) % 5).reshape(n, k)
+    rows = np.arange(n)
+    l0 = np.float32(0.02) * (rows % 7 + 1).astype(np.float32)
+    l1 = np.float32(0.05) * (rows % 5 + 1).astype(np.float32)
+    table = np.stack([np.zeros(n, np.float32), l0, l1, -l0, -l1], axis=1)
+    wf32 = np.take_along_axis(table, codes, axis=1).astype(np.float32)
+    lut = np.zeros((n, 16), dtype=np.float16)
+    lut[:, :5] = table.astype(np.float16)
+    packed = (codes[:, 0::2] | (codes[:, 1::2] << 4)).astype(np.uint8)
+    w_lb = syn.expand_lut4(packed, lut.view(np.uint16))
+    assert np.array_equal(w_lb, oracle.round_f16(wf32))
+    c16 = oracle.gemm(a, oracle.round_f16(wf32))
+    clb = oracle.gemm(a, w_lb)
+    assert np.array_equal(c16, clb)
+    ref = a.astype(np.float64) @ wf32.T.astype(np.float64)
+    assert np.max(np.abs(clb - ref)) < 1e-3
+
+
+def test_layer_norm_matches_float64(oracle):
+    rng = np.random.default_rng(1)
+    x = (rng.normal(0, 3, size=(17, 1024)) + 2.0).astype(np.float32)
+    w = rng.normal(1, 0.1, 1024).astype(np.float32)
+    b = rng.normal(0, 0.1, 1024).astype(np.float32)
+    y = oracle.layer_norm(x, w, b)
+    xd = x.astype(np.float64)
+    mu = xd.mean(1, keepdims=True)
+    var = xd.var(1, keepdims=True)
+    ref = (xd - mu) / np.sqrt(var + 1e-5) * w + b
+    assert np.max(np.abs(y - ref)) < 1e-4
+
+
+def test_elementwise_ops(oracle):
+    rng = np.random.default_rng(2)
+    x = rng.normal(0, 4, size=(9, 2048)).astype(np.float32)
+    assert np.allclose(oracle.silu(x), x / (1 + np.exp(-x.astype(np.float64))), rtol=1e-6, atol=1e-6)
+    g = oracle.glu(x)
+    a, b = x[:, :1024].astype(np.float64), x[:, 1024:].astype(np.float64)
+    assert np.allclose(g, a / (1 + np.exp(-b)), rtol=1e-6, atol=1e-6)
+
+
+def test_dwconv_bn_silu_matches_float64(oracle):
+    rng = np.random.default_rng(4)
+    t, d = 23, 1024
+    x = rng.normal(size=(t, d)).astype(np.float32)
+    dw = rng.normal(0, 0.2, size=(d, 9)).astype(np.float32)
+    ba = rng.normal(1, 0.1, d).astype(np.float32)
+    bb = rng.normal(0, 0.1, d).astype(np.float32)
+    y = oracle.dwconv_bn_silu(x, dw, ba, bb)
+    xp = np.pad(x.astype(np.float64), ((4, 4), (0, 0)))
+    acc = sum(xp[i : i + t] * dw[:, i][None, :] for i in range(9))
+    z = acc * ba + bb
+    ref = z / (1 + np.exp(-z))
+    assert np.max(np.abs(y - ref)) < 1e-5
+
+
+def test_pos_embed(oracle):
+    t = 50
+    p = oracle.pos_embed(t)
+    assert p.shape == (2 * t - 1, 1024)
+    inv = (1.0 / np.power(10000.0, np.arange(512) * 2.0 / 1024.0)).astype(np.float32)
+    pos = (t - 1 - np.arange(2 * t - 1)).astype(np.float32)
+    f = pos[:, None] * inv[None, :]
+    # inv_freq may differ by an f32 ulp between libm's powf and numpy, which
+    # moves the argument (up to |pos| = 49) by ~4e-6
+    assert np.allclose(p[:, 0::2], np.sin(f.astype(np.float64)), atol=2e-5)
+    assert np.allclose(p[:, 1::2], np.cos(f.astype(np.float64)), atol=2e-5)
+    assert np.array_equal(p[t - 1, 0::2], np.zeros(512, np.float32))  # position 0
+
+
+def _block_f64(w, x, syn, oracle):
+    """Independent float64 restatement of one Conformer block (src/cpu/layer.rs
+    order) with the same f16 roundings as the reference (weights, K, V, R)."""
+    f = lambda n: syn.dense_values(w["encoder.layers.0." + n]).astype(np.float64)  # noqa: E731
+    v = lambda n: np.asarray(w["encoder.layers.0." + n], dtype=np.float64)  # noqa: E731
+    r16 = lambda a: a.astype(np.float32).astype(np.float16).astype(np.float64)  # noqa: E731
+    wr = lambda n: r16(f(n))  # noqa: E731
+
+    def ln(z, i):
+        names = syn.NORMS
+        mu = z.mean(1, keepdims=True)
+        var = z.var(1, keepdims=True)
+        return (z - mu) / np.sqrt(var + 1e-5) * v(names[i] + ".weight") + v(names[i] + ".bias")
+
+    silu = lambda z: z / (1 + np.exp(-z))  # noqa: E731
+    t = x.shape[0]
+    x = x.astype(np.float64)
+    x = x + 0.5 * silu(ln(x, 0) @ wr("feed_forward1.linear1.weight").T) @ wr("feed_forward1.linear2.weight").T
+    h = ln(x, 1)
+    q = h @ wr("self_attn.q_proj.weight").T
+    k = r16(h @ wr("self_attn.k_proj.weight").T)
+    vv = r16(h @ wr("self_attn.v_proj.weight").T)
+    bu = v("self_attn.bias_u").reshape(-1)
+    bv = v("self_attn.bias_v").reshape(-1)
+    pos = oracle.pos_embed(t).astype(np.float64)           # row j = position t-1-j
+    R = r16(pos @ wr("self_attn.relative_k_proj.weight").T)
+    out = np.zeros((t, 1024))
+    for hh in range(8):
+        s = slice(128 * hh, 128 * hh + 128)
+        content = (q[:, s] + bu[s]) @ k[:, s].T
+        bd_full = (q[:, s] + bv[s]) @ R[:, s].T             # [t, 2t-1]
+        idx = (t - 1) - np.arange(t)[:, None] + np.arange(t)[None, :]
+        bd = np.take_along_axis(bd_full, idx, axis=1)
+        sc = (content + bd) / np.sqrt(128.0)
+        p = np.exp(sc - sc.max(1, keepdims=True))
+        p /= p.sum(1, keepdims=True)
+        out[:, s] = p @ vv[:, s]
+    x = x + out @ wr("self_attn.o_proj.weight").T
+    h = ln(x, 2) @ wr("conv.pointwise_conv1.weight").T
+    g = h[:, :1024] / (1 + np.exp(-h[:, 1024:]))
+    dw = r16(v("conv.depthwise_conv.weight").reshape(1024, 9))
+    gp = np.pad(g, ((4, 4), (0, 0)))
+    acc = sum(gp[i : i + t] * dw[:, i][None, :] for i in range(9))
+    a = v("conv.norm.weight") / np.sqrt(v("conv.norm.running_var") + 1e-5)
+    bb = v("conv.norm.bias") - v("conv.norm.running_mean") * a
+    z = acc * a + bb
+    x = x + silu(z) @ wr("conv.pointwise_conv2.weight").T
+    x = x + 0.5 * silu(ln(x, 3) @ wr("feed_forward2.linear1.weight").T) @ wr("feed_forward2.linear2.weight").T
+    return x
+
+
+@pytest.mark.parametrize("t", [1, 5, 40, 300])
+def test_oracle_block_matches_float64_restatement(oracle, syn, t):
+    w = syn.encoder_weights(seed=11, n_layers=1, layout="lut4")
+    sub = syn.sub_features(np.random.default_rng(t), t)
+    sw = syn.dense_values(w["encoder.subsampling.linear.weight"]).astype(np.float64)
+    x0 = sub.astype(np.float64) @ sw.T + w["encoder.subsampling.linear.bias"]
+    want = _block_f64(w, x0, syn, oracle)
+    # a 2-block oracle truncated after block 0 returns block 0's pre-norm_out
+    # residual (src/cpu/mod.rs:168-175)
+    w2 = dict(w)
+    for name, val in w.items():
+        if ".layers.0." in name:
+            w2[name.replace(".layers.0.", ".layers.1.")] = val
+    got = oracle.OracleEncoder(w2, 2).encode(sub, layers=1)
+    err = float(np.max(np.abs(got - want)) / np.max(np.abs(want)))
+    assert err < 1e-4, err
+
+
+def test_golden_fixtures(oracle, syn):
+    """Regression guard: small oracle outputs committed under tests/golden/
+    (made by tests/golden/make_golden.py from seeded inputs)."""
+    import importlib.util
+    import pathlib
+
+    here = pathlib.Path(__file__).resolve().parent / "golden"
+    spec = importlib.util.spec_from_file_location("make_golden", here / "make_golden.py")
+    mg = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mg)
+    fixtures = np.load(here / "oracle_golden.npz")
+    current = mg.compute(oracle, syn)
+    assert set(fixtures.files) == set(current)
+    for name in fixtures.files:
+        np.testing.assert_allclose(current[name], fixtures[name], rtol=1e-6, atol=1e-7, err_msg=name)
