@@ -48,7 +48,9 @@ struct GemmOp {
     int epi;
 };
 
-int make_map_2d(CUtensorMap* map, const void* base, bool f16, uint64_t inner, uint64_t outer,
+// TMA 2D map over a row-major matrix; dtype kMapU8 / kMapF16 / kMapF32.
+constexpr int kMapU8 = 0, kMapF16 = 1, kMapF32 = 2;
+int make_map_2d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, uint64_t outer,
                 uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, bool swizzle128);
 int gemm_make_a_map(CUtensorMap* map, const __half* a, int M, int K, int lda);
 int gemm_make_b_map(CUtensorMap* map, const void* w, bool lut, int N, int K);

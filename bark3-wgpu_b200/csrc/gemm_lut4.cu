@@ -54,11 +54,13 @@ struct GemmCfg {
     static constexpr uint32_t kBBytes = BN * kBK * 2;
     static constexpr uint32_t kCBytes = LUT ? BN * kBK / 2 : 0;
     static constexpr uint32_t kStageBytes = SUB * kABytes + kBBytes + kCBytes;
-    static constexpr int kStages = (220 * 1024) / kStageBytes > 8 ? 8 : (220 * 1024) / kStageBytes;
+    static constexpr uint32_t kOutBytes = 4 * 4096;              // one 32 x 128 B slab per epilogue warp
+    static constexpr uint32_t kBarBytes = 512;
+    static constexpr uint32_t kRingBudget = 232448 - kOutBytes - kBarBytes - 1024;
+    static constexpr int kStages = kRingBudget / kStageBytes > 8 ? 8 : kRingBudget / kStageBytes;
     static constexpr uint32_t kAccCols = SUB * BN;               // one accumulator set
     static constexpr uint32_t kTmemCols = 2 * kAccCols <= 32 ? 32 : 2 * kAccCols;
-    static constexpr uint32_t kBarBytes = 512;
-    static constexpr uint32_t kSmemBytes = kStages * kStageBytes + kBarBytes + 1024;
+    static constexpr uint32_t kSmemBytes = kStages * kStageBytes + kOutBytes + kBarBytes + 1024;
     static constexpr int kTPR = kExpThreads / BN;               // expander threads per B row
     static constexpr int kWPT = 8 / kTPR;                       // 16-byte chunks per thread per stage
     static_assert(kSmemBytes <= 232448, "shared memory budget");
@@ -66,8 +68,8 @@ struct GemmCfg {
     static_assert(kStages >= 2, "pipeline depth");
 };
 
-__device__ __forceinline__ float silu_f(float v) { return v / (1.0f + __expf(-v)); }
-__device__ __forceinline__ float sigmoid_f(float v) { return 1.0f / (1.0f + __expf(-v)); }
+__device__ __forceinline__ float silu_f(float v) { return __fdividef(v, 1.0f + __expf(-v)); }
+__device__ __forceinline__ float sigmoid_f(float v) { return __fdividef(1.0f, 1.0f + __expf(-v)); }
 
 __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
     __half2 h = __floats2half2_rn(a, b);
@@ -91,88 +93,157 @@ __device__ __forceinline__ void lut_expand8(uint32_t w, const uint32_t (&lo)[4],
     }
 }
 
-// Epilogue of 32 accumulator columns [n, n+32) of output row gm.
-template <int EPI>
-__device__ __forceinline__ void epilogue32(const GemmParams& p, int gm, int n, float (&v)[32]) {
-    if (EPI == EPI_F32 || EPI == EPI_F16 || EPI == EPI_SILU_F16) {
-        if (p.bias) {
+__device__ __forceinline__ uint32_t f2u(float v) { return __float_as_uint(v); }
+
+// 32 accumulator columns of this thread's TMEM lane.
+__device__ __forceinline__ void load_acc32(uint32_t taddr, float* v) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(taddr, r);
+    tmem_wait_ld();
 #pragma unroll
-            for (int i = 0; i < 32; ++i) v[i] += __ldg(p.bias + n + i);
-        }
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// One epilogue warp's output slab: 32 rows (one per lane) of up to 128 bytes.
+// 128-byte rows use the TMA 128-byte swizzle (16-byte chunk j of row r sits at
+// chunk j ^ (r & 7)), which also makes a warp's row writes bank-conflict free;
+// 64-byte rows (the GLU output of a 64-column tile) are stored plainly.
+template <bool SW>
+__device__ __forceinline__ void slab_put(uint8_t* slab, int r, int j, uint4 v, int row_bytes) {
+    const int off = SW ? r * 128 + ((j ^ (r & 7)) << 4) : r * row_bytes + (j << 4);
+    *reinterpret_cast<uint4*>(slab + off) = v;
+}
+
+// Before rewriting the slab, the previous bulk store must have read it.
+__device__ __forceinline__ void slab_acquire(int lane) {
+    if (lane == 0) bulk_wait_read();
+    __syncwarp();
+}
+
+// The slab goes out as one TMA tile store, or an f32 add-reduction into the
+// destination (the residual update x += alpha * acc, done in L2).
+__device__ __forceinline__ void slab_flush(const CUtensorMap* map, uint8_t* slab, int lane, int x, int y, bool reduce) {
+    fence_async_shared();
+    __syncwarp();
+    if (lane == 0) {
+        if (reduce)
+            tma_reduce_add_2d(map, smem_u32(slab), x, y);
+        else
+            tma_store_2d(map, smem_u32(slab), x, y);
+        bulk_commit();
     }
-    if (EPI == EPI_F32) {
-        float4* dst = reinterpret_cast<float4*>(p.out_f32 + static_cast<size_t>(gm) * p.ldo + n);
+}
+
+__device__ __forceinline__ void add_vec(float* v, const float* b, int n) {
+    const float4* b4 = reinterpret_cast<const float4*>(b);
+    for (int i = 0; i < n / 4; ++i) {
+        const float4 t = __ldg(b4 + i);
+        v[4 * i] += t.x;
+        v[4 * i + 1] += t.y;
+        v[4 * i + 2] += t.z;
+        v[4 * i + 3] += t.w;
+    }
+}
+
+// Packs 64 values (plus an optional per-column bias) to f16 into the slab
+// (8 chunks of 16 bytes).
+__device__ __forceinline__ void slab_put_f16x64(uint8_t* slab, int lane, const float* v, const float* bias) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i) dst[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-    } else if (EPI == EPI_RESID) {
-        float4* dst = reinterpret_cast<float4*>(p.out_f32 + static_cast<size_t>(gm) * p.ldo + n);
-        float4 x[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) x[i] = dst[i];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            x[i].x += p.alpha * v[4 * i];
-            x[i].y += p.alpha * v[4 * i + 1];
-            x[i].z += p.alpha * v[4 * i + 2];
-            x[i].w += p.alpha * v[4 * i + 3];
-            dst[i] = x[i];
+    for (int j = 0; j < 8; ++j) {
+        float4 b0 = make_float4(0.f, 0.f, 0.f, 0.f), b1 = b0;
+        if (bias) {
+            b0 = __ldg(reinterpret_cast<const float4*>(bias + 8 * j));
+            b1 = __ldg(reinterpret_cast<const float4*>(bias + 8 * j + 4));
         }
-    } else if (EPI == EPI_F16 || EPI == EPI_SILU_F16) {
-        uint4* dst = reinterpret_cast<uint4*>(p.out_f16 + static_cast<size_t>(gm) * p.ldo + n);
+        slab_put<true>(slab, lane, j,
+                       make_uint4(pack_h2(v[8 * j] + b0.x, v[8 * j + 1] + b0.y),
+                                  pack_h2(v[8 * j + 2] + b0.z, v[8 * j + 3] + b0.w),
+                                  pack_h2(v[8 * j + 4] + b1.x, v[8 * j + 5] + b1.y),
+                                  pack_h2(v[8 * j + 6] + b1.z, v[8 * j + 7] + b1.w)),
+                       128);
+    }
+}
+
+// Epilogue of one 128-row subtile held in TMEM columns [tacc, tacc + BN):
+// this warp's 32 rows start at output row y0.
+template <int BN, int EPI>
+__device__ __forceinline__ void epilogue_subtile(const GemmParams& p, const CUtensorMap* map_c, uint8_t* slab,
+                                                 uint32_t tacc, int lane, int n0, int y0) {
+    if (EPI == EPI_F32 || EPI == EPI_RESID) {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+            float v[32];
+            load_acc32(tacc + c * 32, v);
+            if (EPI == EPI_F32 && p.bias) add_vec(v, p.bias + n0 + c * 32, 32);
+            if (EPI == EPI_RESID) {
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            float t[8];
+                for (int i = 0; i < 32; ++i) v[i] *= p.alpha;
+            }
+            slab_acquire(lane);
 #pragma unroll
-            for (int j = 0; j < 8; ++j) t[j] = (EPI == EPI_SILU_F16) ? silu_f(v[8 * i + j]) : v[8 * i + j];
-            dst[i] = make_uint4(pack_h2(t[0], t[1]), pack_h2(t[2], t[3]), pack_h2(t[4], t[5]), pack_h2(t[6], t[7]));
+            for (int j = 0; j < 8; ++j)
+                slab_put<true>(slab, lane, j, make_uint4(f2u(v[4 * j]), f2u(v[4 * j + 1]), f2u(v[4 * j + 2]), f2u(v[4 * j + 3])), 128);
+            slab_flush(map_c, slab, lane, n0 + c * 32, y0, EPI == EPI_RESID);
+        }
+    } else if (EPI == EPI_F16 || EPI == EPI_SILU_F16 || EPI == EPI_QKV) {
+#pragma unroll 1
+        for (int c = 0; c < BN / 64; ++c) {
+            const int n = n0 + c * 64;
+            float v[64];
+            load_acc32(tacc + c * 64, v);
+            load_acc32(tacc + c * 64 + 32, v + 32);
+            if (EPI == EPI_QKV) {
+                // row layout [q + bias_u | q + bias_v | k | v], 1024 f16 each
+                if (n < 1024) {
+                    slab_acquire(lane);
+                    slab_put_f16x64(slab, lane, v, p.bias_u + n);
+                    slab_flush(map_c, slab, lane, n, y0, false);
+                    slab_acquire(lane);
+                    slab_put_f16x64(slab, lane, v, p.bias_v + n);
+                    slab_flush(map_c, slab, lane, n + 1024, y0, false);
+                } else {
+                    slab_acquire(lane);
+                    slab_put_f16x64(slab, lane, v, nullptr);
+                    slab_flush(map_c, slab, lane, n + 1024, y0, false);
+                }
+            } else {
+                if (p.bias) add_vec(v, p.bias + n, 64);
+                if (EPI == EPI_SILU_F16) {
+#pragma unroll
+                    for (int i = 0; i < 64; ++i) v[i] = silu_f(v[i]);
+                }
+                slab_acquire(lane);
+                slab_put_f16x64(slab, lane, v, nullptr);
+                slab_flush(map_c, slab, lane, n, y0, false);
+            }
         }
     } else if (EPI == EPI_GLU_F16) {
-        // W rows interleaved (value, gate) at load: column 2i is GLU input a_i,
-        // column 2i+1 its gate b_i.
-        float g[16];
+        // W rows interleaved (value, gate) at load: accumulator column 2i is
+        // GLU input a_i, column 2i+1 its gate b_i.  A BN-column tile gives BN/2
+        // outputs: one slab row of BN bytes.
+        constexpr bool kSw = (BN == 128);
+        slab_acquire(lane);
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+            float v[32];
+            load_acc32(tacc + c * 32, v);
+            if (p.bias) add_vec(v, p.bias + n0 + c * 32, 32);
+            float g[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-            float a = v[2 * i], b = v[2 * i + 1];
-            if (p.bias) {
-                a += __ldg(p.bias + n + 2 * i);
-                b += __ldg(p.bias + n + 2 * i + 1);
-            }
-            g[i] = a * sigmoid_f(b);
+            for (int i = 0; i < 16; ++i) g[i] = v[2 * i] * sigmoid_f(v[2 * i + 1]);
+            slab_put<kSw>(slab, lane, 2 * c,
+                          make_uint4(pack_h2(g[0], g[1]), pack_h2(g[2], g[3]), pack_h2(g[4], g[5]), pack_h2(g[6], g[7])), BN);
+            slab_put<kSw>(slab, lane, 2 * c + 1,
+                          make_uint4(pack_h2(g[8], g[9]), pack_h2(g[10], g[11]), pack_h2(g[12], g[13]), pack_h2(g[14], g[15])), BN);
         }
-        uint4* dst = reinterpret_cast<uint4*>(p.out_f16 + static_cast<size_t>(gm) * p.ldo + n / 2);
-        dst[0] = make_uint4(pack_h2(g[0], g[1]), pack_h2(g[2], g[3]), pack_h2(g[4], g[5]), pack_h2(g[6], g[7]));
-        dst[1] = make_uint4(pack_h2(g[8], g[9]), pack_h2(g[10], g[11]), pack_h2(g[12], g[13]), pack_h2(g[14], g[15]));
-    } else if (EPI == EPI_QKV) {
-        // output row = [q + bias_u | q + bias_v | k | v], 1024 f16 each
-        __half* orow = p.out_f16 + static_cast<size_t>(gm) * p.ldo;
-        if (n < 1024) {
-            uint4* du = reinterpret_cast<uint4*>(orow + n);
-            uint4* dv = reinterpret_cast<uint4*>(orow + 1024 + n);
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                float a[8], b[8];
-#pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    a[j] = v[8 * i + j] + __ldg(p.bias_u + n + 8 * i + j);
-                    b[j] = v[8 * i + j] + __ldg(p.bias_v + n + 8 * i + j);
-                }
-                du[i] = make_uint4(pack_h2(a[0], a[1]), pack_h2(a[2], a[3]), pack_h2(a[4], a[5]), pack_h2(a[6], a[7]));
-                dv[i] = make_uint4(pack_h2(b[0], b[1]), pack_h2(b[2], b[3]), pack_h2(b[4], b[5]), pack_h2(b[6], b[7]));
-            }
-        } else {
-            uint4* dk = reinterpret_cast<uint4*>(orow + n + 1024);
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-                dk[i] = make_uint4(pack_h2(v[8 * i], v[8 * i + 1]), pack_h2(v[8 * i + 2], v[8 * i + 3]),
-                                   pack_h2(v[8 * i + 4], v[8 * i + 5]), pack_h2(v[8 * i + 6], v[8 * i + 7]));
-        }
+        slab_flush(map_c, slab, lane, n0 / 2, y0, false);
     }
 }
 
 template <int BN, int SUB, bool LUT, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     k1_gemm(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-            const GemmParams p) {
+            const __grid_constant__ CUtensorMap tm_c, const GemmParams p) {
     using Cfg = GemmCfg<BN, SUB, LUT>;
     constexpr int S = Cfg::kStages;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -181,7 +252,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* sA = smem;                              // [S][SUB][128 x 64 f16]
     uint8_t* sB = smem + S * SUB * Cfg::kABytes;     // [S][BN x 64 f16]
     uint8_t* sC = sB + S * Cfg::kBBytes;             // [S][BN x 32 B]
-    uint64_t* bars = reinterpret_cast<uint64_t*>(sC + S * Cfg::kCBytes);
+    uint8_t* sOut = sC + S * Cfg::kCBytes;           // [4][32 x 128 B] epilogue slabs
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + Cfg::kOutBytes);
     uint64_t* full = bars;
     uint64_t* bready = bars + S;
     uint64_t* empty = bars + 2 * S;
@@ -199,6 +271,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (threadIdx.x == 0) {
         tma_prefetch_desc(&tm_a);
         tma_prefetch_desc(&tm_b);
+        tma_prefetch_desc(&tm_c);
         for (int s = 0; s < S; ++s) {
             mbar_init(smem_u32(&full[s]), 1);
             mbar_init(smem_u32(&bready[s]), kExpThreads);
@@ -340,6 +413,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         // ── epilogue (4 warps, one TMEM lane quarter each) ──
         const int q = warp & 3;
+        uint8_t* slab = sOut + (warp - kEpiWarp0) * 4096;
         int lt = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++lt) {
             const int m0 = (tile / n_tiles) * SUB * kBM;
@@ -347,25 +421,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int b = lt & 1;
             if (!mbar_wait(smem_u32(&tfull[b]), (lt >> 1) & 1, 0x05)) break;
             tc_fence_after();
+            const uint32_t tq = tmem + (static_cast<uint32_t>(q * 32) << 16) + b * Cfg::kAccCols;
 #pragma unroll 1
-            for (int sub = 0; sub < SUB; ++sub) {
-                const int gm = m0 + sub * kBM + q * 32 + lane;
-                const bool live = gm < p.M;
-#pragma unroll 1
-                for (int c = 0; c < BN / 32; ++c) {
-                    uint32_t r[32];
-                    tmem_ld_32x32b_x32(tmem + (static_cast<uint32_t>(q * 32) << 16) + b * Cfg::kAccCols + sub * BN + c * 32, r);
-                    tmem_wait_ld();
-                    if (!live) continue;
-                    float v[32];
-#pragma unroll
-                    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-                    epilogue32<EPI>(p, gm, n0 + c * 32, v);
-                }
-            }
+            for (int sub = 0; sub < SUB; ++sub)
+                epilogue_subtile<BN, EPI>(p, &tm_c, slab, tq + sub * BN, lane, n0, m0 + sub * kBM + q * 32);
             tc_fence_before();
             mbar_arrive(smem_u32(&tempty[b]));
         }
+        if (lane == 0) bulk_wait_all();
     }
 
     tc_fence_before();
@@ -395,9 +458,22 @@ int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p
         cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
         if (g_num_sms <= 0) g_num_sms = 148;
     }
+    // output map: 32-row boxes of 128-byte rows (64-byte rows for the GLU
+    // output of a 64-column tile), matching the epilogue's slab layout
+    CUtensorMap tc;
+    int rc;
+    if (EPI == EPI_F32 || EPI == EPI_RESID)
+        rc = make_map_2d(&tc, p.out_f32, kMapF32, p.N, p.M, static_cast<uint64_t>(p.ldo) * 4, 32, 32, true);
+    else if (EPI == EPI_GLU_F16)
+        rc = make_map_2d(&tc, p.out_f16, kMapF16, p.N / 2, p.M, static_cast<uint64_t>(p.ldo) * 2, BN / 2, 32, BN == 128);
+    else if (EPI == EPI_QKV)
+        rc = make_map_2d(&tc, p.out_f16, kMapF16, 4096, p.M, static_cast<uint64_t>(p.ldo) * 2, 64, 32, true);
+    else
+        rc = make_map_2d(&tc, p.out_f16, kMapF16, p.N, p.M, static_cast<uint64_t>(p.ldo) * 2, 64, 32, true);
+    if (rc) return rc;
     const int tiles = (p.N / BN) * ((p.M + SUB * kBM - 1) / (SUB * kBM));
     const int grid = tiles < g_num_sms ? tiles : g_num_sms;
-    kern<<<grid, kThreads, Cfg::kSmemBytes, st>>>(ta, tb, p);
+    kern<<<grid, kThreads, Cfg::kSmemBytes, st>>>(ta, tb, tc, p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return set_cuda_error("k1_gemm launch", e);
     return 0;
@@ -439,14 +515,17 @@ int gemm_validate(const GemmParams& p, bool lut) {
     return 0;
 }
 
-// Tile shape by problem size: large M takes 256 x 128 tiles (two MMAs share
-// each expanded B tile); small M takes 128 x 64 tiles to spread over the SMs.
+// Tile shape by problem size: large problems take 256 x 128 tiles (two MMAs
+// share each expanded B tile); small ones take 128 x 64 tiles to spread over
+// the SMs.
 int gemm_launch(const GemmOp& op, cudaStream_t st) {
     const GemmParams& p = op.p;
     int rc = gemm_validate(p, op.lut);
     if (rc) return rc;
+    // 256 x 128 tiles as soon as they fill every SM once; below that the
+    // 128 x 64 tiles win by spreading the work.
     const long big_tiles = static_cast<long>(p.N / 128) * ((p.M + 255) / 256);
-    const bool big = big_tiles >= 2 * 148 || p.M >= 2048;
+    const bool big = big_tiles >= 148;
     if (op.lut) {
         if (big) return launch_epi<128, 2, true>(op.epi, op.map_a, op.map_b, p, st);
         return launch_epi<64, 1, true>(op.epi, op.map_a, op.map_b, p, st);
@@ -476,7 +555,7 @@ EncodeTiledFn encode_fn() {
 }
 }  // namespace
 
-int make_map_2d(CUtensorMap* map, const void* base, bool f16, uint64_t inner, uint64_t outer,
+int make_map_2d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, uint64_t outer,
                 uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, bool swizzle128) {
     EncodeTiledFn fn = encode_fn();
     if (!fn) return set_error(B3_ECUDA, "cuTensorMapEncodeTiled is unavailable");
@@ -486,7 +565,10 @@ int make_map_2d(CUtensorMap* map, const void* base, bool f16, uint64_t inner, ui
     cuuint64_t strides[1] = {row_bytes};
     cuuint32_t box[2] = {box_inner, box_outer};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = fn(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+    const CUtensorMapDataType dt = dtype == kMapF32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                   : dtype == kMapF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                      : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+    CUresult r = fn(map, dt, 2,
                     const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                     swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);

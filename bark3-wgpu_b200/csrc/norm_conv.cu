@@ -102,9 +102,14 @@ __global__ void __launch_bounds__(256) k4_layernorm(const float* __restrict__ x,
 }
 
 // Depthwise conv k=9 + BN(a, b) + SiLU.  Block: 128 threads x 8 channels =
-// all 1024 channels of kRows consecutive frames.  Frame t reads t-4 .. t+4
-// inside its own utterance [seg.x, seg.y); anything outside is zero.
-constexpr int kDwRows = 16;
+// all 1024 channels of kDwRows consecutive frames.  The (kDwRows + 8)-frame
+// input tile is staged in shared memory with cp.async (every load in flight
+// at once); each thread then slides a 9-frame register window over it.
+// Frame t reads t-4 .. t+4 inside its own utterance [seg.x, seg.y); anything
+// outside is zero.
+constexpr int kDwRows = 36;
+constexpr int kDwTile = kDwRows + 8;
+constexpr int kDwSmem = kDwTile * 1024 * 2;
 
 __global__ void __launch_bounds__(128) k3_dwconv_bn_silu(const __half* __restrict__ src,
                                                          const int2* __restrict__ seg, int rows,
@@ -112,8 +117,22 @@ __global__ void __launch_bounds__(128) k3_dwconv_bn_silu(const __half* __restric
                                                          const float* __restrict__ bn_a,
                                                          const float* __restrict__ bn_b,
                                                          __half* __restrict__ dst) {
+    extern __shared__ __align__(16) uint8_t tile[];  // [kDwTile][1024] f16, frame t0-4+i in row i
     const int c0 = threadIdx.x * 8;
     const int t0 = blockIdx.x * kDwRows;
+    {
+        const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(tile));
+        for (int c = threadIdx.x; c < kDwTile * 128; c += 128) {
+            const int r = c >> 7, ch = c & 127;
+            const int t = t0 - 4 + r;
+            const bool ok = t >= 0 && t < rows;
+            const __half* g = src + static_cast<size_t>(ok ? t : 0) * 1024 + ch * 8;
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(base + r * 2048 + ch * 16), "l"(g),
+                         "r"(ok ? 16 : 0)
+                         : "memory");
+        }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    }
     float w[9][8];
 #pragma unroll
     for (int i = 0; i < 9; ++i) {
@@ -133,60 +152,56 @@ __global__ void __launch_bounds__(128) k3_dwconv_bn_silu(const __half* __restric
         bb[0] = b0.x; bb[1] = b0.y; bb[2] = b0.z; bb[3] = b0.w;
         bb[4] = b1.x; bb[5] = b1.y; bb[6] = b1.z; bb[7] = b1.w;
     }
-    // rolling window of 9 input frames (8 channels each)
-    float win[9][8];
-#pragma unroll
-    for (int i = 0; i < 9; ++i)
-#pragma unroll
-        for (int j = 0; j < 8; ++j) win[i][j] = 0.f;
-    auto load = [&](int t, float (&dst8)[8]) {
-        if (t >= 0 && t < rows) {
-            const uint4 u = *reinterpret_cast<const uint4*>(src + static_cast<size_t>(t) * 1024 + c0);
-            const __half2* h = reinterpret_cast<const __half2*>(&u);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-                const float2 f = __half22float2(h[j]);
-                dst8[2 * j] = f.x;
-                dst8[2 * j + 1] = f.y;
-            }
-        } else {
-#pragma unroll
-            for (int j = 0; j < 8; ++j) dst8[j] = 0.f;
-        }
-    };
-#pragma unroll
-    for (int i = 0; i < 8; ++i) load(t0 - 4 + i, win[i + 1]);
-#pragma unroll 1
-    for (int r = 0; r < kDwRows; ++r) {
-        const int t = t0 + r;
-        if (t >= rows) break;
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-#pragma unroll
-            for (int j = 0; j < 8; ++j) win[i][j] = win[i + 1][j];
-        load(t + 4, win[8]);
-        const int2 sg = __ldg(seg + t);
-        float acc[8];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) acc[j] = 0.f;
-#pragma unroll
-        for (int i = 0; i < 9; ++i) {
-            const int tt = t + i - 4;
-            if (tt < sg.x || tt >= sg.y) continue;
-#pragma unroll
-            for (int j = 0; j < 8; ++j) acc[j] += win[i][j] * w[i][j];
-        }
-        uint32_t o[4];
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();
+    auto load = [&](int r, float (&d8)[8]) {
+        const uint4 u = *reinterpret_cast<const uint4*>(tile + r * 2048 + c0 * 2);
+        const __half2* h = reinterpret_cast<const __half2*>(&u);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
-            float y0 = acc[2 * j] * ba[2 * j] + bb[2 * j];
-            float y1 = acc[2 * j + 1] * ba[2 * j + 1] + bb[2 * j + 1];
-            y0 = y0 / (1.0f + __expf(-y0));
-            y1 = y1 / (1.0f + __expf(-y1));
-            __half2 h = __floats2half2_rn(y0, y1);
-            o[j] = *reinterpret_cast<uint32_t*>(&h);
+            const float2 f = __half22float2(h[j]);
+            d8[2 * j] = f.x;
+            d8[2 * j + 1] = f.y;
         }
-        *reinterpret_cast<uint4*>(dst + static_cast<size_t>(t) * 1024 + c0) = make_uint4(o[0], o[1], o[2], o[3]);
+    };
+    // circular 9-frame window: tile row r lives in slot r % 9.  The row loop
+    // is unrolled by 9 so every slot index is a compile-time constant.
+    float win[9][8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) load(i, win[i]);
+#pragma unroll 1
+    for (int r0 = 0; r0 < kDwRows; r0 += 9) {
+#pragma unroll
+        for (int u = 0; u < 9; ++u) {
+            const int r = r0 + u;
+            const int t = t0 + r;
+            if (r < kDwRows && t < rows) {
+                load(r + 8, win[(u + 8) % 9]);
+                const int2 sg = __ldg(seg + t);
+                const int lo = max(sg.x - (t - 4), 0);
+                const int hi = min(sg.y - (t - 4), 9);
+                float acc[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+#pragma unroll
+                for (int i = 0; i < 9; ++i) {
+                    if (i < lo || i >= hi) continue;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) acc[j] += win[(u + i) % 9][j] * w[i][j];
+                }
+                uint32_t o[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    float y0 = acc[2 * j] * ba[2 * j] + bb[2 * j];
+                    float y1 = acc[2 * j + 1] * ba[2 * j + 1] + bb[2 * j + 1];
+                    y0 = __fdividef(y0, 1.0f + __expf(-y0));
+                    y1 = __fdividef(y1, 1.0f + __expf(-y1));
+                    __half2 h = __floats2half2_rn(y0, y1);
+                    o[j] = *reinterpret_cast<uint32_t*>(&h);
+                }
+                *reinterpret_cast<uint4*>(dst + static_cast<size_t>(t) * 1024 + c0) = make_uint4(o[0], o[1], o[2], o[3]);
+            }
+        }
     }
 }
 
@@ -226,7 +241,13 @@ int launch_layernorm(const float* x, int rows, const float* w1, const float* b1,
 int launch_dwconv(const __half* src, const int2* seg, int rows, const float* dw_t, const float* bn_a,
                   const float* bn_b, __half* dst, cudaStream_t st) {
     if (rows <= 0) return 0;
-    k3_dwconv_bn_silu<<<(rows + kDwRows - 1) / kDwRows, 128, 0, st>>>(src, seg, rows, dw_t, bn_a, bn_b, dst);
+    static bool attr_done = false;
+    if (!attr_done) {
+        cudaError_t e = cudaFuncSetAttribute(k3_dwconv_bn_silu, cudaFuncAttributeMaxDynamicSharedMemorySize, kDwSmem);
+        if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(k3)", e);
+        attr_done = true;
+    }
+    k3_dwconv_bn_silu<<<(rows + kDwRows - 1) / kDwRows, 128, kDwSmem, st>>>(src, seg, rows, dw_t, bn_a, bn_b, dst);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? 0 : set_cuda_error("k3_dwconv_bn_silu", e);
 }
