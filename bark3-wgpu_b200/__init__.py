@@ -88,6 +88,8 @@ def lib() -> ctypes.CDLL:
         "b3_profile": (c_i, [c_p, c_i]),
         "b3_profile_read": (c_i, [c_p, c_i, c_p, c_p, c_p, c_p]),
         "b3_shard_lpt": (c_i, [c_p, c_i, c_i, c_p]),
+        "b3_decode_batch": (c_i, [c_p, c_p, c_p, c_i, c_p, c_p, c_i, c_u]),
+        "b3_transcribe_batch": (c_i, [c_p, c_p, c_p, c_i, c_p, c_p, c_i, c_u]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -211,6 +213,35 @@ class Encoder:
         flags = B3_DEVICE_PTRS if dev else 0
         check(self._L.b3_encode_batch(self.ctx, _ptr(sub), _ptr(cu), len(cu) - 1, _ptr(out), flags))
         return out
+
+    def decode_batch(self, pooler, cu_seqlens, max_tokens: int = 4096):
+        """Greedy TDT decode of a varlen pooler; returns a list of (n, 3)
+        uint32 arrays (id, frame, duration) per utterance."""
+        return self._tokens_call("b3_decode_batch", pooler, cu_seqlens, max_tokens)
+
+    def transcribe_batch(self, sub, cu_seqlens, max_tokens: int = 4096):
+        """Encoder + decoder: subsampled frames -> token streams per utterance."""
+        return self._tokens_call("b3_transcribe_batch", sub, cu_seqlens, max_tokens)
+
+    def _tokens_call(self, fn, src, cu_seqlens, max_tokens):
+        cu = np.ascontiguousarray(cu_seqlens, dtype=np.int32)
+        n = len(cu) - 1
+        tokens = np.zeros((n, max_tokens, 3), dtype=np.uint32)
+        counts = np.zeros(n, dtype=np.int32)
+        if _is_device(src):
+            import torch
+
+            tt = torch.zeros((n, max_tokens, 3), dtype=torch.int32, device=src.device)
+            tc = torch.zeros(n, dtype=torch.int32, device=src.device)
+            check(getattr(self._L, fn)(self.ctx, _ptr(src), _ptr(cu), n, _ptr(tt), _ptr(tc), max_tokens,
+                                       B3_DEVICE_PTRS))
+            self.sync()
+            tokens = tt.cpu().numpy().view(np.uint32)
+            counts = tc.cpu().numpy()
+        else:
+            src = np.ascontiguousarray(src, dtype=np.float32)
+            check(getattr(self._L, fn)(self.ctx, _ptr(src), _ptr(cu), n, _ptr(tokens), _ptr(counts), max_tokens, 0))
+        return [tokens[i, : min(int(counts[i]), max_tokens)] for i in range(n)]
 
     def attn_conv(self, layer: int, x) -> None:
         flags = B3_DEVICE_PTRS if _is_device(x) else 0

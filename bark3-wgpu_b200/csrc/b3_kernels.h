@@ -35,4 +35,32 @@ struct AttnParams {
 int launch_attention(const AttnParams& p, int n_work, cudaStream_t st);
 int attention_block_rows();
 
+// Batched greedy TDT decoder state (tdt_decoder.cu).  B rows, one per
+// utterance; GEMM inputs are f16 hi | lo pairs (see tdt_decoder.cu).
+struct DecState {
+    int B, vocab, blank, max_tokens;
+    const int* cu;           // device cu_seqlens [B + 1]
+    const float* pooler;     // [total][640]
+    const __half* emb_hi;    // [vocab][640]
+    const __half* emb_lo;
+    __half* a0;              // [B][2560] x_hi | x_lo | h0_hi | h0_lo  (LSTM layer 0 input)
+    __half* a1;              // [B][2560] h0_hi | h0_lo | h1_hi | h1_lo (layer 1 input)
+    __half* ap;              // [B][1280] h1_hi | h1_lo                 (projector input)
+    __half* aj;              // [B][1280] joint input hi | lo
+    float* gates;            // [B][2560]
+    float* c;                // [B][2][640]
+    float* dec;              // [B][640]
+    float* scores;           // [B][ld_scores]
+    int ld_scores;
+    int *frame, *count, *guard, *emit, *active;
+    uint32_t* tokens;        // [B][max_tokens][3] (id, frame, duration)
+};
+
+int dec_launch_init(const DecState& s, cudaStream_t st);
+int dec_launch_joint_in(const DecState& s, cudaStream_t st);
+int dec_launch_argmax(const DecState& s, cudaStream_t st);
+int dec_launch_lstm_update(const DecState& s, int layer, cudaStream_t st);
+int dec_launch_any_active(const DecState& s, int* out, cudaStream_t st);
+int dec_launch_split(const float* src, __half* hi, __half* lo, int64_t n, cudaStream_t st);
+
 }  // namespace b3

@@ -185,8 +185,27 @@ struct b3_ctx {
     DevBuf scratch16;       // f16 copy of A for the single-linear entry points
     Plan plan;
     Prof prof;
+    // greedy TDT decoder (optional: built when its tensors are loaded)
+    struct Decoder {
+        bool present = false;
+        int vocab = 0, npad = 0;
+        DevBuf emb_hi, emb_lo;                 // [vocab][640] f16 hi | lo of the f32 embedding
+        Linear lstm[2];                        // [2560][2560] = W_ih | W_ih | W_hh | W_hh
+        Linear proj;                           // [640][1280]  = W_p | W_p
+        Linear head;                           // [npad][1280] = W_head | W_head (zero rows past vocab+5)
+        DevBuf bias;                           // f32: lstm0 [2560] | lstm1 [2560] | proj [640] | head [npad]
+        int bcap = 0, tcap = 0;
+        DevBuf a0, a1, ap, aj, gates, cstate, dec, scores, ints, tokens, cu, flag, pooler;
+    } dec;
     ~b3_ctx() {
         for (cudaEvent_t e : prof.pool) cudaEventDestroy(e);
+        for (Linear* l : {&dec.lstm[0], &dec.lstm[1], &dec.proj, &dec.head}) {
+            l->w.release();
+            l->lut16.release();
+        }
+        for (DevBuf* b : {&dec.emb_hi, &dec.emb_lo, &dec.bias, &dec.a0, &dec.a1, &dec.ap, &dec.aj, &dec.gates,
+                          &dec.cstate, &dec.dec, &dec.scores, &dec.ints, &dec.tokens, &dec.cu, &dec.flag, &dec.pooler})
+            b->release();
         auto rel = [](Linear& l) { l.w.release(); l.lut16.release(); };
         rel(sub_w);
         rel(proj_w);
@@ -636,6 +655,211 @@ int encode_any(b3_ctx* c, const float* sub, const int32_t* cu, int n_utt, int la
     return sync_and_check(c);
 }
 
+// ───────────────────────────── TDT decoder ─────────────────────────────
+
+int build_dense(b3_ctx* c, Linear& L, const std::vector<uint16_t>& w, int N, int K) {
+    L.present = true;
+    L.lut = false;
+    L.N = N;
+    L.K = K;
+    B3_TRY(upload(L.w, w.data(), w.size() * 2, c->stream));
+    B3_CUDA(cudaStreamSynchronize(c->stream));
+    return gemm_make_b_map(&L.map_b, L.w.p, false, N, K);
+}
+
+// A (rows, 640) dense matrix staged under `name`, rounded to f16 (pack16,
+// src/tdt.rs:49-55).
+int dec_matrix(b3_ctx* c, const std::string& name, int rows, const std::vector<uint16_t>** out) {
+    const Staged* s = find(c, name);
+    if (!s) return set_error(B3_ENOTFOUND, "tensor %s was not loaded", name.c_str());
+    if (s->lowbit || numel(*s) != static_cast<int64_t>(rows) * 640)
+        return set_error(B3_EINVAL, "tensor %s: expected (%d, 640)", name.c_str(), rows);
+    *out = &s->f16;
+    return 0;
+}
+
+// Builds the decoder from the staged tensors (TdtDecoder::from_source,
+// src/tdt.rs:142-163).  Every GEMM weight is repeated along K so the f16
+// hi | lo halves of an activation meet the same weight.
+int build_decoder(b3_ctx* c) {
+    auto& D = c->dec;
+    const Staged* e = find(c, "decoder.embedding.weight");
+    if (!e) return 0;  // encoder-only checkpoint
+    if (e->lowbit || e->shape.size() != 2 || e->shape[1] != 640 || e->shape[0] < 2)
+        return set_error(B3_EINVAL, "decoder.embedding.weight must be (vocab, 640)");
+    const int V = static_cast<int>(e->shape[0]);
+    const int H = 640, G = 2560;
+    D.vocab = V;
+    D.npad = (V + 5 + 127) / 128 * 128;
+    {
+        DevBuf tmp;
+        B3_TRY(upload(tmp, e->f32.data(), e->f32.size() * 4, c->stream));
+        B3_TRY(D.emb_hi.ensure(static_cast<size_t>(V) * H * 2));
+        B3_TRY(D.emb_lo.ensure(static_cast<size_t>(V) * H * 2));
+        B3_TRY(dec_launch_split(tmp.as<float>(), D.emb_hi.as<__half>(), D.emb_lo.as<__half>(),
+                                static_cast<int64_t>(V) * H, c->stream));
+        B3_CUDA(cudaStreamSynchronize(c->stream));
+        tmp.release();
+    }
+    std::vector<float> bias(2 * G + H + D.npad, 0.f), v1, v2;
+    for (int l = 0; l < 2; ++l) {
+        const std::string sl = std::to_string(l);
+        const std::vector<uint16_t>*wih, *whh;
+        B3_TRY(dec_matrix(c, "decoder.lstm.weight_ih_l" + sl, G, &wih));
+        B3_TRY(dec_matrix(c, "decoder.lstm.weight_hh_l" + sl, G, &whh));
+        std::vector<uint16_t> w(static_cast<size_t>(G) * 4 * H);
+        for (int r = 0; r < G; ++r) {
+            uint16_t* dst = &w[static_cast<size_t>(r) * 4 * H];
+            memcpy(dst, &(*wih)[static_cast<size_t>(r) * H], H * 2);
+            memcpy(dst + H, &(*wih)[static_cast<size_t>(r) * H], H * 2);
+            memcpy(dst + 2 * H, &(*whh)[static_cast<size_t>(r) * H], H * 2);
+            memcpy(dst + 3 * H, &(*whh)[static_cast<size_t>(r) * H], H * 2);
+        }
+        B3_TRY(build_dense(c, D.lstm[l], w, G, 4 * H));
+        B3_TRY(get_vec(c, "decoder.lstm.bias_ih_l" + sl, G, v1));
+        B3_TRY(get_vec(c, "decoder.lstm.bias_hh_l" + sl, G, v2));
+        for (int r = 0; r < G; ++r) bias[l * G + r] = v1[r] + v2[r];
+    }
+    auto doubled = [&](const std::vector<uint16_t>& src, int rows, int out_rows) {
+        std::vector<uint16_t> w(static_cast<size_t>(out_rows) * 2 * H, 0);
+        for (int r = 0; r < rows; ++r) {
+            memcpy(&w[static_cast<size_t>(r) * 2 * H], &src[static_cast<size_t>(r) * H], H * 2);
+            memcpy(&w[static_cast<size_t>(r) * 2 * H + H], &src[static_cast<size_t>(r) * H], H * 2);
+        }
+        return w;
+    };
+    const std::vector<uint16_t>* wp;
+    B3_TRY(dec_matrix(c, "decoder.decoder_projector.weight", H, &wp));
+    B3_TRY(build_dense(c, D.proj, doubled(*wp, H, H), H, 2 * H));
+    B3_TRY(get_vec(c, "decoder.decoder_projector.bias", H, v1));
+    memcpy(&bias[2 * G], v1.data(), H * 4);
+    const std::vector<uint16_t>* wh;
+    B3_TRY(dec_matrix(c, "joint.head.weight", V + 5, &wh));
+    B3_TRY(build_dense(c, D.head, doubled(*wh, V + 5, D.npad), D.npad, 2 * H));
+    B3_TRY(get_vec(c, "joint.head.bias", V + 5, v1));
+    memcpy(&bias[2 * G + H], v1.data(), (V + 5) * 4);
+    B3_TRY(upload(D.bias, bias.data(), bias.size() * 4, c->stream));
+    B3_CUDA(cudaStreamSynchronize(c->stream));
+    D.present = true;
+    return 0;
+}
+
+int dec_ensure(b3_ctx* c, int B, int max_tokens) {
+    auto& D = c->dec;
+    if (B <= D.bcap && max_tokens <= D.tcap) return 0;
+    const size_t b = static_cast<size_t>(B > D.bcap ? B : D.bcap);
+    const size_t t = static_cast<size_t>(max_tokens > D.tcap ? max_tokens : D.tcap);
+    B3_TRY(D.a0.ensure(b * 2560 * 2));
+    B3_TRY(D.a1.ensure(b * 2560 * 2));
+    B3_TRY(D.ap.ensure(b * 1280 * 2));
+    B3_TRY(D.aj.ensure(b * 1280 * 2));
+    B3_TRY(D.gates.ensure(b * 2560 * 4));
+    B3_TRY(D.cstate.ensure(b * 2 * 640 * 4));
+    B3_TRY(D.dec.ensure(b * 640 * 4));
+    B3_TRY(D.scores.ensure(b * D.npad * 4));
+    B3_TRY(D.ints.ensure(b * 5 * 4));
+    B3_TRY(D.tokens.ensure(b * t * 12));
+    B3_TRY(D.cu.ensure((b + 1) * 4));
+    B3_TRY(D.flag.ensure(16));
+    D.bcap = static_cast<int>(b);
+    D.tcap = static_cast<int>(t);
+    return 0;
+}
+
+int dec_lstm_step(b3_ctx* c, const DecState& s) {
+    auto& D = c->dec;
+    const float* bias = D.bias.as<float>();
+    B3_TRY(run_gemm(c, D.lstm[0], s.a0, s.B, 2560, EPI_F32, params_f32(s.gates, 2560, bias)));
+    {
+        ProfScope ps(c, B3_K_DECODER, 0.0, 0.0);
+        B3_TRY(dec_launch_lstm_update(s, 0, c->stream));
+    }
+    B3_TRY(run_gemm(c, D.lstm[1], s.a1, s.B, 2560, EPI_F32, params_f32(s.gates, 2560, bias + 2560)));
+    {
+        ProfScope ps(c, B3_K_DECODER, 0.0, 0.0);
+        B3_TRY(dec_launch_lstm_update(s, 1, c->stream));
+    }
+    return run_gemm(c, D.proj, s.ap, s.B, 1280, EPI_F32, params_f32(s.dec, 640, bias + 5120));
+}
+
+// Greedy-decodes n_utt utterances of a device pooler [total][640]; the
+// tokens and counts are left in the decoder state buffers.
+int decode_device(b3_ctx* c, const float* pooler, const int32_t* cu, int n_utt, int max_tokens) {
+    auto& D = c->dec;
+    if (!D.present) return set_error(B3_ESTATE, "no decoder weights were loaded");
+    if (n_utt <= 0 || max_tokens <= 0) return set_error(B3_EINVAL, "bad decode batch");
+    int tmax = 0;
+    for (int i = 0; i < n_utt; ++i) {
+        const int t = cu[i + 1] - cu[i];
+        if (t < 0) return set_error(B3_EINVAL, "cu_seqlens must be non-decreasing");
+        if (t > tmax) tmax = t;
+    }
+    B3_TRY(dec_ensure(c, n_utt, max_tokens));
+    B3_CUDA(cudaMemcpyAsync(D.cu.p, cu, (n_utt + 1) * sizeof(int32_t), cudaMemcpyHostToDevice, c->stream));
+    DecState s;
+    s.B = n_utt;
+    s.vocab = D.vocab;
+    s.blank = D.vocab - 1;
+    s.max_tokens = max_tokens;
+    s.cu = D.cu.as<int>();
+    s.pooler = pooler;
+    s.emb_hi = D.emb_hi.as<__half>();
+    s.emb_lo = D.emb_lo.as<__half>();
+    s.a0 = D.a0.as<__half>();
+    s.a1 = D.a1.as<__half>();
+    s.ap = D.ap.as<__half>();
+    s.aj = D.aj.as<__half>();
+    s.gates = D.gates.as<float>();
+    s.c = D.cstate.as<float>();
+    s.dec = D.dec.as<float>();
+    s.scores = D.scores.as<float>();
+    s.ld_scores = D.npad;
+    int* ints = D.ints.as<int>();
+    s.frame = ints;
+    s.count = ints + n_utt;
+    s.guard = ints + 2 * n_utt;
+    s.emit = ints + 3 * n_utt;
+    s.active = ints + 4 * n_utt;
+    s.tokens = D.tokens.as<uint32_t>();
+    {
+        ProfScope ps(c, B3_K_DECODER, 0.0, 0.0);
+        B3_TRY(dec_launch_init(s, c->stream));
+    }
+    B3_TRY(dec_lstm_step(c, s));
+    const float* head_bias = D.bias.as<float>() + 5120 + 640;
+    const long max_steps = static_cast<long>(tmax) * 14 + 64;
+    constexpr int kChunk = 16;
+    int any = 1;
+    for (long step = 0; step < max_steps && any; step += kChunk) {
+        for (int k = 0; k < kChunk; ++k) {
+            {
+                ProfScope ps(c, B3_K_DECODER, 0.0, 0.0);
+                B3_TRY(dec_launch_joint_in(s, c->stream));
+            }
+            B3_TRY(run_gemm(c, D.head, s.aj, s.B, 1280, EPI_F32, params_f32(s.scores, D.npad, head_bias)));
+            {
+                ProfScope ps(c, B3_K_DECODER, 0.0, 0.0);
+                B3_TRY(dec_launch_argmax(s, c->stream));
+            }
+            B3_TRY(dec_lstm_step(c, s));
+        }
+        B3_TRY(dec_launch_any_active(s, D.flag.as<int>(), c->stream));
+        B3_CUDA(cudaMemcpyAsync(&any, D.flag.p, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
+        B3_CUDA(cudaStreamSynchronize(c->stream));
+    }
+    return 0;
+}
+
+// Copies the decoder's tokens / counts out (device or host destination).
+int decode_collect(b3_ctx* c, int n_utt, b3_token* tokens, int32_t* counts, int max_tokens, bool dev) {
+    auto& D = c->dec;
+    const cudaMemcpyKind k = dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost;
+    B3_CUDA(cudaMemcpyAsync(tokens, D.tokens.p, static_cast<size_t>(n_utt) * max_tokens * sizeof(b3_token), k,
+                            c->stream));
+    B3_CUDA(cudaMemcpyAsync(counts, D.ints.as<int>() + n_utt, n_utt * sizeof(int32_t), k, c->stream));
+    return 0;
+}
+
 // Single linear (configs 1 / lbtest): c = a . W^T (+ bias), W given per call.
 int linear_any(b3_ctx* c, const float* a, const void* w, const uint16_t* lut16, bool lut,
                const float* bias, float* out, int m, int n, int k, unsigned flags) {
@@ -877,10 +1101,53 @@ int b3_finalize(b3_ctx* ctx, int n_layers) {
         B3_TRY(upload(L.params, prm.data(), prm.size() * 4, ctx->stream));
         B3_CUDA(cudaStreamSynchronize(ctx->stream));
     }
+    B3_TRY(build_decoder(ctx));
     ctx->n_layers = n_layers;
     ctx->finalized = true;
     ctx->staged.clear();
     return 0;
+}
+
+int b3_decode_batch(b3_ctx* ctx, const float* pooler, const int32_t* cu_seqlens, int n_utt, b3_token* tokens,
+                    int32_t* counts, int max_tokens, unsigned flags) {
+    B3_TRY(check_finalized(ctx));
+    if (!pooler || !cu_seqlens || !tokens || !counts) return set_error(B3_EINVAL, "null buffer");
+    if (n_utt <= 0 || cu_seqlens[0] != 0) return set_error(B3_EINVAL, "bad cu_seqlens");
+    DeviceGuard g(ctx->device);
+    const bool dev = flags & B3_DEVICE_PTRS;
+    const float* p = pooler;
+    if (!dev) {
+        const size_t bytes = static_cast<size_t>(cu_seqlens[n_utt]) * 640 * 4;
+        B3_TRY(ctx->dec.pooler.ensure(bytes > 0 ? bytes : 4));
+        B3_CUDA(cudaMemcpyAsync(ctx->dec.pooler.p, pooler, bytes, cudaMemcpyHostToDevice, ctx->stream));
+        p = ctx->dec.pooler.as<float>();
+    }
+    B3_TRY(decode_device(ctx, p, cu_seqlens, n_utt, max_tokens));
+    B3_TRY(decode_collect(ctx, n_utt, tokens, counts, max_tokens, dev));
+    return dev ? 0 : sync_and_check(ctx);
+}
+
+int b3_transcribe_batch(b3_ctx* ctx, const float* sub, const int32_t* cu_seqlens, int n_utt, b3_token* tokens,
+                        int32_t* counts, int max_tokens, unsigned flags) {
+    B3_TRY(check_finalized(ctx));
+    if (!ctx->dec.present) return set_error(B3_ESTATE, "no decoder weights were loaded");
+    if (!sub || !cu_seqlens || !tokens || !counts) return set_error(B3_EINVAL, "null buffer");
+    DeviceGuard g(ctx->device);
+    B3_TRY(make_plan(ctx, cu_seqlens, n_utt));
+    const int M = ctx->plan.M;
+    const bool dev = flags & B3_DEVICE_PTRS;
+    B3_TRY(ctx->dec.pooler.ensure(static_cast<size_t>(M) * 640 * 4));
+    const float* in = sub;
+    if (!dev) {
+        const size_t in_bytes = static_cast<size_t>(M) * kSubIn * 4;
+        B3_TRY(ctx->io_in.ensure(in_bytes));
+        B3_CUDA(cudaMemcpyAsync(ctx->io_in.p, sub, in_bytes, cudaMemcpyHostToDevice, ctx->stream));
+        in = ctx->io_in.as<float>();
+    }
+    B3_TRY(encode_device(ctx, in, M, ctx->n_layers, ctx->dec.pooler.as<float>()));
+    B3_TRY(decode_device(ctx, ctx->dec.pooler.as<float>(), cu_seqlens, n_utt, max_tokens));
+    B3_TRY(decode_collect(ctx, n_utt, tokens, counts, max_tokens, dev));
+    return dev ? 0 : sync_and_check(ctx);
 }
 
 int b3_shard_lpt(const int32_t* frames, int n_utt, int n_ranks, int32_t* rank_of) {

@@ -147,6 +147,28 @@ def encoder_weights(seed: int = 0, n_layers: int = 24, layout: str = "lut4") -> 
     return w
 
 
+def decoder_weights(seed: int = 0, vocab: int = 1025, blank_bias: float = 2.0) -> dict:
+    """Random-init TDT prediction net + joint (2-layer LSTM
+    of 640, joint 640, `vocab` rows including the blank as the last one, 5
+    duration rows), with the reference's tensor names (src/tdt.rs:142-163).
+    LSTM weights follow PyTorch's U(-1/sqrt(640), 1/sqrt(640)) init; the blank
+    row gets `blank_bias` so streams are mostly blanks, as real ones are."""
+    rng = np.random.default_rng(seed)
+    H, G = 640, 2560
+    k = 1.0 / np.sqrt(H)
+    w = {"decoder.embedding.weight": rng.normal(0.0, 1.0, size=(vocab, H)).astype(np.float32)}
+    for l in (0, 1):
+        for name, shape in (("weight_ih", (G, H)), ("weight_hh", (G, H)), ("bias_ih", (G,)), ("bias_hh", (G,))):
+            w[f"decoder.lstm.{name}_l{l}"] = rng.uniform(-k, k, size=shape).astype(np.float32)
+    w["decoder.decoder_projector.weight"] = rng.normal(0.0, k, size=(H, H)).astype(np.float32)
+    w["decoder.decoder_projector.bias"] = rng.normal(0.0, 0.01, size=H).astype(np.float32)
+    w["joint.head.weight"] = rng.normal(0.0, k, size=(vocab + 5, H)).astype(np.float32)
+    hb = rng.normal(0.0, 0.01, size=vocab + 5).astype(np.float32)
+    hb[vocab - 1] += blank_bias
+    w["joint.head.bias"] = hb
+    return w
+
+
 def sub_features(rng: np.random.Generator, t: int) -> np.ndarray:
     """Stand-in for the conv-subsampling output (T, 4096): the reference's
     last op is a ReLU (src/sub.rs:107-286), so non-negative values."""

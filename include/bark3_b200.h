@@ -117,6 +117,36 @@ int b3_encode(b3_ctx* ctx, const float* sub, int t, int layers, float* out, unsi
 int b3_encode_batch(b3_ctx* ctx, const float* sub, const int32_t* cu_seqlens, int n_utt,
                     float* pooler, unsigned flags);
 
+/* ──────────────────────────── TDT decoder ────────────────────────────
+ * Greedy TDT decoding (TdtDecoder::decode, src/tdt.rs:319-467) of every
+ * utterance of a batch in lock step on the GPU.  The decoder is built by
+ * b3_finalize when its tensors were loaded: decoder.embedding.weight
+ * (vocab, 640) — the last row is the blank —, decoder.lstm.{weight_ih,
+ * weight_hh}_l{0,1} (2560, 640), decoder.lstm.{bias_ih,bias_hh}_l{0,1},
+ * decoder.decoder_projector.{weight,bias}, joint.head.weight
+ * (vocab + 5, 640) and joint.head.bias; the 5 rows after the vocabulary are
+ * the durations 0..4.
+ *
+ * One emitted token (src/tdt.rs:33-41): id, frame at emission, duration. */
+typedef struct b3_token {
+    uint32_t id;
+    uint32_t frame;
+    uint32_t dur;
+} b3_token;
+
+/* pooler [total][640] with utterance i at rows cu_seqlens[i] ..
+ * cu_seqlens[i+1]; tokens [n_utt][max_tokens]; counts[i] = tokens utterance
+ * i emitted (may exceed max_tokens: only the first max_tokens are stored).
+ * With B3_DEVICE_PTRS pooler, tokens and counts are device pointers. */
+int b3_decode_batch(b3_ctx* ctx, const float* pooler, const int32_t* cu_seqlens, int n_utt,
+                    b3_token* tokens, int32_t* counts, int max_tokens, unsigned flags);
+
+/* Encoder + decoder in one call: subsampled frames sub [total][4096] ->
+ * tokens (the batched transcription step of BASELINE config 5 from the
+ * encoder input on). */
+int b3_transcribe_batch(b3_ctx* ctx, const float* sub, const int32_t* cu_seqlens, int n_utt,
+                        b3_token* tokens, int32_t* counts, int max_tokens, unsigned flags);
+
 /* ─────────────────────────── single kernels ───────────────────────────
  * one 4-bit linear, c[m][n] = a[m][:] . W[n][:] + bias[n]
  * with W from codes [n][k/2] + lut16 [n][16].  Replaces Ctx::gemm_f32 with a
@@ -176,7 +206,8 @@ int b3_shard_lpt(const int32_t* frames, int n_utt, int n_ranks, int32_t* rank_of
 #define B3_K_DWCONV 4
 #define B3_K_CONVERT 5
 #define B3_K_OTHER 6
-#define B3_K_COUNT 7
+#define B3_K_DECODER 7
+#define B3_K_COUNT 8
 
 int b3_profile(b3_ctx* ctx, int enable);
 int b3_profile_read(b3_ctx* ctx, int kind, double* ms, double* flops, double* bytes, int64_t* launches);

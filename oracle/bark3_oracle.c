@@ -943,3 +943,207 @@ int or_attention_core(const float* qu, const float* qv, const float* kh, const f
     free(probs); free(bd); free(attn_h); free(parts);
     return 0;
 }
+
+/* ───────────────────────────── TDT decoder ─────────────────────────────
+ * Restates TdtDecoder (src/tdt.rs:19-535): 2-layer LSTM prediction net
+ * (hidden 640, gate order i, f, g, o), projector 640 -> 640, joint
+ * ReLU(enc + dec) . head^T + bias over vocab + 5 duration rows, greedy loop
+ * with blank forcing at least one frame and the step guard
+ * T * (MAX_SYMBOLS + 4) + 64.  Matrices are stored f16 (pack16), the
+ * embedding stays f32, as in the reference. */
+
+#define DEC_H 640
+#define DEC_GS (4 * DEC_H)
+#define N_DUR 5
+#define MAX_SYMBOLS 10
+
+/* dot16 (src/tdt.rs:57-97): two 8-lane FMA accumulators over 16-element
+ * blocks, then an 8-lane block, lanes summed 0..7, scalar tail.  `w` holds
+ * the f16 weights widened to f32 (exact), as vcvtph2ps produces them. */
+#if defined(__x86_64__)
+__attribute__((target("avx2,fma")))
+static float dot16_avx2(const float* w, const float* x, int n) {
+    __m256 a0 = _mm256_setzero_ps(), a1 = _mm256_setzero_ps();
+    int i = 0;
+    for (; i + 16 <= n; i += 16) {
+        a0 = _mm256_fmadd_ps(_mm256_loadu_ps(w + i), _mm256_loadu_ps(x + i), a0);
+        a1 = _mm256_fmadd_ps(_mm256_loadu_ps(w + i + 8), _mm256_loadu_ps(x + i + 8), a1);
+    }
+    __m256 acc = _mm256_add_ps(a0, a1);
+    for (; i + 8 <= n; i += 8) acc = _mm256_fmadd_ps(_mm256_loadu_ps(w + i), _mm256_loadu_ps(x + i), acc);
+    float tmp[8];
+    _mm256_storeu_ps(tmp, acc);
+    float sum = 0.0f;
+    for (int l = 0; l < 8; l++) sum += tmp[l];
+    for (; i < n; i++) sum += w[i] * x[i];
+    return sum;
+}
+#endif
+
+static float dot16(const float* w, const float* x, int n) {
+#if defined(__x86_64__)
+    if (have_avx2()) return dot16_avx2(w, x, n);
+#endif
+    float a0[8] = {0}, a1[8] = {0}, acc[8];
+    int i = 0;
+    for (; i + 16 <= n; i += 16)
+        for (int l = 0; l < 8; l++) {
+            a0[l] = fmaf(w[i + l], x[i + l], a0[l]);
+            a1[l] = fmaf(w[i + 8 + l], x[i + 8 + l], a1[l]);
+        }
+    for (int l = 0; l < 8; l++) acc[l] = a0[l] + a1[l];
+    for (; i + 8 <= n; i += 8)
+        for (int l = 0; l < 8; l++) acc[l] = fmaf(w[i + l], x[i + l], acc[l]);
+    float sum = 0.0f;
+    for (int l = 0; l < 8; l++) sum += acc[l];
+    for (; i < n; i++) sum += w[i] * x[i];
+    return sum;
+}
+
+typedef struct {
+    int vocab;            /* token rows incl. blank; blank = vocab - 1 */
+    float* embed;         /* [vocab][640] f32 */
+    float* w_ih;          /* [2][2560][640] f16 values (widened) */
+    float* w_hh;
+    float* b_ih;          /* [2][2560] */
+    float* b_hh;
+    float* proj_w;        /* [640][640] f16 values */
+    float* proj_b;
+    float* head_w;        /* [vocab + 5][640] f16 values */
+    float* head_b;
+} OrTdt;
+
+/* pack16 (src/tdt.rs:49-55): round to f16, kept widened to f32 */
+static float* pack16(const float* v, size_t n) {
+    float* o = (float*)malloc(n * 4);
+    for (size_t i = 0; i < n; i++) o[i] = or_round_f16(v[i]);
+    return o;
+}
+
+static float* dupf(const float* v, size_t n) {
+    float* o = (float*)malloc(n * 4);
+    memcpy(o, v, n * 4);
+    return o;
+}
+
+void* or_tdt_new(int vocab, const float* embed, const float* w_ih, const float* w_hh, const float* b_ih,
+                 const float* b_hh, const float* proj_w, const float* proj_b, const float* head_w,
+                 const float* head_b) {
+    OrTdt* d = (OrTdt*)calloc(1, sizeof(OrTdt));
+    d->vocab = vocab;
+    d->embed = dupf(embed, (size_t)vocab * DEC_H);
+    d->w_ih = pack16(w_ih, (size_t)2 * DEC_GS * DEC_H);
+    d->w_hh = pack16(w_hh, (size_t)2 * DEC_GS * DEC_H);
+    d->b_ih = dupf(b_ih, 2 * DEC_GS);
+    d->b_hh = dupf(b_hh, 2 * DEC_GS);
+    d->proj_w = pack16(proj_w, (size_t)DEC_H * DEC_H);
+    d->proj_b = dupf(proj_b, DEC_H);
+    d->head_w = pack16(head_w, (size_t)(vocab + N_DUR) * DEC_H);
+    d->head_b = dupf(head_b, (size_t)vocab + N_DUR);
+    return d;
+}
+
+void or_tdt_free(void* p) {
+    OrTdt* d = (OrTdt*)p;
+    if (!d) return;
+    free(d->embed); free(d->w_ih); free(d->w_hh); free(d->b_ih); free(d->b_hh);
+    free(d->proj_w); free(d->proj_b); free(d->head_w); free(d->head_b);
+    free(d);
+}
+
+static float sigm(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+/* lstm_step (src/tdt.rs:179-214) */
+static void lstm_step(const OrTdt* d, const float* x, float h[2][DEC_H], float c[2][DEC_H]) {
+    float gates[DEC_GS];
+    for (int layer = 0; layer < 2; layer++) {
+        const float* wih = d->w_ih + (size_t)layer * DEC_GS * DEC_H;
+        const float* whh = d->w_hh + (size_t)layer * DEC_GS * DEC_H;
+        const float* bih = d->b_ih + layer * DEC_GS;
+        const float* bhh = d->b_hh + layer * DEC_GS;
+        const float* xin = layer == 0 ? x : h[0];
+        const float* hin = h[layer];
+        for (int row = 0; row < DEC_GS; row++)
+            gates[row] = bih[row] + bhh[row] + dot16(wih + (size_t)row * DEC_H, xin, DEC_H) +
+                         dot16(whh + (size_t)row * DEC_H, hin, DEC_H);
+        for (int ch = 0; ch < DEC_H; ch++) {
+            float in = sigm(gates[ch]);
+            float fg = sigm(gates[DEC_H + ch]);
+            float cand = tanhf(gates[2 * DEC_H + ch]);
+            c[layer][ch] = fg * c[layer][ch] + in * cand;
+            float out = sigm(gates[3 * DEC_H + ch]);
+            h[layer][ch] = out * tanhf(c[layer][ch]);
+        }
+    }
+}
+
+static void project(const OrTdt* d, const float* x, float* out) {
+    for (int r = 0; r < DEC_H; r++) out[r] = d->proj_b[r] + dot16(d->proj_w + (size_t)r * DEC_H, x, DEC_H);
+}
+
+/* joint (src/tdt.rs:217-290): first maximum wins on ties. */
+static void joint(const OrTdt* d, const float* enc, const float* dec, uint32_t* tok, uint32_t* dur) {
+    float s[DEC_H];
+    for (int i = 0; i < DEC_H; i++) {
+        float v = enc[i] + dec[i];
+        s[i] = v > 0.0f ? v : 0.0f;
+    }
+    float bt = -INFINITY, bd = -INFINITY;
+    uint32_t it = 0, id = (uint32_t)d->vocab;
+    int rows = d->vocab + N_DUR;
+    for (int r = 0; r < rows; r++) {
+        float score = d->head_b[r] + dot16(d->head_w + (size_t)r * DEC_H, s, DEC_H);
+        if (r < d->vocab) {
+            if (score > bt) { bt = score; it = (uint32_t)r; }
+        } else if (score > bd) {
+            bd = score;
+            id = (uint32_t)r;
+        }
+    }
+    *tok = it;
+    *dur = id - (uint32_t)d->vocab;
+}
+
+/* Greedy decode of one utterance (decode_rayon, src/tdt.rs:416-467).  out
+ * receives (id, frame, dur) triples; returns the token count (capped at
+ * max_tokens; the loop still runs to the end). */
+int or_tdt_decode(const void* p, const float* pooler, int t_len, uint32_t* out, int max_tokens) {
+    const OrTdt* d = (const OrTdt*)p;
+    const uint32_t blank = (uint32_t)d->vocab - 1;
+    float h[2][DEC_H] = {{0}}, c[2][DEC_H] = {{0}}, dec[DEC_H];
+    lstm_step(d, d->embed + (size_t)blank * DEC_H, h, c);
+    project(d, h[1], dec);
+    long max_steps = (long)t_len * (MAX_SYMBOLS + 4) + 64;
+    long guard = 0;
+    int n = 0, frame = 0;
+    for (;;) {
+        if (frame >= t_len) break;
+        if (++guard > max_steps) break;
+        uint32_t tok, dur;
+        joint(d, pooler + (size_t)frame * DEC_H, dec, &tok, &dur);
+        if (tok == blank) {
+            frame += dur > 0 ? (int)dur : 1;
+        } else {
+            if (n < max_tokens) {
+                out[3 * n] = tok;
+                out[3 * n + 1] = (uint32_t)frame;
+                out[3 * n + 2] = dur;
+            }
+            n++;
+            lstm_step(d, d->embed + (size_t)tok * DEC_H, h, c);
+            project(d, h[1], dec);
+            frame += (int)dur;
+        }
+    }
+    return n;
+}
+
+/* Decodes n_utt utterances of a varlen pooler [total][640] (cu offsets), one
+ * utterance per thread.  tokens: n_utt * max_tokens triples; counts: n_utt. */
+void or_tdt_decode_batch(const void* p, const float* pooler, const int32_t* cu, int n_utt, uint32_t* tokens,
+                         int32_t* counts, int max_tokens) {
+#pragma omp parallel for schedule(dynamic, 1) num_threads(g_threads)
+    for (int i = 0; i < n_utt; i++)
+        counts[i] = or_tdt_decode(p, pooler + (size_t)cu[i] * DEC_H, cu[i + 1] - cu[i],
+                                  tokens + (size_t)i * max_tokens * 3, max_tokens);
+}

@@ -59,6 +59,10 @@ def lib() -> ctypes.CDLL:
             "or_encode": (_I, [_P, _P, _I, _I, _P]),
             "or_attn_conv": (_I, [_P, _I, _P, _I]),
             "or_attention_core": (_I, [_P, _P, _P, _P, _P, _I, _P]),
+            "or_tdt_new": (_P, [_I] + [_P] * 9),
+            "or_tdt_free": (None, [_P]),
+            "or_tdt_decode": (_I, [_P, _P, _I, _P, _I]),
+            "or_tdt_decode_batch": (None, [_P, _P, _P, _I, _P, _P, _I]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)
@@ -225,4 +229,53 @@ class OracleEncoder:
     def __del__(self):
         if getattr(self, "h", None):
             lib().or_encoder_free(self.h)
+            self.h = None
+
+
+class OracleTdt:
+    """Restated TdtDecoder (src/tdt.rs): greedy TDT over a pooler (t, 640)."""
+
+    def __init__(self, w: dict):
+        emb = f32(w["decoder.embedding.weight"])
+        self.vocab = emb.shape[0]
+        keep = [emb]
+
+        def cat(a, b):
+            x = f32(np.concatenate([f32(w[a]).reshape(-1), f32(w[b]).reshape(-1)]))
+            keep.append(x)
+            return _p(x)
+
+        def one(n):
+            x = f32(w[n])
+            keep.append(x)
+            return _p(x)
+
+        self.h = lib().or_tdt_new(
+            self.vocab, _p(emb),
+            cat("decoder.lstm.weight_ih_l0", "decoder.lstm.weight_ih_l1"),
+            cat("decoder.lstm.weight_hh_l0", "decoder.lstm.weight_hh_l1"),
+            cat("decoder.lstm.bias_ih_l0", "decoder.lstm.bias_ih_l1"),
+            cat("decoder.lstm.bias_hh_l0", "decoder.lstm.bias_hh_l1"),
+            one("decoder.decoder_projector.weight"), one("decoder.decoder_projector.bias"),
+            one("joint.head.weight"), one("joint.head.bias"),
+        )
+
+    def decode(self, pooler: np.ndarray, max_tokens: int = 1 << 16) -> np.ndarray:
+        pooler = f32(pooler)
+        out = np.zeros((max_tokens, 3), dtype=np.uint32)
+        n = lib().or_tdt_decode(self.h, _p(pooler), pooler.shape[0], _p(out), max_tokens)
+        return out[: min(n, max_tokens)]
+
+    def decode_batch(self, pooler: np.ndarray, cu, max_tokens: int = 4096) -> list:
+        pooler = f32(pooler)
+        cu = np.ascontiguousarray(cu, dtype=np.int32)
+        n = len(cu) - 1
+        toks = np.zeros((n, max_tokens, 3), dtype=np.uint32)
+        counts = np.zeros(n, dtype=np.int32)
+        lib().or_tdt_decode_batch(self.h, _p(pooler), _p(cu), n, _p(toks), _p(counts), max_tokens)
+        return [toks[i, : min(int(counts[i]), max_tokens)] for i in range(n)]
+
+    def __del__(self):
+        if getattr(self, "h", None):
+            lib().or_tdt_free(self.h)
             self.h = None

@@ -1,0 +1,83 @@
+"""Batched GPU greedy TDT decoder against the restated reference decoder, and
+the encoder + decoder path end to end.  North-star criterion: greedy token
+streams match in >= 99% of tokens, measured here as 1 - (token edit distance /
+reference length) over a batch."""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+MATCH = 0.99
+
+
+def edit_distance(a, b):
+    a, b = list(a), list(b)
+    prev = list(range(len(b) + 1))
+    for i, x in enumerate(a, 1):
+        cur = [i] + [0] * len(b)
+        for j, y in enumerate(b, 1):
+            cur[j] = min(prev[j] + 1, cur[j - 1] + 1, prev[j - 1] + (x != y))
+        prev = cur
+    return prev[-1]
+
+
+def token_match(got, want):
+    errs = sum(edit_distance([tuple(t) for t in g], [tuple(t) for t in w]) for g, w in zip(got, want))
+    total = sum(len(w) for w in want)
+    return 1.0 - errs / max(total, 1), sum(np.array_equal(g, w) for g, w in zip(got, want)) / len(want)
+
+
+@pytest.fixture(scope="module")
+def dec_model(syn, oracle, pkg):
+    w = syn.encoder_weights(seed=8, n_layers=2, layout="lut4")
+    w.update(syn.decoder_weights(seed=8, vocab=1025))
+    enc = pkg.Encoder(0)
+    enc.load(w)
+    enc.finalize(2)
+    yield w, enc
+    enc.close()
+
+
+def test_decoder_matches_oracle(dec_model, syn, oracle):
+    w, enc = dec_model
+    rng = np.random.default_rng(5)
+    lens = [1, 7, 64, 129, 300, 41]
+    pooler = rng.normal(0, 1, size=(sum(lens), 640)).astype(np.float32)
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    got = enc.decode_batch(pooler, cu)
+    want = oracle.OracleTdt(w).decode_batch(pooler, cu)
+    m, exact = token_match(got, want)
+    print(f"decoder token match {m:.4f}, identical streams {exact:.2f}, tokens {sum(len(x) for x in want)}")
+    assert sum(len(x) for x in want) > 100
+    assert m >= MATCH
+
+
+def test_reference_vocab_size(syn, oracle, pkg):
+    """The released model's joint: 8192 tokens + blank, 5 durations."""
+    w = syn.encoder_weights(seed=9, n_layers=1, layout="lut4")
+    w.update(syn.decoder_weights(seed=9, vocab=8193))
+    enc = pkg.Encoder(0)
+    enc.load(w)
+    enc.finalize(1)
+    pooler = np.random.default_rng(9).normal(0, 1, size=(90, 640)).astype(np.float32)
+    got = enc.decode_batch(pooler, [0, 90])
+    want = oracle.OracleTdt(w).decode_batch(pooler, [0, 90])
+    m, _ = token_match(got, want)
+    assert m >= MATCH
+    enc.close()
+
+
+def test_transcribe_end_to_end(dec_model, syn, oracle):
+    """Encoder + decoder on the GPU vs the oracle encoder + oracle decoder."""
+    w, enc = dec_model
+    rng = np.random.default_rng(6)
+    lens = [50, 133, 20]
+    subs = [syn.sub_features(rng, t) for t in lens]
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    got = enc.transcribe_batch(np.concatenate(subs), cu)
+    oenc = oracle.OracleEncoder(w, 2)
+    odec = oracle.OracleTdt(w)
+    want = [odec.decode(oenc.encode(s)) for s in subs]
+    m, exact = token_match(got, want)
+    print(f"end-to-end token match {m:.4f}, identical streams {exact:.2f}")
+    assert m >= MATCH
