@@ -294,11 +294,11 @@ def shard_lpt(frames, n_ranks: int) -> np.ndarray:
 
 def frames_for_seconds(seconds: float) -> int:
     """Encoder frames T for an utterance of `seconds` at 16 kHz: the pipeline
-    prepends 0.25 s (src/transcription.rs:48-52), the mel front end keeps
-    len/160 valid frames (src/mel.rs:50-51) and three stride-2 convs give
-    l -> (l - 1)//2 + 1 each (src/sub.rs:11-13)."""
+    prepends 0.25 s (src/transcription.rs:48-52), the mel front end produces
+    1 + len/160 frames (src/mel.rs:50) and three stride-2 convs give
+    l -> (l - 1)//2 + 1 each (src/sub.rs:11-13, 283)."""
     n = int(round(seconds * 16000)) + 4000
-    v = n // 160
+    v = 1 + n // 160
     for _ in range(3):
         v = (v - 1) // 2 + 1
     return v

@@ -196,8 +196,12 @@ struct b3_ctx {
         DevBuf bias;                           // f32: lstm0 [2560] | lstm1 [2560] | proj [640] | head [npad]
         int bcap = 0, tcap = 0;
         DevBuf a0, a1, ap, aj, gates, cstate, dec, scores, ints, tokens, cu, flag, pooler;
+        cudaGraphExec_t chunk_exec = nullptr;  // captured decode chunk
+        const void* chunk_key[6] = {};
+        int64_t chunk_launches[B3_K_COUNT] = {};
     } dec;
     ~b3_ctx() {
+        if (dec.chunk_exec) cudaGraphExecDestroy(dec.chunk_exec);
         for (cudaEvent_t e : prof.pool) cudaEventDestroy(e);
         for (Linear* l : {&dec.lstm[0], &dec.lstm[1], &dec.proj, &dec.head}) {
             l->w.release();
@@ -828,9 +832,11 @@ int decode_device(b3_ctx* c, const float* pooler, const int32_t* cu, int n_utt, 
     B3_TRY(dec_lstm_step(c, s));
     const float* head_bias = D.bias.as<float>() + 5120 + 640;
     const long max_steps = static_cast<long>(tmax) * 14 + 64;
+    // One chunk = kChunk lock steps + the "any row still active" reduction.
+    // It is captured once as a CUDA graph and replayed until every row is
+    // done: ~130 tiny launches per chunk would otherwise be launch-bound.
     constexpr int kChunk = 16;
-    int any = 1;
-    for (long step = 0; step < max_steps && any; step += kChunk) {
+    auto chunk = [&]() -> int {
         for (int k = 0; k < kChunk; ++k) {
             {
                 ProfScope ps(c, B3_K_DECODER, 0.0, 0.0);
@@ -843,7 +849,47 @@ int decode_device(b3_ctx* c, const float* pooler, const int32_t* cu, int n_utt, 
             }
             B3_TRY(dec_lstm_step(c, s));
         }
-        B3_TRY(dec_launch_any_active(s, D.flag.as<int>(), c->stream));
+        ProfScope ps(c, B3_K_DECODER, 0.0, 0.0);
+        return dec_launch_any_active(s, D.flag.as<int>(), c->stream);
+    };
+    const void* key[6] = {s.pooler, s.a0, s.tokens, s.scores, s.cu, reinterpret_cast<const void*>(static_cast<intptr_t>(s.B) << 20 | max_tokens)};
+    if (!D.chunk_exec || memcmp(key, D.chunk_key, sizeof(key)) != 0) {
+        if (D.chunk_exec) cudaGraphExecDestroy(D.chunk_exec);
+        D.chunk_exec = nullptr;
+        int64_t before[B3_K_COUNT];
+        memcpy(before, c->prof.launches, sizeof(before));
+        const bool prof_on = c->prof.on;
+        c->prof.on = false;  // no event records inside the graph
+        B3_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+        const int rc = chunk();
+        cudaGraph_t graph = nullptr;
+        const cudaError_t ec = cudaStreamEndCapture(c->stream, &graph);
+        c->prof.on = prof_on;
+        if (rc) {
+            if (graph) cudaGraphDestroy(graph);
+            return rc;
+        }
+        if (ec != cudaSuccess) return set_cuda_error("capturing the decoder chunk", ec);
+        const cudaError_t ei = cudaGraphInstantiate(&D.chunk_exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (ei != cudaSuccess) {
+            D.chunk_exec = nullptr;
+            return set_cuda_error("instantiating the decoder chunk", ei);
+        }
+        for (int k = 0; k < B3_K_COUNT; ++k) {
+            D.chunk_launches[k] = c->prof.launches[k] - before[k];
+            c->prof.launches[k] = before[k];
+        }
+        memcpy(D.chunk_key, key, sizeof(key));
+    }
+    int any = 1;
+    for (long step = 0; step < max_steps && any; step += kChunk) {
+        {
+            ProfScope ps(c, B3_K_DECODER, 0.0, 0.0);
+            B3_CUDA(cudaGraphLaunch(D.chunk_exec, c->stream));
+        }
+        c->prof.launches[B3_K_DECODER]--;  // the replay itself is not a kernel
+        for (int k = 0; k < B3_K_COUNT; ++k) c->prof.launches[k] += D.chunk_launches[k];
         B3_CUDA(cudaMemcpyAsync(&any, D.flag.p, sizeof(int), cudaMemcpyDeviceToHost, c->stream));
         B3_CUDA(cudaStreamSynchronize(c->stream));
     }
@@ -1178,7 +1224,7 @@ int b3_profile(b3_ctx* ctx, int enable) {
     Prof& p = ctx->prof;
     B3_CUDA(cudaStreamSynchronize(ctx->stream));
     if (enable && p.pool.empty()) {
-        p.pool.resize(2 * 16384);
+        p.pool.resize(1 << 17);
         for (auto& e : p.pool) B3_CUDA(cudaEventCreate(&e));
     }
     p.on = enable != 0;

@@ -38,7 +38,9 @@ sys.path.insert(0, str(ROOT))
 from __graft_entry__ import load_oracle, load_package  # noqa: E402
 
 N_LAYERS = 24
-METRIC = "RTFx (audio-s/s), 4-bit Conformer encoder"
+METRIC = "RTFx (audio-s/s), batched transcription (4-bit encoder + greedy TDT)"
+VOCAB = 1025        # 1024 tokens + blank
+MAX_TOKENS = 1024   # token slots per utterance in the output buffer
 
 
 def parse():
@@ -53,8 +55,9 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=5)
-    ap.add_argument("--workload", default="batch", choices=["batch", "linear"],
-                    help="batch: the encoder over the config-5 batch; linear: K1 GEMM shape sweep (config 1)")
+    ap.add_argument("--workload", default="transcribe", choices=["transcribe", "encoder", "linear"],
+                    help="transcribe: encoder + TDT decoder over the config-5 batch; encoder: the encoder "
+                         "alone; linear: K1 GEMM shape sweep (config 1)")
     return ap.parse_args()
 
 
@@ -109,7 +112,10 @@ def run_linear_sweep(args):
 
 
 def pkg_kind(name):
-    return ["gemm_lut4", "gemm_f16", "attention", "layernorm", "dwconv", "convert", "other"].index(name)
+    return KINDS.index(name)
+
+
+KINDS = ["gemm_lut4", "gemm_f16", "attention", "layernorm", "dwconv", "convert", "other", "decoder"]
 
 
 def peaks():
@@ -182,16 +188,20 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(loaded)}
 
 
-def cpu_baseline_sample(oracle, syn, weights, secs, frames, budget_s, seed):
-    """The oracle (restated reference CPU encoder, all host cores) on the first
-    utterances of the batch, in turn, until the time budget is spent."""
+def cpu_baseline_sample(oracle, syn, weights, secs, frames, budget_s, seed, decode):
+    """The oracle (restated reference CPU encoder and TDT decoder, all host
+    cores) on the first utterances of the batch, in turn, until the time
+    budget is spent."""
     enc = oracle.OracleEncoder(weights, N_LAYERS)
+    dec = oracle.OracleTdt(weights) if decode else None
     rng = np.random.default_rng(seed)
     done_audio, used, n = 0.0, 0.0, 0
     for s, t in zip(secs, frames):
         sub = syn.sub_features(rng, t)
         t0 = time.perf_counter()
-        enc.encode(sub)
+        pooled = enc.encode(sub)
+        if dec is not None:
+            dec.decode(pooled)
         used += time.perf_counter() - t0
         done_audio += s
         n += 1
@@ -210,16 +220,26 @@ def run_reference(args, rank, world):
     oracle = load_oracle()
     secs, frames = batch_for_rank(args, 0, 1, pkg, syn)
     weights = syn.encoder_weights(seed=args.seed, n_layers=N_LAYERS, layout="lut4")
+    decode = args.workload == "transcribe"
+    if decode:
+        weights.update(syn.decoder_weights(seed=args.seed, vocab=VOCAB))
     enc = oracle.OracleEncoder(weights, N_LAYERS)
+    dec = oracle.OracleTdt(weights) if decode else None
     rng = np.random.default_rng(args.seed)
     subs = [syn.sub_features(rng, t) for t in frames[: max(1, min(len(frames), 4))]]
+
+    def one(sub):
+        pooled = enc.encode(sub)
+        if dec is not None:
+            dec.decode(pooled)
+
     for w in range(args.warmup):
-        enc.encode(subs[w % len(subs)])
+        one(subs[w % len(subs)])
     audio, wall = 0.0, 0.0
     for k in range(args.steps):
         i = k % len(subs)
         t0 = time.perf_counter()
-        enc.encode(subs[i])
+        one(subs[i])
         wall += time.perf_counter() - t0
         audio += secs[i]
     v = audio / wall
@@ -229,11 +249,13 @@ def run_reference(args, rank, world):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * wall / args.steps, 3),
         "higher_is_better": True, "scaling": "weak" if not args.strong else "strong", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "reference CPU encoder (src/cpu/*, restated in C, AVX2/F16C FMA), "
-                   "one utterance of the config-5 batch per step", "utterances_sampled": len(subs),
+        "config": {"workload": "reference CPU path (src/cpu/* encoder" + (" + src/tdt.rs greedy TDT" if decode else "")
+                   + ", restated in C, AVX2/F16C FMA), one utterance of the config-5 batch per step",
+                   "utterances_sampled": len(subs),
                    "frames": frames[: len(subs)], "layers": N_LAYERS, "weights": "random-init 4-bit LUT"},
         "cpu_baseline": {"value": round(v, 3), "unit": "audio-s/s", "cores": cores, "kind": "port",
-                         "sample": f"{args.steps} encodes of utterances {frames[:len(subs)]} frames"},
+                         "sample": f"{args.steps} utterances (cycling {frames[:len(subs)]} frames), "
+                                   + ("encode + decode" if decode else "encode")},
         "e2e": {"value": round(v, 3), "unit": "audio-s/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -268,7 +290,10 @@ def main():
     cu = np.concatenate([[0], np.cumsum(frames)]).astype(np.int32)
     audio = float(sum(secs))
 
+    decode = args.workload == "transcribe"
     weights = syn.encoder_weights(seed=args.seed, n_layers=N_LAYERS, layout="lut4")
+    if decode:
+        weights.update(syn.decoder_weights(seed=args.seed, vocab=VOCAB))
     enc = pkg.Encoder(local)
     enc.load(weights)
     enc.finalize(N_LAYERS)
@@ -282,8 +307,28 @@ def main():
     host_out = torch.empty((M, 640), dtype=torch.float32, pin_memory=True)
     dev_in = host_in.cuda()
     dev_out = torch.empty((M, 640), dtype=torch.float32, device="cuda")
+    n_utt = len(frames)
+    dev_tok = torch.zeros((n_utt, MAX_TOKENS, 3), dtype=torch.int32, device="cuda")
+    dev_cnt = torch.zeros(n_utt, dtype=torch.int32, device="cuda")
+    host_tok = np.zeros((n_utt, MAX_TOKENS, 3), dtype=np.uint32)
+    host_cnt = np.zeros(n_utt, dtype=np.int32)
     torch.cuda.synchronize()
     stream = torch.cuda.ExternalStream(enc.stream)
+    L = pkg.lib()
+
+    def step_device():
+        if decode:
+            pkg.check(L.b3_transcribe_batch(enc.ctx, dev_in.data_ptr(), cu.ctypes.data, n_utt, dev_tok.data_ptr(),
+                                            dev_cnt.data_ptr(), MAX_TOKENS, pkg.B3_DEVICE_PTRS))
+        else:
+            enc.encode_batch(dev_in, cu, out=dev_out)
+
+    def step_host(hin, hout):
+        if decode:
+            pkg.check(L.b3_transcribe_batch(enc.ctx, hin.ctypes.data, cu.ctypes.data, n_utt, host_tok.ctypes.data,
+                                            host_cnt.ctypes.data, MAX_TOKENS, 0))
+        else:
+            enc.encode_batch(hin, cu, out=hout)
 
     def barrier():
         if world > 1:
@@ -298,9 +343,8 @@ def main():
 
     # ── value: device-resident inputs ──
     for _ in range(args.warmup):
-        enc.encode_batch(dev_in, cu, out=dev_out)
+        step_device()
     enc.sync()
-    L = pkg.lib()
     L.b3_profile(enc.ctx, 1)
     barrier()
     torch.cuda.synchronize()
@@ -310,7 +354,7 @@ def main():
     with ClockSampler(local) as clk:
         ev0.record(stream)
         for _ in range(args.steps):
-            enc.encode_batch(dev_in, cu, out=dev_out)
+            step_device()
         ev1.record(stream)
         enc.sync()
     torch.cuda.synchronize()
@@ -318,7 +362,7 @@ def main():
     clocks = clk.summary()
     prof = {}
     import ctypes
-    for kind, name in enumerate(["gemm_lut4", "gemm_f16", "attention", "layernorm", "dwconv", "convert", "other"]):
+    for kind, name in enumerate(KINDS):
         a, f, b, n = ctypes.c_double(), ctypes.c_double(), ctypes.c_double(), ctypes.c_int64()
         pkg.check(L.b3_profile_read(enc.ctx, kind, ctypes.byref(a), ctypes.byref(f), ctypes.byref(b), ctypes.byref(n)))
         prof[name] = {"ms": a.value, "flops": f.value, "bytes": b.value, "launches": n.value}
@@ -335,13 +379,13 @@ def main():
     # ── e2e: host buffers through the host-pointer ABI call ──
     barrier()
     hin, hout = host_in.numpy(), host_out.numpy()
-    enc.encode_batch(hin, cu, out=hout)  # warm the staging buffers
+    step_host(hin, hout)  # warm the staging buffers
     barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
-        enc.encode_batch(hin, cu, out=hout)
+        step_host(hin, hout)
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
@@ -360,9 +404,10 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         oracle = load_oracle()
-        v, n, a_s, used = cpu_baseline_sample(oracle, syn, weights, secs, frames, args.cpu_seconds, args.seed)
+        v, n, a_s, used = cpu_baseline_sample(oracle, syn, weights, secs, frames, args.cpu_seconds, args.seed, decode)
         cpu = {"value": round(v, 3), "unit": "audio-s/s", "cores": oracle.threads(), "kind": "port",
-               "sample": f"first {n} utterances of the batch ({a_s:.1f} audio-s, {used:.1f} s wall), 24 blocks, in turn"}
+               "sample": f"first {n} utterances of the batch ({a_s:.1f} audio-s, {used:.1f} s wall), "
+                         + ("encoder + decoder" if decode else "encoder") + ", in turn"}
 
     if rank == 0:
         line = {
@@ -370,12 +415,15 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3),
             "higher_is_better": True, "scaling": "strong" if args.strong else "weak", "vs_baseline": None,
             "dtype": "f16", "data": "synthetic",
-            "config": {"workload": "config-5 batch through the 24-block 4-bit LUT encoder (encoder stage)",
+            "config": {"workload": ("config-5 batch: 24-block 4-bit LUT encoder + batched greedy TDT decoder"
+                                    if decode else "config-5 batch through the 24-block 4-bit LUT encoder"),
                        "utterances_per_rank": len(frames), "audio_s_per_rank": round(audio, 1),
                        "frames_per_rank": M, "lengths_s": "U(10,60) seeded", "layers": N_LAYERS,
                        "d_model": 1024, "heads": 8, "ffn": 4096, "conv_kernel": 9,
                        "weights": "random-init 4-bit codes + 16-entry f16 LUT per row",
                        "input": "synthetic (T,4096) subsampled features, f32",
+                       "decoder": (f"2-layer LSTM 640, joint 640, vocab {VOCAB - 1}+blank, durations 0..4, "
+                                   "random-init" if decode else None),
                        "l2": "inputs (%.2f GB) > L2, no flush" % (M * 4096 * 4 / 1e9),
                        "parallelism": f"utterance-sharded x{world}, no collective"},
             "roofline": {"kernel": "k1_gemm (LUT4, tcgen05)", "bound": "tensor",
@@ -392,7 +440,8 @@ def main():
             "gpu_launches": launches,
             "clocks": clocks,
             "e2e": {"value": round(e2e_value, 2), "unit": "audio-s/s",
-                    "h2d_bytes_per_step": int(M * 4096 * 4), "d2h_bytes_per_step": int(M * 640 * 4)},
+                    "h2d_bytes_per_step": int(M * 4096 * 4),
+                    "d2h_bytes_per_step": int(n_utt * (MAX_TOKENS * 12 + 4)) if decode else int(M * 640 * 4)},
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)
