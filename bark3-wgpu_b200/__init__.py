@@ -90,6 +90,10 @@ def lib() -> ctypes.CDLL:
         "b3_shard_lpt": (c_i, [c_p, c_i, c_i, c_p]),
         "b3_decode_batch": (c_i, [c_p, c_p, c_p, c_i, c_p, c_p, c_i, c_u]),
         "b3_transcribe_batch": (c_i, [c_p, c_p, c_p, c_i, c_p, c_p, c_i, c_u]),
+        "b3_transcribe_audio": (c_i, [c_p, c_p, c_p, c_i, c_p, c_p, c_i, c_u]),
+        "b3_mel": (c_i, [c_p, c_p, c_p, c_i, c_p, c_p, c_u]),
+        "b3_subsample": (c_i, [c_p, c_p, c_p, c_p, c_i, c_p, c_p, c_u]),
+        "b3_mel_filters": (c_i, [c_p]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -223,6 +227,45 @@ class Encoder:
         """Encoder + decoder: subsampled frames -> token streams per utterance."""
         return self._tokens_call("b3_transcribe_batch", sub, cu_seqlens, max_tokens)
 
+    def transcribe_audio(self, waves, max_tokens: int = 4096):
+        """16 kHz mono utterances (list of f32 arrays) -> token streams; the
+        0.25 s lead-in of the reference pipeline is added by the library."""
+        off = np.concatenate([[0], np.cumsum([len(w) for w in waves])]).astype(np.int64)
+        samples = np.ascontiguousarray(np.concatenate(waves), dtype=np.float32)
+        n = len(waves)
+        tokens = np.zeros((n, max_tokens, 3), dtype=np.uint32)
+        counts = np.zeros(n, dtype=np.int32)
+        check(self._L.b3_transcribe_audio(self.ctx, _ptr(samples), _ptr(off), n, _ptr(tokens), _ptr(counts),
+                                          max_tokens, 0))
+        return [tokens[i, : min(int(counts[i]), max_tokens)] for i in range(n)]
+
+    def mel(self, waves):
+        """Padded waves -> list of (frames, 128) normalised log-mel arrays."""
+        off = np.concatenate([[0], np.cumsum([len(w) for w in waves])]).astype(np.int64)
+        samples = np.ascontiguousarray(np.concatenate(waves), dtype=np.float32)
+        n = len(waves)
+        frames = int(sum(1 + len(w) // 160 for w in waves))
+        out = np.zeros((frames, 128), dtype=np.float32)
+        foff = np.zeros(n + 1, dtype=np.int32)
+        check(self._L.b3_mel(self.ctx, _ptr(samples), _ptr(off), n, _ptr(out), _ptr(foff), 0))
+        return [out[foff[i]:foff[i + 1]] for i in range(n)]
+
+    def subsample(self, mels, n_valid):
+        """List of (frames, 128) mel arrays -> list of (T, 4096) rows."""
+        foff = np.concatenate([[0], np.cumsum([m.shape[0] for m in mels])]).astype(np.int32)
+        mel = np.ascontiguousarray(np.concatenate(mels), dtype=np.float32)
+        nv = np.ascontiguousarray(n_valid, dtype=np.int32)
+        n = len(mels)
+
+        def clen(v):
+            return (v - 1) // 2 + 1
+
+        total = int(sum(clen(clen(clen(m.shape[0]))) for m in mels))
+        out = np.zeros((total, 4096), dtype=np.float32)
+        roff = np.zeros(n + 1, dtype=np.int32)
+        check(self._L.b3_subsample(self.ctx, _ptr(mel), _ptr(foff), _ptr(nv), n, _ptr(out), _ptr(roff), 0))
+        return [out[roff[i]:roff[i + 1]] for i in range(n)]
+
     def _tokens_call(self, fn, src, cu_seqlens, max_tokens):
         cu = np.ascontiguousarray(cu_seqlens, dtype=np.int32)
         n = len(cu) - 1
@@ -281,6 +324,13 @@ def _empty_like_kind(ref, shape):
     import torch
 
     return torch.empty(shape, dtype=torch.float32, device=ref.device)
+
+
+def mel_filters() -> np.ndarray:
+    """The (128, 257) slaney filterbank the library's front end uses."""
+    out = np.zeros((128, 257), dtype=np.float32)
+    check(lib().b3_mel_filters(_ptr(out)))
+    return out
 
 
 def shard_lpt(frames, n_ranks: int) -> np.ndarray:

@@ -26,6 +26,7 @@ enum GemmEpi {
     EPI_SILU_F16 = 3,  // out_f16 = f16(silu(acc (+ bias)))
     EPI_GLU_F16 = 4,   // out_f16[:, i] = f16(acc[2i] * sigmoid(acc[2i+1]))
     EPI_QKV = 5,       // out_f16 row = [q + bias_u | q + bias_v | k | v]
+    EPI_RELU_F16 = 6,  // out_f16 = f16(max(acc + bias, 0))
 };
 
 struct GemmParams {

@@ -63,4 +63,40 @@ int dec_launch_lstm_update(const DecState& s, int layer, cudaStream_t st);
 int dec_launch_any_active(const DecState& s, int* out, cudaStream_t st);
 int dec_launch_split(const float* src, __half* hi, __half* lo, int64_t n, cudaStream_t st);
 
+// Mel front end (frontend.cu).
+struct MelParams {
+    int n_utt;
+    const float* wave;        // padded waves, concatenated
+    const int64_t* wave_off;  // [n_utt + 1] sample offsets
+    const int* frame_off;     // [n_utt + 1] frame offsets (1 + len/160 frames each)
+    const float* window;      // [512] Hann(400) centred
+    const float2* twiddle;    // [256] exp(-2 pi i k / 512)
+    const float* fb;          // [128][257] slaney filterbank
+    const int* fb_lo;         // [128] first nonzero bin of each filter
+    const int* fb_hi;         // [128] one past the last
+    float* mel;               // [frames][128]
+};
+
+// Conv subsampling (frontend.cu); activations channels-last, f16.
+struct SubParams {
+    int n_utt;
+    const float* mel;         // [frames][128]
+    const int* mel_off;       // [n_utt + 1]
+    const int* n_valid;       // [n_utt] valid mel frames
+    const int4* work;         // (utterance, first t2 row, channel group, 0) per CTA
+    const float *w0, *b0, *w2, *b2, *w5, *b5;  // conv0 and the two depthwise convs, [256][9] + [256]
+    __half* x2;               // [sum F2][32][256]  after depthwise 1
+    const __half* x3;         // [sum F2][32][256]  after pointwise 1
+    __half* x4;               // [sum T][16][256]   after depthwise 2
+    const int* x2_off;        // [n_utt + 1] row offsets of x2 / x3
+    const int* x4_off;        // [n_utt + 1] row offsets of x4 (= encoder frames)
+};
+
+int launch_mel(const MelParams& p, int n_frames, cudaStream_t st);
+int launch_sub_conv0_dw1(const SubParams& p, int n_work, cudaStream_t st);
+int launch_sub_dw2(const SubParams& p, int rows, cudaStream_t st);
+int launch_sub_to_ref(const __half* src, float* dst, int rows, cudaStream_t st);
+int sub_work_rows();
+int sub_work_channels();
+
 }  // namespace b3

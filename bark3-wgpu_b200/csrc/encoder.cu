@@ -200,7 +200,25 @@ struct b3_ctx {
         const void* chunk_key[6] = {};
         int64_t chunk_launches[B3_K_COUNT] = {};
     } dec;
+    // mel front end + conv subsampling (optional: built when the conv
+    // subsampling tensors are loaded)
+    struct Frontend {
+        bool present = false;
+        DevBuf tables;        // window [512] | twiddle [256][2] | fb [128][257] (f32) | fb_lo [128] | fb_hi [128] (i32)
+        DevBuf conv;          // w0 | b0 | w2 | b2 | w5 | b5 (f32, [256][9] + [256] each)
+        Linear pw1, pw2;      // pointwise convs, f16 [256][256]
+        DevBuf pw_bias;       // [2][256] f32
+        Linear sub_w_perm;    // encoder subsampling linear, input columns in (freq, channel) order
+        DevBuf wave, wave_off, frame_off, mel, x2, x3, x4, ints, work;
+    } fe;
     ~b3_ctx() {
+        for (Linear* l : {&fe.pw1, &fe.pw2, &fe.sub_w_perm}) {
+            l->w.release();
+            l->lut16.release();
+        }
+        for (DevBuf* b : {&fe.tables, &fe.conv, &fe.pw_bias, &fe.wave, &fe.wave_off, &fe.frame_off, &fe.mel, &fe.x2,
+                          &fe.x3, &fe.x4, &fe.ints, &fe.work})
+            b->release();
         if (dec.chunk_exec) cudaGraphExecDestroy(dec.chunk_exec);
         for (cudaEvent_t e : prof.pool) cudaEventDestroy(e);
         for (Linear* l : {&dec.lstm[0], &dec.lstm[1], &dec.proj, &dec.head}) {
@@ -582,10 +600,12 @@ int ffn_half(b3_ctx* c, const Linear& w1, const Linear& w2, int M) {
 // sub16 holds the f16 input; runs `layers` blocks.  After the call:
 //   layers == n_layers: a16 = f16(norm_out(x)) of the last block, x = norm_out(x)
 //   otherwise:          x = pre-norm_out residual of block layers-1
-int forward_blocks(b3_ctx* c, int M, int layers) {
+// `subw` is the subsampling linear matching sub16's column order (the
+// reference's (channel, freq) order, or (freq, channel) from the GPU front end).
+int forward_blocks(b3_ctx* c, int M, int layers, const Linear* subw = nullptr) {
     float* x = c->x.as<float>();
     __half* a16 = c->a16.as<__half>();
-    B3_TRY(run_gemm(c, c->sub_w, c->sub16.as<__half>(), M, kSubIn, EPI_F32,
+    B3_TRY(run_gemm(c, subw ? *subw : c->sub_w, c->sub16.as<__half>(), M, kSubIn, EPI_F32,
                     params_f32(x, kHidden, c->sub_b.as<float>())));
     const int upto = layers < c->n_layers ? layers : c->n_layers;
     if (upto > 0) {
@@ -906,6 +926,259 @@ int decode_collect(b3_ctx* c, int n_utt, b3_token* tokens, int32_t* counts, int 
     return 0;
 }
 
+// ───────────────────────────── front end ─────────────────────────────
+
+int conv_len_h(int l) { return (l - 1) / 2 + 1; }
+
+// Slaney mel filterbank (norm "slaney", mel scale "slaney"; the published
+// librosa / transformers definition the reference's data/mel_filters.f32
+// holds): 128 area-normalised triangles over 0..8000 Hz on the 257 bins of a
+// 512-point FFT at 16 kHz, computed in double and stored as f32.
+void slaney_filterbank(std::vector<float>& fb) {
+    const double f_sp = 200.0 / 3.0, min_log_hz = 1000.0, min_log_mel = min_log_hz / f_sp;
+    const double logstep = std::log(6.4) / 27.0;
+    auto hz_to_mel = [&](double f) { return f >= min_log_hz ? min_log_mel + std::log(f / min_log_hz) / logstep : f / f_sp; };
+    auto mel_to_hz = [&](double m) { return m >= min_log_mel ? min_log_hz * std::exp(logstep * (m - min_log_mel)) : m * f_sp; };
+    const int n_mels = 128, n_bins = 257;
+    const double mlo = hz_to_mel(0.0), mhi = hz_to_mel(8000.0);
+    std::vector<double> pts(n_mels + 2);
+    for (int i = 0; i < n_mels + 2; ++i) pts[i] = mel_to_hz(mlo + (mhi - mlo) * i / (n_mels + 1));
+    fb.assign(static_cast<size_t>(n_mels) * n_bins, 0.f);
+    for (int m = 0; m < n_mels; ++m) {
+        const double enorm = 2.0 / (pts[m + 2] - pts[m]);
+        for (int k = 0; k < n_bins; ++k) {
+            const double f = k * 8000.0 / 256.0;
+            const double lower = (f - pts[m]) / (pts[m + 1] - pts[m]);
+            const double upper = (pts[m + 2] - f) / (pts[m + 2] - pts[m + 1]);
+            const double w = std::max(0.0, std::min(lower, upper));
+            fb[static_cast<size_t>(m) * n_bins + k] = static_cast<float>(w * enorm);
+        }
+    }
+}
+
+// Window, twiddles and filterbank, uploaded once per context.
+int build_fe_tables(b3_ctx* c) {
+    std::vector<float> fb;
+    slaney_filterbank(fb);
+    std::vector<float> t(512 + 512 + fb.size() + 256, 0.f);
+    for (int i = 0; i < 400; ++i)  // symmetric Hann(400) centred in 512 (src/mel.rs:27-36)
+        t[56 + i] = 0.5f * (1.0f - cosf(6.2831855f * static_cast<float>(i) / 399.0f));
+    for (int k = 0; k < 256; ++k) {
+        t[512 + 2 * k] = static_cast<float>(std::cos(-2.0 * M_PI * k / 512.0));
+        t[512 + 2 * k + 1] = static_cast<float>(std::sin(-2.0 * M_PI * k / 512.0));
+    }
+    memcpy(&t[1024], fb.data(), fb.size() * 4);
+    int32_t* lohi = reinterpret_cast<int32_t*>(&t[1024 + fb.size()]);
+    for (int m = 0; m < 128; ++m) {
+        int lo = 257, hi = 0;
+        for (int k = 0; k < 257; ++k)
+            if (fb[m * 257 + k] != 0.f) {
+                lo = std::min(lo, k);
+                hi = k + 1;
+            }
+        lohi[m] = lo < hi ? lo : 0;
+        lohi[128 + m] = lo < hi ? hi : 0;
+    }
+    B3_TRY(upload(c->fe.tables, t.data(), t.size() * 4, c->stream));
+    B3_CUDA(cudaStreamSynchronize(c->stream));
+    return 0;
+}
+
+// Conv-subsampling weights (SubsamplingWeights, src/sub.rs:56-103) and the
+// encoder's subsampling linear with its input columns permuted from
+// (channel c, freq m) -> c*16 + m to (m, c) -> m*256 + c, the order the GPU
+// front end writes.
+int build_frontend(b3_ctx* c) {
+    auto& F = c->fe;
+    if (!find(c, "encoder.subsampling.layers.0.weight")) return 0;
+    const std::string p = "encoder.subsampling.layers.";
+    std::vector<float> conv, v;
+    for (const char* l : {"0", "2", "5"}) {
+        B3_TRY(get_vec(c, p + l + ".weight", 256 * 9, v));
+        conv.insert(conv.end(), v.begin(), v.end());
+        B3_TRY(get_vec(c, p + l + ".bias", 256, v));
+        conv.insert(conv.end(), v.begin(), v.end());
+    }
+    B3_TRY(upload(F.conv, conv.data(), conv.size() * 4, c->stream));
+    std::vector<float> pb;
+    for (const char* l : {"3", "6"}) {
+        const Staged* s = find(c, p + l + ".weight");
+        if (!s) return set_error(B3_ENOTFOUND, "tensor %s.weight was not loaded", (p + l).c_str());
+        if (s->lowbit || numel(*s) != 256 * 256) return set_error(B3_EINVAL, "%s.weight must be (256, 256, 1, 1)", (p + l).c_str());
+        B3_TRY(build_dense(c, l[0] == '3' ? F.pw1 : F.pw2, s->f16, 256, 256));
+        B3_TRY(get_vec(c, p + l + ".bias", 256, v));
+        pb.insert(pb.end(), v.begin(), v.end());
+    }
+    B3_TRY(upload(F.pw_bias, pb.data(), pb.size() * 4, c->stream));
+    // permuted subsampling linear
+    const Staged* s = find(c, "encoder.subsampling.linear.weight");
+    if (!s) return set_error(B3_ENOTFOUND, "tensor encoder.subsampling.linear.weight was not loaded");
+    Linear& L = F.sub_w_perm;
+    L.present = true;
+    L.lut = s->lowbit;
+    L.N = kHidden;
+    L.K = kSubIn;
+    auto src_col = [](int col) { return (col % 256) * 16 + col / 256; };  // new (m, c) -> old c*16 + m
+    if (s->lowbit) {
+        std::vector<uint8_t> codes(static_cast<size_t>(kHidden) * kSubIn / 2, 0);
+        for (int r = 0; r < kHidden; ++r) {
+            const uint8_t* old = &s->codes[static_cast<size_t>(r) * kSubIn / 2];
+            uint8_t* dst = &codes[static_cast<size_t>(r) * kSubIn / 2];
+            for (int col = 0; col < kSubIn; ++col) {
+                const int oc = src_col(col);
+                const uint8_t code = (oc & 1) ? (old[oc / 2] >> 4) : (old[oc / 2] & 0xF);
+                dst[col / 2] |= (col & 1) ? static_cast<uint8_t>(code << 4) : code;
+            }
+        }
+        B3_TRY(upload(L.w, codes.data(), codes.size(), c->stream));
+        B3_TRY(upload(L.lut16, s->lut16.data(), s->lut16.size() * 2, c->stream));
+    } else {
+        std::vector<uint16_t> w(static_cast<size_t>(kHidden) * kSubIn);
+        for (int r = 0; r < kHidden; ++r)
+            for (int col = 0; col < kSubIn; ++col)
+                w[static_cast<size_t>(r) * kSubIn + col] = s->f16[static_cast<size_t>(r) * kSubIn + src_col(col)];
+        B3_TRY(upload(L.w, w.data(), w.size() * 2, c->stream));
+    }
+    B3_CUDA(cudaStreamSynchronize(c->stream));
+    B3_TRY(gemm_make_b_map(&L.map_b, L.w.p, L.lut, kHidden, kSubIn));
+    F.present = true;
+    return 0;
+}
+
+// Frame bookkeeping of a batch of padded waves.
+struct FeShape {
+    std::vector<int32_t> foff, nvalid, x2off, x4off;
+    std::vector<int4> work;
+};
+
+void fe_shape_from_frames(FeShape& s, const std::vector<int32_t>& frames, const std::vector<int32_t>& nvalid) {
+    const int n = static_cast<int>(frames.size());
+    s.foff.assign(n + 1, 0);
+    s.x2off.assign(n + 1, 0);
+    s.x4off.assign(n + 1, 0);
+    s.nvalid = nvalid;
+    s.work.clear();
+    const int rows = sub_work_rows(), groups = 256 / sub_work_channels();
+    for (int u = 0; u < n; ++u) {
+        const int f2 = conv_len_h(conv_len_h(frames[u]));
+        const int t = conv_len_h(f2);
+        s.foff[u + 1] = s.foff[u] + frames[u];
+        s.x2off[u + 1] = s.x2off[u] + f2;
+        s.x4off[u + 1] = s.x4off[u] + t;
+        for (int t2 = 0; t2 < f2; t2 += rows)
+            for (int g = 0; g < groups; ++g) s.work.push_back(make_int4(u, t2, g, 0));
+    }
+}
+
+// mel [frames][128] (device, in c->fe.mel) -> c->sub16 [sum T][4096] in
+// (freq, channel) column order; sets up the encoder plan for the T offsets.
+int fe_subsample(b3_ctx* c, const FeShape& s) {
+    auto& F = c->fe;
+    const int n = static_cast<int>(s.nvalid.size());
+    const int rows2 = s.x2off[n], T = s.x4off[n];
+    B3_TRY(make_plan(c, s.x4off.data(), n));
+    B3_TRY(F.x2.ensure(static_cast<size_t>(rows2) * 32 * 256 * 2 + 16));
+    B3_TRY(F.x3.ensure(static_cast<size_t>(rows2) * 32 * 256 * 2 + 16));
+    B3_TRY(F.x4.ensure(static_cast<size_t>(T) * 16 * 256 * 2 + 16));
+    B3_TRY(F.ints.ensure((3 * n + 2) * sizeof(int32_t)));
+    B3_TRY(F.work.ensure(s.work.size() * sizeof(int4) + 16));
+    int32_t* ints = F.ints.as<int32_t>();
+    B3_CUDA(cudaMemcpyAsync(ints, s.nvalid.data(), n * 4, cudaMemcpyHostToDevice, c->stream));
+    B3_CUDA(cudaMemcpyAsync(ints + n, s.x2off.data(), (n + 1) * 4, cudaMemcpyHostToDevice, c->stream));
+    B3_CUDA(cudaMemcpyAsync(ints + 2 * n + 1, s.x4off.data(), (n + 1) * 4, cudaMemcpyHostToDevice, c->stream));
+    B3_CUDA(cudaMemcpyAsync(F.work.p, s.work.data(), s.work.size() * sizeof(int4), cudaMemcpyHostToDevice, c->stream));
+    SubParams sp;
+    sp.n_utt = n;
+    sp.mel = F.mel.as<float>();
+    sp.mel_off = F.frame_off.as<int>();
+    sp.n_valid = ints;
+    sp.work = F.work.as<int4>();
+    const float* cv = F.conv.as<float>();
+    sp.w0 = cv;
+    sp.b0 = cv + 2304;
+    sp.w2 = cv + 2560;
+    sp.b2 = cv + 4864;
+    sp.w5 = cv + 5120;
+    sp.b5 = cv + 7424;
+    sp.x2 = F.x2.as<__half>();
+    sp.x3 = F.x3.as<__half>();
+    sp.x4 = F.x4.as<__half>();
+    sp.x2_off = ints + n;
+    sp.x4_off = ints + 2 * n + 1;
+    {
+        ProfScope ps(c, B3_K_FRONTEND, 0.0, 0.0);
+        B3_TRY(launch_sub_conv0_dw1(sp, static_cast<int>(s.work.size()), c->stream));
+    }
+    GemmParams p1 = params_f16(F.x3.as<__half>(), 256);
+    p1.bias = F.pw_bias.as<float>();
+    B3_TRY(run_gemm(c, F.pw1, F.x2.as<__half>(), rows2 * 32, 256, EPI_RELU_F16, p1));
+    {
+        ProfScope ps(c, B3_K_FRONTEND, 0.0, 0.0);
+        B3_TRY(launch_sub_dw2(sp, T, c->stream));
+    }
+    GemmParams p2 = params_f16(c->sub16.as<__half>(), 256);
+    p2.bias = F.pw_bias.as<float>() + 256;
+    return run_gemm(c, F.pw2, F.x4.as<__half>(), T * 16, 256, EPI_RELU_F16, p2);
+}
+
+// Padded waves (device, concatenated at woff) -> c->fe.mel; fills s.
+int fe_mel(b3_ctx* c, const float* wave, const std::vector<int64_t>& woff, FeShape& s) {
+    auto& F = c->fe;
+    const int n = static_cast<int>(woff.size()) - 1;
+    std::vector<int32_t> frames(n), nvalid(n);
+    for (int u = 0; u < n; ++u) {
+        const int64_t len = woff[u + 1] - woff[u];
+        if (len < 0) return set_error(B3_EINVAL, "sample offsets must be non-decreasing");
+        frames[u] = static_cast<int32_t>(1 + len / 160);
+        nvalid[u] = static_cast<int32_t>(len / 160);
+    }
+    fe_shape_from_frames(s, frames, nvalid);
+    const int nf = s.foff[n];
+    B3_TRY(F.wave_off.ensure((n + 1) * 8));
+    B3_TRY(F.frame_off.ensure((n + 1) * 4));
+    B3_TRY(F.mel.ensure(static_cast<size_t>(nf) * 128 * 4 + 16));
+    B3_CUDA(cudaMemcpyAsync(F.wave_off.p, woff.data(), (n + 1) * 8, cudaMemcpyHostToDevice, c->stream));
+    B3_CUDA(cudaMemcpyAsync(F.frame_off.p, s.foff.data(), (n + 1) * 4, cudaMemcpyHostToDevice, c->stream));
+    const float* t = F.tables.as<float>();
+    MelParams mp;
+    mp.n_utt = n;
+    mp.wave = wave;
+    mp.wave_off = F.wave_off.as<int64_t>();
+    mp.frame_off = F.frame_off.as<int>();
+    mp.window = t;
+    mp.twiddle = reinterpret_cast<const float2*>(t + 512);
+    mp.fb = t + 1024;
+    mp.fb_lo = reinterpret_cast<const int*>(t + 1024 + 128 * 257);
+    mp.fb_hi = mp.fb_lo + 128;
+    mp.mel = F.mel.as<float>();
+    ProfScope ps(c, B3_K_FRONTEND, 0.0, nf * (160.0 * 4 + 512.0));
+    return launch_mel(mp, nf, c->stream);
+}
+
+// Samples (host or device, one utterance per offset range) -> padded waves
+// in c->fe.wave with the reference's 0.25 s of leading silence
+// (src/transcription.rs:48-52).  Returns the padded offsets.
+int fe_pad(b3_ctx* c, const float* samples, const int64_t* off, int n, bool dev, std::vector<int64_t>& woff) {
+    auto& F = c->fe;
+    constexpr int64_t kPad = 4000;
+    woff.assign(n + 1, 0);
+    for (int u = 0; u < n; ++u) {
+        const int64_t len = off[u + 1] - off[u];
+        if (len < 0) return set_error(B3_EINVAL, "sample offsets must be non-decreasing");
+        woff[u + 1] = woff[u] + kPad + len;
+    }
+    B3_TRY(F.wave.ensure(static_cast<size_t>(woff[n]) * 4 + 16));
+    float* w = F.wave.as<float>();
+    const cudaMemcpyKind k = dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+    for (int u = 0; u < n; ++u) {
+        B3_CUDA(cudaMemsetAsync(w + woff[u], 0, kPad * 4, c->stream));
+        const int64_t len = off[u + 1] - off[u];
+        if (len > 0)
+            B3_CUDA(cudaMemcpyAsync(w + woff[u] + kPad, samples + off[u], static_cast<size_t>(len) * 4, k, c->stream));
+    }
+    return 0;
+}
+
 // Single linear (configs 1 / lbtest): c = a . W^T (+ bias), W given per call.
 int linear_any(b3_ctx* c, const float* a, const void* w, const uint16_t* lut16, bool lut,
                const float* bias, float* out, int m, int n, int k, unsigned flags) {
@@ -1003,7 +1276,8 @@ b3_ctx* b3_create(int device) {
     // inverse frequencies exactly as src/encoder.rs:231-234 computes them (f32)
     float inv[512];
     for (int i = 0; i < 512; ++i) inv[i] = 1.0f / powf(10000.0f, (2.0f * static_cast<float>(i)) / 1024.0f);
-    if (upload(c->inv_freq, inv, sizeof(inv), c->stream) || cudaStreamSynchronize(c->stream) != cudaSuccess) {
+    if (upload(c->inv_freq, inv, sizeof(inv), c->stream) || cudaStreamSynchronize(c->stream) != cudaSuccess ||
+        build_fe_tables(c)) {
         delete c;
         return nullptr;
     }
@@ -1148,6 +1422,7 @@ int b3_finalize(b3_ctx* ctx, int n_layers) {
         B3_CUDA(cudaStreamSynchronize(ctx->stream));
     }
     B3_TRY(build_decoder(ctx));
+    B3_TRY(build_frontend(ctx));
     ctx->n_layers = n_layers;
     ctx->finalized = true;
     ctx->staged.clear();
@@ -1192,6 +1467,96 @@ int b3_transcribe_batch(b3_ctx* ctx, const float* sub, const int32_t* cu_seqlens
     }
     B3_TRY(encode_device(ctx, in, M, ctx->n_layers, ctx->dec.pooler.as<float>()));
     B3_TRY(decode_device(ctx, ctx->dec.pooler.as<float>(), cu_seqlens, n_utt, max_tokens));
+    B3_TRY(decode_collect(ctx, n_utt, tokens, counts, max_tokens, dev));
+    return dev ? 0 : sync_and_check(ctx);
+}
+
+int b3_mel_filters(float* out) {
+    if (!out) return set_error(B3_EINVAL, "null buffer");
+    std::vector<float> fb;
+    slaney_filterbank(fb);
+    memcpy(out, fb.data(), fb.size() * 4);
+    return 0;
+}
+
+int b3_mel(b3_ctx* ctx, const float* wave, const int64_t* offsets, int n_utt, float* mel, int32_t* frame_offsets,
+           unsigned flags) {
+    if (!ctx) return set_error(B3_EINVAL, "null context");
+    if (!wave || !offsets || !mel || !frame_offsets || n_utt <= 0) return set_error(B3_EINVAL, "bad arguments");
+    if (offsets[0] != 0) return set_error(B3_EINVAL, "offsets[0] must be 0");
+    DeviceGuard g(ctx->device);
+    const bool dev = flags & B3_DEVICE_PTRS;
+    std::vector<int64_t> woff(offsets, offsets + n_utt + 1);
+    const float* w = wave;
+    if (!dev) {
+        B3_TRY(ctx->fe.wave.ensure(static_cast<size_t>(woff[n_utt]) * 4 + 16));
+        B3_CUDA(cudaMemcpyAsync(ctx->fe.wave.p, wave, static_cast<size_t>(woff[n_utt]) * 4, cudaMemcpyHostToDevice, ctx->stream));
+        w = ctx->fe.wave.as<float>();
+    }
+    FeShape s;
+    B3_TRY(fe_mel(ctx, w, woff, s));
+    memcpy(frame_offsets, s.foff.data(), (n_utt + 1) * 4);
+    B3_CUDA(cudaMemcpyAsync(mel, ctx->fe.mel.p, static_cast<size_t>(s.foff[n_utt]) * 128 * 4,
+                            dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost, ctx->stream));
+    return dev ? 0 : sync_and_check(ctx);
+}
+
+int b3_subsample(b3_ctx* ctx, const float* mel, const int32_t* frame_offsets, const int32_t* n_valid, int n_utt,
+                 float* sub, int32_t* row_offsets, unsigned flags) {
+    B3_TRY(check_finalized(ctx));
+    if (!ctx->fe.present) return set_error(B3_ESTATE, "no conv subsampling weights were loaded");
+    if (!mel || !frame_offsets || !n_valid || !sub || !row_offsets || n_utt <= 0)
+        return set_error(B3_EINVAL, "bad arguments");
+    DeviceGuard g(ctx->device);
+    const bool dev = flags & B3_DEVICE_PTRS;
+    std::vector<int32_t> frames(n_utt), nv(n_valid, n_valid + n_utt);
+    for (int u = 0; u < n_utt; ++u) {
+        frames[u] = frame_offsets[u + 1] - frame_offsets[u];
+        if (frames[u] <= 0) return set_error(B3_EINVAL, "utterance %d has no frames", u);
+    }
+    FeShape s;
+    fe_shape_from_frames(s, frames, nv);
+    auto& F = ctx->fe;
+    const int nf = s.foff[n_utt];
+    B3_TRY(F.frame_off.ensure((n_utt + 1) * 4));
+    B3_TRY(F.mel.ensure(static_cast<size_t>(nf) * 128 * 4 + 16));
+    B3_CUDA(cudaMemcpyAsync(F.frame_off.p, s.foff.data(), (n_utt + 1) * 4, cudaMemcpyHostToDevice, ctx->stream));
+    B3_CUDA(cudaMemcpyAsync(F.mel.p, mel, static_cast<size_t>(nf) * 128 * 4,
+                            dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, ctx->stream));
+    B3_TRY(fe_subsample(ctx, s));
+    const int T = s.x4off[n_utt];
+    memcpy(row_offsets, s.x4off.data(), (n_utt + 1) * 4);
+    float* out = sub;
+    if (!dev) {
+        B3_TRY(ctx->io_out.ensure(static_cast<size_t>(T) * 4096 * 4));
+        out = ctx->io_out.as<float>();
+    }
+    B3_TRY(launch_sub_to_ref(ctx->sub16.as<__half>(), out, T, ctx->stream));
+    if (dev) return 0;
+    B3_CUDA(cudaMemcpyAsync(sub, out, static_cast<size_t>(T) * 4096 * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    return sync_and_check(ctx);
+}
+
+int b3_transcribe_audio(b3_ctx* ctx, const float* samples, const int64_t* offsets, int n_utt, b3_token* tokens,
+                        int32_t* counts, int max_tokens, unsigned flags) {
+    B3_TRY(check_finalized(ctx));
+    if (!ctx->fe.present) return set_error(B3_ESTATE, "no conv subsampling weights were loaded");
+    if (!ctx->dec.present) return set_error(B3_ESTATE, "no decoder weights were loaded");
+    if (!samples || !offsets || !tokens || !counts || n_utt <= 0) return set_error(B3_EINVAL, "bad arguments");
+    if (offsets[0] != 0) return set_error(B3_EINVAL, "offsets[0] must be 0");
+    DeviceGuard g(ctx->device);
+    const bool dev = flags & B3_DEVICE_PTRS;
+    std::vector<int64_t> woff;
+    B3_TRY(fe_pad(ctx, samples, offsets, n_utt, dev, woff));
+    FeShape s;
+    B3_TRY(fe_mel(ctx, ctx->fe.wave.as<float>(), woff, s));
+    B3_TRY(fe_subsample(ctx, s));
+    const int M = s.x4off[n_utt];
+    B3_TRY(forward_blocks(ctx, M, ctx->n_layers, &ctx->fe.sub_w_perm));
+    B3_TRY(ctx->dec.pooler.ensure(static_cast<size_t>(M) * 640 * 4));
+    B3_TRY(run_gemm(ctx, ctx->proj_w, ctx->a16.as<__half>(), M, kHidden, EPI_F32,
+                    params_f32(ctx->dec.pooler.as<float>(), kProj, ctx->proj_b.as<float>())));
+    B3_TRY(decode_device(ctx, ctx->dec.pooler.as<float>(), s.x4off.data(), n_utt, max_tokens));
     B3_TRY(decode_collect(ctx, n_utt, tokens, counts, max_tokens, dev));
     return dev ? 0 : sync_and_check(ctx);
 }

@@ -185,7 +185,7 @@ __device__ __forceinline__ void epilogue_subtile(const GemmParams& p, const CUte
                 slab_put<true>(slab, lane, j, make_uint4(f2u(v[4 * j]), f2u(v[4 * j + 1]), f2u(v[4 * j + 2]), f2u(v[4 * j + 3])), 128);
             slab_flush(map_c, slab, lane, n0 + c * 32, y0, EPI == EPI_RESID);
         }
-    } else if (EPI == EPI_F16 || EPI == EPI_SILU_F16 || EPI == EPI_QKV) {
+    } else if (EPI == EPI_F16 || EPI == EPI_SILU_F16 || EPI == EPI_QKV || EPI == EPI_RELU_F16) {
 #pragma unroll 1
         for (int c = 0; c < BN / 64; ++c) {
             const int n = n0 + c * 64;
@@ -211,6 +211,10 @@ __device__ __forceinline__ void epilogue_subtile(const GemmParams& p, const CUte
                 if (EPI == EPI_SILU_F16) {
 #pragma unroll
                     for (int i = 0; i < 64; ++i) v[i] = silu_f(v[i]);
+                }
+                if (EPI == EPI_RELU_F16) {
+#pragma unroll
+                    for (int i = 0; i < 64; ++i) v[i] = fmaxf(v[i], 0.f);
                 }
                 slab_acquire(lane);
                 slab_put_f16x64(slab, lane, v, nullptr);
@@ -488,6 +492,7 @@ int launch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const Gemm
         case EPI_SILU_F16: return launch_one<BN, SUB, LUT, EPI_SILU_F16>(ta, tb, p, st);
         case EPI_GLU_F16: return launch_one<BN, SUB, LUT, EPI_GLU_F16>(ta, tb, p, st);
         case EPI_QKV: return launch_one<BN, SUB, LUT, EPI_QKV>(ta, tb, p, st);
+        case EPI_RELU_F16: return launch_one<BN, SUB, LUT, EPI_RELU_F16>(ta, tb, p, st);
         default: return set_error(B3_EINVAL, "unknown GEMM epilogue %d", epi);
     }
 }

@@ -169,6 +169,34 @@ def decoder_weights(seed: int = 0, vocab: int = 1025, blank_bias: float = 2.0) -
     return w
 
 
+def frontend_weights(seed: int = 0) -> dict:
+    """Random-init conv subsampling (src/sub.rs:56-103 names): conv 1->256
+    3x3, two depthwise 3x3 and two pointwise 256->256, PyTorch's default
+    U(-1/sqrt(fan_in), 1/sqrt(fan_in)) init."""
+    rng = np.random.default_rng(seed)
+    w = {}
+    p = "encoder.subsampling.layers."
+    for l, shape, fan in (("0", (256, 1, 3, 3), 9), ("2", (256, 1, 3, 3), 9), ("3", (256, 256, 1, 1), 256),
+                          ("5", (256, 1, 3, 3), 9), ("6", (256, 256, 1, 1), 256)):
+        k = 1.0 / np.sqrt(fan)
+        w[p + l + ".weight"] = rng.uniform(-k, k, size=shape).astype(np.float32)
+        w[p + l + ".bias"] = rng.uniform(-k, k, size=shape[0]).astype(np.float32)
+    return w
+
+
+def synth_audio(rng: np.random.Generator, seconds: float) -> np.ndarray:
+    """BASELINE configs 2/5 input: 16 kHz white noise U(-0.1, 0.1) plus three
+    sines of amplitude 0.1 at seeded frequencies U(100, 4000) Hz and phases."""
+    n = int(round(seconds * 16000))
+    t = np.arange(n, dtype=np.float64) / 16000.0
+    x = rng.uniform(-0.1, 0.1, size=n)
+    for _ in range(3):
+        f = rng.uniform(100.0, 4000.0)
+        ph = rng.uniform(0.0, 2 * np.pi)
+        x += 0.1 * np.sin(2 * np.pi * f * t + ph)
+    return x.astype(np.float32)
+
+
 def sub_features(rng: np.random.Generator, t: int) -> np.ndarray:
     """Stand-in for the conv-subsampling output (T, 4096): the reference's
     last op is a ReLU (src/sub.rs:107-286), so non-negative values."""

@@ -147,6 +147,37 @@ int b3_decode_batch(b3_ctx* ctx, const float* pooler, const int32_t* cu_seqlens,
 int b3_transcribe_batch(b3_ctx* ctx, const float* sub, const int32_t* cu_seqlens, int n_utt,
                         b3_token* tokens, int32_t* counts, int max_tokens, unsigned flags);
 
+/* ──────────────────────────── front end ────────────────────────────
+ * The mel front end (MelFrontend::compute, src/mel.rs:41-138) and the conv
+ * subsampling (subsample, src/sub.rs:107-300) on the GPU.  The subsampling
+ * is built by b3_finalize when encoder.subsampling.layers.{0,2,3,5,6}.
+ * {weight,bias} were loaded.
+ *
+ * Batched transcription from audio, the AsrInference::transcribe_samples
+ * pipeline (src/inference.rs:446, src/transcription.rs:21-260) for many
+ * utterances at once: 16 kHz mono samples, utterance i at
+ * samples[offsets[i] .. offsets[i+1]] (offsets host, n_utt + 1 entries); the
+ * 0.25 s of leading silence the reference prepends is added here.  Tokens as
+ * for b3_decode_batch (frames count from the start of the padded audio). */
+int b3_transcribe_audio(b3_ctx* ctx, const float* samples, const int64_t* offsets, int n_utt,
+                        b3_token* tokens, int32_t* counts, int max_tokens, unsigned flags);
+
+/* Log-mel features of already padded waves: mel [sum frames][128],
+ * frame_offsets (host, n_utt + 1) receives the per-utterance frame offsets
+ * (1 + len / 160 frames each; frames past len / 160 are zero). */
+int b3_mel(b3_ctx* ctx, const float* wave, const int64_t* offsets, int n_utt, float* mel,
+           int32_t* frame_offsets, unsigned flags);
+
+/* Conv subsampling of mel features (frame_offsets and n_valid host):
+ * sub [sum T][4096] in the reference's row order (channel * 16 + freq), f32;
+ * row_offsets (host, n_utt + 1) receives the per-utterance T offsets,
+ * T = conv_len^3(frames), conv_len(l) = (l - 1) / 2 + 1. */
+int b3_subsample(b3_ctx* ctx, const float* mel, const int32_t* frame_offsets, const int32_t* n_valid,
+                 int n_utt, float* sub, int32_t* row_offsets, unsigned flags);
+
+/* The 128 x 257 slaney mel filterbank the front end uses (host copy). */
+int b3_mel_filters(float* out);
+
 /* ─────────────────────────── single kernels ───────────────────────────
  * one 4-bit linear, c[m][n] = a[m][:] . W[n][:] + bias[n]
  * with W from codes [n][k/2] + lut16 [n][16].  Replaces Ctx::gemm_f32 with a
@@ -207,7 +238,8 @@ int b3_shard_lpt(const int32_t* frames, int n_utt, int n_ranks, int32_t* rank_of
 #define B3_K_CONVERT 5
 #define B3_K_OTHER 6
 #define B3_K_DECODER 7
-#define B3_K_COUNT 8
+#define B3_K_FRONTEND 8
+#define B3_K_COUNT 9
 
 int b3_profile(b3_ctx* ctx, int enable);
 int b3_profile_read(b3_ctx* ctx, int kind, double* ms, double* flops, double* bytes, int64_t* launches);

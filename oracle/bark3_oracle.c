@@ -1147,3 +1147,199 @@ void or_tdt_decode_batch(const void* p, const float* pooler, const int32_t* cu, 
         counts[i] = or_tdt_decode(p, pooler + (size_t)cu[i] * DEC_H, cu[i + 1] - cu[i],
                                   tokens + (size_t)i * max_tokens * 3, max_tokens);
 }
+
+/* ───────────────────────────── front end ─────────────────────────────
+ * Mel features (MelFrontend::compute, src/mel.rs:41-138) and the conv
+ * subsampling (subsample, src/sub.rs:107-300), restated for parity tests
+ * and the end-to-end CPU baseline. */
+
+#define MEL_BINS 128
+#define N_FFT 512
+#define HOP 160
+#define WIN 400
+
+/* In-place radix-2 complex FFT of size 512 (double precision). */
+static void fft512(double* re, double* im) {
+    for (int i = 1, j = 0; i < N_FFT; i++) {
+        int bit = N_FFT >> 1;
+        for (; j & bit; bit >>= 1) j ^= bit;
+        j ^= bit;
+        if (i < j) {
+            double t = re[i]; re[i] = re[j]; re[j] = t;
+            t = im[i]; im[i] = im[j]; im[j] = t;
+        }
+    }
+    for (int len = 2; len <= N_FFT; len <<= 1) {
+        double ang = -2.0 * M_PI / len;
+        for (int i = 0; i < N_FFT; i += len)
+            for (int k = 0; k < len / 2; k++) {
+                double wr = cos(ang * k), wi = sin(ang * k);
+                double ur = re[i + k], ui = im[i + k];
+                double vr = re[i + k + len / 2] * wr - im[i + k + len / 2] * wi;
+                double vi = re[i + k + len / 2] * wi + im[i + k + len / 2] * wr;
+                re[i + k] = ur + vr; im[i + k] = ui + vi;
+                re[i + k + len / 2] = ur - vr; im[i + k + len / 2] = ui - vi;
+            }
+    }
+}
+
+/* wave: samples (the 0.25 s pad already prepended), fb: (128, 257) slaney
+ * filterbank.  out: (n_frames, 128) normalised log-mel, frames >= n_valid
+ * zero.  Returns n_frames; *n_valid_out = len / 160. */
+int or_mel(const float* wave_in, int64_t len, const float* fb, float* out, int* n_valid_out) {
+    float* wave = (float*)malloc((size_t)(len > 0 ? len : 1) * 4);
+    for (int64_t i = 0; i < len; i++) wave[i] = i == 0 ? wave_in[0] : wave_in[i] - 0.97f * wave_in[i - 1];
+    int n_frames = (int)(1 + len / HOP);
+    int n_valid = (int)(len / HOP);
+    float window[N_FFT] = {0};
+    for (int i = 0; i < WIN; i++)
+        window[(N_FFT - WIN) / 2 + i] = 0.5f * (1.0f - cosf(6.2831855f * (float)i / (float)(WIN - 1)));
+    float* mel = (float*)malloc((size_t)MEL_BINS * n_frames * 4);
+#pragma omp parallel for schedule(static) num_threads(g_threads)
+    for (int t = 0; t < n_frames; t++) {
+        double re[N_FFT], im[N_FFT];
+        int64_t start = (int64_t)t * HOP - N_FFT / 2;
+        for (int i = 0; i < N_FFT; i++) {
+            int64_t s = start + i;
+            re[i] = (s >= 0 && s < len) ? (double)(wave[s] * window[i]) : 0.0;
+            im[i] = 0.0;
+        }
+        fft512(re, im);
+        float power[257];
+        for (int k = 0; k < 257; k++) power[k] = (float)(re[k] * re[k] + im[k] * im[k]);
+        for (int m = 0; m < MEL_BINS; m++) {
+            const float* row = fb + m * 257;
+            float s = 0.0f;
+            for (int k = 0; k < 257; k++)
+                if (row[k] != 0.0f) s += row[k] * power[k];
+            mel[(size_t)m * n_frames + t] = logf(s + 5.9604645e-08f);
+        }
+    }
+    int nv = n_valid > 1 ? n_valid : 1;
+    for (int m = 0; m < MEL_BINS; m++) {
+        float s = 0.0f;
+        for (int t = 0; t < n_valid; t++) s += mel[(size_t)m * n_frames + t];
+        float mean = s / (float)nv;
+        float q = 0.0f;
+        for (int t = 0; t < n_valid; t++) {
+            float d = mel[(size_t)m * n_frames + t] - mean;
+            q += d * d;
+        }
+        float sd = sqrtf(q / (float)(nv - 1 > 1 ? nv - 1 : 1) + 0.0f);
+        for (int t = 0; t < n_frames; t++)
+            out[(size_t)t * MEL_BINS + m] = t < n_valid ? (mel[(size_t)m * n_frames + t] - mean) / (sd + 1e-5f) : 0.0f;
+    }
+    free(mel);
+    free(wave);
+    if (n_valid_out) *n_valid_out = n_valid;
+    return n_frames;
+}
+
+static int conv_len(int l) { return (l + 2 - 3) / 2 + 1; }
+
+static void mask_time(float* x, int ch, int t, int m, int vlen) {
+    if (vlen >= t) return;
+    for (int c = 0; c < ch; c++)
+        for (int i = vlen; i < t; i++)
+            for (int j = 0; j < m; j++) x[((size_t)c * t + i) * m + j] = 0.0f;
+}
+
+/* depthwise 3x3 stride 2, padding 1 (src/sub.rs:173-201): s = b, then taps
+ * ki, kj ascending, unfused, out-of-range taps skipped. */
+static float* sub_dw(const float* x, const float* w, const float* b, int t_in, int m_in, int* t_out_p, int* m_out_p) {
+    int t_out = conv_len(t_in), m_out = conv_len(m_in);
+    float* out = (float*)malloc((size_t)256 * t_out * m_out * 4);
+#pragma omp parallel for schedule(static) num_threads(g_threads)
+    for (int c = 0; c < 256; c++)
+        for (int i = 0; i < t_out; i++)
+            for (int j = 0; j < m_out; j++) {
+                float s = b[c];
+                for (int ki = 0; ki < 3; ki++) {
+                    int ii = 2 * i + ki - 1;
+                    if (ii < 0 || ii >= t_in) continue;
+                    for (int kj = 0; kj < 3; kj++) {
+                        int jj = 2 * j + kj - 1;
+                        if (jj < 0 || jj >= m_in) continue;
+                        s += w[c * 9 + ki * 3 + kj] * x[((size_t)c * t_in + ii) * m_in + jj];
+                    }
+                }
+                out[((size_t)c * t_out + i) * m_out + j] = s;
+            }
+    *t_out_p = t_out;
+    *m_out_p = m_out;
+    return out;
+}
+
+/* pointwise 256 -> 256 (src/sub.rs:206-260): acc over ci ascending starting
+ * at 0 (zero weights skipped), then (acc + b).max(0). */
+static float* sub_pw(const float* x, const float* w, const float* b, int t, int m) {
+    size_t p = (size_t)t * m;
+    float* out = (float*)calloc((size_t)256 * p, 4);
+#pragma omp parallel for schedule(static) num_threads(g_threads)
+    for (int co = 0; co < 256; co++) {
+        float* o = out + (size_t)co * p;
+        for (int ci = 0; ci < 256; ci++) {
+            float wv = w[co * 256 + ci];
+            if (wv == 0.0f) continue;
+            const float* xr = x + (size_t)ci * p;
+            for (size_t q = 0; q < p; q++) o[q] += wv * xr[q];
+        }
+        for (size_t q = 0; q < p; q++) {
+            float v = o[q] + b[co];
+            o[q] = v > 0.0f ? v : 0.0f;
+        }
+    }
+    return out;
+}
+
+/* mel (f, 128) -> (T, 4096) with T = conv_len^3(f), row t = [c * 16 + m].
+ * w0/w2/w5: (256, 9); w3/w6: (256, 256); b*: (256).  Returns T. */
+int or_subsample(const float* mel, int f, int n_valid, const float* w0, const float* b0, const float* w2,
+                 const float* b2, const float* w3, const float* b3, const float* w5, const float* b5,
+                 const float* w6, const float* b6, float* out) {
+    const int m0 = MEL_BINS;
+    int f1 = conv_len(f), m1 = conv_len(m0);
+    size_t p = (size_t)f1 * m1;
+    float* x = (float*)malloc((size_t)256 * p * 4);
+    /* layer 0 (src/sub.rs:110-167): bias, taps t = ki*3 + kj in order, ReLU */
+#pragma omp parallel for schedule(static) num_threads(g_threads)
+    for (int co = 0; co < 256; co++)
+        for (int i = 0; i < f1; i++)
+            for (int j = 0; j < m1; j++) {
+                float s = b0[co];
+                for (int t = 0; t < 9; t++) {
+                    int ki = t / 3, kj = t % 3;
+                    int ii = 2 * i + ki, jj = 2 * j + kj;
+                    float v = 0.0f;
+                    if (ii > 0 && ii <= 2 * f && jj > 0 && jj <= 2 * m0) {
+                        int si = ii - 1, sj = jj - 1;
+                        if (si < f && sj < m0) v = mel[(size_t)si * m0 + sj];
+                    }
+                    s += w0[co * 9 + t] * v;
+                }
+                x[((size_t)co * f1 + i) * m1 + j] = s > 0.0f ? s : 0.0f;
+            }
+    int vlen = conv_len(n_valid > 1 ? n_valid : 1);
+    mask_time(x, 256, f1, m1, vlen < f1 ? vlen : f1);
+    int len, mlen;
+    float* x2 = sub_dw(x, w2, b2, f1, m1, &len, &mlen);
+    free(x);
+    vlen = conv_len(vlen);
+    mask_time(x2, 256, len, mlen, vlen < len ? vlen : len);
+    float* x3 = sub_pw(x2, w3, b3, len, mlen);
+    free(x2);
+    int len2, mlen2;
+    float* x4 = sub_dw(x3, w5, b5, len, mlen, &len2, &mlen2);
+    free(x3);
+    vlen = conv_len(vlen);
+    mask_time(x4, 256, len2, mlen2, vlen < len2 ? vlen : len2);
+    float* x5 = sub_pw(x4, w6, b6, len2, mlen2);
+    free(x4);
+    int t = len2;
+    for (int c = 0; c < 256; c++)
+        for (int i = 0; i < t; i++)
+            for (int j = 0; j < mlen2; j++)
+                out[(size_t)i * 256 * mlen2 + c * mlen2 + j] = x5[((size_t)c * t + i) * mlen2 + j];
+    free(x5);
+    return t;
+}

@@ -63,6 +63,8 @@ def lib() -> ctypes.CDLL:
             "or_tdt_free": (None, [_P]),
             "or_tdt_decode": (_I, [_P, _P, _I, _P, _I]),
             "or_tdt_decode_batch": (None, [_P, _P, _P, _I, _P, _P, _I]),
+            "or_mel": (_I, [_P, ctypes.c_int64, _P, _P, _P]),
+            "or_subsample": (_I, [_P, _I, _I] + [_P] * 11),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)
@@ -159,6 +161,35 @@ def dwconv_bn_silu(x, dw, bn_a, bn_b):
 def pos_embed(t: int) -> np.ndarray:
     out = np.empty((2 * t - 1, 1024), dtype=np.float32)
     lib().or_pos_embed(t, _p(out))
+    return out
+
+
+def mel(wave: np.ndarray, filters: np.ndarray):
+    """MelFrontend::compute restated: padded wave -> ((frames, 128), n_valid)."""
+    wave = f32(wave)
+    filters = f32(filters)
+    n_frames = 1 + len(wave) // 160
+    out = np.zeros((n_frames, 128), dtype=np.float32)
+    nv = ctypes.c_int()
+    lib().or_mel(_p(wave), len(wave), _p(filters), _p(out), ctypes.byref(nv))
+    return out, nv.value
+
+
+def subsample(mel_rows: np.ndarray, n_valid: int, w: dict) -> np.ndarray:
+    """subsample (src/sub.rs:107-300) restated: (frames, 128) -> (T, 4096)."""
+    mel_rows = f32(mel_rows)
+    f = mel_rows.shape[0]
+
+    def clen(v):
+        return (v - 1) // 2 + 1
+
+    t = clen(clen(clen(f)))
+    out = np.zeros((t, 4096), dtype=np.float32)
+    p = "encoder.subsampling.layers."
+    keep = [f32(w[p + n].reshape(-1)) for n in ("0.weight", "0.bias", "2.weight", "2.bias", "3.weight", "3.bias",
+                                                 "5.weight", "5.bias", "6.weight", "6.bias")]
+    got = lib().or_subsample(_p(mel_rows), f, n_valid, *[_p(a) for a in keep], _p(out))
+    assert got == t
     return out
 
 

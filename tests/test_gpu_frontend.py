@@ -1,0 +1,75 @@
+"""GPU mel front end, conv subsampling and audio -> tokens against the
+restated reference CPU pipeline (oracle).
+
+Tolerances: mel values are normalised log energies (~N(0, 1)); the GPU FFT is
+f32 (the reference's rustfft is f32 too) -> 5e-3 absolute.  Subsampling keeps
+f16 activations between the convs -> 1e-2 normwise.  Tokens: >= 99% match
+(1 - edit distance / reference tokens), the north-star criterion."""
+import numpy as np
+import pytest
+
+from conftest import rel_err
+from test_gpu_decoder import token_match
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module")
+def fe_model(syn, pkg):
+    w = syn.encoder_weights(seed=12, n_layers=2, layout="lut4")
+    w.update(syn.decoder_weights(seed=12, vocab=1025))
+    w.update(syn.frontend_weights(seed=12))
+    enc = pkg.Encoder(0)
+    enc.load(w)
+    enc.finalize(2)
+    yield w, enc
+    enc.close()
+
+
+def test_mel_matches_oracle(fe_model, syn, oracle, pkg):
+    w, enc = fe_model
+    rng = np.random.default_rng(1)
+    waves = [np.concatenate([np.zeros(4000, np.float32), syn.synth_audio(rng, s)]) for s in (0.0, 1.37, 10.0, 4.01)]
+    got = enc.mel(waves)
+    fb = pkg.mel_filters()
+    for g, wv in zip(got, waves):
+        want, _ = oracle.mel(wv, fb)
+        assert g.shape == want.shape
+        assert np.max(np.abs(g - want)) < 5e-3
+
+
+def test_subsample_matches_oracle(fe_model, syn, oracle):
+    w, enc = fe_model
+    rng = np.random.default_rng(2)
+    shapes = [(1, 0), (26, 25), (301, 300), (1001, 1000)]
+    mels = []
+    for f, nv in shapes:
+        m = rng.normal(size=(f, 128)).astype(np.float32)
+        m[nv:] = 0
+        mels.append(m)
+    got = enc.subsample(mels, [nv for _, nv in shapes])
+    for g, m, (f, nv) in zip(got, mels, shapes):
+        want = oracle.subsample(m, nv, w)
+        assert g.shape == want.shape
+        e = rel_err(g, want)
+        print(f"subsample frames={f}: err {e:.2e}")
+        assert e < 1e-2
+
+
+def test_audio_to_tokens(fe_model, syn, oracle, pkg):
+    """transcribe_samples end to end (pad, mel, subsampling, encoder, greedy
+    TDT) against the oracle pipeline on the same audio."""
+    w, enc = fe_model
+    rng = np.random.default_rng(3)
+    waves = [syn.synth_audio(rng, s) for s in (2.0, 7.5, 0.3)]
+    got = enc.transcribe_audio(waves)
+    fb = pkg.mel_filters()
+    oenc = oracle.OracleEncoder(w, 2)
+    odec = oracle.OracleTdt(w)
+    want = []
+    for wv in waves:
+        mel, nv = oracle.mel(np.concatenate([np.zeros(4000, np.float32), wv]), fb)
+        want.append(odec.decode(oenc.encode(oracle.subsample(mel, nv, w))))
+    m, exact = token_match(got, want)
+    print(f"audio -> tokens match {m:.4f}, identical streams {exact:.2f}, tokens {sum(len(x) for x in want)}")
+    assert m >= 0.99
