@@ -38,7 +38,7 @@ sys.path.insert(0, str(ROOT))
 from __graft_entry__ import load_oracle, load_package  # noqa: E402
 
 N_LAYERS = 24
-METRIC = "RTFx (audio-s/s), batched transcription (4-bit encoder + greedy TDT)"
+METRIC = "RTFx (audio-s/s), batched transcription"
 VOCAB = 1025        # 1024 tokens + blank
 MAX_TOKENS = 1024   # token slots per utterance in the output buffer
 
@@ -55,9 +55,10 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=5)
-    ap.add_argument("--workload", default="transcribe", choices=["transcribe", "encoder", "linear"],
-                    help="transcribe: encoder + TDT decoder over the config-5 batch; encoder: the encoder "
-                         "alone; linear: K1 GEMM shape sweep (config 1)")
+    ap.add_argument("--workload", default="audio", choices=["audio", "transcribe", "encoder", "linear"],
+                    help="audio: 16 kHz audio -> tokens (mel, subsampling, encoder, greedy TDT) over the "
+                         "config-5 batch; transcribe: the same from subsampled features; encoder: the "
+                         "encoder alone; linear: K1 GEMM shape sweep (config 1)")
     return ap.parse_args()
 
 
@@ -115,7 +116,7 @@ def pkg_kind(name):
     return KINDS.index(name)
 
 
-KINDS = ["gemm_lut4", "gemm_f16", "attention", "layernorm", "dwconv", "convert", "other", "decoder"]
+KINDS = ["gemm_lut4", "gemm_f16", "attention", "layernorm", "dwconv", "convert", "other", "decoder", "frontend"]
 
 
 def peaks():
@@ -188,26 +189,53 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(loaded)}
 
 
-def cpu_baseline_sample(oracle, syn, weights, secs, frames, budget_s, seed, decode):
-    """The oracle (restated reference CPU encoder and TDT decoder, all host
-    cores) on the first utterances of the batch, in turn, until the time
-    budget is spent."""
+def make_cpu_pipeline(oracle, syn, pkg, weights, workload):
+    """The reference's CPU path restated (oracle): one utterance in, tokens
+    (or the pooler) out, every stage on all host cores."""
     enc = oracle.OracleEncoder(weights, N_LAYERS)
-    dec = oracle.OracleTdt(weights) if decode else None
+    dec = oracle.OracleTdt(weights) if workload in ("audio", "transcribe") else None
+    fb = pkg.mel_filters() if workload == "audio" else None
+
+    def run(x):
+        if workload == "audio":
+            mel, nv = oracle.mel(np.concatenate([np.zeros(4000, np.float32), x]), fb)
+            x = oracle.subsample(mel, nv, weights)
+        pooled = enc.encode(x)
+        if dec is not None:
+            dec.decode(pooled)
+
+    return run
+
+
+def cpu_input(syn, rng, workload, secs, frames):
+    return syn.synth_audio(rng, secs) if workload == "audio" else syn.sub_features(rng, frames)
+
+
+def cpu_baseline_sample(oracle, syn, pkg, weights, secs, frames, budget_s, seed, workload):
+    """The oracle (restated reference CPU pipeline, all host cores) on the
+    first utterances of the batch, in turn, until the time budget is spent."""
+    run = make_cpu_pipeline(oracle, syn, pkg, weights, workload)
     rng = np.random.default_rng(seed)
     done_audio, used, n = 0.0, 0.0, 0
     for s, t in zip(secs, frames):
-        sub = syn.sub_features(rng, t)
+        x = cpu_input(syn, rng, workload, s, t)
         t0 = time.perf_counter()
-        pooled = enc.encode(sub)
-        if dec is not None:
-            dec.decode(pooled)
+        run(x)
         used += time.perf_counter() - t0
         done_audio += s
         n += 1
         if used >= budget_s:
             break
     return done_audio / used, n, done_audio, used
+
+
+def make_weights(args, syn):
+    weights = syn.encoder_weights(seed=args.seed, n_layers=N_LAYERS, layout="lut4")
+    if args.workload in ("audio", "transcribe"):
+        weights.update(syn.decoder_weights(seed=args.seed, vocab=VOCAB))
+    if args.workload == "audio":
+        weights.update(syn.frontend_weights(seed=args.seed))
+    return weights
 
 
 def run_reference(args, rank, world):
@@ -219,19 +247,11 @@ def run_reference(args, rank, world):
     import bark3_b200.synthetic as syn
     oracle = load_oracle()
     secs, frames = batch_for_rank(args, 0, 1, pkg, syn)
-    weights = syn.encoder_weights(seed=args.seed, n_layers=N_LAYERS, layout="lut4")
-    decode = args.workload == "transcribe"
-    if decode:
-        weights.update(syn.decoder_weights(seed=args.seed, vocab=VOCAB))
-    enc = oracle.OracleEncoder(weights, N_LAYERS)
-    dec = oracle.OracleTdt(weights) if decode else None
+    weights = make_weights(args, syn)
+    one = make_cpu_pipeline(oracle, syn, pkg, weights, args.workload)
     rng = np.random.default_rng(args.seed)
-    subs = [syn.sub_features(rng, t) for t in frames[: max(1, min(len(frames), 4))]]
-
-    def one(sub):
-        pooled = enc.encode(sub)
-        if dec is not None:
-            dec.decode(pooled)
+    k = max(1, min(len(frames), 4))
+    subs = [cpu_input(syn, rng, args.workload, secs[i], frames[i]) for i in range(k)]
 
     for w in range(args.warmup):
         one(subs[w % len(subs)])
@@ -249,13 +269,14 @@ def run_reference(args, rank, world):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * wall / args.steps, 3),
         "higher_is_better": True, "scaling": "weak" if not args.strong else "strong", "vs_baseline": None,
         "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "reference CPU path (src/cpu/* encoder" + (" + src/tdt.rs greedy TDT" if decode else "")
+        "config": {"workload": "reference CPU path (" + {"audio": "src/mel.rs + src/sub.rs + src/cpu/* encoder + "
+                   "src/tdt.rs greedy TDT", "transcribe": "src/cpu/* encoder + src/tdt.rs greedy TDT",
+                   "encoder": "src/cpu/* encoder"}[args.workload]
                    + ", restated in C, AVX2/F16C FMA), one utterance of the config-5 batch per step",
                    "utterances_sampled": len(subs),
                    "frames": frames[: len(subs)], "layers": N_LAYERS, "weights": "random-init 4-bit LUT"},
         "cpu_baseline": {"value": round(v, 3), "unit": "audio-s/s", "cores": cores, "kind": "port",
-                         "sample": f"{args.steps} utterances (cycling {frames[:len(subs)]} frames), "
-                                   + ("encode + decode" if decode else "encode")},
+                         "sample": f"{args.steps} utterances (cycling {frames[:len(subs)]} frames), {args.workload}"},
         "e2e": {"value": round(v, 3), "unit": "audio-s/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -290,20 +311,28 @@ def main():
     cu = np.concatenate([[0], np.cumsum(frames)]).astype(np.int32)
     audio = float(sum(secs))
 
-    decode = args.workload == "transcribe"
-    weights = syn.encoder_weights(seed=args.seed, n_layers=N_LAYERS, layout="lut4")
-    if decode:
-        weights.update(syn.decoder_weights(seed=args.seed, vocab=VOCAB))
+    decode = args.workload in ("audio", "transcribe")
+    audio_in = args.workload == "audio"
+    weights = make_weights(args, syn)
     enc = pkg.Encoder(local)
     enc.load(weights)
     enc.finalize(N_LAYERS)
 
     # inputs: pinned host copy (e2e) and device-resident copy (value)
     rng = np.random.default_rng(args.seed + 17 * rank)
-    host_in = torch.empty((M, 4096), dtype=torch.float32, pin_memory=True)
-    hv = host_in.numpy()
-    for i in range(len(frames)):
-        hv[cu[i]:cu[i + 1]] = syn.sub_features(rng, frames[i])
+    if audio_in:
+        waves = [syn.synth_audio(rng, s) for s in secs]
+        soff = np.concatenate([[0], np.cumsum([len(x) for x in waves])]).astype(np.int64)
+        host_in = torch.empty((int(soff[-1]),), dtype=torch.float32, pin_memory=True)
+        hv = host_in.numpy()
+        for i, x in enumerate(waves):
+            hv[soff[i]:soff[i + 1]] = x
+        del waves
+    else:
+        host_in = torch.empty((M, 4096), dtype=torch.float32, pin_memory=True)
+        hv = host_in.numpy()
+        for i in range(len(frames)):
+            hv[cu[i]:cu[i + 1]] = syn.sub_features(rng, frames[i])
     host_out = torch.empty((M, 640), dtype=torch.float32, pin_memory=True)
     dev_in = host_in.cuda()
     dev_out = torch.empty((M, 640), dtype=torch.float32, device="cuda")
@@ -317,14 +346,20 @@ def main():
     L = pkg.lib()
 
     def step_device():
-        if decode:
+        if audio_in:
+            pkg.check(L.b3_transcribe_audio(enc.ctx, dev_in.data_ptr(), soff.ctypes.data, n_utt, dev_tok.data_ptr(),
+                                            dev_cnt.data_ptr(), MAX_TOKENS, pkg.B3_DEVICE_PTRS))
+        elif decode:
             pkg.check(L.b3_transcribe_batch(enc.ctx, dev_in.data_ptr(), cu.ctypes.data, n_utt, dev_tok.data_ptr(),
                                             dev_cnt.data_ptr(), MAX_TOKENS, pkg.B3_DEVICE_PTRS))
         else:
             enc.encode_batch(dev_in, cu, out=dev_out)
 
     def step_host(hin, hout):
-        if decode:
+        if audio_in:
+            pkg.check(L.b3_transcribe_audio(enc.ctx, hin.ctypes.data, soff.ctypes.data, n_utt, host_tok.ctypes.data,
+                                            host_cnt.ctypes.data, MAX_TOKENS, 0))
+        elif decode:
             pkg.check(L.b3_transcribe_batch(enc.ctx, hin.ctypes.data, cu.ctypes.data, n_utt, host_tok.ctypes.data,
                                             host_cnt.ctypes.data, MAX_TOKENS, 0))
         else:
@@ -404,10 +439,11 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         oracle = load_oracle()
-        v, n, a_s, used = cpu_baseline_sample(oracle, syn, weights, secs, frames, args.cpu_seconds, args.seed, decode)
+        v, n, a_s, used = cpu_baseline_sample(oracle, syn, pkg, weights, secs, frames, args.cpu_seconds, args.seed,
+                                              args.workload)
         cpu = {"value": round(v, 3), "unit": "audio-s/s", "cores": oracle.threads(), "kind": "port",
                "sample": f"first {n} utterances of the batch ({a_s:.1f} audio-s, {used:.1f} s wall), "
-                         + ("encoder + decoder" if decode else "encoder") + ", in turn"}
+                         + args.workload + " pipeline, in turn"}
 
     if rank == 0:
         line = {
@@ -415,16 +451,19 @@ def main():
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3),
             "higher_is_better": True, "scaling": "strong" if args.strong else "weak", "vs_baseline": None,
             "dtype": "f16", "data": "synthetic",
-            "config": {"workload": ("config-5 batch: 24-block 4-bit LUT encoder + batched greedy TDT decoder"
-                                    if decode else "config-5 batch through the 24-block 4-bit LUT encoder"),
+            "config": {"workload": {"audio": "config 5: batched transcription, 16 kHz audio -> tokens (mel, conv "
+                                             "subsampling, 24-block 4-bit LUT encoder, greedy TDT)",
+                                    "transcribe": "config-5 batch from subsampled features: 4-bit encoder + greedy TDT",
+                                    "encoder": "config-5 batch through the 24-block 4-bit LUT encoder"}[args.workload],
                        "utterances_per_rank": len(frames), "audio_s_per_rank": round(audio, 1),
                        "frames_per_rank": M, "lengths_s": "U(10,60) seeded", "layers": N_LAYERS,
                        "d_model": 1024, "heads": 8, "ffn": 4096, "conv_kernel": 9,
                        "weights": "random-init 4-bit codes + 16-entry f16 LUT per row",
-                       "input": "synthetic (T,4096) subsampled features, f32",
+                       "input": ("synthetic audio: white noise U(-0.1,0.1) + 3 sines of amplitude 0.1, "
+                                 "16 kHz f32" if audio_in else "synthetic (T,4096) subsampled features, f32"),
                        "decoder": (f"2-layer LSTM 640, joint 640, vocab {VOCAB - 1}+blank, durations 0..4, "
                                    "random-init" if decode else None),
-                       "l2": "inputs (%.2f GB) > L2, no flush" % (M * 4096 * 4 / 1e9),
+                       "l2": "per-step working set (%.2f GB of encoder activations) > L2, no flush" % (M * 4096 * 2 * 3 / 1e9),
                        "parallelism": f"utterance-sharded x{world}, no collective"},
             "roofline": {"kernel": "k1_gemm (LUT4, tcgen05)", "bound": "tensor",
                          "achieved": round(achieved, 1) if achieved else None,
@@ -440,7 +479,7 @@ def main():
             "gpu_launches": launches,
             "clocks": clocks,
             "e2e": {"value": round(e2e_value, 2), "unit": "audio-s/s",
-                    "h2d_bytes_per_step": int(M * 4096 * 4),
+                    "h2d_bytes_per_step": int(host_in.numel() * 4),
                     "d2h_bytes_per_step": int(n_utt * (MAX_TOKENS * 12 + 4)) if decode else int(M * 640 * 4)},
             "cpu_baseline": cpu,
         }
