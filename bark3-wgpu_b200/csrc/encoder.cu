@@ -144,6 +144,13 @@ struct Plan {
     int M = 0, tmax = 0, n_work = 0;
 };
 
+// Frame bookkeeping of a front-end batch: frame / depthwise-1 / encoder row
+// offsets per utterance and the subsampling CTA work list.
+struct FeShape {
+    std::vector<int32_t> foff, nvalid, x2off, x4off;
+    std::vector<int4> work;
+};
+
 // Per-kernel-class CUDA-event timing (the analogue of the reference's
 // BARK3_ENC_PROFILE timestamp queries, src/encoder/prof.rs:1-121).  Launch
 // counts are always kept; events are recorded only while enabled.
@@ -210,6 +217,9 @@ struct b3_ctx {
         DevBuf pw_bias;       // [2][256] f32
         Linear sub_w_perm;    // encoder subsampling linear, input columns in (freq, channel) order
         DevBuf wave, wave_off, frame_off, mel, x2, x3, x4, ints, work;
+        std::vector<int32_t> sub_key;   // batch shape whose tables are on the device
+        std::vector<int64_t> mel_key;   // padded wave offsets of the cached shape
+        FeShape mel_shape;
     } fe;
     ~b3_ctx() {
         for (Linear* l : {&fe.pw1, &fe.pw2, &fe.sub_w_perm}) {
@@ -1045,12 +1055,6 @@ int build_frontend(b3_ctx* c) {
     return 0;
 }
 
-// Frame bookkeeping of a batch of padded waves.
-struct FeShape {
-    std::vector<int32_t> foff, nvalid, x2off, x4off;
-    std::vector<int4> work;
-};
-
 void fe_shape_from_frames(FeShape& s, const std::vector<int32_t>& frames, const std::vector<int32_t>& nvalid) {
     const int n = static_cast<int>(frames.size());
     s.foff.assign(n + 1, 0);
@@ -1080,13 +1084,21 @@ int fe_subsample(b3_ctx* c, const FeShape& s) {
     B3_TRY(F.x2.ensure(static_cast<size_t>(rows2) * 32 * 256 * 2 + 16));
     B3_TRY(F.x3.ensure(static_cast<size_t>(rows2) * 32 * 256 * 2 + 16));
     B3_TRY(F.x4.ensure(static_cast<size_t>(T) * 16 * 256 * 2 + 16));
-    B3_TRY(F.ints.ensure((3 * n + 2) * sizeof(int32_t)));
-    B3_TRY(F.work.ensure(s.work.size() * sizeof(int4) + 16));
-    int32_t* ints = F.ints.as<int32_t>();
-    B3_CUDA(cudaMemcpyAsync(ints, s.nvalid.data(), n * 4, cudaMemcpyHostToDevice, c->stream));
-    B3_CUDA(cudaMemcpyAsync(ints + n, s.x2off.data(), (n + 1) * 4, cudaMemcpyHostToDevice, c->stream));
-    B3_CUDA(cudaMemcpyAsync(ints + 2 * n + 1, s.x4off.data(), (n + 1) * 4, cudaMemcpyHostToDevice, c->stream));
-    B3_CUDA(cudaMemcpyAsync(F.work.p, s.work.data(), s.work.size() * sizeof(int4), cudaMemcpyHostToDevice, c->stream));
+    // the per-batch tables go up once per batch shape
+    std::vector<int32_t> key(s.foff);
+    key.insert(key.end(), s.nvalid.begin(), s.nvalid.end());
+    int32_t* ints = nullptr;
+    if (key != F.sub_key) {
+        B3_TRY(F.ints.ensure((3 * n + 2) * sizeof(int32_t)));
+        B3_TRY(F.work.ensure(s.work.size() * sizeof(int4) + 16));
+        ints = F.ints.as<int32_t>();
+        B3_CUDA(cudaMemcpyAsync(ints, s.nvalid.data(), n * 4, cudaMemcpyHostToDevice, c->stream));
+        B3_CUDA(cudaMemcpyAsync(ints + n, s.x2off.data(), (n + 1) * 4, cudaMemcpyHostToDevice, c->stream));
+        B3_CUDA(cudaMemcpyAsync(ints + 2 * n + 1, s.x4off.data(), (n + 1) * 4, cudaMemcpyHostToDevice, c->stream));
+        B3_CUDA(cudaMemcpyAsync(F.work.p, s.work.data(), s.work.size() * sizeof(int4), cudaMemcpyHostToDevice, c->stream));
+        F.sub_key = key;
+    }
+    ints = F.ints.as<int32_t>();
     SubParams sp;
     sp.n_utt = n;
     sp.mel = F.mel.as<float>();
@@ -1125,20 +1137,26 @@ int fe_subsample(b3_ctx* c, const FeShape& s) {
 int fe_mel(b3_ctx* c, const float* wave, const std::vector<int64_t>& woff, FeShape& s) {
     auto& F = c->fe;
     const int n = static_cast<int>(woff.size()) - 1;
-    std::vector<int32_t> frames(n), nvalid(n);
-    for (int u = 0; u < n; ++u) {
-        const int64_t len = woff[u + 1] - woff[u];
-        if (len < 0) return set_error(B3_EINVAL, "sample offsets must be non-decreasing");
-        frames[u] = static_cast<int32_t>(1 + len / 160);
-        nvalid[u] = static_cast<int32_t>(len / 160);
+    if (woff == F.mel_key) {
+        s = F.mel_shape;  // same batch shape as the previous call: tables are on the device
+    } else {
+        std::vector<int32_t> frames(n), nvalid(n);
+        for (int u = 0; u < n; ++u) {
+            const int64_t len = woff[u + 1] - woff[u];
+            if (len < 0) return set_error(B3_EINVAL, "sample offsets must be non-decreasing");
+            frames[u] = static_cast<int32_t>(1 + len / 160);
+            nvalid[u] = static_cast<int32_t>(len / 160);
+        }
+        fe_shape_from_frames(s, frames, nvalid);
+        B3_TRY(F.wave_off.ensure((n + 1) * 8));
+        B3_TRY(F.frame_off.ensure((n + 1) * 4));
+        B3_TRY(F.mel.ensure(static_cast<size_t>(s.foff[n]) * 128 * 4 + 16));
+        B3_CUDA(cudaMemcpyAsync(F.wave_off.p, woff.data(), (n + 1) * 8, cudaMemcpyHostToDevice, c->stream));
+        B3_CUDA(cudaMemcpyAsync(F.frame_off.p, s.foff.data(), (n + 1) * 4, cudaMemcpyHostToDevice, c->stream));
+        F.mel_key = woff;
+        F.mel_shape = s;
     }
-    fe_shape_from_frames(s, frames, nvalid);
     const int nf = s.foff[n];
-    B3_TRY(F.wave_off.ensure((n + 1) * 8));
-    B3_TRY(F.frame_off.ensure((n + 1) * 4));
-    B3_TRY(F.mel.ensure(static_cast<size_t>(nf) * 128 * 4 + 16));
-    B3_CUDA(cudaMemcpyAsync(F.wave_off.p, woff.data(), (n + 1) * 8, cudaMemcpyHostToDevice, c->stream));
-    B3_CUDA(cudaMemcpyAsync(F.frame_off.p, s.foff.data(), (n + 1) * 4, cudaMemcpyHostToDevice, c->stream));
     const float* t = F.tables.as<float>();
     MelParams mp;
     mp.n_utt = n;
@@ -1517,6 +1535,7 @@ int b3_subsample(b3_ctx* ctx, const float* mel, const int32_t* frame_offsets, co
     FeShape s;
     fe_shape_from_frames(s, frames, nv);
     auto& F = ctx->fe;
+    F.mel_key.clear();  // frame_off is rewritten below: the cached mel shape is stale
     const int nf = s.foff[n_utt];
     B3_TRY(F.frame_off.ensure((n_utt + 1) * 4));
     B3_TRY(F.mel.ensure(static_cast<size_t>(nf) * 128 * 4 + 16));
