@@ -39,6 +39,13 @@ struct GemmParams {
     const uint16_t* lut;      // [N][16] f16 bits (LUT4 weights)
     float* out_f32;
     __half* out_f16;
+    // split-K (EPI_F32 only): the K range is cut into ksplit equal parts and
+    // part s writes its partial sums to rows
+    // [s * gemm_split_rows(M), s * gemm_split_rows(M) + M) of out_f32 (the
+    // bias goes into part 0 only); the consumer adds the parts in order.
+    // 0 or 1 = no split.
+    int ksplit;
+    int tiles;                // 0 = by size, 1 = 128 x 64 tiles, 2 = 256 x 128 tiles
 };
 
 struct GemmOp {
@@ -57,6 +64,11 @@ int gemm_make_a_map(CUtensorMap* map, const __half* a, int M, int K, int lda);
 int gemm_make_b_map(CUtensorMap* map, const void* w, bool lut, int N, int K);
 int gemm_validate(const GemmParams& p, bool lut);
 int gemm_launch(const GemmOp& op, cudaStream_t st);
+// Rows of one split-K part in the output (M rounded up to the 256-row tile).
+__host__ __device__ inline int gemm_split_rows(int M) { return (M + 255) / 256 * 256; }
+// Split-K plan for a small-M GEMM: tile shape (1 = 128 x 64, 2 = 256 x 128)
+// and number of K parts that keep every SM busy with the fewest bytes each.
+void gemm_plan_split(int M, int N, int K, bool lut, int num_sms, int max_parts, int* tiles, int* ksplit);
 int gemm_take_dev_error(cudaStream_t st, unsigned int* out);
 
 }  // namespace b3

@@ -41,21 +41,26 @@ struct DecState {
     int B, vocab, blank, max_tokens;
     const int* cu;           // device cu_seqlens [B + 1]
     const float* pooler;     // [total][640]
-    const __half* emb_hi;    // [vocab][640]
-    const __half* emb_lo;
-    __half* a0;              // [B][2560] x_hi | x_lo | h0_hi | h0_lo  (LSTM layer 0 input)
+    const float* e0;         // [vocab][2560] W_ih0 . emb(token) + b_ih0 + b_hh0
+    int* tok;                // [B] last emitted token (blank before the first)
+    __half* a0;              // [B][1280] h0_hi | h0_lo                 (LSTM layer 0 input)
     __half* a1;              // [B][2560] h0_hi | h0_lo | h1_hi | h1_lo (layer 1 input)
     __half* ap;              // [B][1280] h1_hi | h1_lo                 (projector input)
     __half* aj;              // [B][1280] joint input hi | lo
-    float* gates;            // [B][2560]
+    // split-K GEMM outputs: part p of a GEMM with output [B][n] sits at
+    // rows [p * prow, p * prow + B); the consumer adds the parts in order
+    float* gates;            // layer gates, n = 2560
+    float* dec;              // projector output, n = 640
+    float* scores;           // joint head, n = ld_scores
     float* c;                // [B][2][640]
-    float* dec;              // [B][640]
-    float* scores;           // [B][ld_scores]
+    int prow;                // rows per part
+    int ks_g0, ks_g1, ks_p, ks_h;  // parts of the layer 0 / layer 1 / projector / head GEMMs
     int ld_scores;
     int *frame, *count, *guard, *emit, *active;
     uint32_t* tokens;        // [B][max_tokens][3] (id, frame, duration)
 };
 
+int dec_max_parts();   // most split-K parts the decoder kernels add
 int dec_launch_init(const DecState& s, cudaStream_t st);
 int dec_launch_joint_in(const DecState& s, cudaStream_t st);
 int dec_launch_argmax(const DecState& s, cudaStream_t st);

@@ -196,12 +196,11 @@ struct b3_ctx {
     struct Decoder {
         bool present = false;
         int vocab = 0, npad = 0;
-        DevBuf emb_hi, emb_lo;                 // [vocab][640] f16 hi | lo of the f32 embedding
-        Linear lstm[2];                        // [2560][2560] = W_ih | W_ih | W_hh | W_hh
+        DevBuf e0;                             // [vocab][2560] f32: W_ih0 . emb + b_ih0 + b_hh0
+        Linear lstm[2];                        // layer 0 [2560][1280] = W_hh | W_hh; layer 1 [2560][2560] = W_ih | W_ih | W_hh | W_hh
         Linear proj;                           // [640][1280]  = W_p | W_p
         Linear head;                           // [npad][1280] = W_head | W_head (zero rows past vocab+5)
-        DevBuf bias;                           // f32: lstm0 [2560] | lstm1 [2560] | proj [640] | head [npad]
-        int bcap = 0, tcap = 0;
+        DevBuf bias;                           // f32: lstm0 [2560] (unused) | lstm1 [2560] | proj [640] | head [npad]
         DevBuf a0, a1, ap, aj, gates, cstate, dec, scores, ints, tokens, cu, flag, pooler;
         cudaGraphExec_t chunk_exec = nullptr;  // captured decode chunk
         const void* chunk_key[6] = {};
@@ -235,7 +234,7 @@ struct b3_ctx {
             l->w.release();
             l->lut16.release();
         }
-        for (DevBuf* b : {&dec.emb_hi, &dec.emb_lo, &dec.bias, &dec.a0, &dec.a1, &dec.ap, &dec.aj, &dec.gates,
+        for (DevBuf* b : {&dec.e0, &dec.bias, &dec.a0, &dec.a1, &dec.ap, &dec.aj, &dec.gates,
                           &dec.cstate, &dec.dec, &dec.scores, &dec.ints, &dec.tokens, &dec.cu, &dec.flag, &dec.pooler})
             b->release();
         auto rel = [](Linear& l) { l.w.release(); l.lut16.release(); };
@@ -725,34 +724,62 @@ int build_decoder(b3_ctx* c) {
     const int H = 640, G = 2560;
     D.vocab = V;
     D.npad = (V + 5 + 127) / 128 * 128;
-    {
-        DevBuf tmp;
-        B3_TRY(upload(tmp, e->f32.data(), e->f32.size() * 4, c->stream));
-        B3_TRY(D.emb_hi.ensure(static_cast<size_t>(V) * H * 2));
-        B3_TRY(D.emb_lo.ensure(static_cast<size_t>(V) * H * 2));
-        B3_TRY(dec_launch_split(tmp.as<float>(), D.emb_hi.as<__half>(), D.emb_lo.as<__half>(),
-                                static_cast<int64_t>(V) * H, c->stream));
-        B3_CUDA(cudaStreamSynchronize(c->stream));
-        tmp.release();
-    }
     std::vector<float> bias(2 * G + H + D.npad, 0.f), v1, v2;
+    std::vector<float> bias0(G);
+    Linear wih0;   // [2560][1280] = W_ih0 | W_ih0, used once for the E0 table
     for (int l = 0; l < 2; ++l) {
         const std::string sl = std::to_string(l);
         const std::vector<uint16_t>*wih, *whh;
         B3_TRY(dec_matrix(c, "decoder.lstm.weight_ih_l" + sl, G, &wih));
         B3_TRY(dec_matrix(c, "decoder.lstm.weight_hh_l" + sl, G, &whh));
-        std::vector<uint16_t> w(static_cast<size_t>(G) * 4 * H);
+        const int parts = l == 0 ? 2 : 4;   // layer 0: W_hh | W_hh only
+        std::vector<uint16_t> w(static_cast<size_t>(G) * parts * H);
         for (int r = 0; r < G; ++r) {
-            uint16_t* dst = &w[static_cast<size_t>(r) * 4 * H];
-            memcpy(dst, &(*wih)[static_cast<size_t>(r) * H], H * 2);
-            memcpy(dst + H, &(*wih)[static_cast<size_t>(r) * H], H * 2);
-            memcpy(dst + 2 * H, &(*whh)[static_cast<size_t>(r) * H], H * 2);
-            memcpy(dst + 3 * H, &(*whh)[static_cast<size_t>(r) * H], H * 2);
+            uint16_t* dst = &w[static_cast<size_t>(r) * parts * H];
+            const uint16_t* src_ih = &(*wih)[static_cast<size_t>(r) * H];
+            const uint16_t* src_hh = &(*whh)[static_cast<size_t>(r) * H];
+            if (l == 1) {
+                memcpy(dst, src_ih, H * 2);
+                memcpy(dst + H, src_ih, H * 2);
+                dst += 2 * H;
+            }
+            memcpy(dst, src_hh, H * 2);
+            memcpy(dst + H, src_hh, H * 2);
         }
-        B3_TRY(build_dense(c, D.lstm[l], w, G, 4 * H));
+        B3_TRY(build_dense(c, D.lstm[l], w, G, parts * H));
+        if (l == 0) {
+            std::vector<uint16_t> wi(static_cast<size_t>(G) * 2 * H);
+            for (int r = 0; r < G; ++r) {
+                memcpy(&wi[static_cast<size_t>(r) * 2 * H], &(*wih)[static_cast<size_t>(r) * H], H * 2);
+                memcpy(&wi[static_cast<size_t>(r) * 2 * H + H], &(*wih)[static_cast<size_t>(r) * H], H * 2);
+            }
+            B3_TRY(build_dense(c, wih0, wi, G, 2 * H));
+        }
         B3_TRY(get_vec(c, "decoder.lstm.bias_ih_l" + sl, G, v1));
         B3_TRY(get_vec(c, "decoder.lstm.bias_hh_l" + sl, G, v2));
-        for (int r = 0; r < G; ++r) bias[l * G + r] = v1[r] + v2[r];
+        for (int r = 0; r < G; ++r) (l == 0 ? bias0[r] : bias[l * G + r]) = v1[r] + v2[r];
+    }
+    {
+        // E0 = [emb_hi | emb_lo] . [W_ih0 | W_ih0]^T + b0 on the tensor cores
+        DevBuf tmp, hl, b0;
+        B3_TRY(upload(tmp, e->f32.data(), e->f32.size() * 4, c->stream));
+        B3_TRY(upload(b0, bias0.data(), bias0.size() * 4, c->stream));
+        B3_TRY(hl.ensure(static_cast<size_t>(V) * 2 * H * 2));
+        __half* hi = hl.as<__half>();
+        DevBuf lo;
+        B3_TRY(lo.ensure(static_cast<size_t>(V) * H * 2));
+        B3_TRY(dec_launch_split(tmp.as<float>(), hi, lo.as<__half>(), static_cast<int64_t>(V) * H, c->stream));
+        // hi rows were written densely [V][640]: spread them to [V][1280] and put lo beside them
+        DevBuf packed;
+        B3_TRY(packed.ensure(static_cast<size_t>(V) * 2 * H * 2));
+        B3_CUDA(cudaMemcpy2DAsync(packed.p, 2 * H * 2, hi, H * 2, H * 2, V, cudaMemcpyDeviceToDevice, c->stream));
+        B3_CUDA(cudaMemcpy2DAsync(packed.as<__half>() + H, 2 * H * 2, lo.p, H * 2, H * 2, V, cudaMemcpyDeviceToDevice,
+                                  c->stream));
+        B3_TRY(D.e0.ensure(static_cast<size_t>(V) * G * 4));
+        B3_TRY(run_gemm(c, wih0, packed.as<__half>(), V, 2 * H, EPI_F32, params_f32(D.e0.as<float>(), G, b0.as<float>())));
+        B3_CUDA(cudaStreamSynchronize(c->stream));
+        wih0.w.release();
+        wih0.lut16.release();
     }
     auto doubled = [&](const std::vector<uint16_t>& src, int rows, int out_rows) {
         std::vector<uint16_t> w(static_cast<size_t>(out_rows) * 2 * H, 0);
@@ -778,42 +805,63 @@ int build_decoder(b3_ctx* c) {
     return 0;
 }
 
-int dec_ensure(b3_ctx* c, int B, int max_tokens) {
+// Split-K plans of the four decoder GEMMs for a batch of B rows.
+struct DecPlan {
+    int tiles[4], ks[4];   // layer 0, layer 1, projector, head
+};
+
+DecPlan dec_plan(b3_ctx* c, int B) {
     auto& D = c->dec;
-    if (B <= D.bcap && max_tokens <= D.tcap) return 0;
-    const size_t b = static_cast<size_t>(B > D.bcap ? B : D.bcap);
-    const size_t t = static_cast<size_t>(max_tokens > D.tcap ? max_tokens : D.tcap);
-    B3_TRY(D.a0.ensure(b * 2560 * 2));
+    int sms = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, c->device);
+    if (sms <= 0) sms = 148;
+    DecPlan pl;
+    const Linear* w[4] = {&D.lstm[0], &D.lstm[1], &D.proj, &D.head};
+    for (int i = 0; i < 4; ++i) gemm_plan_split(B, w[i]->N, w[i]->K, false, sms, dec_max_parts(), &pl.tiles[i], &pl.ks[i]);
+    return pl;
+}
+
+int dec_ensure(b3_ctx* c, int B, int max_tokens, const DecPlan& pl) {
+    auto& D = c->dec;
+    const size_t b = static_cast<size_t>(B);
+    const size_t prow = static_cast<size_t>(gemm_split_rows(B));
+    const int ksg = std::max(pl.ks[0], pl.ks[1]);
+    B3_TRY(D.a0.ensure(b * 1280 * 2));
     B3_TRY(D.a1.ensure(b * 2560 * 2));
     B3_TRY(D.ap.ensure(b * 1280 * 2));
     B3_TRY(D.aj.ensure(b * 1280 * 2));
-    B3_TRY(D.gates.ensure(b * 2560 * 4));
+    B3_TRY(D.gates.ensure(ksg * prow * 2560 * 4));
     B3_TRY(D.cstate.ensure(b * 2 * 640 * 4));
-    B3_TRY(D.dec.ensure(b * 640 * 4));
-    B3_TRY(D.scores.ensure(b * D.npad * 4));
-    B3_TRY(D.ints.ensure(b * 5 * 4));
-    B3_TRY(D.tokens.ensure(b * t * 12));
+    B3_TRY(D.dec.ensure(pl.ks[2] * prow * 640 * 4));
+    B3_TRY(D.scores.ensure(pl.ks[3] * prow * D.npad * 4));
+    B3_TRY(D.ints.ensure(b * 6 * 4));
+    B3_TRY(D.tokens.ensure(b * static_cast<size_t>(max_tokens) * 12));
     B3_TRY(D.cu.ensure((b + 1) * 4));
     B3_TRY(D.flag.ensure(16));
-    D.bcap = static_cast<int>(b);
-    D.tcap = static_cast<int>(t);
     return 0;
 }
 
-int dec_lstm_step(b3_ctx* c, const DecState& s) {
+GemmParams dec_params(float* out, int ldo, const float* bias, const DecPlan& pl, int i) {
+    GemmParams p = params_f32(out, ldo, bias);
+    p.ksplit = pl.ks[i];
+    p.tiles = pl.tiles[i];
+    return p;
+}
+
+int dec_lstm_step(b3_ctx* c, const DecState& s, const DecPlan& pl) {
     auto& D = c->dec;
     const float* bias = D.bias.as<float>();
-    B3_TRY(run_gemm(c, D.lstm[0], s.a0, s.B, 2560, EPI_F32, params_f32(s.gates, 2560, bias)));
+    B3_TRY(run_gemm(c, D.lstm[0], s.a0, s.B, 1280, EPI_F32, dec_params(s.gates, 2560, nullptr, pl, 0)));
     {
         ProfScope ps(c, B3_K_DECODER, 0.0, 0.0);
         B3_TRY(dec_launch_lstm_update(s, 0, c->stream));
     }
-    B3_TRY(run_gemm(c, D.lstm[1], s.a1, s.B, 2560, EPI_F32, params_f32(s.gates, 2560, bias + 2560)));
+    B3_TRY(run_gemm(c, D.lstm[1], s.a1, s.B, 2560, EPI_F32, dec_params(s.gates, 2560, bias + 2560, pl, 1)));
     {
         ProfScope ps(c, B3_K_DECODER, 0.0, 0.0);
         B3_TRY(dec_launch_lstm_update(s, 1, c->stream));
     }
-    return run_gemm(c, D.proj, s.ap, s.B, 1280, EPI_F32, params_f32(s.dec, 640, bias + 5120));
+    return run_gemm(c, D.proj, s.ap, s.B, 1280, EPI_F32, dec_params(s.dec, 640, bias + 5120, pl, 2));
 }
 
 // Greedy-decodes n_utt utterances of a device pooler [total][640]; the
@@ -828,7 +876,8 @@ int decode_device(b3_ctx* c, const float* pooler, const int32_t* cu, int n_utt, 
         if (t < 0) return set_error(B3_EINVAL, "cu_seqlens must be non-decreasing");
         if (t > tmax) tmax = t;
     }
-    B3_TRY(dec_ensure(c, n_utt, max_tokens));
+    const DecPlan pl = dec_plan(c, n_utt);
+    B3_TRY(dec_ensure(c, n_utt, max_tokens, pl));
     B3_CUDA(cudaMemcpyAsync(D.cu.p, cu, (n_utt + 1) * sizeof(int32_t), cudaMemcpyHostToDevice, c->stream));
     DecState s;
     s.B = n_utt;
@@ -837,8 +886,7 @@ int decode_device(b3_ctx* c, const float* pooler, const int32_t* cu, int n_utt, 
     s.max_tokens = max_tokens;
     s.cu = D.cu.as<int>();
     s.pooler = pooler;
-    s.emb_hi = D.emb_hi.as<__half>();
-    s.emb_lo = D.emb_lo.as<__half>();
+    s.e0 = D.e0.as<float>();
     s.a0 = D.a0.as<__half>();
     s.a1 = D.a1.as<__half>();
     s.ap = D.ap.as<__half>();
@@ -848,18 +896,24 @@ int decode_device(b3_ctx* c, const float* pooler, const int32_t* cu, int n_utt, 
     s.dec = D.dec.as<float>();
     s.scores = D.scores.as<float>();
     s.ld_scores = D.npad;
+    s.prow = gemm_split_rows(n_utt);
+    s.ks_g0 = pl.ks[0];
+    s.ks_g1 = pl.ks[1];
+    s.ks_p = pl.ks[2];
+    s.ks_h = pl.ks[3];
     int* ints = D.ints.as<int>();
     s.frame = ints;
     s.count = ints + n_utt;
     s.guard = ints + 2 * n_utt;
     s.emit = ints + 3 * n_utt;
     s.active = ints + 4 * n_utt;
+    s.tok = ints + 5 * n_utt;
     s.tokens = D.tokens.as<uint32_t>();
     {
         ProfScope ps(c, B3_K_DECODER, 0.0, 0.0);
         B3_TRY(dec_launch_init(s, c->stream));
     }
-    B3_TRY(dec_lstm_step(c, s));
+    B3_TRY(dec_lstm_step(c, s, pl));
     const float* head_bias = D.bias.as<float>() + 5120 + 640;
     const long max_steps = static_cast<long>(tmax) * 14 + 64;
     // One chunk = kChunk lock steps + the "any row still active" reduction.
@@ -872,12 +926,12 @@ int decode_device(b3_ctx* c, const float* pooler, const int32_t* cu, int n_utt, 
                 ProfScope ps(c, B3_K_DECODER, 0.0, 0.0);
                 B3_TRY(dec_launch_joint_in(s, c->stream));
             }
-            B3_TRY(run_gemm(c, D.head, s.aj, s.B, 1280, EPI_F32, params_f32(s.scores, D.npad, head_bias)));
+            B3_TRY(run_gemm(c, D.head, s.aj, s.B, 1280, EPI_F32, dec_params(s.scores, D.npad, head_bias, pl, 3)));
             {
                 ProfScope ps(c, B3_K_DECODER, 0.0, 0.0);
                 B3_TRY(dec_launch_argmax(s, c->stream));
             }
-            B3_TRY(dec_lstm_step(c, s));
+            B3_TRY(dec_lstm_step(c, s, pl));
         }
         ProfScope ps(c, B3_K_DECODER, 0.0, 0.0);
         return dec_launch_any_active(s, D.flag.as<int>(), c->stream);
@@ -1455,10 +1509,13 @@ int b3_decode_batch(b3_ctx* ctx, const float* pooler, const int32_t* cu_seqlens,
     DeviceGuard g(ctx->device);
     const bool dev = flags & B3_DEVICE_PTRS;
     const float* p = pooler;
-    if (!dev) {
+    // the decoder reads pooler rows as float4: host buffers and unaligned
+    // device buffers go through the context's own copy
+    if (!dev || (reinterpret_cast<uintptr_t>(pooler) & 15)) {
         const size_t bytes = static_cast<size_t>(cu_seqlens[n_utt]) * 640 * 4;
         B3_TRY(ctx->dec.pooler.ensure(bytes > 0 ? bytes : 4));
-        B3_CUDA(cudaMemcpyAsync(ctx->dec.pooler.p, pooler, bytes, cudaMemcpyHostToDevice, ctx->stream));
+        B3_CUDA(cudaMemcpyAsync(ctx->dec.pooler.p, pooler, bytes, dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
+                                ctx->stream));
         p = ctx->dec.pooler.as<float>();
     }
     B3_TRY(decode_device(ctx, p, cu_seqlens, n_utt, max_tokens));

@@ -2,11 +2,12 @@
 // reference computes the mel on the CPU, src/mel.rs:41-138, and subsamples
 // on the CPU or with WGSL, src/sub.rs:107-300, src/sub_gpu.rs).
 //
-// Mel: one CTA per frame: pre-emphasis (0.97), 512-point centred frame with
-// the symmetric Hann(400) window, radix-2 complex FFT in shared memory (f32),
-// power of the 257 bins, 128 slaney mel bins (sparse rows), log(x + 2^-24).
-// Normalisation: one CTA per utterance, one thread per mel bin, mean and
-// sample std over the valid frames (frames >= len/160 zeroed).
+// Mel: one warp per frame: pre-emphasis (0.97), 512-point centred frame with
+// the symmetric Hann(400) window, a real 512-point FFT as a 256-point complex
+// FFT in shared memory (f32), power of the 257 bins, 128 slaney mel bins
+// (sparse rows), log(x + 2^-24).  Normalisation: one CTA per (utterance, 32
+// mel bins), mean and sample std over the valid frames (frames >= len/160
+// zeroed).
 //
 // Subsampling, channels-last in HBM ([time][freq][channel]):
 //   conv0 (1 -> 256, 3x3, stride 2, pad 1) + ReLU + time mask and the first
@@ -34,11 +35,27 @@ constexpr int kMel = 128;
 
 __device__ __forceinline__ int conv_len_d(int l) { return (l - 1) / 2 + 1; }
 
-// One frame per CTA (256 threads).  frame -> utterance by binary search in
-// the frame offsets.
-__global__ void __launch_bounds__(256) k_mel_frames(MelParams p) {
-    __shared__ float re[kNfft], im[kNfft], pw[257];
-    const int f = blockIdx.x;
+// One frame per warp, 8 frames per CTA.  The 512 real samples x[n] are
+// packed as 256 complex values z[m] = x[2m] + i x[2m+1]; a 256-point radix-2
+// FFT of z in shared memory (eight stages, __syncwarp between them) gives the
+// 512-point spectrum by the standard real-input split
+//   X[k] = (Z[k] + conj Z[256-k]) / 2 + W512^k (Z[k] - conj Z[256-k]) / 2i.
+constexpr int kMelWarps = 8;
+
+__device__ __forceinline__ float mel_sample(const float* x, int64_t len, int64_t s, float w) {
+    if (s < 0 || s >= len) return 0.f;
+    const float cur = __ldg(x + s);
+    return (s == 0 ? cur : cur - 0.97f * __ldg(x + s - 1)) * w;
+}
+
+__global__ void __launch_bounds__(256) k_mel_frames(MelParams p, int n_frames) {
+    __shared__ float zre[kMelWarps][256], zim[kMelWarps][256], pwr[kMelWarps][260];
+    __shared__ float2 tw[256];
+    tw[threadIdx.x] = p.twiddle[threadIdx.x];
+    __syncthreads();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int f = blockIdx.x * kMelWarps + warp;
+    if (f >= n_frames) return;
     int lo = 0, hi = p.n_utt;
     while (hi - lo > 1) {
         const int mid = (lo + hi) >> 1;
@@ -49,83 +66,132 @@ __global__ void __launch_bounds__(256) k_mel_frames(MelParams p) {
     const float* x = p.wave + p.wave_off[u];
     const int64_t len = p.wave_off[u + 1] - p.wave_off[u];
     const int64_t start = static_cast<int64_t>(t) * kHop - kNfft / 2;
-    for (int i = threadIdx.x; i < kNfft; i += blockDim.x) {
-        const int64_t s = start + i;
-        float v = 0.f;
-        if (s >= 0 && s < len) {
-            const float cur = x[s];
-            v = (s == 0 ? cur : cur - 0.97f * x[s - 1]) * p.window[i];
+    float* re = zre[warp];
+    float* im = zim[warp];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+        const int m = lane + 32 * q;
+        const int r = __brev(m) >> 24;  // 8-bit reversal
+        re[r] = mel_sample(x, len, start + 2 * m, __ldg(p.window + 2 * m));
+        im[r] = mel_sample(x, len, start + 2 * m + 1, __ldg(p.window + 2 * m + 1));
+    }
+    __syncwarp();
+#pragma unroll
+    for (int lh = 0; lh < 8; ++lh) {
+        const int half = 1 << lh;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const int b = lane + 32 * q;
+            const int k = b & (half - 1);
+            const int i0 = ((b - k) << 1) + k, i1 = i0 + half;
+            const float2 w = tw[k << (8 - lh)];  // W256^(k * 128 / half) = W512^(k * 256 / half)
+            const float vr = re[i1] * w.x - im[i1] * w.y;
+            const float vi = re[i1] * w.y + im[i1] * w.x;
+            const float ur = re[i0], ui = im[i0];
+            re[i0] = ur + vr;
+            im[i0] = ui + vi;
+            re[i1] = ur - vr;
+            im[i1] = ui - vi;
         }
-        const int r = __brev(i) >> (32 - 9);  // bit-reversed position
-        re[r] = v;
-        im[r] = 0.f;
+        __syncwarp();
     }
-    __syncthreads();
-    for (int half = 1; half < kNfft; half <<= 1) {
-        const int b = threadIdx.x;  // 256 butterflies per stage
-        const int grp = b / half, k = b % half;
-        const int i0 = grp * 2 * half + k, i1 = i0 + half;
-        const float2 w = p.twiddle[k * (kNfft / (2 * half))];  // exp(-2 pi i k / (2 half))
-        const float vr = re[i1] * w.x - im[i1] * w.y;
-        const float vi = re[i1] * w.y + im[i1] * w.x;
-        const float ur = re[i0], ui = im[i0];
-        re[i0] = ur + vr;
-        im[i0] = ui + vi;
-        re[i1] = ur - vr;
-        im[i1] = ui - vi;
-        __syncthreads();
+    float* pw = pwr[warp];
+#pragma unroll
+    for (int q = 0; q < 9; ++q) {
+        const int k = lane + 32 * q;
+        if (k <= 256) {
+            const int ka = k & 255, kb = (256 - k) & 255;
+            const float ar = re[ka], ai = im[ka], br = re[kb], bi = -im[kb];
+            const float er = 0.5f * (ar + br), ei = 0.5f * (ai + bi);
+            const float orr = 0.5f * (ai - bi), oi = -0.5f * (ar - br);
+            const float2 w = k < 256 ? tw[k] : make_float2(-1.f, 0.f);
+            const float xr = er + (w.x * orr - w.y * oi);
+            const float xi = ei + (w.x * oi + w.y * orr);
+            pw[k] = xr * xr + xi * xi;
+        }
     }
-    for (int k = threadIdx.x; k < 257; k += blockDim.x) pw[k] = re[k] * re[k] + im[k] * im[k];
-    __syncthreads();
-    if (threadIdx.x < kMel) {
-        const int m = threadIdx.x;
-        const int k0 = p.fb_lo[m], k1 = p.fb_hi[m];
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+        const int m = lane + 32 * q;
+        const int k0 = __ldg(p.fb_lo + m), k1 = __ldg(p.fb_hi + m);
+        const float* fb = p.fb + m * 257;
         float s = 0.f;
-        for (int k = k0; k < k1; ++k) s += p.fb[m * 257 + k] * pw[k];
+        for (int k = k0; k < k1; ++k) s += __ldg(fb + k) * pw[k];
         p.mel[static_cast<size_t>(f) * kMel + m] = logf(s + 5.9604645e-08f);
     }
 }
 
-// Per-utterance normalisation over the valid frames (src/mel.rs:103-136).
-__global__ void k_mel_norm(MelParams p) {
+// Per-utterance normalisation over the valid frames (src/mel.rs:103-136):
+// one CTA per (utterance, 32 mel bins); 8 frame lanes per bin, reduced in
+// shared memory; two passes (mean, then squared deviations) as the reference.
+__global__ void __launch_bounds__(256) k_mel_norm(MelParams p) {
+    __shared__ float red[8][33];
+    __shared__ float stat[32];
     const int u = blockIdx.x;
-    const int m = threadIdx.x;
-    if (u >= p.n_utt || m >= kMel) return;
+    const int b = threadIdx.x & 31, fl = threadIdx.x >> 5;
+    const int m = blockIdx.y * 32 + b;
     const int f0 = p.frame_off[u];
     const int nf = p.frame_off[u + 1] - f0;
     const int nvalid = static_cast<int>((p.wave_off[u + 1] - p.wave_off[u]) / kHop);
     const int nv = nvalid > 1 ? nvalid : 1;
     float* mel = p.mel + static_cast<size_t>(f0) * kMel + m;
     float s = 0.f;
-    for (int t = 0; t < nvalid; ++t) s += mel[static_cast<size_t>(t) * kMel];
-    const float mean = s / static_cast<float>(nv);
+#pragma unroll 4
+    for (int t = fl; t < nvalid; t += 8) s += mel[static_cast<size_t>(t) * kMel];
+    red[fl][b] = s;
+    __syncthreads();
+    if (fl == 0) {
+        float tot = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) tot += red[i][b];
+        stat[b] = tot / static_cast<float>(nv);
+    }
+    __syncthreads();
+    const float mean = stat[b];
     float q = 0.f;
-    for (int t = 0; t < nvalid; ++t) {
+#pragma unroll 4
+    for (int t = fl; t < nvalid; t += 8) {
         const float d = mel[static_cast<size_t>(t) * kMel] - mean;
         q += d * d;
     }
-    const float sd = sqrtf(q / static_cast<float>(nv - 1 > 1 ? nv - 1 : 1));
-    const float inv = 1.0f / (sd + 1e-5f);
-    for (int t = 0; t < nf; ++t) {
+    red[fl][b] = q;
+    __syncthreads();
+    if (fl == 0) {
+        float tot = 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) tot += red[i][b];
+        stat[b] = sqrtf(tot / static_cast<float>(nv - 1 > 1 ? nv - 1 : 1)) + 1e-5f;
+    }
+    __syncthreads();
+    const float den = stat[b];
+    for (int t = fl; t < nf; t += 8) {
         float& v = mel[static_cast<size_t>(t) * kMel];
-        v = t < nvalid ? (v - mean) * inv : 0.f;
+        v = t < nvalid ? (v - mean) / den : 0.f;
     }
 }
 
-// conv0 + ReLU + mask, then depthwise conv1 + mask, for 8 output rows (t2) x
-// all 32 freq columns x 16 channels.  The conv0 tile (17 rows x 64 cols x 16
-// channels, f32) and the mel rows it needs (35 x 128) stay in shared memory.
-constexpr int kT2 = 8;
-constexpr int kC = 16;
-constexpr int kT1 = 2 * kT2 + 1;   // conv0 rows needed
-constexpr int kTm = 2 * kT1 + 1;   // mel rows needed
+// conv0 + ReLU + mask, then depthwise conv1 + mask, for kT2 output rows (t2)
+// x all 32 freq columns x kC channels.  Shared memory holds the mel rows the
+// tile needs with even and odd columns split (conv0's stride-2 taps are then
+// unit-stride across lanes) and the conv0 output tile [kT1][kC][65] (column
+// -1 is the zero pad; the odd row stride keeps the channel-per-lane reads of
+// the depthwise conv free of bank conflicts).  conv0: a warp owns 4 channels
+// with their 9 taps in registers, lanes walk the 64 columns; conv1: a lane
+// owns a channel, warps walk (row, 16-column run) with a sliding window.
+constexpr int kT2 = 4;
+constexpr int kC = 32;
+constexpr int kT1 = 2 * kT2 + 1;   // conv0 rows needed (9)
+constexpr int kTm = 2 * kT1 + 1;   // mel rows needed (19)
+constexpr int kMelS = 130;         // [0, 64]: even cols 0..126 (+ zero); [65, 129]: odd cols -1..127
+constexpr int kC0S = 65;           // conv0 row of one channel: cols -1..63
+constexpr int kC0Row = kC * kC0S;  // one conv0 row of all kC channels
+constexpr int kSubSmem = (kTm * kMelS + kT1 * kC0Row) * 4;
 
-constexpr int kSubSmem = (kTm * (kMel + 2) + kT1 * 65 * kC) * 4;
-
-__global__ void __launch_bounds__(256) k_sub_conv0_dw1(SubParams p) {
+__global__ void __launch_bounds__(256, 2) k_sub_conv0_dw1(SubParams p) {
     extern __shared__ float sub_smem[];
-    auto mel = reinterpret_cast<float(*)[kMel + 2]>(sub_smem);                    // [kTm][130]: cols -1 .. 128
-    auto c0 = reinterpret_cast<float(*)[65][kC]>(sub_smem + kTm * (kMel + 2));   // [kT1][65][kC]: cols -1 .. 63
+    float* mel = sub_smem;                 // [kTm][kMelS]
+    float* c0 = sub_smem + kTm * kMelS;    // [kT1][kC][kC0S]
     const int4 wk = p.work[blockIdx.x];    // (utterance, t2_0, channel group)
     const int u = wk.x, t2_0 = wk.y, cg = wk.z * kC;
     const int F = p.mel_off[u + 1] - p.mel_off[u];
@@ -136,52 +202,89 @@ __global__ void __launch_bounds__(256) k_sub_conv0_dw1(SubParams p) {
     const float* melu = p.mel + static_cast<size_t>(p.mel_off[u]) * kMel;
     const int t1_0 = 2 * t2_0 - 1;      // first conv0 row
     const int tm_0 = 2 * t1_0 - 1;      // first mel row
-    for (int i = threadIdx.x; i < kTm * (kMel + 2); i += blockDim.x) {
-        const int r = i / (kMel + 2), cidx = i % (kMel + 2);
-        const int tm = tm_0 + r, fm = cidx - 1;
-        mel[r][cidx] = (tm >= 0 && tm < F && fm >= 0 && fm < kMel) ? melu[static_cast<size_t>(tm) * kMel + fm] : 0.f;
+    for (int i = threadIdx.x; i < kTm * kMel; i += blockDim.x) {
+        const int r = i >> 7, col = i & 127;
+        const int tm = tm_0 + r;
+        const float v = (tm >= 0 && tm < F) ? melu[static_cast<size_t>(tm) * kMel + col] : 0.f;
+        mel[r * kMelS + ((col & 1) ? 65 + ((col + 1) >> 1) : (col >> 1))] = v;
     }
-    __syncthreads();
-    // conv0: out(t1, j) = relu(b + sum_{ki,kj} w * mel[2 t1 + ki - 1][2 j + kj - 1]), zero when masked or outside
-    for (int i = threadIdx.x; i < kT1 * 65 * kC; i += blockDim.x) {
-        const int c = i % kC, jj = (i / kC) % 65, r = i / (kC * 65);
-        const int t1 = t1_0 + r, j = jj - 1;
-        float s = 0.f;
-        if (t1 >= 0 && t1 < F1 && t1 < v1 && j >= 0 && j < 64) {
-            const float* w = p.w0 + (cg + c) * 9;
-            s = p.b0[cg + c];
+    if (threadIdx.x < kTm) {
+        mel[threadIdx.x * kMelS + 64] = 0.f;   // even col 128 (never read)
+        mel[threadIdx.x * kMelS + 65] = 0.f;   // col -1
+    }
+    for (int i = threadIdx.x; i < kT1 * kC; i += blockDim.x) c0[i * kC0S] = 0.f;  // col -1
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    {
+        const int cb = cg + warp * 4;
+        float w[4][9], bias[4];
 #pragma unroll
-            for (int t = 0; t < 9; ++t) {
-                const int ki = t / 3, kj = t % 3;
-                s += w[t] * mel[2 * r + ki][2 * j + kj];  // mel row tm_0 + 2r + ki, col 2j + kj - 1 (+1 pad)
-            }
-            s = s > 0.f ? s : 0.f;
+        for (int q = 0; q < 4; ++q) {
+            bias[q] = __ldg(p.b0 + cb + q);
+#pragma unroll
+            for (int t = 0; t < 9; ++t) w[q][t] = __ldg(p.w0 + (cb + q) * 9 + t);
         }
-        c0[r][jj][c] = s;
+        __syncthreads();
+        for (int r = 0; r < kT1; ++r) {
+            const int t1 = t1_0 + r;
+            const bool live = t1 >= 0 && t1 < F1 && t1 < v1;
+            const float* m0 = mel + 2 * r * kMelS;   // mel rows 2 t1 - 1 + ki
+            float* out = c0 + (r * kC + warp * 4) * kC0S + 1;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int j = lane + 32 * h;
+                float acc[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) acc[q] = bias[q];
+                if (live) {
+#pragma unroll
+                    for (int ki = 0; ki < 3; ++ki) {
+                        const float* row = m0 + ki * kMelS;
+                        const float a = row[65 + j], b = row[j], c = row[66 + j];  // cols 2j-1, 2j, 2j+1
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            acc[q] += w[q][ki * 3] * a;
+                            acc[q] += w[q][ki * 3 + 1] * b;
+                            acc[q] += w[q][ki * 3 + 2] * c;
+                        }
+                    }
+                }
+#pragma unroll
+                for (int q = 0; q < 4; ++q) out[q * kC0S + j] = live ? fmaxf(acc[q], 0.f) : 0.f;
+            }
+        }
     }
     __syncthreads();
-    // depthwise conv1 (+ mask): out(t2, j2) = b + sum w * c0(2 t2 + ki - 1, 2 j2 + kj - 1)
-    for (int i = threadIdx.x; i < kT2 * 32 * kC; i += blockDim.x) {
-        const int c = i % kC, j2 = (i / kC) % 32, r2 = i / (kC * 32);
+    {
+        const int c = lane;
+        float w[9];
+#pragma unroll
+        for (int t = 0; t < 9; ++t) w[t] = __ldg(p.w2 + (cg + c) * 9 + t);
+        const float bias = __ldg(p.b2 + cg + c);
+        const int r2 = warp >> 1, jb = (warp & 1) * 16;
         const int t2 = t2_0 + r2;
-        if (t2 >= F2) continue;
-        float s = 0.f;
-        if (t2 < v2) {
-            const float* w = p.w2 + (cg + c) * 9;
-            s = p.b2[cg + c];
+        if (t2 >= F2) return;
+        const bool live = t2 < v2;
+        // conv0 local rows 2 r2 + ki hold t1 = 2 t2 - 1 + ki
+        const float* base = c0 + (2 * r2 * kC + c) * kC0S;
+        __half* out = p.x2 + static_cast<size_t>(p.x2_off[u] + t2) * 32 * 256 + cg + c;
+        float prev[3];
+#pragma unroll
+        for (int ki = 0; ki < 3; ++ki) prev[ki] = base[ki * kC0Row + 2 * jb];   // col 2 jb - 1
+#pragma unroll 4
+        for (int jj = 0; jj < 16; ++jj) {
+            const int j2 = jb + jj;
+            float s = bias;
 #pragma unroll
             for (int ki = 0; ki < 3; ++ki) {
-                const int t1 = 2 * t2 + ki - 1;
-                if (t1 < 0 || t1 >= F1) continue;
-#pragma unroll
-                for (int kj = 0; kj < 3; ++kj) {
-                    const int j1 = 2 * j2 + kj - 1;
-                    if (j1 < 0 || j1 >= 64) continue;
-                    s += w[ki * 3 + kj] * c0[t1 - t1_0][j1 + 1][c];
-                }
+                const float* row = base + ki * kC0Row;
+                const float x1 = row[2 * j2 + 1], x2 = row[2 * j2 + 2];   // cols 2 j2, 2 j2 + 1
+                s += w[ki * 3] * prev[ki];
+                s += w[ki * 3 + 1] * x1;
+                s += w[ki * 3 + 2] * x2;
+                prev[ki] = x2;
             }
+            out[j2 * 256] = __float2half_rn(live ? s : 0.f);
         }
-        p.x2[(static_cast<size_t>(p.x2_off[u] + t2) * 32 + j2) * 256 + cg + c] = __float2half_rn(s);
     }
 }
 
@@ -200,11 +303,17 @@ __global__ void __launch_bounds__(256) k_sub_dw2(SubParams p) {
     const int nvalid = p.n_valid[u];
     const int v3 = conv_len_d(conv_len_d(conv_len_d(nvalid > 1 ? nvalid : 1)));
     const __half* x3 = p.x3 + static_cast<size_t>(p.x2_off[u]) * 32 * 256;
-    for (int i = threadIdx.x; i < 16 * 256; i += blockDim.x) {
-        const int c = i % 256, j3 = i / 256;
+    const int c = threadIdx.x;   // blockDim.x == 256: one channel per thread
+    float w[9];
+#pragma unroll
+    for (int t = 0; t < 9; ++t) w[t] = __ldg(p.w5 + c * 9 + t);
+    const float bias = __ldg(p.b5 + c);
+    const bool live = t3 < v3;
+#pragma unroll 2
+    for (int j3 = 0; j3 < 16; ++j3) {
         float s = 0.f;
-        if (t3 < v3) {
-            s = p.b5[c];
+        if (live) {
+            s = bias;
 #pragma unroll
             for (int ki = 0; ki < 3; ++ki) {
                 const int t2 = 2 * t3 + ki - 1;
@@ -212,8 +321,8 @@ __global__ void __launch_bounds__(256) k_sub_dw2(SubParams p) {
 #pragma unroll
                 for (int kj = 0; kj < 3; ++kj) {
                     const int j2 = 2 * j3 + kj - 1;
-                    if (j2 < 0 || j2 >= 32) continue;
-                    s += p.w5[c * 9 + ki * 3 + kj] * __half2float(x3[(static_cast<size_t>(t2) * 32 + j2) * 256 + c]);
+                    if (j2 < 0) continue;   // j2 <= 31 always
+                    s += w[ki * 3 + kj] * __half2float(x3[(static_cast<size_t>(t2) * 32 + j2) * 256 + c]);
                 }
             }
         }
@@ -241,10 +350,10 @@ int check_launch(const char* what) {
 
 int launch_mel(const MelParams& p, int n_frames, cudaStream_t st) {
     if (n_frames <= 0) return 0;
-    k_mel_frames<<<n_frames, 256, 0, st>>>(p);
+    k_mel_frames<<<(n_frames + kMelWarps - 1) / kMelWarps, 256, 0, st>>>(p, n_frames);
     const int rc = check_launch("k_mel_frames");
     if (rc) return rc;
-    k_mel_norm<<<p.n_utt, kMel, 0, st>>>(p);
+    k_mel_norm<<<dim3(p.n_utt, kMel / 32), 256, 0, st>>>(p);
     return check_launch("k_mel_norm");
 }
 

@@ -168,13 +168,13 @@ __device__ __forceinline__ void slab_put_f16x64(uint8_t* slab, int lane, const f
 // this warp's 32 rows start at output row y0.
 template <int BN, int EPI>
 __device__ __forceinline__ void epilogue_subtile(const GemmParams& p, const CUtensorMap* map_c, uint8_t* slab,
-                                                 uint32_t tacc, int lane, int n0, int y0) {
+                                                 uint32_t tacc, int lane, int n0, int y0, bool with_bias) {
     if (EPI == EPI_F32 || EPI == EPI_RESID) {
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
             float v[32];
             load_acc32(tacc + c * 32, v);
-            if (EPI == EPI_F32 && p.bias) add_vec(v, p.bias + n0 + c * 32, 32);
+            if (EPI == EPI_F32 && p.bias && with_bias) add_vec(v, p.bias + n0 + c * 32, 32);
             if (EPI == EPI_RESID) {
 #pragma unroll
                 for (int i = 0; i < 32; ++i) v[i] *= p.alpha;
@@ -267,10 +267,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int num_k = p.K / kBK;
+    const int ksplit = (EPI == EPI_F32 && p.ksplit > 1) ? p.ksplit : 1;   // split-K: f32 epilogue only
+    const int num_k = p.K / kBK / ksplit;    // k-blocks per tile (per K part)
     const int n_tiles = p.N / BN;
     const int m_tiles = (p.M + SUB * kBM - 1) / (SUB * kBM);
-    const int num_tiles = n_tiles * m_tiles;
+    const int mn_tiles = n_tiles * m_tiles;
+    const int num_tiles = mn_tiles * ksplit;  // tile = (K part, m tile, n tile)
 
     if (threadIdx.x == 0) {
         tma_prefetch_desc(&tm_a);
@@ -302,9 +304,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             int it = 0;
             bool ok = true;
             for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-                const int m0 = (tile / n_tiles) * SUB * kBM;
-                const int n0 = (tile % n_tiles) * BN;
-                for (int kb = 0; kb < num_k; ++kb, ++it) {
+                const int t = EPI == EPI_F32 ? tile % mn_tiles : tile;
+                const int m0 = (t / n_tiles) * SUB * kBM;
+                const int n0 = (t % n_tiles) * BN;
+                const int kb0 = EPI == EPI_F32 ? (tile / mn_tiles) * num_k : 0;
+                for (int kb = kb0; kb < kb0 + num_k; ++kb, ++it) {
                     const int s = it % S;
                     const uint32_t ph = (it / S) & 1;
                     if (it >= S && !(ok = mbar_wait(smem_u32(&empty[s]), ph ^ 1, 0x01))) break;
@@ -338,7 +342,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (use > 0 && !(ok = mbar_wait(smem_u32(&tempty[b]), (use - 1) & 1, 0x06))) break;
                 tc_fence_after();
                 const uint32_t acc = tmem + b * Cfg::kAccCols;
-                for (int kb = 0; kb < num_k; ++kb, ++it) {
+                for (int kb = 0; kb < num_k; ++kb, ++it) {   // k-blocks of this tile's K part
                     const int s = it % S;
                     const uint32_t ph = (it / S) & 1;
                     ok = mbar_wait(smem_u32(&full[s]), ph, 0x02);
@@ -369,7 +373,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int w0 = (e % TPR) * WPT;    // first 16-byte chunk of this thread
             int it = 0;
             for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-                const int n0 = (tile % n_tiles) * BN;
+                const int n0 = ((EPI == EPI_F32 ? tile % mn_tiles : tile) % n_tiles) * BN;
                 uint32_t lo[4], hi[4];
                 {
                     const uint4* src = reinterpret_cast<const uint4*>(p.lut + static_cast<size_t>(n0 + row) * 16);
@@ -420,15 +424,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t* slab = sOut + (warp - kEpiWarp0) * 4096;
         int lt = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++lt) {
-            const int m0 = (tile / n_tiles) * SUB * kBM;
-            const int n0 = (tile % n_tiles) * BN;
+            const int t = EPI == EPI_F32 ? tile % mn_tiles : tile;
+            const int ks = EPI == EPI_F32 ? tile / mn_tiles : 0;
+            // K part ks writes its own block of rows; the first part carries the bias
+            const int m0 = ks * (ksplit > 1 ? gemm_split_rows(p.M) : 0) + (t / n_tiles) * SUB * kBM;
+            const int n0 = (t % n_tiles) * BN;
             const int b = lt & 1;
             if (!mbar_wait(smem_u32(&tfull[b]), (lt >> 1) & 1, 0x05)) break;
             tc_fence_after();
             const uint32_t tq = tmem + (static_cast<uint32_t>(q * 32) << 16) + b * Cfg::kAccCols;
 #pragma unroll 1
             for (int sub = 0; sub < SUB; ++sub)
-                epilogue_subtile<BN, EPI>(p, &tm_c, slab, tq + sub * BN, lane, n0, m0 + sub * kBM + q * 32);
+                epilogue_subtile<BN, EPI>(p, &tm_c, slab, tq + sub * BN, lane, n0, m0 + sub * kBM + q * 32, ks == 0);
             tc_fence_before();
             mbar_arrive(smem_u32(&tempty[b]));
         }
@@ -466,8 +473,10 @@ int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p
     // output of a 64-column tile), matching the epilogue's slab layout
     CUtensorMap tc;
     int rc;
+    const int ksplit = p.ksplit > 1 ? p.ksplit : 1;
     if (EPI == EPI_F32 || EPI == EPI_RESID)
-        rc = make_map_2d(&tc, p.out_f32, kMapF32, p.N, p.M, static_cast<uint64_t>(p.ldo) * 4, 32, 32, true);
+        rc = make_map_2d(&tc, p.out_f32, kMapF32, p.N, ksplit > 1 ? static_cast<uint64_t>(ksplit) * gemm_split_rows(p.M) : p.M,
+                         static_cast<uint64_t>(p.ldo) * 4, 32, 32, true);
     else if (EPI == EPI_GLU_F16)
         rc = make_map_2d(&tc, p.out_f16, kMapF16, p.N / 2, p.M, static_cast<uint64_t>(p.ldo) * 2, BN / 2, 32, BN == 128);
     else if (EPI == EPI_QKV)
@@ -475,7 +484,7 @@ int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p
     else
         rc = make_map_2d(&tc, p.out_f16, kMapF16, p.N, p.M, static_cast<uint64_t>(p.ldo) * 2, 64, 32, true);
     if (rc) return rc;
-    const int tiles = (p.N / BN) * ((p.M + SUB * kBM - 1) / (SUB * kBM));
+    const int tiles = (p.N / BN) * ((p.M + SUB * kBM - 1) / (SUB * kBM)) * ksplit;
     const int grid = tiles < g_num_sms ? tiles : g_num_sms;
     kern<<<grid, kThreads, Cfg::kSmemBytes, st>>>(ta, tb, tc, p);
     cudaError_t e = cudaGetLastError();
@@ -517,7 +526,36 @@ int gemm_validate(const GemmParams& p, bool lut) {
     if (p.K % kBK) return set_error(B3_EINVAL, "GEMM K=%d must be a multiple of %d", p.K, kBK);
     if (p.N % 128) return set_error(B3_EINVAL, "GEMM N=%d must be a multiple of 128", p.N);
     if (lut && !p.lut) return set_error(B3_EINVAL, "LUT4 GEMM needs a level table");
+    if (p.ksplit > 1 && (p.K / kBK) % p.ksplit)
+        return set_error(B3_EINVAL, "GEMM split-K: %d parts do not divide %d k-blocks", p.ksplit, p.K / kBK);
     return 0;
+}
+
+void gemm_plan_split(int M, int N, int K, bool lut, int num_sms, int max_parts, int* tiles, int* ksplit) {
+    // cost of one SM's share: waves x (k-blocks per part x bytes per k-block
+    // + a fixed per-tile cost of about two k-blocks for the fill and the
+    // epilogue); parts of fewer than 2 k-blocks are not considered
+    const int nk = K / kBK;
+    double best = 1e300;
+    *tiles = 1;
+    *ksplit = 1;
+    for (int shape = 1; shape <= 2; ++shape) {
+        const int bn = shape == 2 ? 128 : 64, bm = shape == 2 ? 256 : 128;
+        if (N % bn) continue;
+        const double kb_bytes = (bm * kBK * 2.0) + (lut ? bn * kBK / 2.0 : bn * kBK * 2.0);
+        const long t = static_cast<long>(N / bn) * ((M + bm - 1) / bm);
+        for (int s = 1; s <= nk; ++s) {
+            if (nk % s || s > max_parts || (s > 1 && nk / s < 2)) continue;
+            const long units = t * s;
+            const long waves = (units + num_sms - 1) / num_sms;
+            const double cost = waves * ((nk / s + 2) * kb_bytes);
+            if (cost < best * 0.999) {
+                best = cost;
+                *tiles = shape;
+                *ksplit = s;
+            }
+        }
+    }
 }
 
 // Tile shape by problem size: large problems take 256 x 128 tiles (two MMAs
@@ -530,7 +568,8 @@ int gemm_launch(const GemmOp& op, cudaStream_t st) {
     // 256 x 128 tiles as soon as they fill every SM once; below that the
     // 128 x 64 tiles win by spreading the work.
     const long big_tiles = static_cast<long>(p.N / 128) * ((p.M + 255) / 256);
-    const bool big = big_tiles >= 148;
+    const bool big = p.tiles ? p.tiles == 2 : big_tiles >= 148;
+    if (p.ksplit > 1 && op.epi != EPI_F32) return set_error(B3_EINVAL, "GEMM split-K needs the f32 epilogue");
     if (op.lut) {
         if (big) return launch_epi<128, 2, true>(op.epi, op.map_a, op.map_b, p, st);
         return launch_epi<64, 1, true>(op.epi, op.map_a, op.map_b, p, st);
