@@ -45,7 +45,7 @@ struct GemmParams {
     // bias goes into part 0 only); the consumer adds the parts in order.
     // 0 or 1 = no split.
     int ksplit;
-    int tiles;                // 0 = by size, 1 = 128 x 64 tiles, 2 = 256 x 128 tiles
+    int tiles;                // 0 = by size, 1 = 128 x 64 tiles, 2 = 256 x 128 tiles, 3 = 256 x 256 on CTA pairs
 };
 
 struct GemmOp {

@@ -131,9 +131,10 @@ __device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, uint32
 
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 
-// Wait until every committed bulk store has finished reading shared memory.
+// Wait until at most N committed bulk stores are still reading shared memory.
+template <int N = 0>
 __device__ __forceinline__ void bulk_wait_read() {
-    asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
 }
 
 // Wait until every committed bulk store is complete.
@@ -231,6 +232,112 @@ template <int M, int N>
 __host__ __device__ constexpr uint32_t idesc_f16_f32() {
     return (1u << 4) | (0u << 7) | (0u << 10) | (0u << 15) | (0u << 16) |
            (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
+}
+
+// ─────────────────────── CTA pairs (cta_group::2) ───────────────────────
+// A cluster of two CTAs on two SMs shares one MMA: the even CTA (rank 0)
+// issues it, each CTA holds half of A (its 128 rows) and half of B (its N/2
+// rows) at the same shared-memory offsets, and each CTA's TMEM receives its
+// 128 rows of the accumulator.
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+
+// Shared::cluster address of the same shared-memory variable in CTA `rank`.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+    return r;
+}
+
+// Every thread of both CTAs; orders shared-memory state across the pair.
+__device__ __forceinline__ void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// Arrive on an mbarrier that may live in the peer CTA (shared::cluster address).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+
+// Remote arrive with the default (CTA-scope release) semantics: for shared
+// memory the arriving thread's CTA wrote and fenced to the async proxy, which
+// only the pair MMA (async proxy) reads afterwards.
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_bar) {
+    asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+
+// Bounded wait with cluster-scope acquire (arrivals came from the peer CTA).
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, unsigned int site) {
+    const unsigned long long t0 = globaltimer();
+    for (;;) {
+        uint32_t ok;
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(bar), "r"(parity), "r"(100000u)
+            : "memory");
+        if (ok) return true;
+        if (globaltimer() - t0 > kWaitLimitNs) {
+            record_error(B3_ERR_TIMEOUT | site);
+            return false;
+        }
+    }
+}
+
+// 2D tiled load into this CTA's shared memory whose completion is counted on
+// an mbarrier of either CTA of the pair (`cluster_bar`, shared::cluster).
+// Every CTA loads its own tile from this GPU's memory.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t cluster_bar,
+                                                 int32_t x, int32_t y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(cluster_bar), "r"(x), "r"(y)
+        : "memory");
+}
+
+// Executed by one warp in each CTA of the pair.
+template <uint32_t kCols>
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+                 "n"(kCols)
+                 : "memory");
+}
+
+__device__ __forceinline__ void tmem_relinquish_pair() {
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+
+template <uint32_t kCols>
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "n"(kCols)
+                 : "memory");
+}
+
+// D(tmem of both CTAs) (+)= A(both CTAs' smem) * B(both CTAs' smem)^T.
+__device__ __forceinline__ void mma_f16_ss_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// Arrive on the mbarrier at this shared-memory offset in every CTA of
+// `cta_mask` once the pair MMAs issued so far are done.
+__device__ __forceinline__ void mma_commit_pair_mc(uint32_t bar, uint16_t cta_mask) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+        "h"(cta_mask)
+        : "memory");
 }
 
 // ───────────────────────── byte-permute helpers ─────────────────────────

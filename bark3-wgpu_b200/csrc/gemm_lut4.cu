@@ -114,11 +114,21 @@ __device__ __forceinline__ void slab_put(uint8_t* slab, int r, int j, uint4 v, i
     *reinterpret_cast<uint4*>(slab + off) = v;
 }
 
-// Before rewriting the slab, the previous bulk store must have read it.
-__device__ __forceinline__ void slab_acquire(int lane) {
-    if (lane == 0) bulk_wait_read();
-    __syncwarp();
-}
+// An epilogue warp's NS output slabs (32 x 128 B each), used in turn: a slab
+// is rewritten only after the bulk store that last read it has finished
+// reading, so with NS = 2 the next slab fills while the previous one drains.
+template <int NS>
+struct Slabs {
+    uint8_t* base;
+    int idx;
+    __device__ __forceinline__ uint8_t* acquire(int lane) {
+        uint8_t* s = base + idx * 4096;
+        idx = NS == 1 ? 0 : (idx + 1) % NS;
+        if (lane == 0) bulk_wait_read<NS - 1>();
+        __syncwarp();
+        return s;
+    }
+};
 
 // The slab goes out as one TMA tile store, or an f32 add-reduction into the
 // destination (the residual update x += alpha * acc, done in L2).
@@ -166,8 +176,8 @@ __device__ __forceinline__ void slab_put_f16x64(uint8_t* slab, int lane, const f
 
 // Epilogue of one 128-row subtile held in TMEM columns [tacc, tacc + BN):
 // this warp's 32 rows start at output row y0.
-template <int BN, int EPI>
-__device__ __forceinline__ void epilogue_subtile(const GemmParams& p, const CUtensorMap* map_c, uint8_t* slab,
+template <int BN, int EPI, int NS>
+__device__ __forceinline__ void epilogue_subtile(const GemmParams& p, const CUtensorMap* map_c, Slabs<NS>& slabs,
                                                  uint32_t tacc, int lane, int n0, int y0, bool with_bias) {
     if (EPI == EPI_F32 || EPI == EPI_RESID) {
 #pragma unroll 1
@@ -179,7 +189,7 @@ __device__ __forceinline__ void epilogue_subtile(const GemmParams& p, const CUte
 #pragma unroll
                 for (int i = 0; i < 32; ++i) v[i] *= p.alpha;
             }
-            slab_acquire(lane);
+            uint8_t* slab = slabs.acquire(lane);
 #pragma unroll
             for (int j = 0; j < 8; ++j)
                 slab_put<true>(slab, lane, j, make_uint4(f2u(v[4 * j]), f2u(v[4 * j + 1]), f2u(v[4 * j + 2]), f2u(v[4 * j + 3])), 128);
@@ -195,14 +205,14 @@ __device__ __forceinline__ void epilogue_subtile(const GemmParams& p, const CUte
             if (EPI == EPI_QKV) {
                 // row layout [q + bias_u | q + bias_v | k | v], 1024 f16 each
                 if (n < 1024) {
-                    slab_acquire(lane);
+                    uint8_t* slab = slabs.acquire(lane);
                     slab_put_f16x64(slab, lane, v, p.bias_u + n);
                     slab_flush(map_c, slab, lane, n, y0, false);
-                    slab_acquire(lane);
+                    slab = slabs.acquire(lane);
                     slab_put_f16x64(slab, lane, v, p.bias_v + n);
                     slab_flush(map_c, slab, lane, n + 1024, y0, false);
                 } else {
-                    slab_acquire(lane);
+                    uint8_t* slab = slabs.acquire(lane);
                     slab_put_f16x64(slab, lane, v, nullptr);
                     slab_flush(map_c, slab, lane, n + 1024, y0, false);
                 }
@@ -216,7 +226,7 @@ __device__ __forceinline__ void epilogue_subtile(const GemmParams& p, const CUte
 #pragma unroll
                     for (int i = 0; i < 64; ++i) v[i] = fmaxf(v[i], 0.f);
                 }
-                slab_acquire(lane);
+                uint8_t* slab = slabs.acquire(lane);
                 slab_put_f16x64(slab, lane, v, nullptr);
                 slab_flush(map_c, slab, lane, n, y0, false);
             }
@@ -226,7 +236,7 @@ __device__ __forceinline__ void epilogue_subtile(const GemmParams& p, const CUte
         // GLU input a_i, column 2i+1 its gate b_i.  A BN-column tile gives BN/2
         // outputs: one slab row of BN bytes.
         constexpr bool kSw = (BN == 128);
-        slab_acquire(lane);
+        uint8_t* slab = slabs.acquire(lane);
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
             float v[32];
@@ -421,7 +431,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
         // ── epilogue (4 warps, one TMEM lane quarter each) ──
         const int q = warp & 3;
-        uint8_t* slab = sOut + (warp - kEpiWarp0) * 4096;
+        Slabs<1> slabs{sOut + (warp - kEpiWarp0) * 4096, 0};
         int lt = 0;
         for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++lt) {
             const int t = EPI == EPI_F32 ? tile % mn_tiles : tile;
@@ -435,7 +445,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t tq = tmem + (static_cast<uint32_t>(q * 32) << 16) + b * Cfg::kAccCols;
 #pragma unroll 1
             for (int sub = 0; sub < SUB; ++sub)
-                epilogue_subtile<BN, EPI>(p, &tm_c, slab, tq + sub * BN, lane, n0, m0 + sub * kBM + q * 32, ks == 0);
+                epilogue_subtile<BN, EPI>(p, &tm_c, slabs, tq + sub * BN, lane, n0, m0 + sub * kBM + q * 32, ks == 0);
             tc_fence_before();
             mbar_arrive(smem_u32(&tempty[b]));
         }
@@ -450,7 +460,266 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// ─────────────────────── K1 on CTA pairs (256 x 256 tiles) ───────────────────────
+//
+// A cluster of two CTAs computes one 256 x 256 tile with tcgen05.mma
+// cta_group::2 (M = 256, N = 256, K = 16): CTA r holds A rows [128 r, 128 r +
+// 128) and B rows (output columns) [128 r, 128 r + 128) of the tile, and its
+// TMEM receives accumulator rows [128 r, 128 r + 128) x all 256 columns.  Per
+// SM and k-block this moves 16 KB of A and 4 KB of codes (LUT4) instead of
+// 32 KB + 4 KB for a 256 x 128 single-CTA tile at the same FLOPs, so the ring
+// is deeper and L2 traffic per FLOP is ~1.8x lower.
+//
+// Roles per CTA are those of k1_gemm.  Only CTA 0's MMA thread issues MMAs;
+// it waits on CTA 0's barriers, which count both CTAs' work:
+//   full[s]    A (and f16 B) tiles of both CTAs: CTA 0 posts the expected
+//              bytes of both, each CTA's TMA completes on CTA 0's barrier;
+//   bready[s]  LUT4 B tiles expanded in both CTAs: one arrival per expander
+//              warp of either CTA (16);
+//   tempty[b]  accumulator set b drained by both CTAs' epilogues: one
+//              arrival per epilogue warp (8).
+// CTA-local barriers: empty[s] (stage s free again; the MMA commit arrives
+// on it in both CTAs), cfull[s] (this CTA's codes landed) and tfull[b]
+// (accumulator set b complete; the MMA commit arrives in both CTAs).
+namespace pair {
+constexpr int kBN = 256;                      // tile columns (both CTAs)
+constexpr int kHalfN = 128;                   // B rows per CTA
+constexpr uint32_t kABytes = kBM * kBK * 2;   // 16 KB
+constexpr uint32_t kBBytes = kHalfN * kBK * 2;
+constexpr uint32_t kCBytes = kHalfN * kBK / 2;
+constexpr uint32_t kOutBytes = 4 * 2 * 4096;    // two slabs per epilogue warp
+constexpr uint32_t kBarBytes = 512;
+constexpr uint32_t kAccCols = kBN;            // one accumulator set: 256 f32 columns
+constexpr uint32_t kTmemCols = 2 * kAccCols;  // double-buffered: all 512 columns
+template <bool LUT>
+struct Cfg {
+    static constexpr uint32_t kStageBytes = kABytes + kBBytes + (LUT ? kCBytes : 0);
+    static constexpr uint32_t kRingBudget = 232448 - kOutBytes - kBarBytes - 1024;
+    static constexpr int kStages = kRingBudget / kStageBytes > 8 ? 8 : kRingBudget / kStageBytes;
+    static constexpr uint32_t kSmemBytes = kStages * kStageBytes + kOutBytes + kBarBytes + 1024;
+    static_assert(kSmemBytes <= 232448, "shared memory budget");
+    static_assert(kStages * 5 * 8 + 4 * 8 + 8 <= kBarBytes, "barrier space");
+};
+}  // namespace pair
+
+template <bool LUT, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    k1_gemm_pair(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                 const __grid_constant__ CUtensorMap tm_c, const GemmParams p) {
+    using Cfg = pair::Cfg<LUT>;
+    constexpr int S = Cfg::kStages;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // identical offsets in both CTAs: the MMA addresses the peer's tiles by them
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    uint8_t* sA = smem;                              // [S][128 x 64 f16]
+    uint8_t* sB = smem + S * pair::kABytes;          // [S][128 x 64 f16]
+    uint8_t* sC = sB + S * pair::kBBytes;            // [S][128 x 32 B] (LUT4)
+    uint8_t* sOut = sC + (LUT ? S * pair::kCBytes : 0);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + pair::kOutBytes);
+    uint64_t* full = bars;
+    uint64_t* bready = bars + S;
+    uint64_t* empty = bars + 2 * S;
+    uint64_t* cfull = bars + 3 * S;
+    uint64_t* tfull = bars + 4 * S;       // [2]
+    uint64_t* tempty = bars + 4 * S + 2;  // [2]
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 4 * S + 4);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const int pair_id = blockIdx.x >> 1;
+    const int n_pairs = gridDim.x >> 1;
+    const int num_k = p.K / kBK;
+    const int n_tiles = p.N / pair::kBN;
+    const int m_tiles = (p.M + 2 * kBM - 1) / (2 * kBM);
+    const int num_tiles = n_tiles * m_tiles;
+
+    if (threadIdx.x == 0) {
+        tma_prefetch_desc(&tm_a);
+        tma_prefetch_desc(&tm_b);
+        tma_prefetch_desc(&tm_c);
+        for (int s = 0; s < S; ++s) {
+            mbar_init(smem_u32(&full[s]), 1);
+            mbar_init(smem_u32(&bready[s]), 16);
+            mbar_init(smem_u32(&empty[s]), 1);
+            mbar_init(smem_u32(&cfull[s]), 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(smem_u32(&tfull[b]), 1);
+            mbar_init(smem_u32(&tempty[b]), 8);
+        }
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc_pair<pair::kTmemCols>(smem_u32(tmem_slot));
+        tmem_relinquish_pair();
+    }
+    tc_fence_before();
+    cluster_sync();   // barriers of both CTAs initialised before any remote arrival
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ── TMA producer (both CTAs) ──
+        if (lane == 0) {
+            const uint32_t full0 = mapa_shared(smem_u32(full), 0);   // CTA 0's full[0]
+            int it = 0;
+            bool ok = true;
+            for (int tile = pair_id; tile < num_tiles && ok; tile += n_pairs) {
+                const int m0 = (tile / n_tiles) * 2 * kBM + rank * kBM;
+                const int n0 = (tile % n_tiles) * pair::kBN + rank * pair::kHalfN;
+                for (int kb = 0; kb < num_k; ++kb, ++it) {
+                    const int s = it % S;
+                    const uint32_t ph = (it / S) & 1;
+                    if (it >= S && !(ok = mbar_wait(smem_u32(&empty[s]), ph ^ 1, 0x11))) break;
+                    const uint32_t fb = full0 + s * 8;
+                    if (rank == 0)
+                        mbar_arrive_expect_tx(smem_u32(&full[s]), 2 * (pair::kABytes + (LUT ? 0 : pair::kBBytes)));
+                    tma_load_2d_pair(smem_u32(sA + s * pair::kABytes), &tm_a, fb, kb * kBK, m0);
+                    if (LUT) {
+                        const uint32_t cb = smem_u32(&cfull[s]);
+                        mbar_arrive_expect_tx(cb, pair::kCBytes);
+#pragma unroll
+                        for (int r = 0; r < pair::kHalfN / kBoxN; ++r)
+                            tma_load_2d(smem_u32(sC + s * pair::kCBytes + r * kBoxN * (kBK / 2)), &tm_b, cb,
+                                        kb * (kBK / 2), n0 + r * kBoxN);
+                    } else {
+#pragma unroll
+                        for (int r = 0; r < pair::kHalfN / kBoxN; ++r)
+                            tma_load_2d_pair(smem_u32(sB + s * pair::kBBytes + r * kBoxN * kBK * 2), &tm_b, fb,
+                                             kb * kBK, n0 + r * kBoxN);
+                    }
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ── MMA issuer (CTA 0 only) ──
+        if (rank == 0 && lane == 0) {
+            constexpr uint32_t idesc = idesc_f16_f32<2 * kBM, pair::kBN>();
+            int it = 0, lt = 0;
+            bool ok = true;
+            for (int tile = pair_id; tile < num_tiles && ok; tile += n_pairs, ++lt) {
+                const int b = lt & 1;
+                const int use = lt >> 1;
+                if (use > 0 && !(ok = mbar_wait_cluster(smem_u32(&tempty[b]), (use - 1) & 1, 0x16))) break;
+                tc_fence_after();
+                const uint32_t acc = tmem + b * pair::kAccCols;
+                for (int kb = 0; kb < num_k; ++kb, ++it) {
+                    const int s = it % S;
+                    const uint32_t ph = (it / S) & 1;
+                    ok = mbar_wait_cluster(smem_u32(&full[s]), ph, 0x12);
+                    if (ok && LUT) ok = mbar_wait(smem_u32(&bready[s]), ph, 0x13);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(sA + s * pair::kABytes);
+                    const uint32_t b0 = smem_u32(sB + s * pair::kBBytes);
+#pragma unroll
+                    for (int kk = 0; kk < kBK / 16; ++kk)
+                        mma_f16_ss_pair(acc, smem_desc_sw128(a0 + kk * 32), smem_desc_sw128(b0 + kk * 32), idesc,
+                                        (kb | kk) != 0);
+                    mma_commit_pair_mc(smem_u32(&empty[s]), 0x3);
+                }
+                if (ok) mma_commit_pair_mc(smem_u32(&tfull[b]), 0x3);
+            }
+        }
+    } else if (warp < kEpiWarp0) {
+        // ── LUT expanders (both CTAs): this CTA's 128 B rows ──
+        if (LUT) {
+            constexpr int TPR = kExpThreads / pair::kHalfN, WPT = 8 / TPR;
+            const int e = threadIdx.x - 64;
+            const int row = e / TPR;
+            const int w0 = (e % TPR) * WPT;
+            const uint32_t bready0 = mapa_shared(smem_u32(bready), 0);
+            int it = 0;
+            for (int tile = pair_id; tile < num_tiles; tile += n_pairs) {
+                const int n0 = (tile % n_tiles) * pair::kBN + rank * pair::kHalfN;
+                uint32_t lo[4], hi[4];
+                {
+                    const uint4* src = reinterpret_cast<const uint4*>(p.lut + static_cast<size_t>(n0 + row) * 16);
+                    const uint4 u0 = __ldg(src), u1 = __ldg(src + 1);
+                    lo[0] = prmt(u0.x, u0.y, 0x6420u);
+                    hi[0] = prmt(u0.x, u0.y, 0x7531u);
+                    lo[1] = prmt(u0.z, u0.w, 0x6420u);
+                    hi[1] = prmt(u0.z, u0.w, 0x7531u);
+                    lo[2] = prmt(u1.x, u1.y, 0x6420u);
+                    hi[2] = prmt(u1.x, u1.y, 0x7531u);
+                    lo[3] = prmt(u1.z, u1.w, 0x6420u);
+                    hi[3] = prmt(u1.z, u1.w, 0x7531u);
+                }
+                bool ok = true;
+                for (int kb = 0; kb < num_k; ++kb, ++it) {
+                    const int s = it % S;
+                    const uint32_t ph = (it / S) & 1;
+                    if (!(ok = mbar_wait(smem_u32(&cfull[s]), ph, 0x14))) break;
+                    const uint8_t* codes = sC + s * pair::kCBytes + row * 32 + w0 * 4;
+                    const uint4 c = *reinterpret_cast<const uint4*>(codes);
+                    const uint32_t wds[4] = {c.x, c.y, c.z, c.w};
+                    uint8_t* brow = sB + s * pair::kBBytes + (row >> 3) * 1024 + (row & 7) * 128;
+#pragma unroll
+                    for (int j = 0; j < WPT; ++j) {
+                        uint32_t o[4];
+                        lut_expand8(wds[j], lo, hi, o);
+                        *reinterpret_cast<uint4*>(brow + (((w0 + j) ^ (row & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+                    }
+                    fence_async_shared();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive_remote(bready0 + s * 8);
+                }
+                if (!ok) break;
+            }
+        }
+    } else {
+        // ── epilogue (both CTAs): 4 warps, one TMEM lane quarter each ──
+        const int q = warp & 3;
+        Slabs<2> slabs{sOut + (warp - kEpiWarp0) * 8192, 0};
+        const uint32_t tempty0 = mapa_shared(smem_u32(tempty), 0);
+        int lt = 0;
+        for (int tile = pair_id; tile < num_tiles; tile += n_pairs, ++lt) {
+            const int m0 = (tile / n_tiles) * 2 * kBM + rank * kBM;
+            const int n0 = (tile % n_tiles) * pair::kBN;
+            const int b = lt & 1;
+            if (!mbar_wait(smem_u32(&tfull[b]), (lt >> 1) & 1, 0x15)) break;
+            tc_fence_after();
+            const uint32_t tq = tmem + (static_cast<uint32_t>(q * 32) << 16) + b * pair::kAccCols;
+#pragma unroll 1
+            for (int h = 0; h < 2; ++h)
+                epilogue_subtile<128, EPI>(p, &tm_c, slabs, tq + h * 128, lane, n0 + h * 128, m0 + q * 32, true);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(tempty0 + b * 8);
+        }
+        if (lane == 0) bulk_wait_all();
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync();   // no CTA leaves while the pair MMA or a remote arrival may touch it
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair<pair::kTmemCols>(tmem);
+    }
+}
+
+// Output map of one epilogue warp's slab (32 rows of 128 bytes, or the GLU
+// output of a 128-column half tile), shared by both kernels.
+template <int EPI>
+int make_out_map(CUtensorMap* tc, const GemmParams& p, int ksplit) {
+    if (EPI == EPI_F32 || EPI == EPI_RESID)
+        return make_map_2d(tc, p.out_f32, kMapF32, p.N,
+                           ksplit > 1 ? static_cast<uint64_t>(ksplit) * gemm_split_rows(p.M) : p.M,
+                           static_cast<uint64_t>(p.ldo) * 4, 32, 32, true);
+    if (EPI == EPI_GLU_F16)
+        return make_map_2d(tc, p.out_f16, kMapF16, p.N / 2, p.M, static_cast<uint64_t>(p.ldo) * 2, 64, 32, true);
+    if (EPI == EPI_QKV)
+        return make_map_2d(tc, p.out_f16, kMapF16, 4096, p.M, static_cast<uint64_t>(p.ldo) * 2, 64, 32, true);
+    return make_map_2d(tc, p.out_f16, kMapF16, p.N, p.M, static_cast<uint64_t>(p.ldo) * 2, 64, 32, true);
+}
+
 int g_num_sms = 0;
+
+template <bool LUT, int EPI>
+int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t st);
 
 template <int BN, int SUB, bool LUT, int EPI>
 int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t st) {
@@ -472,17 +741,12 @@ int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p
     // output map: 32-row boxes of 128-byte rows (64-byte rows for the GLU
     // output of a 64-column tile), matching the epilogue's slab layout
     CUtensorMap tc;
-    int rc;
     const int ksplit = p.ksplit > 1 ? p.ksplit : 1;
-    if (EPI == EPI_F32 || EPI == EPI_RESID)
-        rc = make_map_2d(&tc, p.out_f32, kMapF32, p.N, ksplit > 1 ? static_cast<uint64_t>(ksplit) * gemm_split_rows(p.M) : p.M,
-                         static_cast<uint64_t>(p.ldo) * 4, 32, 32, true);
-    else if (EPI == EPI_GLU_F16)
-        rc = make_map_2d(&tc, p.out_f16, kMapF16, p.N / 2, p.M, static_cast<uint64_t>(p.ldo) * 2, BN / 2, 32, BN == 128);
-    else if (EPI == EPI_QKV)
-        rc = make_map_2d(&tc, p.out_f16, kMapF16, 4096, p.M, static_cast<uint64_t>(p.ldo) * 2, 64, 32, true);
+    int rc;
+    if (EPI == EPI_GLU_F16 && BN != 128)
+        rc = make_map_2d(&tc, p.out_f16, kMapF16, p.N / 2, p.M, static_cast<uint64_t>(p.ldo) * 2, BN / 2, 32, false);
     else
-        rc = make_map_2d(&tc, p.out_f16, kMapF16, p.N, p.M, static_cast<uint64_t>(p.ldo) * 2, 64, 32, true);
+        rc = make_out_map<EPI>(&tc, p, ksplit);
     if (rc) return rc;
     const int tiles = (p.N / BN) * ((p.M + SUB * kBM - 1) / (SUB * kBM)) * ksplit;
     const int grid = tiles < g_num_sms ? tiles : g_num_sms;
@@ -502,6 +766,42 @@ int launch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const Gemm
         case EPI_GLU_F16: return launch_one<BN, SUB, LUT, EPI_GLU_F16>(ta, tb, p, st);
         case EPI_QKV: return launch_one<BN, SUB, LUT, EPI_QKV>(ta, tb, p, st);
         case EPI_RELU_F16: return launch_one<BN, SUB, LUT, EPI_RELU_F16>(ta, tb, p, st);
+        default: return set_error(B3_EINVAL, "unknown GEMM epilogue %d", epi);
+    }
+}
+
+template <bool LUT, int EPI>
+int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t st) {
+    using Cfg = pair::Cfg<LUT>;
+    auto kern = k1_gemm_pair<LUT, EPI>;
+    static bool attr_done = false;  // per template instance
+    if (!attr_done) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(Cfg::kSmemBytes));
+        if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(k1_gemm_pair)", e);
+        attr_done = true;
+    }
+    CUtensorMap tc;
+    int rc = make_out_map<EPI>(&tc, p, 1);
+    if (rc) return rc;
+    const int tiles = (p.N / pair::kBN) * ((p.M + 2 * kBM - 1) / (2 * kBM));
+    const int pairs = tiles < g_num_sms / 2 ? tiles : g_num_sms / 2;
+    kern<<<2 * pairs, kThreads, Cfg::kSmemBytes, st>>>(ta, tb, tc, p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return set_cuda_error("k1_gemm_pair launch", e);
+    return 0;
+}
+
+template <bool LUT>
+int launch_pair_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t st) {
+    switch (epi) {
+        case EPI_F32: return launch_pair<LUT, EPI_F32>(ta, tb, p, st);
+        case EPI_RESID: return launch_pair<LUT, EPI_RESID>(ta, tb, p, st);
+        case EPI_F16: return launch_pair<LUT, EPI_F16>(ta, tb, p, st);
+        case EPI_SILU_F16: return launch_pair<LUT, EPI_SILU_F16>(ta, tb, p, st);
+        case EPI_GLU_F16: return launch_pair<LUT, EPI_GLU_F16>(ta, tb, p, st);
+        case EPI_QKV: return launch_pair<LUT, EPI_QKV>(ta, tb, p, st);
+        case EPI_RELU_F16: return launch_pair<LUT, EPI_RELU_F16>(ta, tb, p, st);
         default: return set_error(B3_EINVAL, "unknown GEMM epilogue %d", epi);
     }
 }
@@ -570,6 +870,20 @@ int gemm_launch(const GemmOp& op, cudaStream_t st) {
     const long big_tiles = static_cast<long>(p.N / 128) * ((p.M + 255) / 256);
     const bool big = p.tiles ? p.tiles == 2 : big_tiles >= 148;
     if (p.ksplit > 1 && op.epi != EPI_F32) return set_error(B3_EINVAL, "GEMM split-K needs the f32 epilogue");
+    // CTA pairs with 256 x 256 tiles once they fill every SM pair once
+    if (!g_num_sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
+        if (g_num_sms <= 0) g_num_sms = 148;
+    }
+    const long pair_tiles = static_cast<long>(p.N / 256) * ((p.M + 255) / 256);
+    const bool use_pair = p.tiles ? p.tiles == 3 : (p.N % 256 == 0 && p.ksplit <= 1 && pair_tiles >= g_num_sms / 2);
+    if (use_pair) {
+        if (p.N % 256) return set_error(B3_EINVAL, "GEMM pair tiles need N %% 256 == 0 (N=%d)", p.N);
+        return op.lut ? launch_pair_epi<true>(op.epi, op.map_a, op.map_b, p, st)
+                      : launch_pair_epi<false>(op.epi, op.map_a, op.map_b, p, st);
+    }
     if (op.lut) {
         if (big) return launch_epi<128, 2, true>(op.epi, op.map_a, op.map_b, p, st);
         return launch_epi<64, 1, true>(op.epi, op.map_a, op.map_b, p, st);

@@ -115,3 +115,35 @@ def test_bad_shapes_rejected(enc, pkg, syn):
     with pytest.raises(pkg.B3Error) as ei:
         enc.linear_lut4(a, codes, lut16)
     assert ei.value.code == pkg.B3_EINVAL
+
+
+@pytest.mark.parametrize("lut", [True, False])
+def test_pair_tiles_equal_single_cta_tiles(enc, syn, lut):
+    """Problems that fill every SM pair run on 256 x 256 CTA-pair tiles
+    (tcgen05 cta_group::2); small ones on single-CTA tiles.  Both issue the
+    same K-ordered MMAs per output element, so a row slice computed alone
+    (single-CTA tiles) must equal the same rows of the large problem."""
+    rng = np.random.default_rng(7 if lut else 8)
+    m, n, k = 2304, 4096, 1024
+    a = rng.normal(0, 1, size=(m, k)).astype(np.float32)
+    codes, lut16 = syn.make_lut4(rng, n, k)
+    bias = rng.normal(0, 0.01, size=n).astype(np.float32)
+    if lut:
+        run = lambda x: enc.linear_lut4(x, codes, lut16, bias)
+    else:
+        w16 = syn.expand_lut4(codes, lut16).astype(np.float16).view(np.uint16)
+        run = lambda x: enc.linear_f16(x, w16, bias)
+    big = run(a)
+    for r0, r1 in [(0, 100), (1000, 1077), (2200, 2304)]:
+        part = run(np.ascontiguousarray(a[r0:r1]))
+        assert np.array_equal(part.view(np.uint32), big[r0:r1].view(np.uint32)), (r0, r1)
+
+
+def test_pair_tiles_lowbit_equals_f16(enc, syn):
+    """lbtest's bit-exact criterion at a size that runs on CTA-pair tiles."""
+    rng = np.random.default_rng(11)
+    m, n, k = 2048, 4096, 1024
+    a = rng.normal(0, 1, size=(m, k)).astype(np.float32)
+    codes, lut16 = syn.make_lut4(rng, n, k)
+    w16 = syn.expand_lut4(codes, lut16).astype(np.float16).view(np.uint16)
+    assert np.array_equal(enc.linear_lut4(a, codes, lut16).view(np.uint32), enc.linear_f16(a, w16).view(np.uint32))
