@@ -91,6 +91,7 @@ def lib() -> ctypes.CDLL:
         "b3_decode_batch": (c_i, [c_p, c_p, c_p, c_i, c_p, c_p, c_i, c_u]),
         "b3_transcribe_batch": (c_i, [c_p, c_p, c_p, c_i, c_p, c_p, c_i, c_u]),
         "b3_transcribe_audio": (c_i, [c_p, c_p, c_p, c_i, c_p, c_p, c_i, c_u]),
+        "b3_encode_audio": (c_i, [c_p, c_p, c_p, c_i, c_p, c_p, ctypes.c_int64, c_u]),
         "b3_mel": (c_i, [c_p, c_p, c_p, c_i, c_p, c_p, c_u]),
         "b3_subsample": (c_i, [c_p, c_p, c_p, c_p, c_i, c_p, c_p, c_u]),
         "b3_mel_filters": (c_i, [c_p]),
@@ -238,6 +239,18 @@ class Encoder:
         check(self._L.b3_transcribe_audio(self.ctx, _ptr(samples), _ptr(off), n, _ptr(tokens), _ptr(counts),
                                           max_tokens, 0))
         return [tokens[i, : min(int(counts[i]), max_tokens)] for i in range(n)]
+
+    def encode_audio(self, waves):
+        """16 kHz utterances -> (pooler [sum T][640] f32, row offsets): the
+        encoder half of transcribe_audio on the same audio."""
+        off = np.concatenate([[0], np.cumsum([len(w) for w in waves])]).astype(np.int64)
+        samples = np.ascontiguousarray(np.concatenate(waves), dtype=np.float32)
+        n = len(waves)
+        rows = sum(frames_for_seconds(len(w) / 16000.0) for w in waves)
+        pooler = np.zeros((rows, 640), dtype=np.float32)
+        roff = np.zeros(n + 1, dtype=np.int32)
+        check(self._L.b3_encode_audio(self.ctx, _ptr(samples), _ptr(off), n, _ptr(pooler), _ptr(roff), rows, 0))
+        return pooler[: roff[n]], roff
 
     def mel(self, waves):
         """Padded waves -> list of (frames, 128) normalised log-mel arrays."""

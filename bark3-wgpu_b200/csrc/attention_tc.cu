@@ -1,0 +1,392 @@
+// attention_tc.cu — K2: fused relative-position multi-head self-attention on
+// 5th-generation tensor cores (tcgen05, accumulators in TMEM).
+//
+// For one utterance of T frames, head h (dh = 128), query i and key j:
+//   s[i, j] = (qu_i . k_j + qv_i . r_(i-j)) / sqrt(128),   p = softmax_j(s),
+//   o_i = sum_j p[i, j] v_j
+// where qu = q + bias_u, qv = q + bias_v and r_d is the relative-position key
+// for offset d = i - j (the reference's rel_shift: BD[q, T-1-q+k], with row
+// T-1-j of its position table holding position j; src/cpu/layer.rs:234-294,
+// src/cpu/ops.rs:133-189, src/encoder.rs:2161-2412).  Q / K / V / R are f16
+// (the reference also rounds K, V and R to f16, src/cpu/ops.rs:258-259,
+// src/cpu/layer.rs:234-247); scores, softmax and O accumulate in f32.
+//
+// One CTA per (utterance, 128-query block, head); key blocks of 64.
+//   warp 0      TMA: Qu (staging) and Qv once; per key block K, V and the
+//               new rows of the R band into a 2-stage ring;
+//   warp 1      TMEM owner; one thread issues the MMAs:
+//                 S  = Qu K^T      M128 N64  K128  (A: Qu in TMEM)
+//                 G  = Qv R_band^T M128 N192 K128  (three N64 pieces)
+//                 O += P V         M128 N128 K64   (A: P in TMEM, B: V MN-major)
+//   warps 2..5  softmax, one query row per thread (its TMEM lane): reads S
+//               and the 96 band columns its warp spans, adds the row's
+//               diagonal of the band, online softmax in f32, rescales O in
+//               TMEM, writes P (f16) over its S columns.
+// The band of a 128 x 64 score tile covers offsets q0-k0-63 .. q0-k0+127 (191
+// R rows, loaded as 192).  Consecutive key blocks share all but 64 of them,
+// so R rows live in a 256-row ring and each key block loads one 64-row chunk.
+// S is double-buffered in TMEM, so the S and G MMAs of the next key block run
+// while the softmax of this one is still working.
+//
+// The diagonal read: row i of the tile needs band column 127 - i + j for key
+// j, a window whose start moves by one column per row.  TMEM loads address
+// the same columns for all lanes of a warp, so each softmax thread parks its
+// lane's 96 loaded columns in a private shared-memory row and reads the 64 it
+// needs back at its own offset.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "b3_internal.h"
+#include "b3_kernels.h"
+#include "b3_ptx.cuh"
+
+namespace b3 {
+
+namespace {
+
+constexpr int kBQ = 128;          // queries per CTA
+constexpr int kBK = 64;           // keys per block
+constexpr int kThreads = 192;     // warp 0 TMA, warp 1 MMA, warps 2..5 softmax
+constexpr int kRing = 256;        // R ring rows
+constexpr int kShStride = 100;    // floats per row of the diagonal buffer (odd quads: conflict-free)
+
+// shared memory (offsets from a 1024-aligned base)
+constexpr uint32_t kQvOff = 0;                   // Qv: 2 dim-halves x (128 rows x 128 B)
+constexpr uint32_t kKOff = 32768;                // K: 2 stages x 2 halves x (64 rows x 128 B)
+constexpr uint32_t kVOff = kKOff + 32768;        // V: same
+constexpr uint32_t kROff = kVOff + 32768;        // R ring: 2 halves x (256 rows x 128 B)
+constexpr uint32_t kShOff = kROff + 65536;       // diagonal buffer 128 x 100 f32 (Qu staging first)
+constexpr uint32_t kBarOff = kShOff + kBQ * kShStride * 4;
+constexpr uint32_t kSmem = kBarOff + 256 + 1024;
+static_assert(kBQ * kShStride * 4 >= 32768, "Qu staging fits the diagonal buffer");
+static_assert(kSmem <= 232448, "shared memory budget");
+
+// TMEM columns
+constexpr uint32_t kTS = 0;       // S / P, 2 buffers x 64
+constexpr uint32_t kTG = 128;     // band, 192
+constexpr uint32_t kTO = 320;     // O, 128
+constexpr uint32_t kTQ = 448;     // Qu (A operand), 64
+
+constexpr uint32_t kIdescS = idesc_f16_f32_b<128, 64, 0>();
+constexpr uint32_t kIdescPV = idesc_f16_f32_b<128, 128, 1>();
+
+__device__ __forceinline__ uint32_t h2u(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ void named_sync_softmax() {
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    k2_relpos_attention_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_kv,
+                           const __grid_constant__ CUtensorMap tm_r, const AttnParams p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    uint8_t* sQv = smem + kQvOff;
+    uint8_t* sK = smem + kKOff;
+    uint8_t* sV = smem + kVOff;
+    uint8_t* sR = smem + kROff;
+    float* sSh = reinterpret_cast<float*>(smem + kShOff);
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBarOff);
+    uint64_t* kv_full = bars;        // [2]
+    uint64_t* kv_empty = bars + 2;   // [2]
+    uint64_t* qld = bars + 4;
+    uint64_t* q_tmem = bars + 5;
+    uint64_t* sg_full = bars + 6;
+    uint64_t* g_free = bars + 7;
+    uint64_t* p_ready = bars + 8;
+    uint64_t* o_ready = bars + 9;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+
+    const int warp = threadIdx.x >> 5;
+    const int lane = threadIdx.x & 31;
+    const int head = blockIdx.y;
+    const int2 wk = p.work[blockIdx.x];
+    const int seg0 = p.cu[wk.x];
+    const int T = p.cu[wk.x + 1] - seg0;
+    const int q0 = wk.y;
+    const int nkb = (T + kBK - 1) / kBK;
+    // band of key block kb: R rows [r_lo0 + 64 kb, r_lo0 + 64 kb + 191]; ring
+    // slot of R row r is (r - r_lo0) mod 256, so every 64-row chunk is contiguous
+    const int r_lo0 = p.r_center - q0 - (kBQ - 1);
+
+    if (threadIdx.x == 0) {
+        tma_prefetch_desc(&tm_q);
+        tma_prefetch_desc(&tm_kv);
+        tma_prefetch_desc(&tm_r);
+        for (int s = 0; s < 2; ++s) {
+            mbar_init(smem_u32(&kv_full[s]), 1);
+            mbar_init(smem_u32(&kv_empty[s]), 1);
+        }
+        mbar_init(smem_u32(qld), 1);
+        mbar_init(smem_u32(q_tmem), 4);
+        mbar_init(smem_u32(sg_full), 1);
+        mbar_init(smem_u32(g_free), 4);
+        mbar_init(smem_u32(p_ready), 4);
+        mbar_init(smem_u32(o_ready), 1);
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc<512>(smem_u32(tmem_slot));
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ── TMA producer ──
+        if (lane == 0) {
+            const uint32_t qb = smem_u32(qld);
+            mbar_arrive_expect_tx(qb, 4 * 16384);
+            for (int h = 0; h < 2; ++h) {
+                tma_load_2d(smem_u32(sQv + h * 16384), &tm_q, qb, 1024 + head * 128 + h * 64, seg0 + q0);
+                tma_load_2d(smem_u32(reinterpret_cast<uint8_t*>(sSh) + h * 16384), &tm_q, qb, head * 128 + h * 64,
+                            seg0 + q0);
+            }
+            for (int kb = 0; kb < nkb; ++kb) {
+                const int st = kb & 1;
+                if (kb >= 2 && !mbar_wait(smem_u32(&kv_empty[st]), ((kb >> 1) - 1) & 1, 0x21)) break;
+                const int nchunks = kb == 0 ? 3 : 1;
+                const uint32_t fb = smem_u32(&kv_full[st]);
+                mbar_arrive_expect_tx(fb, 2 * 16384 + nchunks * 16384);
+                const int krow = seg0 + kb * kBK;
+                for (int h = 0; h < 2; ++h) {
+                    tma_load_2d(smem_u32(sK + st * 16384 + h * 8192), &tm_kv, fb, 2048 + head * 128 + h * 64, krow);
+                    tma_load_2d(smem_u32(sV + st * 16384 + h * 8192), &tm_kv, fb, 3072 + head * 128 + h * 64, krow);
+                }
+                for (int c = (kb == 0 ? 0 : 2); c < 3; ++c) {
+                    const int rel = kb * kBK + c * 64;            // band row - r_lo0
+                    const uint32_t slot = static_cast<uint32_t>(rel) & (kRing - 1);
+                    for (int h = 0; h < 2; ++h)
+                        tma_load_2d(smem_u32(sR + h * 32768 + slot * 128), &tm_r, fb, head * 128 + h * 64,
+                                    r_lo0 + rel);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ── MMA issuer ──
+        if (lane == 0) {
+            bool ok = mbar_wait(smem_u32(qld), 0, 0x22) && mbar_wait(smem_u32(q_tmem), 0, 0x23);
+            for (int kb = 0; kb <= nkb && ok; ++kb) {
+                if (kb < nkb) {
+                    const int st = kb & 1;
+                    if (!(ok = mbar_wait(smem_u32(&kv_full[st]), (kb >> 1) & 1, 0x24))) break;
+                    if (kb >= 1 && !(ok = mbar_wait(smem_u32(g_free), (kb - 1) & 1, 0x25))) break;
+                    tc_fence_after();
+                    const uint32_t dS = tmem + kTS + 64 * st;
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const uint64_t bd = smem_desc_sw128(smem_u32(sK + st * 16384 + (kk >> 2) * 8192) + (kk & 3) * 32);
+                        mma_f16_ts(dS, tmem + kTQ + 8 * kk, bd, kIdescS, kk > 0);
+                    }
+#pragma unroll
+                    for (int c = 0; c < 3; ++c) {
+                        const uint32_t slot = static_cast<uint32_t>(kb * kBK + c * 64) & (kRing - 1);
+#pragma unroll
+                        for (int kk = 0; kk < 8; ++kk) {
+                            const uint64_t ad = smem_desc_sw128(smem_u32(sQv + (kk >> 2) * 16384) + (kk & 3) * 32);
+                            const uint64_t bd =
+                                smem_desc_sw128(smem_u32(sR + (kk >> 2) * 32768 + slot * 128) + (kk & 3) * 32);
+                            mma_f16_ss(tmem + kTG + 64 * c, ad, bd, kIdescS, kk > 0);
+                        }
+                    }
+                    mma_commit(smem_u32(sg_full));
+                }
+                if (kb >= 1) {
+                    const int j = kb - 1, st = j & 1;
+                    if (!(ok = mbar_wait(smem_u32(p_ready), j & 1, 0x26))) break;
+                    tc_fence_after();
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) {
+                        // V [64 keys][128 dims] as the MN-major B operand: 64-dim halves 8 KB
+                        // apart, 8-key atoms 1 KB apart, 16 keys per MMA
+                        const uint64_t bd = smem_desc_sw128_mn(smem_u32(sV + st * 16384) + kk * 2048, 8192, 1024);
+                        mma_f16_ts(tmem + kTO, tmem + kTS + 64 * st + 8 * kk, bd, kIdescPV, (j > 0 || kk > 0));
+                    }
+                    mma_commit(smem_u32(o_ready));
+                    mma_commit(smem_u32(&kv_empty[st]));
+                }
+            }
+        }
+    } else {
+        // ── softmax: thread = query row i (TMEM lane) ──
+        const int q = warp & 3;
+        const int i = q * 32 + lane;
+        const uint32_t lrow = static_cast<uint32_t>(q * 32) << 16;
+        // Qu row i: staging (two 128-byte-swizzled dim halves) -> TMEM columns kTQ..kTQ+63
+        bool ok = mbar_wait(smem_u32(qld), 0, 0x27);
+        if (ok) {
+            for (int h = 0; h < 2; ++h) {
+                uint32_t r[32];
+                const uint8_t* row = reinterpret_cast<const uint8_t*>(sSh) + h * 16384 + i * 128;
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    const uint4 v = *reinterpret_cast<const uint4*>(row + ((c ^ (i & 7)) << 4));
+                    r[4 * c] = v.x;
+                    r[4 * c + 1] = v.y;
+                    r[4 * c + 2] = v.z;
+                    r[4 * c + 3] = v.w;
+                }
+                tmem_st_32x32b_x32(tmem + lrow + kTQ + 32 * h, r);
+            }
+            tmem_wait_st();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(q_tmem));
+        named_sync_softmax();   // the staging area becomes the diagonal buffer
+        float* sh = sSh + i * kShStride;
+        float m_run = -INFINITY, l_run = 0.f;
+        for (int kb = 0; kb < nkb && ok; ++kb) {
+            const int st = kb & 1;
+            if (!(ok = mbar_wait(smem_u32(sg_full), kb & 1, 0x28))) break;
+            tc_fence_after();
+            float s[64];
+            {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(tmem + lrow + kTS + 64 * st, r);
+                tmem_wait_ld();
+#pragma unroll
+                for (int e = 0; e < 32; ++e) s[e] = __uint_as_float(r[e]);
+                tmem_ld_32x32b_x32(tmem + lrow + kTS + 64 * st + 32, r);
+                tmem_wait_ld();
+#pragma unroll
+                for (int e = 0; e < 32; ++e) s[32 + e] = __uint_as_float(r[e]);
+            }
+            // this warp's band window: columns [96 - 32q, 192 - 32q)
+#pragma unroll
+            for (int c = 0; c < 3; ++c) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(tmem + lrow + kTG + 96 - 32 * q + 32 * c, r);
+                tmem_wait_ld();
+#pragma unroll
+                for (int e = 0; e < 32; e += 4)
+                    *reinterpret_cast<float4*>(sh + 32 * c + e) =
+                        make_float4(__uint_as_float(r[e]), __uint_as_float(r[e + 1]), __uint_as_float(r[e + 2]),
+                                    __uint_as_float(r[e + 3]));
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(g_free));
+            // row i, key j: band column 127 - i + j = window column 31 - lane + j
+            const float* dg = sh + 31 - lane;
+            const int kvalid = T - kb * kBK;
+            float mloc = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 64; ++j) {
+                float v = (s[j] + dg[j]) * p.scale_log2;
+                if (j >= kvalid) v = -INFINITY;
+                s[j] = v;
+                mloc = fmaxf(mloc, v);
+            }
+            const float m_new = fmaxf(m_run, mloc);
+            const float corr = exp2f(m_run - m_new);
+            float lsum = 0.f;
+            uint32_t pk[32];
+#pragma unroll
+            for (int j = 0; j < 64; j += 2) {
+                const float a = exp2f(s[j] - m_new), b = exp2f(s[j + 1] - m_new);
+                lsum += a + b;
+                pk[j >> 1] = h2u(a, b);
+            }
+            l_run = l_run * corr + lsum;
+            m_run = m_new;
+            if (kb >= 1) {
+                // O (after P_{kb-1} V) *= corr
+                if (!(ok = mbar_wait(smem_u32(o_ready), (kb - 1) & 1, 0x29))) break;
+                tc_fence_after();
+#pragma unroll 1
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(tmem + lrow + kTO + 32 * c, r);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * corr);
+                    tmem_st_32x32b_x32(tmem + lrow + kTO + 32 * c, r);
+                }
+            }
+            tmem_st_32x32b_x32(tmem + lrow + kTS + 64 * st, pk);   // P over this block's S columns
+            tmem_wait_st();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(smem_u32(p_ready));
+        }
+        // ── O / l -> f16 row ──
+        if (ok && nkb > 0 && mbar_wait(smem_u32(o_ready), (nkb - 1) & 1, 0x2A)) {
+            tc_fence_after();
+            const float inv = 1.0f / l_run;
+            const bool store = q0 + i < T;
+            __half* dst = p.out + static_cast<size_t>(seg0 + q0 + i) * 1024 + head * 128;
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(tmem + lrow + kTO + 32 * c, r);
+                tmem_wait_ld();
+                if (store) {
+#pragma unroll
+                    for (int e = 0; e < 32; e += 8)
+                        *reinterpret_cast<uint4*>(dst + 32 * c + e) =
+                            make_uint4(h2u(__uint_as_float(r[e]) * inv, __uint_as_float(r[e + 1]) * inv),
+                                       h2u(__uint_as_float(r[e + 2]) * inv, __uint_as_float(r[e + 3]) * inv),
+                                       h2u(__uint_as_float(r[e + 4]) * inv, __uint_as_float(r[e + 5]) * inv),
+                                       h2u(__uint_as_float(r[e + 6]) * inv, __uint_as_float(r[e + 7]) * inv));
+                }
+            }
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc<512>(tmem);
+    }
+}
+
+int check_launch(const char* what) {
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? 0 : set_cuda_error(what, e);
+}
+
+}  // namespace
+
+int launch_attention_tc(const AttnParams& p, int M, int n_work, cudaStream_t st) {
+    if (n_work <= 0) return 0;
+    static bool attr_done = false;
+    if (!attr_done) {
+        cudaError_t e = cudaFuncSetAttribute(k2_relpos_attention_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(kSmem));
+        if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(k2 tc)", e);
+        attr_done = true;
+    }
+    CUtensorMap tq, tkv, tr;
+    int rc = make_map_2d(&tq, p.qkv, kMapF16, 4096, static_cast<uint64_t>(M), 8192, 64, kBQ, true);
+    if (!rc) rc = make_map_2d(&tkv, p.qkv, kMapF16, 4096, static_cast<uint64_t>(M), 8192, 64, kBK, true);
+    if (!rc) rc = make_map_2d(&tr, p.R, kMapF16, 1024, static_cast<uint64_t>(p.r_rows), 2048, 64, 64, true);
+    if (rc) return rc;
+    k2_relpos_attention_tc<<<dim3(n_work, 8), kThreads, kSmem, st>>>(tq, tkv, tr, p);
+    return check_launch("k2_relpos_attention_tc");
+}
+
+int attention_tc_block_rows() { return kBQ; }
+
+// Reads and clears this translation unit's device error word (stream-ordered).
+int attention_take_dev_error(cudaStream_t st, unsigned int* out) {
+    static const unsigned int zero = 0;
+    cudaError_t e = cudaMemcpyFromSymbolAsync(out, g_b3_dev_error, sizeof(unsigned int), 0,
+                                              cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e == cudaSuccess)
+        e = cudaMemcpyToSymbolAsync(g_b3_dev_error, &zero, sizeof(unsigned int), 0, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    return e == cudaSuccess ? 0 : set_cuda_error("reading the attention device error word", e);
+}
+
+}  // namespace b3

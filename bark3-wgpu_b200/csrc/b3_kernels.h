@@ -32,8 +32,10 @@ struct AttnParams {
     float scale_log2;    // log2(e) / sqrt(128)
 };
 
-int launch_attention(const AttnParams& p, int n_work, cudaStream_t st);
-int attention_block_rows();
+// attention_tc.cu: M rows in the qkv buffer.
+int launch_attention_tc(const AttnParams& p, int M, int n_work, cudaStream_t st);
+int attention_tc_block_rows();
+int attention_take_dev_error(cudaStream_t st, unsigned int* out);
 
 // Batched greedy TDT decoder state (tdt_decoder.cu).  B rows, one per
 // utterance; GEMM inputs are f16 hi | lo pairs (see tdt_decoder.cu).

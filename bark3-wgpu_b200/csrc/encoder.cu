@@ -529,13 +529,18 @@ int make_plan(b3_ctx* c, const int32_t* cu, int n_utt) {
     if (key == c->plan.cu && c->mcap >= M && c->tcap >= tmax) return 0;
     B3_TRY(ensure_arena(c, M));
     B3_TRY(ensure_pos(c, tmax));
-    const int bq = attention_block_rows();
+    const int bq = attention_tc_block_rows();
     std::vector<int2> work;
     std::vector<int2> seg(M);
     for (int i = 0; i < n_utt; ++i) {
         for (int q = 0; q < cu[i + 1] - cu[i]; q += bq) work.push_back(make_int2(i, q));
         for (int r = cu[i]; r < cu[i + 1]; ++r) seg[r] = make_int2(cu[i], cu[i + 1]);
     }
+    // attention CTAs of the longest utterances first (their key loops are
+    // longest), so the last wave is made of short ones
+    std::stable_sort(work.begin(), work.end(), [&](const int2& a, const int2& b) {
+        return cu[a.x + 1] - cu[a.x] > cu[b.x + 1] - cu[b.x];
+    });
     B3_TRY(c->work_d.ensure(work.size() * sizeof(int2)));
     B3_TRY(c->cu_d.ensure(key.size() * sizeof(int32_t)));
     B3_CUDA(cudaMemcpyAsync(c->work_d.p, work.data(), work.size() * sizeof(int2), cudaMemcpyHostToDevice, c->stream));
@@ -584,7 +589,7 @@ int attention_section(b3_ctx* c, const Layer& L, int M) {
             by += t * 1024 * 2 * 5 + (2 * t - 1) * 2048; // qu qv k v in, out; R band
         }
         ProfScope ps(c, B3_K_ATTENTION, fl, by);
-        B3_TRY(launch_attention(ap, c->plan.n_work, c->stream));
+        B3_TRY(launch_attention_tc(ap, M, c->plan.n_work, c->stream));
     }
     return run_gemm(c, L.o, a16, M, kHidden, EPI_RESID, params_resid(x, 1.0f));
 }
@@ -650,9 +655,10 @@ int check_finalized(b3_ctx* c) {
 
 int sync_and_check(b3_ctx* c) {
     B3_CUDA(cudaStreamSynchronize(c->stream));
-    unsigned int flag = 0;
+    unsigned int flag = 0, aflag = 0;
     B3_TRY(gemm_take_dev_error(c->stream, &flag));
-    if (flag) return set_error(B3_ETIMEOUT, "device wait ran out (code 0x%x)", flag);
+    B3_TRY(attention_take_dev_error(c->stream, &aflag));
+    if (flag | aflag) return set_error(B3_ETIMEOUT, "device wait ran out (code 0x%x)", flag | aflag);
     return 0;
 }
 
@@ -1634,6 +1640,36 @@ int b3_transcribe_audio(b3_ctx* ctx, const float* samples, const int64_t* offset
                     params_f32(ctx->dec.pooler.as<float>(), kProj, ctx->proj_b.as<float>())));
     B3_TRY(decode_device(ctx, ctx->dec.pooler.as<float>(), s.x4off.data(), n_utt, max_tokens));
     B3_TRY(decode_collect(ctx, n_utt, tokens, counts, max_tokens, dev));
+    return dev ? 0 : sync_and_check(ctx);
+}
+
+int b3_encode_audio(b3_ctx* ctx, const float* samples, const int64_t* offsets, int n_utt, float* pooler,
+                    int32_t* row_offsets, int64_t max_rows, unsigned flags) {
+    B3_TRY(check_finalized(ctx));
+    if (!ctx->fe.present) return set_error(B3_ESTATE, "no conv subsampling weights were loaded");
+    if (ctx->n_layers <= 0) return set_error(B3_ESTATE, "no encoder layers were loaded");
+    if (!samples || !offsets || !pooler || !row_offsets || n_utt <= 0) return set_error(B3_EINVAL, "bad arguments");
+    if (offsets[0] != 0) return set_error(B3_EINVAL, "offsets[0] must be 0");
+    DeviceGuard g(ctx->device);
+    const bool dev = flags & B3_DEVICE_PTRS;
+    std::vector<int64_t> woff;
+    B3_TRY(fe_pad(ctx, samples, offsets, n_utt, dev, woff));
+    FeShape s;
+    B3_TRY(fe_mel(ctx, ctx->fe.wave.as<float>(), woff, s));
+    const int M = s.x4off[n_utt];
+    if (M > max_rows) return set_error(B3_EINVAL, "pooler needs %d rows, capacity is %lld", M, static_cast<long long>(max_rows));
+    B3_TRY(fe_subsample(ctx, s));
+    B3_TRY(forward_blocks(ctx, M, ctx->n_layers, &ctx->fe.sub_w_perm));
+    float* dst = dev ? pooler : nullptr;
+    if (!dev) {
+        B3_TRY(ctx->dec.pooler.ensure(static_cast<size_t>(M) * kProj * 4 + 16));
+        dst = ctx->dec.pooler.as<float>();
+    }
+    B3_TRY(run_gemm(ctx, ctx->proj_w, ctx->a16.as<__half>(), M, kHidden, EPI_F32,
+                    params_f32(dst, kProj, ctx->proj_b.as<float>())));
+    if (!dev)
+        B3_CUDA(cudaMemcpyAsync(pooler, dst, static_cast<size_t>(M) * kProj * 4, cudaMemcpyDeviceToHost, ctx->stream));
+    memcpy(row_offsets, s.x4off.data(), (n_utt + 1) * sizeof(int32_t));
     return dev ? 0 : sync_and_check(ctx);
 }
 

@@ -162,6 +162,14 @@ int b3_transcribe_batch(b3_ctx* ctx, const float* sub, const int32_t* cu_seqlens
 int b3_transcribe_audio(b3_ctx* ctx, const float* samples, const int64_t* offsets, int n_utt,
                         b3_token* tokens, int32_t* counts, int max_tokens, unsigned flags);
 
+/* The encoder half of b3_transcribe_audio (Encoder::encode_pre's pooler,
+ * src/encoder.rs:2005, from audio): pooler [sum T][640] f32 for the same
+ * audio, row_offsets (host, n_utt + 1) the per-utterance encoder rows.
+ * max_rows is the capacity of pooler in rows (B3_EINVAL if too small).  The
+ * pooler is exactly what b3_transcribe_audio decodes. */
+int b3_encode_audio(b3_ctx* ctx, const float* samples, const int64_t* offsets, int n_utt, float* pooler,
+                    int32_t* row_offsets, int64_t max_rows, unsigned flags);
+
 /* Log-mel features of already padded waves: mel [sum frames][128],
  * frame_offsets (host, n_utt + 1) receives the per-utterance frame offsets
  * (1 + len / 160 frames each; frames past len / 160 are zero). */

@@ -68,16 +68,33 @@ def test_reference_vocab_size(syn, oracle, pkg):
 
 
 def test_transcribe_end_to_end(dec_model, syn, oracle):
-    """Encoder + decoder on the GPU vs the oracle encoder + oracle decoder."""
+    """Encoder + decoder on the GPU vs the oracle, stage by stage on identical
+    inputs: the GPU pooler against the oracle encoder (per-layer tolerance),
+    and the GPU token streams against the oracle decoder run on that same GPU
+    pooler (>= 99% of tokens).
+
+    The token streams of the whole oracle pipeline are printed, not asserted:
+    this random-init joint emits a token at nearly every step from 1025
+    near-equal logits, so a 3e-4 change of the pooler (the f16-activation
+    error of the encoder) flips some argmaxes.  Perturbing the oracle's own
+    pooler by 3e-4 normwise noise moves its streams just as far (0.89 to 1.00
+    token match over seeds)."""
     w, enc = dec_model
     rng = np.random.default_rng(6)
     lens = [50, 133, 20]
     subs = [syn.sub_features(rng, t) for t in lens]
     cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
-    got = enc.transcribe_batch(np.concatenate(subs), cu)
+    sub = np.concatenate(subs)
+    got = enc.transcribe_batch(sub, cu)
+    pooler = enc.encode_batch(sub, cu)
     oenc = oracle.OracleEncoder(w, 2)
     odec = oracle.OracleTdt(w)
-    want = [odec.decode(oenc.encode(s)) for s in subs]
-    m, exact = token_match(got, want)
-    print(f"end-to-end token match {m:.4f}, identical streams {exact:.2f}")
+    for i, s in enumerate(subs):
+        ref = oenc.encode(s)
+        assert np.max(np.abs(pooler[cu[i]:cu[i + 1]] - ref)) / np.max(np.abs(ref)) <= 2e-2
+    same_input = odec.decode_batch(pooler, cu)
+    m, exact = token_match(got, same_input)
+    full = token_match(got, [odec.decode(oenc.encode(s)) for s in subs])
+    print(f"GPU tokens vs oracle decoder on the GPU pooler: match {m:.4f}, identical streams {exact:.2f}; "
+          f"vs the whole oracle pipeline: match {full[0]:.4f}")
     assert m >= MATCH

