@@ -12,16 +12,20 @@
 // src/cpu/layer.rs:234-247); scores, softmax and O accumulate in f32.
 //
 // One CTA per (utterance, 128-query block, head); key blocks of 64.
-//   warp 0      TMA: Qu (staging) and Qv once; per key block K, V and the
+//   warp 0      TMA: Qu and Qv (staging) once; per key block K, V and the
 //               new rows of the R band into a 2-stage ring;
 //   warp 1      TMEM owner; one thread issues the MMAs:
-//                 S  = Qu K^T      M128 N64  K128  (A: Qu in TMEM)
-//                 G  = Qv R_band^T M128 N192 K128  (three N64 pieces)
+//                 S  = Qu K^T      M128 N64  K128  (A: Qu in shared memory)
+//                 G  = Qv R_band^T M128 N192 K128  (three N64 pieces, A: Qv in TMEM)
 //                 O += P V         M128 N128 K64   (A: P in TMEM, B: V MN-major)
-//   warps 2..5  softmax, one query row per thread (its TMEM lane): reads S
-//               and the 96 band columns its warp spans, adds the row's
-//               diagonal of the band, online softmax in f32, rescales O in
-//               TMEM, writes P (f16) over its S columns.
+//   warps 2..9  softmax, two warps per TMEM lane quarter: one query row per
+//               lane, each warp of a pair owns 32 of the block's 64 keys (and
+//               64 of O's 128 columns).  A thread reads its S columns and the
+//               band columns its warp spans, adds the row's diagonal of the
+//               band, and the pair exchanges row maxima through shared memory;
+//               online softmax in f32 with a lazily moved reference max (O and
+//               l are rescaled only when the block max exceeds it by 2^8);
+//               P (f16) is written over the block's S columns.
 // The band of a 128 x 64 score tile covers offsets q0-k0-63 .. q0-k0+127 (191
 // R rows, loaded as 192).  Consecutive key blocks share all but 64 of them,
 // so R rows live in a 256-row ring and each key block loads one 64-row chunk.
@@ -31,8 +35,8 @@
 // The diagonal read: row i of the tile needs band column 127 - i + j for key
 // j, a window whose start moves by one column per row.  TMEM loads address
 // the same columns for all lanes of a warp, so each softmax thread parks its
-// lane's 96 loaded columns in a private shared-memory row and reads the 64 it
-// needs back at its own offset.
+// lane's loaded band columns in a private shared-memory row and reads the 32
+// it needs back at its own offset.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -48,28 +52,31 @@ namespace {
 
 constexpr int kBQ = 128;          // queries per CTA
 constexpr int kBK = 64;           // keys per block
-constexpr int kThreads = 192;     // warp 0 TMA, warp 1 MMA, warps 2..5 softmax
+constexpr int kThreads = 320;     // warp 0 TMA, warp 1 MMA, warps 2..9 softmax
+constexpr int kSoftThreads = 256;
 constexpr int kRing = 256;        // R ring rows
-constexpr int kShStride = 100;    // floats per row of the diagonal buffer (odd quads: conflict-free)
+constexpr int kShStride = 65;     // floats per softmax thread's diagonal row (odd: conflict-free)
 
 // shared memory (offsets from a 1024-aligned base)
-constexpr uint32_t kQvOff = 0;                   // Qv: 2 dim-halves x (128 rows x 128 B)
+constexpr uint32_t kQuOff = 0;                   // Qu: 2 dim-halves x (128 rows x 128 B)
 constexpr uint32_t kKOff = 32768;                // K: 2 stages x 2 halves x (64 rows x 128 B)
 constexpr uint32_t kVOff = kKOff + 32768;        // V: same
 constexpr uint32_t kROff = kVOff + 32768;        // R ring: 2 halves x (256 rows x 128 B)
-constexpr uint32_t kShOff = kROff + 65536;       // diagonal buffer 128 x 100 f32 (Qu staging first)
-constexpr uint32_t kBarOff = kShOff + kBQ * kShStride * 4;
+constexpr uint32_t kShOff = kROff + 65536;       // diagonal rows 256 x 65 f32 (Qv staging first)
+constexpr uint32_t kBarOff = kShOff + kSoftThreads * kShStride * 4;
 constexpr uint32_t kSmem = kBarOff + 256 + 1024;
-static_assert(kBQ * kShStride * 4 >= 32768, "Qu staging fits the diagonal buffer");
+static_assert(kSoftThreads * kShStride * 4 >= 32768, "Qv staging fits the diagonal rows");
 static_assert(kSmem <= 232448, "shared memory budget");
 
 // TMEM columns
 constexpr uint32_t kTS = 0;       // S / P, 2 buffers x 64
 constexpr uint32_t kTG = 128;     // band, 192
 constexpr uint32_t kTO = 320;     // O, 128
-constexpr uint32_t kTQ = 448;     // Qu (A operand), 64
+constexpr uint32_t kTQ = 448;     // Qv (A operand of the band GEMM), 64
 
 constexpr uint32_t kIdescS = idesc_f16_f32_b<128, 64, 0>();
+constexpr uint32_t kIdescG192 = idesc_f16_f32_b<128, 192, 0>();
+constexpr uint32_t kIdescG128 = idesc_f16_f32_b<128, 128, 0>();
 constexpr uint32_t kIdescPV = idesc_f16_f32_b<128, 128, 1>();
 
 __device__ __forceinline__ uint32_t h2u(float a, float b) {
@@ -78,7 +85,16 @@ __device__ __forceinline__ uint32_t h2u(float a, float b) {
 }
 
 __device__ __forceinline__ void named_sync_softmax() {
-    asm volatile("bar.sync 1, 128;" ::: "memory");
+    asm volatile("bar.sync 1, 256;" ::: "memory");
+}
+
+// The two softmax warps of a lane quarter meet on their mbarrier (one arrival
+// per warp; a bounded wait, so a warp that left early ends its partner's wait
+// with an error instead of a hang).
+__device__ __forceinline__ bool pair_exchange(uint64_t* bar, int lane, uint32_t parity, unsigned int site) {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(bar));
+    return mbar_wait(smem_u32(bar), parity, site);
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -87,21 +103,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
-    uint8_t* sQv = smem + kQvOff;
+    uint8_t* sQu = smem + kQuOff;
     uint8_t* sK = smem + kKOff;
     uint8_t* sV = smem + kVOff;
     uint8_t* sR = smem + kROff;
     float* sSh = reinterpret_cast<float*>(smem + kShOff);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBarOff);
-    uint64_t* kv_full = bars;        // [2]
-    uint64_t* kv_empty = bars + 2;   // [2]
-    uint64_t* qld = bars + 4;
-    uint64_t* q_tmem = bars + 5;
-    uint64_t* sg_full = bars + 6;
-    uint64_t* g_free = bars + 7;
-    uint64_t* p_ready = bars + 8;
-    uint64_t* o_ready = bars + 9;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+    // K + R chunk and V have separate 2-stage rings: a K / R stage is free
+    // again once the S and band MMAs that read it are done, long before the
+    // P.V that frees its V stage, so the next loads start a softmax earlier
+    uint64_t* kr_full = bars;        // [2]
+    uint64_t* kr_empty = bars + 2;   // [2]
+    uint64_t* v_full = bars + 4;     // [2]
+    uint64_t* v_empty = bars + 6;    // [2]
+    uint64_t* qld = bars + 8;
+    uint64_t* q_tmem = bars + 9;
+    uint64_t* sg_full = bars + 10;
+    uint64_t* g_free = bars + 11;
+    uint64_t* p_ready = bars + 12;
+    uint64_t* o_ready = bars + 13;   // every P.V (waited only when O is rescaled)
+    uint64_t* o_final = bars + 14;   // the last P.V
+    uint64_t* xchg = bars + 15;      // [4] softmax warp pairs
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -120,15 +143,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_prefetch_desc(&tm_kv);
         tma_prefetch_desc(&tm_r);
         for (int s = 0; s < 2; ++s) {
-            mbar_init(smem_u32(&kv_full[s]), 1);
-            mbar_init(smem_u32(&kv_empty[s]), 1);
+            mbar_init(smem_u32(&kr_full[s]), 1);
+            mbar_init(smem_u32(&kr_empty[s]), 1);
+            mbar_init(smem_u32(&v_full[s]), 1);
+            mbar_init(smem_u32(&v_empty[s]), 1);
         }
         mbar_init(smem_u32(qld), 1);
-        mbar_init(smem_u32(q_tmem), 4);
+        mbar_init(smem_u32(q_tmem), 8);
         mbar_init(smem_u32(sg_full), 1);
-        mbar_init(smem_u32(g_free), 4);
-        mbar_init(smem_u32(p_ready), 4);
+        mbar_init(smem_u32(g_free), 8);
+        mbar_init(smem_u32(p_ready), 8);
         mbar_init(smem_u32(o_ready), 1);
+        mbar_init(smem_u32(o_final), 1);
+        for (int c = 0; c < 4; ++c) mbar_init(smem_u32(&xchg[c]), 2);
         fence_mbar_init();
     }
     if (warp == 1) {
@@ -146,27 +173,37 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t qb = smem_u32(qld);
             mbar_arrive_expect_tx(qb, 4 * 16384);
             for (int h = 0; h < 2; ++h) {
-                tma_load_2d(smem_u32(sQv + h * 16384), &tm_q, qb, 1024 + head * 128 + h * 64, seg0 + q0);
-                tma_load_2d(smem_u32(reinterpret_cast<uint8_t*>(sSh) + h * 16384), &tm_q, qb, head * 128 + h * 64,
-                            seg0 + q0);
+                tma_load_2d(smem_u32(sQu + h * 16384), &tm_q, qb, head * 128 + h * 64, seg0 + q0);
+                tma_load_2d(smem_u32(reinterpret_cast<uint8_t*>(sSh) + h * 16384), &tm_q, qb,
+                            1024 + head * 128 + h * 64, seg0 + q0);
             }
-            for (int kb = 0; kb < nkb; ++kb) {
-                const int st = kb & 1;
-                if (kb >= 2 && !mbar_wait(smem_u32(&kv_empty[st]), ((kb >> 1) - 1) & 1, 0x21)) break;
-                const int nchunks = kb == 0 ? 3 : 1;
-                const uint32_t fb = smem_u32(&kv_full[st]);
-                mbar_arrive_expect_tx(fb, 2 * 16384 + nchunks * 16384);
-                const int krow = seg0 + kb * kBK;
-                for (int h = 0; h < 2; ++h) {
-                    tma_load_2d(smem_u32(sK + st * 16384 + h * 8192), &tm_kv, fb, 2048 + head * 128 + h * 64, krow);
-                    tma_load_2d(smem_u32(sV + st * 16384 + h * 8192), &tm_kv, fb, 3072 + head * 128 + h * 64, krow);
-                }
-                for (int c = (kb == 0 ? 0 : 2); c < 3; ++c) {
-                    const int rel = kb * kBK + c * 64;            // band row - r_lo0
-                    const uint32_t slot = static_cast<uint32_t>(rel) & (kRing - 1);
+            // in the order the MMAs need them: K / R of block kb, then V of kb - 1
+            for (int kb = 0; kb <= nkb; ++kb) {
+                if (kb < nkb) {
+                    const int st = kb & 1;
+                    if (kb >= 2 && !mbar_wait(smem_u32(&kr_empty[st]), ((kb >> 1) - 1) & 1, 0x21)) break;
+                    const int nchunks = kb == 0 ? 3 : 1;
+                    const uint32_t fb = smem_u32(&kr_full[st]);
+                    mbar_arrive_expect_tx(fb, 16384 + nchunks * 16384);
                     for (int h = 0; h < 2; ++h)
-                        tma_load_2d(smem_u32(sR + h * 32768 + slot * 128), &tm_r, fb, head * 128 + h * 64,
-                                    r_lo0 + rel);
+                        tma_load_2d(smem_u32(sK + st * 16384 + h * 8192), &tm_kv, fb, 2048 + head * 128 + h * 64,
+                                    seg0 + kb * kBK);
+                    for (int c = (kb == 0 ? 0 : 2); c < 3; ++c) {
+                        const int rel = kb * kBK + c * 64;            // band row - r_lo0
+                        const uint32_t slot = static_cast<uint32_t>(rel) & (kRing - 1);
+                        for (int h = 0; h < 2; ++h)
+                            tma_load_2d(smem_u32(sR + h * 32768 + slot * 128), &tm_r, fb, head * 128 + h * 64,
+                                        r_lo0 + rel);
+                    }
+                }
+                if (kb >= 1) {
+                    const int j = kb - 1, st = j & 1;
+                    if (j >= 2 && !mbar_wait(smem_u32(&v_empty[st]), ((j >> 1) - 1) & 1, 0x2D)) break;
+                    const uint32_t fb = smem_u32(&v_full[st]);
+                    mbar_arrive_expect_tx(fb, 16384);
+                    for (int h = 0; h < 2; ++h)
+                        tma_load_2d(smem_u32(sV + st * 16384 + h * 8192), &tm_kv, fb, 3072 + head * 128 + h * 64,
+                                    seg0 + j * kBK);
                 }
             }
         }
@@ -177,166 +214,202 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int kb = 0; kb <= nkb && ok; ++kb) {
                 if (kb < nkb) {
                     const int st = kb & 1;
-                    if (!(ok = mbar_wait(smem_u32(&kv_full[st]), (kb >> 1) & 1, 0x24))) break;
+                    if (!(ok = mbar_wait(smem_u32(&kr_full[st]), (kb >> 1) & 1, 0x24))) break;
                     if (kb >= 1 && !(ok = mbar_wait(smem_u32(g_free), (kb - 1) & 1, 0x25))) break;
                     tc_fence_after();
                     const uint32_t dS = tmem + kTS + 64 * st;
+                    // descriptors advance by 32 bytes (2 in the start-address field) per k-step
+                    const uint64_t aq0 = smem_desc_sw128(smem_u32(sQu));
+                    const uint64_t aq1 = smem_desc_sw128(smem_u32(sQu + 16384));
+                    const uint64_t bk0 = smem_desc_sw128(smem_u32(sK + st * 16384));
+                    const uint64_t bk1 = smem_desc_sw128(smem_u32(sK + st * 16384 + 8192));
 #pragma unroll
-                    for (int kk = 0; kk < 8; ++kk) {
-                        const uint64_t bd = smem_desc_sw128(smem_u32(sK + st * 16384 + (kk >> 2) * 8192) + (kk & 3) * 32);
-                        mma_f16_ts(dS, tmem + kTQ + 8 * kk, bd, kIdescS, kk > 0);
-                    }
+                    for (int kk = 0; kk < 8; ++kk)
+                        mma_f16_ss(dS, (kk < 4 ? aq0 : aq1) + 2 * (kk & 3), (kk < 4 ? bk0 : bk1) + 2 * (kk & 3), kIdescS,
+                                   kk > 0);
+                    // band rows [64 kb, 64 kb + 192) of the ring: one N192 piece when contiguous,
+                    // else N128 + N64 or N64 + N128 around the wrap
+                    const uint32_t s0 = static_cast<uint32_t>(kb * kBK) & (kRing - 1);
+                    const int n1 = s0 <= kRing - 192 ? 192 : static_cast<int>(kRing - s0);
+                    const uint64_t br0 = smem_desc_sw128(smem_u32(sR + s0 * 128));
+                    const uint64_t br1 = smem_desc_sw128(smem_u32(sR + 32768 + s0 * 128));
 #pragma unroll
-                    for (int c = 0; c < 3; ++c) {
-                        const uint32_t slot = static_cast<uint32_t>(kb * kBK + c * 64) & (kRing - 1);
+                    for (int kk = 0; kk < 8; ++kk)
+                        mma_f16_ts(tmem + kTG, tmem + kTQ + 8 * kk, (kk < 4 ? br0 : br1) + 2 * (kk & 3),
+                                   n1 == 192 ? kIdescG192 : (n1 == 128 ? kIdescG128 : kIdescS), kk > 0);
+                    if (n1 < 192) {
+                        const uint64_t bw0 = smem_desc_sw128(smem_u32(sR));
+                        const uint64_t bw1 = smem_desc_sw128(smem_u32(sR + 32768));
 #pragma unroll
-                        for (int kk = 0; kk < 8; ++kk) {
-                            const uint64_t ad = smem_desc_sw128(smem_u32(sQv + (kk >> 2) * 16384) + (kk & 3) * 32);
-                            const uint64_t bd =
-                                smem_desc_sw128(smem_u32(sR + (kk >> 2) * 32768 + slot * 128) + (kk & 3) * 32);
-                            mma_f16_ss(tmem + kTG + 64 * c, ad, bd, kIdescS, kk > 0);
-                        }
+                        for (int kk = 0; kk < 8; ++kk)
+                            mma_f16_ts(tmem + kTG + n1, tmem + kTQ + 8 * kk, (kk < 4 ? bw0 : bw1) + 2 * (kk & 3),
+                                       n1 == 128 ? kIdescS : kIdescG128, kk > 0);
                     }
                     mma_commit(smem_u32(sg_full));
+                    mma_commit(smem_u32(&kr_empty[st]));
                 }
                 if (kb >= 1) {
                     const int j = kb - 1, st = j & 1;
                     if (!(ok = mbar_wait(smem_u32(p_ready), j & 1, 0x26))) break;
+                    if (!(ok = mbar_wait(smem_u32(&v_full[st]), (j >> 1) & 1, 0x2E))) break;
                     tc_fence_after();
+                    // V [64 keys][128 dims] as the MN-major B operand: 64-dim halves 8 KB
+                    // apart, 8-key atoms 1 KB apart, 16 keys (2 KB) per MMA
+                    const uint64_t bv = smem_desc_sw128_mn(smem_u32(sV + st * 16384), 8192, 1024);
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk) {
-                        // V [64 keys][128 dims] as the MN-major B operand: 64-dim halves 8 KB
-                        // apart, 8-key atoms 1 KB apart, 16 keys per MMA
-                        const uint64_t bd = smem_desc_sw128_mn(smem_u32(sV + st * 16384) + kk * 2048, 8192, 1024);
-                        mma_f16_ts(tmem + kTO, tmem + kTS + 64 * st + 8 * kk, bd, kIdescPV, (j > 0 || kk > 0));
-                    }
+                    for (int kk = 0; kk < 4; ++kk)
+                        mma_f16_ts(tmem + kTO, tmem + kTS + 64 * st + 8 * kk, bv + 128 * kk, kIdescPV, (j > 0 || kk > 0));
                     mma_commit(smem_u32(o_ready));
-                    mma_commit(smem_u32(&kv_empty[st]));
+                    mma_commit(smem_u32(&v_empty[st]));
+                    if (j == nkb - 1) mma_commit(smem_u32(o_final));
                 }
             }
         }
     } else {
-        // ── softmax: thread = query row i (TMEM lane) ──
+        // ── softmax: warps 2..9, pair (q, hf): lane quarter q, key half hf ──
         const int q = warp & 3;
-        const int i = q * 32 + lane;
+        const int hf = (warp - 2) >> 2;
+        const int i = q * 32 + lane;                   // query row / TMEM lane
+        const int t = (warp - 2) * 32 + lane;          // diagonal row
+        const int tp = t ^ 128;                        // the pair partner's diagonal row
         const uint32_t lrow = static_cast<uint32_t>(q * 32) << 16;
-        // Qu row i: staging (two 128-byte-swizzled dim halves) -> TMEM columns kTQ..kTQ+63
+        // Qv row i, dim half hf: staging -> TMEM columns kTQ + 32 hf
         bool ok = mbar_wait(smem_u32(qld), 0, 0x27);
         if (ok) {
-            for (int h = 0; h < 2; ++h) {
-                uint32_t r[32];
-                const uint8_t* row = reinterpret_cast<const uint8_t*>(sSh) + h * 16384 + i * 128;
+            uint32_t r[32];
+            const uint8_t* row = reinterpret_cast<const uint8_t*>(sSh) + hf * 16384 + i * 128;
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    const uint4 v = *reinterpret_cast<const uint4*>(row + ((c ^ (i & 7)) << 4));
-                    r[4 * c] = v.x;
-                    r[4 * c + 1] = v.y;
-                    r[4 * c + 2] = v.z;
-                    r[4 * c + 3] = v.w;
-                }
-                tmem_st_32x32b_x32(tmem + lrow + kTQ + 32 * h, r);
+            for (int c = 0; c < 8; ++c) {
+                const uint4 v = *reinterpret_cast<const uint4*>(row + ((c ^ (i & 7)) << 4));
+                r[4 * c] = v.x;
+                r[4 * c + 1] = v.y;
+                r[4 * c + 2] = v.z;
+                r[4 * c + 3] = v.w;
             }
+            tmem_st_32x32b_x32(tmem + lrow + kTQ + 32 * hf, r);
             tmem_wait_st();
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(q_tmem));
-        named_sync_softmax();   // the staging area becomes the diagonal buffer
-        float* sh = sSh + i * kShStride;
-        float m_run = -INFINITY, l_run = 0.f;
+        named_sync_softmax();   // the staging area becomes the diagonal rows
+        float* sh = sSh + t * kShStride;
+        const float* shp = sSh + tp * kShStride;
+        // m_use: the max the row's exponentials are taken against.  It moves
+        // (and O, l are rescaled) only when a block's max exceeds it by more
+        // than kRescale (log2 units), for the pair of warps as a whole; in
+        // between, probabilities up to 2^kRescale are exact in f32 l and in
+        // the f16 P operand.
+        constexpr float kRescale = 8.0f;
+        float m_use = -INFINITY, l_half = 0.f;
         for (int kb = 0; kb < nkb && ok; ++kb) {
             const int st = kb & 1;
             if (!(ok = mbar_wait(smem_u32(sg_full), kb & 1, 0x28))) break;
             tc_fence_after();
-            float s[64];
+            float s[32];
             {
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(tmem + lrow + kTS + 64 * st, r);
+                // S columns [32 hf, 32 hf + 32) and band columns [96 - 32q + 32hf, +64): one wait
+                uint32_t r0[32], g0[32], g1[32];
+                tmem_ld_32x32b_x32(tmem + lrow + kTS + 64 * st + 32 * hf, r0);
+                tmem_ld_32x32b_x32(tmem + lrow + kTG + 96 - 32 * q + 32 * hf, g0);
+                tmem_ld_32x32b_x32(tmem + lrow + kTG + 128 - 32 * q + 32 * hf, g1);
                 tmem_wait_ld();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(g_free));
 #pragma unroll
-                for (int e = 0; e < 32; ++e) s[e] = __uint_as_float(r[e]);
-                tmem_ld_32x32b_x32(tmem + lrow + kTS + 64 * st + 32, r);
-                tmem_wait_ld();
+                for (int e = 0; e < 32; ++e) s[e] = __uint_as_float(r0[e]);
+                // window column c (0..62 are used) goes to position (c + lane) mod 64:
+                // the columns a row needs, 31 - lane + j, then sit at 31 + j for every
+                // lane (conflict-free reads at the odd row stride); position
+                // (63 + lane) mod 64 and position 64 stay free for the pair exchange
 #pragma unroll
-                for (int e = 0; e < 32; ++e) s[32 + e] = __uint_as_float(r[e]);
+                for (int e = 0; e < 32; ++e) sh[(e + lane) & 63] = __uint_as_float(g0[e]);
+#pragma unroll
+                for (int e = 0; e < 31; ++e) sh[(32 + e + lane) & 63] = __uint_as_float(g1[e]);
             }
-            // this warp's band window: columns [96 - 32q, 192 - 32q)
+            // row i, key 32 hf + j: band column 127 - i + 32 hf + j = window column 31 - lane + j
+            const float* dg = sh + 31;
+            const int kvalid = T - kb * kBK - 32 * hf;
+            float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-            for (int c = 0; c < 3; ++c) {
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(tmem + lrow + kTG + 96 - 32 * q + 32 * c, r);
-                tmem_wait_ld();
-#pragma unroll
-                for (int e = 0; e < 32; e += 4)
-                    *reinterpret_cast<float4*>(sh + 32 * c + e) =
-                        make_float4(__uint_as_float(r[e]), __uint_as_float(r[e + 1]), __uint_as_float(r[e + 2]),
-                                    __uint_as_float(r[e + 3]));
-            }
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(g_free));
-            // row i, key j: band column 127 - i + j = window column 31 - lane + j
-            const float* dg = sh + 31 - lane;
-            const int kvalid = T - kb * kBK;
-            float mloc = -INFINITY;
-#pragma unroll
-            for (int j = 0; j < 64; ++j) {
+            for (int j = 0; j < 32; ++j) {
                 float v = (s[j] + dg[j]) * p.scale_log2;
                 if (j >= kvalid) v = -INFINITY;
                 s[j] = v;
-                mloc = fmaxf(mloc, v);
+                mx[j & 3] = fmaxf(mx[j & 3], v);
             }
-            const float m_new = fmaxf(m_run, mloc);
-            const float corr = exp2f(m_run - m_new);
-            float lsum = 0.f;
-            uint32_t pk[32];
-#pragma unroll
-            for (int j = 0; j < 64; j += 2) {
-                const float a = exp2f(s[j] - m_new), b = exp2f(s[j + 1] - m_new);
-                lsum += a + b;
-                pk[j >> 1] = h2u(a, b);
-            }
-            l_run = l_run * corr + lsum;
-            m_run = m_new;
-            if (kb >= 1) {
-                // O (after P_{kb-1} V) *= corr
-                if (!(ok = mbar_wait(smem_u32(o_ready), (kb - 1) & 1, 0x29))) break;
-                tc_fence_after();
-#pragma unroll 1
-                for (int c = 0; c < 4; ++c) {
-                    uint32_t r[32];
-                    tmem_ld_32x32b_x32(tmem + lrow + kTO + 32 * c, r);
+            const float mloc = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+            const int xs = st ? 64 : ((63 + lane) & 63);   // exchange slot, by block parity
+            sh[xs] = mloc;
+            if (!(ok = pair_exchange(&xchg[q], lane, kb & 1, 0x2B))) break;
+            const float m_blk = fmaxf(mloc, shp[xs]);
+            const bool grow = m_blk > m_use + kRescale;
+            float corr = 1.f;
+            if (__any_sync(0xffffffffu, grow)) {
+                const float m_new = grow ? m_blk : m_use;
+                corr = exp2f(m_use - m_new);   // 0 for the first block
+                m_use = m_new;
+                if (kb >= 1) {
+                    // O columns [64 hf, 64 hf + 64) (after P_{kb-1} V) *= corr.
+                    // Passing sg_full(kb) implies P_{kb-2} V is done and P_kb V is not
+                    // issued yet, so o_ready is at phase kb-1 or kb: the parity is exact.
+                    if (!(ok = mbar_wait(smem_u32(o_ready), (kb - 1) & 1, 0x29))) break;
+                    tc_fence_after();
+                    uint32_t o0[32], o1[32];
+                    tmem_ld_32x32b_x32(tmem + lrow + kTO + 64 * hf, o0);
+                    tmem_ld_32x32b_x32(tmem + lrow + kTO + 64 * hf + 32, o1);
                     tmem_wait_ld();
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * corr);
-                    tmem_st_32x32b_x32(tmem + lrow + kTO + 32 * c, r);
+                    for (int e = 0; e < 32; ++e) {
+                        o0[e] = __float_as_uint(__uint_as_float(o0[e]) * corr);
+                        o1[e] = __float_as_uint(__uint_as_float(o1[e]) * corr);
+                    }
+                    tmem_st_32x32b_x32(tmem + lrow + kTO + 64 * hf, o0);
+                    tmem_st_32x32b_x32(tmem + lrow + kTO + 64 * hf + 32, o1);
                 }
             }
-            tmem_st_32x32b_x32(tmem + lrow + kTS + 64 * st, pk);   // P over this block's S columns
+            float ls[4] = {0.f, 0.f, 0.f, 0.f};
+            uint32_t pk[16];
+#pragma unroll
+            for (int j = 0; j < 32; j += 2) {
+                const float a = exp2f(s[j] - m_use), b = exp2f(s[j + 1] - m_use);
+                ls[(j >> 1) & 3] += a + b;
+                pk[j >> 1] = h2u(a, b);
+            }
+            l_half = l_half * corr + ((ls[0] + ls[1]) + (ls[2] + ls[3]));
+            tmem_st_32x32b_x16(tmem + lrow + kTS + 64 * st + 16 * hf, pk);   // P over this block's S columns
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(smem_u32(p_ready));
         }
-        // ── O / l -> f16 row ──
-        if (ok && nkb > 0 && mbar_wait(smem_u32(o_ready), (nkb - 1) & 1, 0x2A)) {
+        // ── O / l -> f16 row, columns [64 hf, 64 hf + 64) ──
+        if (ok && nkb > 0 && mbar_wait(smem_u32(o_final), 0, 0x2A)) {
             tc_fence_after();
-            const float inv = 1.0f / l_run;
-            const bool store = q0 + i < T;
-            __half* dst = p.out + static_cast<size_t>(seg0 + q0 + i) * 1024 + head * 128;
-#pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(tmem + lrow + kTO + 32 * c, r);
-                tmem_wait_ld();
-                if (store) {
+            const int xs = (nkb & 1) ? 64 : ((63 + lane) & 63);   // the slot the last block did not use
+            sh[xs] = l_half;
+            const bool xok = pair_exchange(&xchg[q], lane, nkb & 1, 0x2C);
+            const float inv = 1.0f / (l_half + shp[xs]);
+            const bool store = xok && q0 + i < T;
+            __half* dst = p.out + static_cast<size_t>(seg0 + q0 + i) * 1024 + head * 128 + 64 * hf;
+            uint32_t o0[32], o1[32];
+            tmem_ld_32x32b_x32(tmem + lrow + kTO + 64 * hf, o0);
+            tmem_ld_32x32b_x32(tmem + lrow + kTO + 64 * hf + 32, o1);
+            tmem_wait_ld();
+            if (store) {
 #pragma unroll
-                    for (int e = 0; e < 32; e += 8)
-                        *reinterpret_cast<uint4*>(dst + 32 * c + e) =
-                            make_uint4(h2u(__uint_as_float(r[e]) * inv, __uint_as_float(r[e + 1]) * inv),
-                                       h2u(__uint_as_float(r[e + 2]) * inv, __uint_as_float(r[e + 3]) * inv),
-                                       h2u(__uint_as_float(r[e + 4]) * inv, __uint_as_float(r[e + 5]) * inv),
-                                       h2u(__uint_as_float(r[e + 6]) * inv, __uint_as_float(r[e + 7]) * inv));
+                for (int e = 0; e < 32; e += 8) {
+                    *reinterpret_cast<uint4*>(dst + e) =
+                        make_uint4(h2u(__uint_as_float(o0[e]) * inv, __uint_as_float(o0[e + 1]) * inv),
+                                   h2u(__uint_as_float(o0[e + 2]) * inv, __uint_as_float(o0[e + 3]) * inv),
+                                   h2u(__uint_as_float(o0[e + 4]) * inv, __uint_as_float(o0[e + 5]) * inv),
+                                   h2u(__uint_as_float(o0[e + 6]) * inv, __uint_as_float(o0[e + 7]) * inv));
+                    *reinterpret_cast<uint4*>(dst + 32 + e) =
+                        make_uint4(h2u(__uint_as_float(o1[e]) * inv, __uint_as_float(o1[e + 1]) * inv),
+                                   h2u(__uint_as_float(o1[e + 2]) * inv, __uint_as_float(o1[e + 3]) * inv),
+                                   h2u(__uint_as_float(o1[e + 4]) * inv, __uint_as_float(o1[e + 5]) * inv),
+                                   h2u(__uint_as_float(o1[e + 6]) * inv, __uint_as_float(o1[e + 7]) * inv));
                 }
             }
         }
