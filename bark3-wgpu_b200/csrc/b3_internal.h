@@ -46,6 +46,7 @@ struct GemmParams {
     // 0 or 1 = no split.
     int ksplit;
     int tiles;                // 0 = by size, 1 = 128 x 64 tiles, 2 = 256 x 128 tiles, 3 = 256 x 256 on CTA pairs
+    int pdl;                  // launch with programmatic stream serialization (single-CTA tiles)
 };
 
 struct GemmOp {

@@ -295,6 +295,17 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32_b() {
            (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// ───────────────────── programmatic dependent launch ─────────────────────
+// A kernel launched with programmatic stream serialization may start while
+// the previous kernel on the stream is still running: it must not touch
+// global memory the previous kernel writes (or reads) before pdl_wait(),
+// which returns once that kernel has completed and its writes are visible.
+// Without the launch attribute both are no-ops.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ─────────────────────── CTA pairs (cta_group::2) ───────────────────────
 // A cluster of two CTAs on two SMs shares one MMA: the even CTA (rank 0)
 // issues it, each CTA holds half of A (its 128 rows) and half of B (its N/2

@@ -851,6 +851,7 @@ GemmParams dec_params(float* out, int ldo, const float* bias, const DecPlan& pl,
     GemmParams p = params_f32(out, ldo, bias);
     p.ksplit = pl.ks[i];
     p.tiles = pl.tiles[i];
+    p.pdl = 1;
     return p;
 }
 

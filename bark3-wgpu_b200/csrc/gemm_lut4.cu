@@ -80,14 +80,18 @@ __device__ __forceinline__ uint32_t pack_h2(float a, float b) {
 // lo[q] / hi[q] hold the low / high bytes of entries 4q..4q+3.
 __device__ __forceinline__ void lut_expand8(uint32_t w, const uint32_t (&lo)[4],
                                             const uint32_t (&hi)[4], uint32_t (&out)[4]) {
+    // index within 8 entries for all eight nibbles at once (PRMT reads only
+    // the low 16 bits of its selector, so half 1 takes the upper half shifted)
+    const uint32_t s3a = w & 0x77777777u;
+    const uint32_t s3[2] = {s3a, s3a >> 16};
+    // byte i of m[h] = 0xFF where nibble i of half h is >= 8: the sign bit of
+    // the byte holding that nibble's bit 3 (w for odd nibbles, w << 4 for even)
+    const uint32_t w4 = w << 4;
+    const uint32_t m[2] = {prmt(w, w4, 0x9D8Cu), prmt(w, w4, 0xBFAEu)};
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
-        const uint32_t sel = half ? (w >> 16) : w;  // four 4-bit indices
-        const uint32_t s3 = sel & 0x7777u;          // index within 8 entries
-        // byte i = 0xFF where index i >= 8 (bit 3 of nibble i, sign-replicated)
-        const uint32_t m = prmt(sel, sel << 4, 0x9D8Cu);
-        const uint32_t l = bitsel(prmt(lo[0], lo[1], s3), prmt(lo[2], lo[3], s3), m);
-        const uint32_t h = bitsel(prmt(hi[0], hi[1], s3), prmt(hi[2], hi[3], s3), m);
+        const uint32_t l = bitsel(prmt(lo[0], lo[1], s3[half]), prmt(lo[2], lo[3], s3[half]), m[half]);
+        const uint32_t h = bitsel(prmt(hi[0], hi[1], s3[half]), prmt(hi[2], hi[3], s3[half]), m[half]);
         out[2 * half + 0] = prmt(l, h, 0x5140u);  // f16 of columns 0,1 of this half
         out[2 * half + 1] = prmt(l, h, 0x7362u);  // columns 2,3
     }
@@ -307,6 +311,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // everything above touches only this CTA's shared memory and TMEM
+    pdl_wait();
+    pdl_launch_dependents();
 
     if (warp == 0) {
         // ── TMA producer ──
@@ -750,8 +757,17 @@ int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p
     if (rc) return rc;
     const int tiles = (p.N / BN) * ((p.M + SUB * kBM - 1) / (SUB * kBM)) * ksplit;
     const int grid = tiles < g_num_sms ? tiles : g_num_sms;
-    kern<<<grid, kThreads, Cfg::kSmemBytes, st>>>(ta, tb, tc, p);
-    cudaError_t e = cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = p.pdl ? 1 : 0;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, tc, p);
     if (e != cudaSuccess) return set_cuda_error("k1_gemm launch", e);
     return 0;
 }

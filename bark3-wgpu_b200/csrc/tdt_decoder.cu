@@ -29,6 +29,7 @@
 
 #include "b3_internal.h"
 #include "b3_kernels.h"
+#include "b3_ptx.cuh"
 
 namespace b3 {
 
@@ -97,6 +98,8 @@ __device__ __forceinline__ void split_store4(__half* hi, __half* lo, float4 v) {
 // Initial state: h = c = 0, every row runs one LSTM step on the blank
 // embedding (src/tdt.rs:424-428).
 __global__ void k_dec_init(DecState s) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int b = blockIdx.x;
     if (b >= s.B) return;
     const int T = s.cu[b + 1] - s.cu[b];
@@ -124,6 +127,8 @@ __global__ void k_dec_init(DecState s) {
 // x_b = ReLU(enc[frame_b] + dec_b), split into hi | lo (zeros for finished
 // rows).  One block of 160 threads per row, 4 columns per thread.
 __global__ void __launch_bounds__(160) k_dec_joint_in(DecState s) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int b = blockIdx.x;
     if (b >= s.B) return;
     const int j = 4 * threadIdx.x;
@@ -160,6 +165,8 @@ __device__ __forceinline__ void warp_argmax(float& v, int& i) {
 // 256 threads per utterance; each thread scans 4 consecutive vocabulary
 // entries per 1024-wide chunk; ties keep the lowest index.
 __global__ void __launch_bounds__(256) k_dec_argmax(DecState s) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int b = blockIdx.x;
     if (b >= s.B) return;
     __shared__ float wv[8];
@@ -238,6 +245,8 @@ __global__ void __launch_bounds__(256) k_dec_argmax(DecState s) {
 // LSTM cell update for rows that emitted: gates [B][2560] (i, f, g, o).
 // One block of 160 threads per row, 4 columns per thread.
 __global__ void __launch_bounds__(160) k_dec_lstm_update(DecState s, int layer) {
+    pdl_wait();
+    pdl_launch_dependents();
     const int b = blockIdx.x;
     if (b >= s.B || !s.emit[b]) return;
     const int j = 4 * threadIdx.x;
@@ -280,6 +289,8 @@ __global__ void __launch_bounds__(160) k_dec_lstm_update(DecState s, int layer) 
 }
 
 __global__ void k_dec_any_active(const int* active, int B, int* out) {
+    pdl_wait();
+    pdl_launch_dependents();
     __shared__ int any;
     if (threadIdx.x == 0) any = 0;
     __syncthreads();
@@ -305,25 +316,40 @@ int check_launch(const char* what) {
 
 int dec_max_parts() { return kMaxParts; }
 
+// The step kernels are launched with programmatic stream serialization: each
+// one's CTAs are scheduled while its predecessor drains and wait in pdl_wait()
+// for its results.
+template <typename... Args>
+int launch_pdl(void (*kern)(Args...), dim3 grid, dim3 block, cudaStream_t st, const char* what, Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, args...);
+    return e == cudaSuccess ? 0 : set_cuda_error(what, e);
+}
+
 int dec_launch_init(const DecState& s, cudaStream_t st) {
-    k_dec_init<<<s.B, 128, 0, st>>>(s);
-    return check_launch("k_dec_init");
+    return launch_pdl(k_dec_init, dim3(s.B), dim3(128), st, "k_dec_init", s);
 }
 int dec_launch_joint_in(const DecState& s, cudaStream_t st) {
-    k_dec_joint_in<<<s.B, kH / 4, 0, st>>>(s);
-    return check_launch("k_dec_joint_in");
+    return launch_pdl(k_dec_joint_in, dim3(s.B), dim3(kH / 4), st, "k_dec_joint_in", s);
 }
 int dec_launch_argmax(const DecState& s, cudaStream_t st) {
-    k_dec_argmax<<<s.B, 256, 0, st>>>(s);
-    return check_launch("k_dec_argmax");
+    return launch_pdl(k_dec_argmax, dim3(s.B), dim3(256), st, "k_dec_argmax", s);
 }
 int dec_launch_lstm_update(const DecState& s, int layer, cudaStream_t st) {
-    k_dec_lstm_update<<<s.B, kH / 4, 0, st>>>(s, layer);
-    return check_launch("k_dec_lstm_update");
+    return launch_pdl(k_dec_lstm_update, dim3(s.B), dim3(kH / 4), st, "k_dec_lstm_update", s, layer);
 }
 int dec_launch_any_active(const DecState& s, int* out, cudaStream_t st) {
-    k_dec_any_active<<<1, 256, 0, st>>>(s.active, s.B, out);
-    return check_launch("k_dec_any_active");
+    return launch_pdl(k_dec_any_active, dim3(1), dim3(256), st, "k_dec_any_active", static_cast<const int*>(s.active),
+                      s.B, out);
 }
 int dec_launch_split(const float* src, __half* hi, __half* lo, int64_t n, cudaStream_t st) {
     int blocks = static_cast<int>((n + 255) / 256);
