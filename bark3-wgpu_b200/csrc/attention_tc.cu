@@ -84,10 +84,6 @@ __device__ __forceinline__ uint32_t h2u(float a, float b) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
-__device__ __forceinline__ void named_sync_softmax() {
-    asm volatile("bar.sync 1, 256;" ::: "memory");
-}
-
 // The two softmax warps of a lane quarter meet on their mbarrier (one arrival
 // per warp; a bounded wait, so a warp that left early ends its partner's wait
 // with an error instead of a hang).
@@ -99,7 +95,7 @@ __device__ __forceinline__ bool pair_exchange(uint64_t* bar, int lane, uint32_t 
 
 __global__ void __launch_bounds__(kThreads, 1)
     k2_relpos_attention_tc(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_kv,
-                           const __grid_constant__ CUtensorMap tm_r, const AttnParams p) {
+                           const __grid_constant__ CUtensorMap tm_r, const AttnParams p, int n_items) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
@@ -111,32 +107,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBarOff);
     // K + R chunk and V have separate 2-stage rings: a K / R stage is free
     // again once the S and band MMAs that read it are done, long before the
-    // P.V that frees its V stage, so the next loads start a softmax earlier
+    // P.V that frees its V stage, so the next loads start a softmax earlier.
+    // Every phase is counted over the CTA's whole run (g = key block, n =
+    // item, x = pair exchange), so the rings keep prefetching across items.
     uint64_t* kr_full = bars;        // [2]
     uint64_t* kr_empty = bars + 2;   // [2]
     uint64_t* v_full = bars + 4;     // [2]
     uint64_t* v_empty = bars + 6;    // [2]
-    uint64_t* qld = bars + 8;
-    uint64_t* q_tmem = bars + 9;
+    uint64_t* qld = bars + 8;        // Qu of item n in shared memory
+    uint64_t* q_tmem = bars + 9;     // Qv of item n in TMEM
     uint64_t* sg_full = bars + 10;
     uint64_t* g_free = bars + 11;
     uint64_t* p_ready = bars + 12;
     uint64_t* o_ready = bars + 13;   // every P.V (waited only when O is rescaled)
-    uint64_t* o_final = bars + 14;   // the last P.V
+    uint64_t* o_final = bars + 14;   // the last P.V of an item
     uint64_t* xchg = bars + 15;      // [4] softmax warp pairs
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
-    const int head = blockIdx.y;
-    const int2 wk = p.work[blockIdx.x];
-    const int seg0 = p.cu[wk.x];
-    const int T = p.cu[wk.x + 1] - seg0;
-    const int q0 = wk.y;
-    const int nkb = (T + kBK - 1) / kBK;
-    // band of key block kb: R rows [r_lo0 + 64 kb, r_lo0 + 64 kb + 191]; ring
-    // slot of R row r is (r - r_lo0) mod 256, so every 64-row chunk is contiguous
-    const int r_lo0 = p.r_center - q0 - (kBQ - 1);
 
     if (threadIdx.x == 0) {
         tma_prefetch_desc(&tm_q);
@@ -167,102 +156,134 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
 
+    // item i: work entry i / 8 (utterance, first query), head i % 8
+    struct Item {
+        int seg0, T, q0, head, nkb, r_lo0;
+    };
+    auto item = [&](int i) {
+        Item it;
+        const int2 wk = p.work[i >> 3];
+        it.head = i & 7;
+        it.seg0 = p.cu[wk.x];
+        it.T = p.cu[wk.x + 1] - it.seg0;
+        it.q0 = wk.y;
+        it.nkb = (it.T + kBK - 1) / kBK;
+        // band of key block kb: R rows [r_lo0 + 64 kb, r_lo0 + 64 kb + 191]; ring
+        // slot of R row r is (r - r_lo0) mod 256, so every 64-row chunk is contiguous
+        it.r_lo0 = p.r_center - it.q0 - (kBQ - 1);
+        return it;
+    };
+
     if (warp == 0) {
         // ── TMA producer ──
         if (lane == 0) {
-            const uint32_t qb = smem_u32(qld);
-            mbar_arrive_expect_tx(qb, 4 * 16384);
-            for (int h = 0; h < 2; ++h) {
-                tma_load_2d(smem_u32(sQu + h * 16384), &tm_q, qb, head * 128 + h * 64, seg0 + q0);
-                tma_load_2d(smem_u32(reinterpret_cast<uint8_t*>(sSh) + h * 16384), &tm_q, qb,
-                            1024 + head * 128 + h * 64, seg0 + q0);
-            }
-            // in the order the MMAs need them: K / R of block kb, then V of kb - 1
-            for (int kb = 0; kb <= nkb; ++kb) {
-                if (kb < nkb) {
-                    const int st = kb & 1;
-                    if (kb >= 2 && !mbar_wait(smem_u32(&kr_empty[st]), ((kb >> 1) - 1) & 1, 0x21)) break;
-                    const int nchunks = kb == 0 ? 3 : 1;
-                    const uint32_t fb = smem_u32(&kr_full[st]);
-                    mbar_arrive_expect_tx(fb, 16384 + nchunks * 16384);
-                    for (int h = 0; h < 2; ++h)
-                        tma_load_2d(smem_u32(sK + st * 16384 + h * 8192), &tm_kv, fb, 2048 + head * 128 + h * 64,
-                                    seg0 + kb * kBK);
-                    for (int c = (kb == 0 ? 0 : 2); c < 3; ++c) {
-                        const int rel = kb * kBK + c * 64;            // band row - r_lo0
-                        const uint32_t slot = static_cast<uint32_t>(rel) & (kRing - 1);
+            int g0 = 0, n = 0;
+            bool ok = true;
+            for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++n) {
+                const Item it = item(i);
+                // Qu and the item's first R rows reuse shared memory that the previous
+                // item's last S / band MMAs read: wait for those (block g0 - 1)
+                if (g0 >= 1 && !(ok = mbar_wait(smem_u32(&kr_empty[(g0 - 1) & 1]), ((g0 - 1) >> 1) & 1, 0x20)))
+                    break;
+                const uint32_t qb = smem_u32(qld);
+                mbar_arrive_expect_tx(qb, 2 * 16384);
+                for (int h = 0; h < 2; ++h)
+                    tma_load_2d(smem_u32(sQu + h * 16384), &tm_q, qb, it.head * 128 + h * 64, it.seg0 + it.q0);
+                // in the order the MMAs need them: K / R of block kb, then V of kb - 1
+                for (int kb = 0; kb <= it.nkb; ++kb) {
+                    if (kb < it.nkb) {
+                        const int g = g0 + kb, st = g & 1;
+                        if (g >= 2 && !(ok = mbar_wait(smem_u32(&kr_empty[st]), ((g >> 1) - 1) & 1, 0x21))) break;
+                        const int nchunks = kb == 0 ? 3 : 1;
+                        const uint32_t fb = smem_u32(&kr_full[st]);
+                        mbar_arrive_expect_tx(fb, 16384 + nchunks * 16384);
                         for (int h = 0; h < 2; ++h)
-                            tma_load_2d(smem_u32(sR + h * 32768 + slot * 128), &tm_r, fb, head * 128 + h * 64,
-                                        r_lo0 + rel);
+                            tma_load_2d(smem_u32(sK + st * 16384 + h * 8192), &tm_kv, fb,
+                                        2048 + it.head * 128 + h * 64, it.seg0 + kb * kBK);
+                        for (int c = (kb == 0 ? 0 : 2); c < 3; ++c) {
+                            const int rel = kb * kBK + c * 64;            // band row - r_lo0
+                            const uint32_t slot = static_cast<uint32_t>(rel) & (kRing - 1);
+                            for (int h = 0; h < 2; ++h)
+                                tma_load_2d(smem_u32(sR + h * 32768 + slot * 128), &tm_r, fb, it.head * 128 + h * 64,
+                                            it.r_lo0 + rel);
+                        }
+                    }
+                    if (kb >= 1) {
+                        const int gv = g0 + kb - 1, st = gv & 1;
+                        if (gv >= 2 && !(ok = mbar_wait(smem_u32(&v_empty[st]), ((gv >> 1) - 1) & 1, 0x2D))) break;
+                        const uint32_t fb = smem_u32(&v_full[st]);
+                        mbar_arrive_expect_tx(fb, 16384);
+                        for (int h = 0; h < 2; ++h)
+                            tma_load_2d(smem_u32(sV + st * 16384 + h * 8192), &tm_kv, fb,
+                                        3072 + it.head * 128 + h * 64, it.seg0 + (kb - 1) * kBK);
                     }
                 }
-                if (kb >= 1) {
-                    const int j = kb - 1, st = j & 1;
-                    if (j >= 2 && !mbar_wait(smem_u32(&v_empty[st]), ((j >> 1) - 1) & 1, 0x2D)) break;
-                    const uint32_t fb = smem_u32(&v_full[st]);
-                    mbar_arrive_expect_tx(fb, 16384);
-                    for (int h = 0; h < 2; ++h)
-                        tma_load_2d(smem_u32(sV + st * 16384 + h * 8192), &tm_kv, fb, 3072 + head * 128 + h * 64,
-                                    seg0 + j * kBK);
-                }
+                g0 += it.nkb;
             }
         }
     } else if (warp == 1) {
         // ── MMA issuer ──
         if (lane == 0) {
-            bool ok = mbar_wait(smem_u32(qld), 0, 0x22) && mbar_wait(smem_u32(q_tmem), 0, 0x23);
-            for (int kb = 0; kb <= nkb && ok; ++kb) {
-                if (kb < nkb) {
-                    const int st = kb & 1;
-                    if (!(ok = mbar_wait(smem_u32(&kr_full[st]), (kb >> 1) & 1, 0x24))) break;
-                    if (kb >= 1 && !(ok = mbar_wait(smem_u32(g_free), (kb - 1) & 1, 0x25))) break;
-                    tc_fence_after();
-                    const uint32_t dS = tmem + kTS + 64 * st;
-                    // descriptors advance by 32 bytes (2 in the start-address field) per k-step
-                    const uint64_t aq0 = smem_desc_sw128(smem_u32(sQu));
-                    const uint64_t aq1 = smem_desc_sw128(smem_u32(sQu + 16384));
-                    const uint64_t bk0 = smem_desc_sw128(smem_u32(sK + st * 16384));
-                    const uint64_t bk1 = smem_desc_sw128(smem_u32(sK + st * 16384 + 8192));
-#pragma unroll
-                    for (int kk = 0; kk < 8; ++kk)
-                        mma_f16_ss(dS, (kk < 4 ? aq0 : aq1) + 2 * (kk & 3), (kk < 4 ? bk0 : bk1) + 2 * (kk & 3), kIdescS,
-                                   kk > 0);
-                    // band rows [64 kb, 64 kb + 192) of the ring: one N192 piece when contiguous,
-                    // else N128 + N64 or N64 + N128 around the wrap
-                    const uint32_t s0 = static_cast<uint32_t>(kb * kBK) & (kRing - 1);
-                    const int n1 = s0 <= kRing - 192 ? 192 : static_cast<int>(kRing - s0);
-                    const uint64_t br0 = smem_desc_sw128(smem_u32(sR + s0 * 128));
-                    const uint64_t br1 = smem_desc_sw128(smem_u32(sR + 32768 + s0 * 128));
-#pragma unroll
-                    for (int kk = 0; kk < 8; ++kk)
-                        mma_f16_ts(tmem + kTG, tmem + kTQ + 8 * kk, (kk < 4 ? br0 : br1) + 2 * (kk & 3),
-                                   n1 == 192 ? kIdescG192 : (n1 == 128 ? kIdescG128 : kIdescS), kk > 0);
-                    if (n1 < 192) {
-                        const uint64_t bw0 = smem_desc_sw128(smem_u32(sR));
-                        const uint64_t bw1 = smem_desc_sw128(smem_u32(sR + 32768));
+            int g0 = 0, n = 0;
+            bool ok = true;
+            for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++n) {
+                const Item it = item(i);
+                if (!(ok = mbar_wait(smem_u32(qld), n & 1, 0x22) && mbar_wait(smem_u32(q_tmem), n & 1, 0x23))) break;
+                for (int kb = 0; kb <= it.nkb && ok; ++kb) {
+                    if (kb < it.nkb) {
+                        const int g = g0 + kb, st = g & 1;
+                        if (!(ok = mbar_wait(smem_u32(&kr_full[st]), (g >> 1) & 1, 0x24))) break;
+                        if (g >= 1 && !(ok = mbar_wait(smem_u32(g_free), (g - 1) & 1, 0x25))) break;
+                        tc_fence_after();
+                        const uint32_t dS = tmem + kTS + 64 * st;
+                        // descriptors advance by 32 bytes (2 in the start-address field) per k-step
+                        const uint64_t aq0 = smem_desc_sw128(smem_u32(sQu));
+                        const uint64_t aq1 = smem_desc_sw128(smem_u32(sQu + 16384));
+                        const uint64_t bk0 = smem_desc_sw128(smem_u32(sK + st * 16384));
+                        const uint64_t bk1 = smem_desc_sw128(smem_u32(sK + st * 16384 + 8192));
 #pragma unroll
                         for (int kk = 0; kk < 8; ++kk)
-                            mma_f16_ts(tmem + kTG + n1, tmem + kTQ + 8 * kk, (kk < 4 ? bw0 : bw1) + 2 * (kk & 3),
-                                       n1 == 128 ? kIdescS : kIdescG128, kk > 0);
-                    }
-                    mma_commit(smem_u32(sg_full));
-                    mma_commit(smem_u32(&kr_empty[st]));
-                }
-                if (kb >= 1) {
-                    const int j = kb - 1, st = j & 1;
-                    if (!(ok = mbar_wait(smem_u32(p_ready), j & 1, 0x26))) break;
-                    if (!(ok = mbar_wait(smem_u32(&v_full[st]), (j >> 1) & 1, 0x2E))) break;
-                    tc_fence_after();
-                    // V [64 keys][128 dims] as the MN-major B operand: 64-dim halves 8 KB
-                    // apart, 8-key atoms 1 KB apart, 16 keys (2 KB) per MMA
-                    const uint64_t bv = smem_desc_sw128_mn(smem_u32(sV + st * 16384), 8192, 1024);
+                            mma_f16_ss(dS, (kk < 4 ? aq0 : aq1) + 2 * (kk & 3), (kk < 4 ? bk0 : bk1) + 2 * (kk & 3),
+                                       kIdescS, kk > 0);
+                        // band rows [64 kb, 64 kb + 192) of the ring: one N192 piece when contiguous,
+                        // else N128 + N64 or N64 + N128 around the wrap
+                        const uint32_t s0 = static_cast<uint32_t>(kb * kBK) & (kRing - 1);
+                        const int n1 = s0 <= kRing - 192 ? 192 : static_cast<int>(kRing - s0);
+                        const uint64_t br0 = smem_desc_sw128(smem_u32(sR + s0 * 128));
+                        const uint64_t br1 = smem_desc_sw128(smem_u32(sR + 32768 + s0 * 128));
 #pragma unroll
-                    for (int kk = 0; kk < 4; ++kk)
-                        mma_f16_ts(tmem + kTO, tmem + kTS + 64 * st + 8 * kk, bv + 128 * kk, kIdescPV, (j > 0 || kk > 0));
-                    mma_commit(smem_u32(o_ready));
-                    mma_commit(smem_u32(&v_empty[st]));
-                    if (j == nkb - 1) mma_commit(smem_u32(o_final));
+                        for (int kk = 0; kk < 8; ++kk)
+                            mma_f16_ts(tmem + kTG, tmem + kTQ + 8 * kk, (kk < 4 ? br0 : br1) + 2 * (kk & 3),
+                                       n1 == 192 ? kIdescG192 : (n1 == 128 ? kIdescG128 : kIdescS), kk > 0);
+                        if (n1 < 192) {
+                            const uint64_t bw0 = smem_desc_sw128(smem_u32(sR));
+                            const uint64_t bw1 = smem_desc_sw128(smem_u32(sR + 32768));
+#pragma unroll
+                            for (int kk = 0; kk < 8; ++kk)
+                                mma_f16_ts(tmem + kTG + n1, tmem + kTQ + 8 * kk, (kk < 4 ? bw0 : bw1) + 2 * (kk & 3),
+                                           n1 == 128 ? kIdescS : kIdescG128, kk > 0);
+                        }
+                        mma_commit(smem_u32(sg_full));
+                        mma_commit(smem_u32(&kr_empty[st]));
+                    }
+                    if (kb >= 1) {
+                        const int j = kb - 1, gj = g0 + j, st = gj & 1;
+                        if (!(ok = mbar_wait(smem_u32(p_ready), gj & 1, 0x26))) break;
+                        if (!(ok = mbar_wait(smem_u32(&v_full[st]), (gj >> 1) & 1, 0x2E))) break;
+                        tc_fence_after();
+                        // V [64 keys][128 dims] as the MN-major B operand: 64-dim halves 8 KB
+                        // apart, 8-key atoms 1 KB apart, 16 keys (2 KB) per MMA
+                        const uint64_t bv = smem_desc_sw128_mn(smem_u32(sV + st * 16384), 8192, 1024);
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk)
+                            mma_f16_ts(tmem + kTO, tmem + kTS + 64 * st + 8 * kk, bv + 128 * kk, kIdescPV,
+                                       (j > 0 || kk > 0));
+                        mma_commit(smem_u32(o_ready));
+                        mma_commit(smem_u32(&v_empty[st]));
+                        if (j == it.nkb - 1) mma_commit(smem_u32(o_final));
+                    }
                 }
+                g0 += it.nkb;
             }
         }
     } else {
@@ -273,145 +294,172 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int t = (warp - 2) * 32 + lane;          // diagonal row
         const int tp = t ^ 128;                        // the pair partner's diagonal row
         const uint32_t lrow = static_cast<uint32_t>(q * 32) << 16;
-        // Qv row i, dim half hf: staging -> TMEM columns kTQ + 32 hf
-        bool ok = mbar_wait(smem_u32(qld), 0, 0x27);
-        if (ok) {
-            uint32_t r[32];
-            const uint8_t* row = reinterpret_cast<const uint8_t*>(sSh) + hf * 16384 + i * 128;
+        float* sh = sSh + t * kShStride;
+        const float* shp = sSh + tp * kShStride;
+        // Qv row i, dim half hf of an item, from global memory (rows past the
+        // utterance read its last row: their results are never stored)
+        auto load_qv = [&](const Item& it, uint32_t (&r)[32]) {
+            const int row = it.q0 + i < it.T ? it.q0 + i : it.T - 1;
+            const uint4* src = reinterpret_cast<const uint4*>(p.qkv + static_cast<size_t>(it.seg0 + row) * 4096 + 1024 +
+                                                              it.head * 128 + 64 * hf);
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
-                const uint4 v = *reinterpret_cast<const uint4*>(row + ((c ^ (i & 7)) << 4));
+                const uint4 v = __ldg(src + c);
                 r[4 * c] = v.x;
                 r[4 * c + 1] = v.y;
                 r[4 * c + 2] = v.z;
                 r[4 * c + 3] = v.w;
             }
+        };
+        auto store_qv = [&](const uint32_t (&r)[32]) {
             tmem_st_32x32b_x32(tmem + lrow + kTQ + 32 * hf, r);
-            tmem_wait_st();
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(q_tmem));
-        named_sync_softmax();   // the staging area becomes the diagonal rows
-        float* sh = sSh + t * kShStride;
-        const float* shp = sSh + tp * kShStride;
-        // m_use: the max the row's exponentials are taken against.  It moves
-        // (and O, l are rescaled) only when a block's max exceeds it by more
-        // than kRescale (log2 units), for the pair of warps as a whole; in
-        // between, probabilities up to 2^kRescale are exact in f32 l and in
-        // the f16 P operand.
-        constexpr float kRescale = 8.0f;
-        float m_use = -INFINITY, l_half = 0.f;
-        for (int kb = 0; kb < nkb && ok; ++kb) {
-            const int st = kb & 1;
-            if (!(ok = mbar_wait(smem_u32(sg_full), kb & 1, 0x28))) break;
-            tc_fence_after();
-            float s[32];
-            {
-                // S columns [32 hf, 32 hf + 32) and band columns [96 - 32q + 32hf, +64): one wait
-                uint32_t r0[32], g0[32], g1[32];
-                tmem_ld_32x32b_x32(tmem + lrow + kTS + 64 * st + 32 * hf, r0);
-                tmem_ld_32x32b_x32(tmem + lrow + kTG + 96 - 32 * q + 32 * hf, g0);
-                tmem_ld_32x32b_x32(tmem + lrow + kTG + 128 - 32 * q + 32 * hf, g1);
-                tmem_wait_ld();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(smem_u32(g_free));
-#pragma unroll
-                for (int e = 0; e < 32; ++e) s[e] = __uint_as_float(r0[e]);
-                // window column c (0..62 are used) goes to position (c + lane) mod 64:
-                // the columns a row needs, 31 - lane + j, then sit at 31 + j for every
-                // lane (conflict-free reads at the odd row stride); position
-                // (63 + lane) mod 64 and position 64 stay free for the pair exchange
-#pragma unroll
-                for (int e = 0; e < 32; ++e) sh[(e + lane) & 63] = __uint_as_float(g0[e]);
-#pragma unroll
-                for (int e = 0; e < 31; ++e) sh[(32 + e + lane) & 63] = __uint_as_float(g1[e]);
-            }
-            // row i, key 32 hf + j: band column 127 - i + 32 hf + j = window column 31 - lane + j
-            const float* dg = sh + 31;
-            const int kvalid = T - kb * kBK - 32 * hf;
-            float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-                float v = (s[j] + dg[j]) * p.scale_log2;
-                if (j >= kvalid) v = -INFINITY;
-                s[j] = v;
-                mx[j & 3] = fmaxf(mx[j & 3], v);
-            }
-            const float mloc = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
-            const int xs = st ? 64 : ((63 + lane) & 63);   // exchange slot, by block parity
-            sh[xs] = mloc;
-            if (!(ok = pair_exchange(&xchg[q], lane, kb & 1, 0x2B))) break;
-            const float m_blk = fmaxf(mloc, shp[xs]);
-            const bool grow = m_blk > m_use + kRescale;
-            float corr = 1.f;
-            if (__any_sync(0xffffffffu, grow)) {
-                const float m_new = grow ? m_blk : m_use;
-                corr = exp2f(m_use - m_new);   // 0 for the first block
-                m_use = m_new;
-                if (kb >= 1) {
-                    // O columns [64 hf, 64 hf + 64) (after P_{kb-1} V) *= corr.
-                    // Passing sg_full(kb) implies P_{kb-2} V is done and P_kb V is not
-                    // issued yet, so o_ready is at phase kb-1 or kb: the parity is exact.
-                    if (!(ok = mbar_wait(smem_u32(o_ready), (kb - 1) & 1, 0x29))) break;
-                    tc_fence_after();
-                    uint32_t o0[32], o1[32];
-                    tmem_ld_32x32b_x32(tmem + lrow + kTO + 64 * hf, o0);
-                    tmem_ld_32x32b_x32(tmem + lrow + kTO + 64 * hf + 32, o1);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int e = 0; e < 32; ++e) {
-                        o0[e] = __float_as_uint(__uint_as_float(o0[e]) * corr);
-                        o1[e] = __float_as_uint(__uint_as_float(o1[e]) * corr);
-                    }
-                    tmem_st_32x32b_x32(tmem + lrow + kTO + 64 * hf, o0);
-                    tmem_st_32x32b_x32(tmem + lrow + kTO + 64 * hf + 32, o1);
-                }
-            }
-            float ls[4] = {0.f, 0.f, 0.f, 0.f};
-            uint32_t pk[16];
-#pragma unroll
-            for (int j = 0; j < 32; j += 2) {
-                const float a = exp2f(s[j] - m_use), b = exp2f(s[j + 1] - m_use);
-                ls[(j >> 1) & 3] += a + b;
-                pk[j >> 1] = h2u(a, b);
-            }
-            l_half = l_half * corr + ((ls[0] + ls[1]) + (ls[2] + ls[3]));
-            tmem_st_32x32b_x16(tmem + lrow + kTS + 64 * st + 16 * hf, pk);   // P over this block's S columns
             tmem_wait_st();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(p_ready));
+            if (lane == 0) mbar_arrive(smem_u32(q_tmem));
+        };
+        bool ok = true;
+        int g0 = 0, n = 0, x = 0;
+        if (static_cast<int>(blockIdx.x) < n_items) {
+            uint32_t r[32];
+            load_qv(item(blockIdx.x), r);
+            store_qv(r);
         }
-        // ── O / l -> f16 row, columns [64 hf, 64 hf + 64) ──
-        if (ok && nkb > 0 && mbar_wait(smem_u32(o_final), 0, 0x2A)) {
-            tc_fence_after();
-            const int xs = (nkb & 1) ? 64 : ((63 + lane) & 63);   // the slot the last block did not use
-            sh[xs] = l_half;
-            const bool xok = pair_exchange(&xchg[q], lane, nkb & 1, 0x2C);
-            const float inv = 1.0f / (l_half + shp[xs]);
-            const bool store = xok && q0 + i < T;
-            __half* dst = p.out + static_cast<size_t>(seg0 + q0 + i) * 1024 + head * 128 + 64 * hf;
-            uint32_t o0[32], o1[32];
-            tmem_ld_32x32b_x32(tmem + lrow + kTO + 64 * hf, o0);
-            tmem_ld_32x32b_x32(tmem + lrow + kTO + 64 * hf + 32, o1);
-            tmem_wait_ld();
-            if (store) {
+        for (int ii = blockIdx.x; ii < n_items && ok; ii += gridDim.x, ++n) {
+            const Item it = item(ii);
+            const bool has_next = ii + static_cast<int>(gridDim.x) < n_items;
+            // m_use: the max the row's exponentials are taken against.  It moves
+            // (and O, l are rescaled) only when a block's max exceeds it by more
+            // than kRescale (log2 units), for the pair of warps as a whole; in
+            // between, probabilities up to 2^kRescale are exact in f32 l and in
+            // the f16 P operand.
+            constexpr float kRescale = 8.0f;
+            float m_use = -INFINITY, l_half = 0.f;
+            for (int kb = 0; kb < it.nkb && ok; ++kb) {
+                const int g = g0 + kb, st = g & 1;
+                const bool handoff = kb == it.nkb - 1 && has_next;
+                uint32_t qn[32];   // the next item's Qv row (last block only)
+                if (handoff) load_qv(item(ii + gridDim.x), qn);
+                if (!(ok = mbar_wait(smem_u32(sg_full), g & 1, 0x28))) break;
+                tc_fence_after();
+                // every band MMA of this item is done (sg_full of its last block
+                // passed): the next item's Qv replaces this one in TMEM, so the
+                // next item's S / band MMAs run under this block's softmax
+                if (handoff) store_qv(qn);
+                float s[32];
+                {
+                    // S columns [32 hf, 32 hf + 32) and band columns [96 - 32q + 32hf, +64): one wait
+                    uint32_t r0[32], g0r[32], g1r[32];
+                    tmem_ld_32x32b_x32(tmem + lrow + kTS + 64 * st + 32 * hf, r0);
+                    tmem_ld_32x32b_x32(tmem + lrow + kTG + 96 - 32 * q + 32 * hf, g0r);
+                    tmem_ld_32x32b_x32(tmem + lrow + kTG + 128 - 32 * q + 32 * hf, g1r);
+                    tmem_wait_ld();
+                    tc_fence_before();
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(smem_u32(g_free));
 #pragma unroll
-                for (int e = 0; e < 32; e += 8) {
-                    *reinterpret_cast<uint4*>(dst + e) =
-                        make_uint4(h2u(__uint_as_float(o0[e]) * inv, __uint_as_float(o0[e + 1]) * inv),
-                                   h2u(__uint_as_float(o0[e + 2]) * inv, __uint_as_float(o0[e + 3]) * inv),
-                                   h2u(__uint_as_float(o0[e + 4]) * inv, __uint_as_float(o0[e + 5]) * inv),
-                                   h2u(__uint_as_float(o0[e + 6]) * inv, __uint_as_float(o0[e + 7]) * inv));
-                    *reinterpret_cast<uint4*>(dst + 32 + e) =
-                        make_uint4(h2u(__uint_as_float(o1[e]) * inv, __uint_as_float(o1[e + 1]) * inv),
-                                   h2u(__uint_as_float(o1[e + 2]) * inv, __uint_as_float(o1[e + 3]) * inv),
-                                   h2u(__uint_as_float(o1[e + 4]) * inv, __uint_as_float(o1[e + 5]) * inv),
-                                   h2u(__uint_as_float(o1[e + 6]) * inv, __uint_as_float(o1[e + 7]) * inv));
+                    for (int e = 0; e < 32; ++e) s[e] = __uint_as_float(r0[e]);
+                    // window column c (0..62 are used) goes to position (c + lane) mod 64:
+                    // the columns a row needs, 31 - lane + j, then sit at 31 + j for every
+                    // lane (conflict-free reads at the odd row stride); position
+                    // (63 + lane) mod 64 and position 64 stay free for the pair exchange
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) sh[(e + lane) & 63] = __uint_as_float(g0r[e]);
+#pragma unroll
+                    for (int e = 0; e < 31; ++e) sh[(32 + e + lane) & 63] = __uint_as_float(g1r[e]);
                 }
+                // row i, key 32 hf + j: band column 127 - i + 32 hf + j = window column 31 - lane + j
+                const float* dg = sh + 31;
+                const int kvalid = it.T - kb * kBK - 32 * hf;
+                float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    float v = (s[j] + dg[j]) * p.scale_log2;
+                    if (j >= kvalid) v = -INFINITY;
+                    s[j] = v;
+                    mx[j & 3] = fmaxf(mx[j & 3], v);
+                }
+                const float mloc = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
+                const int xs = (x & 1) ? 64 : ((63 + lane) & 63);   // exchange slot, by exchange parity
+                sh[xs] = mloc;
+                if (!(ok = pair_exchange(&xchg[q], lane, x & 1, 0x2B))) break;
+                ++x;
+                const float m_blk = fmaxf(mloc, shp[xs]);
+                const bool grow = m_blk > m_use + kRescale;
+                float corr = 1.f;
+                if (__any_sync(0xffffffffu, grow)) {
+                    const float m_new = grow ? m_blk : m_use;
+                    corr = exp2f(m_use - m_new);   // 0 for the first block
+                    m_use = m_new;
+                    if (kb >= 1) {
+                        // O columns [64 hf, 64 hf + 64) (after P_{g-1} V) *= corr.
+                        // Passing sg_full(g) implies P_{g-2} V is done and P_g V is not
+                        // issued yet, so o_ready is at phase g-1 or g: the parity is exact.
+                        if (!(ok = mbar_wait(smem_u32(o_ready), (g - 1) & 1, 0x29))) break;
+                        tc_fence_after();
+                        uint32_t o0[32], o1[32];
+                        tmem_ld_32x32b_x32(tmem + lrow + kTO + 64 * hf, o0);
+                        tmem_ld_32x32b_x32(tmem + lrow + kTO + 64 * hf + 32, o1);
+                        tmem_wait_ld();
+#pragma unroll
+                        for (int e = 0; e < 32; ++e) {
+                            o0[e] = __float_as_uint(__uint_as_float(o0[e]) * corr);
+                            o1[e] = __float_as_uint(__uint_as_float(o1[e]) * corr);
+                        }
+                        tmem_st_32x32b_x32(tmem + lrow + kTO + 64 * hf, o0);
+                        tmem_st_32x32b_x32(tmem + lrow + kTO + 64 * hf + 32, o1);
+                    }
+                }
+                float ls[4] = {0.f, 0.f, 0.f, 0.f};
+                uint32_t pk[16];
+#pragma unroll
+                for (int j = 0; j < 32; j += 2) {
+                    const float a = exp2f(s[j] - m_use), b = exp2f(s[j + 1] - m_use);
+                    ls[(j >> 1) & 3] += a + b;
+                    pk[j >> 1] = h2u(a, b);
+                }
+                l_half = l_half * corr + ((ls[0] + ls[1]) + (ls[2] + ls[3]));
+                tmem_st_32x32b_x16(tmem + lrow + kTS + 64 * st + 16 * hf, pk);   // P over this block's S columns
+                tmem_wait_st();
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(smem_u32(p_ready));
             }
+            // ── O / l -> f16 row, columns [64 hf, 64 hf + 64) ──
+            if (ok && mbar_wait(smem_u32(o_final), n & 1, 0x2A)) {
+                tc_fence_after();
+                const int xs = (x & 1) ? 64 : ((63 + lane) & 63);
+                sh[xs] = l_half;
+                const bool xok = pair_exchange(&xchg[q], lane, x & 1, 0x2C);
+                ++x;
+                const float inv = 1.0f / (l_half + shp[xs]);
+                const bool store = xok && it.q0 + i < it.T;
+                __half* dst = p.out + static_cast<size_t>(it.seg0 + it.q0 + i) * 1024 + it.head * 128 + 64 * hf;
+                uint32_t o0[32], o1[32];
+                tmem_ld_32x32b_x32(tmem + lrow + kTO + 64 * hf, o0);
+                tmem_ld_32x32b_x32(tmem + lrow + kTO + 64 * hf + 32, o1);
+                tmem_wait_ld();
+                if (store) {
+#pragma unroll
+                    for (int e = 0; e < 32; e += 8) {
+                        *reinterpret_cast<uint4*>(dst + e) =
+                            make_uint4(h2u(__uint_as_float(o0[e]) * inv, __uint_as_float(o0[e + 1]) * inv),
+                                       h2u(__uint_as_float(o0[e + 2]) * inv, __uint_as_float(o0[e + 3]) * inv),
+                                       h2u(__uint_as_float(o0[e + 4]) * inv, __uint_as_float(o0[e + 5]) * inv),
+                                       h2u(__uint_as_float(o0[e + 6]) * inv, __uint_as_float(o0[e + 7]) * inv));
+                        *reinterpret_cast<uint4*>(dst + 32 + e) =
+                            make_uint4(h2u(__uint_as_float(o1[e]) * inv, __uint_as_float(o1[e + 1]) * inv),
+                                       h2u(__uint_as_float(o1[e + 2]) * inv, __uint_as_float(o1[e + 3]) * inv),
+                                       h2u(__uint_as_float(o1[e + 4]) * inv, __uint_as_float(o1[e + 5]) * inv),
+                                       h2u(__uint_as_float(o1[e + 6]) * inv, __uint_as_float(o1[e + 7]) * inv));
+                    }
+                }
+                tc_fence_before();
+                ok = xok;
+            } else {
+                ok = false;
+            }
+            g0 += it.nkb;
         }
     }
 
@@ -444,7 +492,16 @@ int launch_attention_tc(const AttnParams& p, int M, int n_work, cudaStream_t st)
     if (!rc) rc = make_map_2d(&tkv, p.qkv, kMapF16, 4096, static_cast<uint64_t>(M), 8192, 64, kBK, true);
     if (!rc) rc = make_map_2d(&tr, p.R, kMapF16, 1024, static_cast<uint64_t>(p.r_rows), 2048, 64, 64, true);
     if (rc) return rc;
-    k2_relpos_attention_tc<<<dim3(n_work, 8), kThreads, kSmem, st>>>(tq, tkv, tr, p);
+    // persistent: one CTA per SM walks the (work entry, head) items
+    static int sms = 0;
+    if (!sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (sms <= 0) sms = 148;
+    }
+    const int n_items = n_work * 8;
+    k2_relpos_attention_tc<<<n_items < sms ? n_items : sms, kThreads, kSmem, st>>>(tq, tkv, tr, p, n_items);
     return check_launch("k2_relpos_attention_tc");
 }
 
