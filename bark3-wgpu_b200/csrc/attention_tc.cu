@@ -55,7 +55,8 @@ constexpr int kBK = 64;           // keys per block
 constexpr int kThreads = 320;     // warp 0 TMA, warp 1 MMA, warps 2..9 softmax
 constexpr int kSoftThreads = 256;
 constexpr int kRing = 256;        // R ring rows
-constexpr int kShStride = 65;     // floats per softmax thread's diagonal row (odd: conflict-free)
+constexpr int kShStride = 66;     // floats per softmax thread's diagonal row: 64 band columns + 2 exchange
+                                  // slots; 8-byte stores and lane-shifted scalar reads are both conflict-free
 
 // shared memory (offsets from a 1024-aligned base)
 constexpr uint32_t kQuOff = 0;                   // Qu: 2 dim-halves x (128 rows x 128 B)
@@ -64,9 +65,12 @@ constexpr uint32_t kVOff = kKOff + 32768;        // V: same
 constexpr uint32_t kROff = kVOff + 32768;        // R ring: 2 halves x (256 rows x 128 B)
 constexpr uint32_t kShOff = kROff + 65536;       // diagonal rows 256 x 65 f32 (Qv staging first)
 constexpr uint32_t kBarOff = kShOff + kSoftThreads * kShStride * 4;
-constexpr uint32_t kSmem = kBarOff + 256 + 1024;
+constexpr uint32_t kBarBytes = 160;                   // 19 mbarriers + the TMEM address
+constexpr uint32_t kSmemMax = 232448;
+constexpr uint32_t kSmem = kSmemMax;
+constexpr uint32_t kAlignSlack = kSmemMax - kBarOff - kBarBytes;   // room to align the base to 1024 B
 static_assert(kSoftThreads * kShStride * 4 >= 32768, "Qv staging fits the diagonal rows");
-static_assert(kSmem <= 232448, "shared memory budget");
+static_assert(kBarOff + kBarBytes + 256 <= kSmemMax, "shared memory budget");
 
 // TMEM columns
 constexpr uint32_t kTS = 0;       // S / P, 2 buffers x 64
@@ -99,6 +103,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                ~static_cast<uintptr_t>(1023));
+    if (static_cast<uint32_t>(smem - smem_raw) > kAlignSlack) {   // never expected: the base is 1 KB aligned
+        if (threadIdx.x == 0) record_error(B3_ERR_TIMEOUT | 0x2F);
+        return;
+    }
     uint8_t* sQu = smem + kQuOff;
     uint8_t* sK = smem + kKOff;
     uint8_t* sV = smem + kVOff;
@@ -123,6 +131,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* o_final = bars + 14;   // the last P.V of an item
     uint64_t* xchg = bars + 15;      // [4] softmax warp pairs
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
+    static_assert(19 * 8 + 4 <= kBarBytes, "barrier area");
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -359,17 +368,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (lane == 0) mbar_arrive(smem_u32(g_free));
 #pragma unroll
                     for (int e = 0; e < 32; ++e) s[e] = __uint_as_float(r0[e]);
-                    // window column c (0..62 are used) goes to position (c + lane) mod 64:
-                    // the columns a row needs, 31 - lane + j, then sit at 31 + j for every
-                    // lane (conflict-free reads at the odd row stride); position
-                    // (63 + lane) mod 64 and position 64 stay free for the pair exchange
+                    // window columns 0..63 (0..62 are used) as 8-byte stores: with the
+                    // row stride of 66 words a half-warp's stores cover all 32 banks
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) sh[(e + lane) & 63] = __uint_as_float(g0r[e]);
-#pragma unroll
-                    for (int e = 0; e < 31; ++e) sh[(32 + e + lane) & 63] = __uint_as_float(g1r[e]);
+                    for (int e = 0; e < 32; e += 2) {
+                        *reinterpret_cast<uint2*>(sh + e) = make_uint2(g0r[e], g0r[e + 1]);
+                        *reinterpret_cast<uint2*>(sh + 32 + e) = make_uint2(g1r[e], g1r[e + 1]);
+                    }
                 }
-                // row i, key 32 hf + j: band column 127 - i + 32 hf + j = window column 31 - lane + j
-                const float* dg = sh + 31;
+                // row i, key 32 hf + j: band column 127 - i + 32 hf + j = window column
+                // 31 - lane + j; across a warp the word index moves by 65 per lane: no conflicts
+                const float* dg = sh + 31 - lane;
                 const int kvalid = it.T - kb * kBK - 32 * hf;
                 float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
@@ -380,7 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     mx[j & 3] = fmaxf(mx[j & 3], v);
                 }
                 const float mloc = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
-                const int xs = (x & 1) ? 64 : ((63 + lane) & 63);   // exchange slot, by exchange parity
+                const int xs = 64 + (x & 1);   // exchange slot, by exchange parity
                 sh[xs] = mloc;
                 if (!(ok = pair_exchange(&xchg[q], lane, x & 1, 0x2B))) break;
                 ++x;
@@ -428,7 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // ── O / l -> f16 row, columns [64 hf, 64 hf + 64) ──
             if (ok && mbar_wait(smem_u32(o_final), n & 1, 0x2A)) {
                 tc_fence_after();
-                const int xs = (x & 1) ? 64 : ((63 + lane) & 63);
+                const int xs = 64 + (x & 1);
                 sh[xs] = l_half;
                 const bool xok = pair_exchange(&xchg[q], lane, x & 1, 0x2C);
                 ++x;
