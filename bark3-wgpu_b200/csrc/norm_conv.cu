@@ -101,28 +101,30 @@ __global__ void __launch_bounds__(256) k4_layernorm(const float* __restrict__ x,
     }
 }
 
-// Depthwise conv k=9 + BN(a, b) + SiLU.  Block: 128 threads x 8 channels =
+// Depthwise conv k=9 + BN(a, b) + SiLU.  Block: 256 threads x 4 channels =
 // all 1024 channels of kDwRows consecutive frames.  The (kDwRows + 8)-frame
-// input tile is staged in shared memory with cp.async (every load in flight
-// at once); each thread then slides a 9-frame register window over it.
-// Frame t reads t-4 .. t+4 inside its own utterance [seg.x, seg.y); anything
-// outside is zero.
-constexpr int kDwRows = 36;
+// input tile is staged in shared memory with cp.async in two groups, so the
+// first rows are convolved while the rest are still arriving; each thread
+// slides a 9-frame register window (pairs of channels, packed f32x2 FMAs)
+// over it.  Frame t reads t-4 .. t+4 inside its own utterance [seg.x,
+// seg.y); anything outside is zero.
+constexpr int kDwRows = 40;
 constexpr int kDwTile = kDwRows + 8;
+constexpr int kDwSplit = 24;                 // tile rows in the first cp.async group
 constexpr int kDwSmem = kDwTile * 1024 * 2;
 
-__global__ void __launch_bounds__(128) k3_dwconv_bn_silu(const __half* __restrict__ src,
-                                                         const int2* __restrict__ seg, int rows,
-                                                         const float* __restrict__ dw_t,  // [9][1024]
-                                                         const float* __restrict__ bn_a,
-                                                         const float* __restrict__ bn_b,
-                                                         __half* __restrict__ dst) {
+__global__ void __launch_bounds__(256, 2) k3_dwconv_bn_silu(const __half* __restrict__ src,
+                                                            const int2* __restrict__ seg, int rows,
+                                                            const float* __restrict__ dw_t,  // [9][1024]
+                                                            const float* __restrict__ bn_a,
+                                                            const float* __restrict__ bn_b,
+                                                            __half* __restrict__ dst) {
     extern __shared__ __align__(16) uint8_t tile[];  // [kDwTile][1024] f16, frame t0-4+i in row i
-    const int c0 = threadIdx.x * 8;
+    const int c0 = threadIdx.x * 4;
     const int t0 = blockIdx.x * kDwRows;
     {
         const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(tile));
-        for (int c = threadIdx.x; c < kDwTile * 128; c += 128) {
+        for (int c = threadIdx.x; c < kDwTile * 128; c += 256) {
             const int r = c >> 7, ch = c & 127;
             const int t = t0 - 4 + r;
             const bool ok = t >= 0 && t < rows;
@@ -130,47 +132,44 @@ __global__ void __launch_bounds__(128) k3_dwconv_bn_silu(const __half* __restric
             asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(base + r * 2048 + ch * 16), "l"(g),
                          "r"(ok ? 16 : 0)
                          : "memory");
+            if (c + 256 >= kDwSplit * 128 && c < kDwSplit * 128) asm volatile("cp.async.commit_group;" ::: "memory");
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     }
-    float w[9][8];
+    float2 w[9][2];
 #pragma unroll
     for (int i = 0; i < 9; ++i) {
         const float4 a = __ldg(reinterpret_cast<const float4*>(dw_t + i * 1024 + c0));
-        const float4 b = __ldg(reinterpret_cast<const float4*>(dw_t + i * 1024 + c0 + 4));
-        w[i][0] = a.x; w[i][1] = a.y; w[i][2] = a.z; w[i][3] = a.w;
-        w[i][4] = b.x; w[i][5] = b.y; w[i][6] = b.z; w[i][7] = b.w;
+        w[i][0] = make_float2(a.x, a.y);
+        w[i][1] = make_float2(a.z, a.w);
     }
-    float ba[8], bb[8];
+    float2 ba[2], bb[2];
     {
-        const float4 a0 = __ldg(reinterpret_cast<const float4*>(bn_a + c0));
-        const float4 a1 = __ldg(reinterpret_cast<const float4*>(bn_a + c0 + 4));
-        const float4 b0 = __ldg(reinterpret_cast<const float4*>(bn_b + c0));
-        const float4 b1 = __ldg(reinterpret_cast<const float4*>(bn_b + c0 + 4));
-        ba[0] = a0.x; ba[1] = a0.y; ba[2] = a0.z; ba[3] = a0.w;
-        ba[4] = a1.x; ba[5] = a1.y; ba[6] = a1.z; ba[7] = a1.w;
-        bb[0] = b0.x; bb[1] = b0.y; bb[2] = b0.z; bb[3] = b0.w;
-        bb[4] = b1.x; bb[5] = b1.y; bb[6] = b1.z; bb[7] = b1.w;
+        const float4 a = __ldg(reinterpret_cast<const float4*>(bn_a + c0));
+        const float4 b = __ldg(reinterpret_cast<const float4*>(bn_b + c0));
+        ba[0] = make_float2(a.x, a.y);
+        ba[1] = make_float2(a.z, a.w);
+        bb[0] = make_float2(b.x, b.y);
+        bb[1] = make_float2(b.z, b.w);
     }
-    asm volatile("cp.async.wait_group 0;" ::: "memory");
-    __syncthreads();
-    auto load = [&](int r, float (&d8)[8]) {
-        const uint4 u = *reinterpret_cast<const uint4*>(tile + r * 2048 + c0 * 2);
-        const __half2* h = reinterpret_cast<const __half2*>(&u);
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-            const float2 f = __half22float2(h[j]);
-            d8[2 * j] = f.x;
-            d8[2 * j + 1] = f.y;
-        }
+    auto load = [&](int r, float2 (&d)[2]) {
+        const uint2 u = *reinterpret_cast<const uint2*>(tile + r * 2048 + c0 * 2);
+        d[0] = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+        d[1] = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
     };
+    asm volatile("cp.async.wait_group 1;" ::: "memory");
+    __syncthreads();
     // circular 9-frame window: tile row r lives in slot r % 9.  The row loop
     // is unrolled by 9 so every slot index is a compile-time constant.
-    float win[9][8];
+    float2 win[9][2];
 #pragma unroll
     for (int i = 0; i < 8; ++i) load(i, win[i]);
 #pragma unroll 1
     for (int r0 = 0; r0 < kDwRows; r0 += 9) {
+        if (r0 + 8 + 8 >= kDwSplit && r0 < kDwSplit) {   // rows up to r0 + 16 may come from the second group
+            asm volatile("cp.async.wait_group 0;" ::: "memory");
+            __syncthreads();
+        }
 #pragma unroll
         for (int u = 0; u < 9; ++u) {
             const int r = r0 + u;
@@ -180,26 +179,23 @@ __global__ void __launch_bounds__(128) k3_dwconv_bn_silu(const __half* __restric
                 const int2 sg = __ldg(seg + t);
                 const int lo = max(sg.x - (t - 4), 0);
                 const int hi = min(sg.y - (t - 4), 9);
-                float acc[8];
-#pragma unroll
-                for (int j = 0; j < 8; ++j) acc[j] = 0.f;
+                float2 acc[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
                 for (int i = 0; i < 9; ++i) {
                     if (i < lo || i >= hi) continue;
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) acc[j] += win[(u + i) % 9][j] * w[i][j];
+                    acc[0] = __ffma2_rn(win[(u + i) % 9][0], w[i][0], acc[0]);
+                    acc[1] = __ffma2_rn(win[(u + i) % 9][1], w[i][1], acc[1]);
                 }
-                uint32_t o[4];
+                uint32_t o[2];
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    float y0 = acc[2 * j] * ba[2 * j] + bb[2 * j];
-                    float y1 = acc[2 * j + 1] * ba[2 * j + 1] + bb[2 * j + 1];
-                    y0 = __fdividef(y0, 1.0f + __expf(-y0));
-                    y1 = __fdividef(y1, 1.0f + __expf(-y1));
+                for (int j = 0; j < 2; ++j) {
+                    const float2 y = __ffma2_rn(acc[j], ba[j], bb[j]);
+                    const float y0 = __fdividef(y.x, 1.0f + __expf(-y.x));
+                    const float y1 = __fdividef(y.y, 1.0f + __expf(-y.y));
                     __half2 h = __floats2half2_rn(y0, y1);
                     o[j] = *reinterpret_cast<uint32_t*>(&h);
                 }
-                *reinterpret_cast<uint4*>(dst + static_cast<size_t>(t) * 1024 + c0) = make_uint4(o[0], o[1], o[2], o[3]);
+                *reinterpret_cast<uint2*>(dst + static_cast<size_t>(t) * 1024 + c0) = make_uint2(o[0], o[1]);
             }
         }
     }
@@ -247,7 +243,7 @@ int launch_dwconv(const __half* src, const int2* seg, int rows, const float* dw_
         if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(k3)", e);
         attr_done = true;
     }
-    k3_dwconv_bn_silu<<<(rows + kDwRows - 1) / kDwRows, 128, kDwSmem, st>>>(src, seg, rows, dw_t, bn_a, bn_b, dst);
+    k3_dwconv_bn_silu<<<(rows + kDwRows - 1) / kDwRows, 256, kDwSmem, st>>>(src, seg, rows, dw_t, bn_a, bn_b, dst);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? 0 : set_cuda_error("k3_dwconv_bn_silu", e);
 }
