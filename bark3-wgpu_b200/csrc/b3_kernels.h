@@ -41,7 +41,8 @@ int attention_take_dev_error(cudaStream_t st, unsigned int* out);
 // utterance; GEMM inputs are f16 hi | lo pairs (see tdt_decoder.cu).
 struct DecState {
     int B, vocab, blank, max_tokens;
-    const int* cu;           // device cu_seqlens [B + 1]
+    const int* row0;         // [B] first pooler row of each utterance
+    const int* len;          // [B] encoder frames of each utterance
     const float* pooler;     // [total][640]
     const float* e0;         // [vocab][2560] W_ih0 . emb(token) + b_ih0 + b_hh0
     int* tok;                // [B] last emitted token (blank before the first)
@@ -69,6 +70,8 @@ int dec_launch_argmax(const DecState& s, cudaStream_t st);
 int dec_launch_lstm_update(const DecState& s, int layer, cudaStream_t st);
 int dec_launch_any_active(const DecState& s, int* out, cudaStream_t st);
 int dec_launch_split(const float* src, __half* hi, __half* lo, int64_t n, cudaStream_t st);
+// Scatters the group's tokens / counts to rows out_row[b] of the batch outputs.
+int dec_launch_gather(const DecState& s, const int* out_row, uint32_t* out_tokens, int* out_count, cudaStream_t st);
 
 // Mel front end (frontend.cu).
 struct MelParams {

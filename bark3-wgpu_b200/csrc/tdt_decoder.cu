@@ -102,7 +102,7 @@ __global__ void k_dec_init(DecState s) {
     pdl_launch_dependents();
     const int b = blockIdx.x;
     if (b >= s.B) return;
-    const int T = s.cu[b + 1] - s.cu[b];
+    const int T = s.len[b];
     const __half z = __float2half_rn(0.f);
     for (int j = threadIdx.x; j < kH; j += blockDim.x) {
         __half* a0 = s.a0 + static_cast<size_t>(b) * 2 * kH;
@@ -136,7 +136,7 @@ __global__ void __launch_bounds__(160) k_dec_joint_in(DecState s) {
     __half* aj = s.aj + static_cast<size_t>(b) * 2 * kH;
     float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
     if (act) {
-        const float4 e = __ldg(reinterpret_cast<const float4*>(s.pooler + static_cast<size_t>(s.cu[b] + s.frame[b]) * kH + j));
+        const float4 e = __ldg(reinterpret_cast<const float4*>(s.pooler + static_cast<size_t>(s.row0[b] + s.frame[b]) * kH + j));
         const float4 d = parts_sum4(s.dec, s.ks_p, s.prow, kH, b, j);
         v = make_float4(fmaxf(e.x + d.x, 0.f), fmaxf(e.y + d.y, 0.f), fmaxf(e.z + d.z, 0.f), fmaxf(e.w + d.w, 0.f));
     }
@@ -218,7 +218,7 @@ __global__ void __launch_bounds__(256) k_dec_argmax(DecState s) {
     int dur = wdur;
     if (tok == 0x7fffffff) tok = 0;   // every score NaN: mirrors the reference's initial index
     if (dur == 0x7fffffff) dur = 0;
-    const int T = s.cu[b + 1] - s.cu[b];
+    const int T = s.len[b];
     const bool emit = tok != s.blank;
     const int frame = s.frame[b];
     if (emit) {
@@ -307,6 +307,21 @@ __global__ void k_split_rows(const float* __restrict__ src, __half* hi, __half* 
         split_store(hi + i, lo + i, src[i]);
 }
 
+// Row b of a decoder group -> utterance out_row[b] of the batch outputs.
+__global__ void __launch_bounds__(256) k_dec_gather(const uint32_t* __restrict__ tokens, const int* __restrict__ count,
+                                                    const int* __restrict__ out_row, int B, int max_tokens,
+                                                    uint32_t* __restrict__ out_tokens, int* __restrict__ out_count) {
+    const int b = blockIdx.x;
+    if (b >= B) return;
+    const int u = out_row[b];
+    const int n = count[b];
+    if (threadIdx.x == 0) out_count[u] = n;
+    const int words = 3 * (n < max_tokens ? n : max_tokens);
+    const uint32_t* src = tokens + static_cast<size_t>(b) * max_tokens * 3;
+    uint32_t* dst = out_tokens + static_cast<size_t>(u) * max_tokens * 3;
+    for (int i = threadIdx.x; i < words; i += blockDim.x) dst[i] = src[i];
+}
+
 int check_launch(const char* what) {
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? 0 : set_cuda_error(what, e);
@@ -351,6 +366,11 @@ int dec_launch_any_active(const DecState& s, int* out, cudaStream_t st) {
     return launch_pdl(k_dec_any_active, dim3(1), dim3(256), st, "k_dec_any_active", static_cast<const int*>(s.active),
                       s.B, out);
 }
+int dec_launch_gather(const DecState& s, const int* out_row, uint32_t* out_tokens, int* out_count, cudaStream_t st) {
+    k_dec_gather<<<s.B, 256, 0, st>>>(s.tokens, s.count, out_row, s.B, s.max_tokens, out_tokens, out_count);
+    return check_launch("k_dec_gather");
+}
+
 int dec_launch_split(const float* src, __half* hi, __half* lo, int64_t n, cudaStream_t st) {
     int blocks = static_cast<int>((n + 255) / 256);
     if (blocks > 4096) blocks = 4096;
