@@ -95,6 +95,11 @@ def lib() -> ctypes.CDLL:
         "b3_mel": (c_i, [c_p, c_p, c_p, c_i, c_p, c_p, c_u]),
         "b3_subsample": (c_i, [c_p, c_p, c_p, c_p, c_i, c_p, c_p, c_u]),
         "b3_mel_filters": (c_i, [c_p]),
+        "b3_bark_ans_cdf": (c_i, [c_p, c_i, c_p]),
+        "b3_bark_ans_decode": (c_i, [c_p, c_i, c_p, ctypes.c_int64, ctypes.c_int64, c_p]),
+        "b3_bark_decode_levels2": (c_i, [c_p, ctypes.c_int64, c_p, ctypes.c_int64, c_i, c_i, c_i, c_p]),
+        "b3_bark_decode_ansint": (c_i, [c_p, c_i, c_p, ctypes.c_int64, ctypes.c_int64, c_i, c_p, ctypes.c_int64,
+                                        c_p]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -120,6 +125,16 @@ def last_error() -> str:
 def check(rc: int) -> None:
     if rc != B3_OK:
         raise B3Error(rc, last_error())
+
+
+def check_bark(name: str, fn: str, *args) -> None:
+    """Calls a .bark stream decoder of the library; a failure raises
+    BarkError("<tensor>: <reason>")."""
+    from .bark import BarkError
+
+    rc = getattr(lib(), fn)(*args)
+    if rc != 0:
+        raise BarkError(f"{name}: {last_error()}")
 
 
 def _ptr(a) -> int | None:
@@ -190,6 +205,34 @@ class Encoder:
             arr = np.ascontiguousarray(v, dtype=np.float32)
             shape = (ctypes.c_int64 * arr.ndim)(*arr.shape)
             check(L.b3_load_tensor(self.ctx, nm, DTYPE_F32, shape, arr.ndim, _ptr(arr)))
+
+    def load_source(self, src, threads: int | None = None) -> int:
+        """Loads every float tensor of a checkpoint source (bark.BarkContainer
+        or bark.SafetensorsSource, see bark.open_weights) the way the
+        reference's Encoder::load_with reads a WeightSource
+        (src/encoder.rs:412-560): 4-bit tensors in their code-word + level
+        form, everything else at its stored precision (f16 / bf16 bits, or
+        f32 for dequantised integer matrices); integer tensors are skipped.
+        Returns the encoder layer count the source describes."""
+        from . import bark
+
+        src.prefetch(threads)
+        for name in src.tensor_names():
+            lb = src.read_lowbit(name)
+            if lb is not None:
+                self.load_one(name, ("levels", lb.codes, lb.levels, lb.k, lb.cols))
+                continue
+            if isinstance(src, bark.SafetensorsSource) and src.read_dtype(name) == "BF16":
+                self.load_one(name, ("bf16", src.read(name)))
+                continue
+            v = src.read(name)
+            if v.dtype == np.float16:
+                self.load_one(name, ("f16", v.view(np.uint16)))
+            elif v.dtype == np.float32:
+                self.load_one(name, v)
+        if isinstance(src, bark.BarkContainer):
+            return src.layers()
+        return len({n.split(".")[2] for n in src.tensor_names() if n.startswith("encoder.layers.")})
 
     def finalize(self, n_layers: int = N_LAYERS) -> None:
         check(self._L.b3_finalize(self.ctx, n_layers))

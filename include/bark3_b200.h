@@ -221,6 +221,34 @@ int b3_linear_lut4_noalloc(const float* a, const uint8_t* codes, const uint16_t*
  * x is [t][1024]. */
 int b3_attn_conv(b3_ctx* ctx, int layer, float* x, int t, unsigned flags);
 
+/* ─────────────────────── .bark container streams ───────────────────────
+ * Host-only entropy decoding of the `model.bark` weight container (no GPU
+ * work; callable without a device).  The container's JSON index, LZMA fields
+ * and level tables are parsed by the caller (bark3-wgpu_b200/bark.py mirrors
+ * BarkContainer, src/bark.rs:98-560); these calls replace its constriction
+ * 0.5.0 ANS decoding: a stack ANS coder with u32 words and a u64 state over a
+ * 24-bit categorical model quantised by from_floating_point_probabilities_fast.
+ * Malformed input returns B3_EINVAL with the reference's message. */
+
+/* The model's quantised cumulative table: cdf[0..n_symbols] (cdf[n] = 2^24). */
+int b3_bark_ans_cdf(const uint32_t* counts, int n_symbols, uint32_t* cdf);
+
+/* n i.i.d. symbols of one model from one stream (decode_iid_symbols). */
+int b3_bark_ans_decode(const uint32_t* counts, int n_symbols, const uint32_t* words, int64_t n_words,
+                       int64_t n, uint16_t* symbols);
+
+/* A "levels2" entry (decode_levels2, src/bark.rs:277-366): meta = column
+ * classes (4 bits per column, high nibble even) then 16 x (2k+1) u32 counts;
+ * words = the ANS stream.  Writes rows x ceil(cols/8) code words, nibble
+ * col % 8 of word col / 8 — the layout b3_load_lowbit_levels takes. */
+int b3_bark_decode_levels2(const uint8_t* meta, int64_t meta_bytes, const uint32_t* words, int64_t n_words,
+                           int rows, int cols, int k, uint32_t* code_words);
+
+/* An "ansint<bits>" entry (src/bark.rs:387-431): out[i] = (symbol_i -
+ * (2^(bits-1) - 1)) * f16 row_scales[i / (n / rows)]. */
+int b3_bark_decode_ansint(const uint32_t* counts, int n_symbols, const uint32_t* words, int64_t n_words,
+                          int64_t n, int bits, const uint16_t* row_scales, int64_t rows, float* out);
+
 /* ──────────────────────────── multi-GPU ────────────────────────────
  * Utterance sharding for one process (or host thread) per GPU.  The reference
  * is single-device; utterances are independent, so a batch is split across

@@ -1343,3 +1343,96 @@ int or_subsample(const float* mel, int f, int n_valid, const float* w0, const fl
     free(x5);
     return t;
 }
+
+/* ─────────────────────── .bark entropy coding (ANS) ───────────────────────
+ * constriction 0.5.0, the crate src/bark.rs decodes the container with
+ * (src/bark.rs:314-326, 398-421): `DefaultAnsCoder` = stack ANS over u32 words
+ * with a u64 state; `DefaultContiguousCategoricalEntropyModel` = 24-bit
+ * probabilities quantised by `from_floating_point_probabilities_fast`.  Its
+ * published algorithm, restated: each symbol keeps one unit of mass and the
+ * remaining 2^24 - n units follow the floor of the scaled running sum.  No
+ * constriction-written stream or `.bark` file is available here, so these
+ * restatements are checked only against each other and round trips
+ * (parity unpinned).  The encoder exists to build test containers. */
+
+int or_ans_cdf(const uint32_t* counts, int n, uint32_t* cdf) {
+    if (n < 2 || n >= (1 << 24)) return -1;
+    double total = 0.0, norm = 0.0, run = 0.0;
+    for (int i = 0; i < n; i++) total += (double)counts[i];
+    if (!(total > 0.0)) return -1;
+    for (int i = 0; i < n; i++) norm += (double)counts[i] / total;
+    if (!isnormal(norm) || norm < 0.0) return -1;
+    double scale = (double)((1u << 24) - (uint32_t)n) / norm;
+    for (int i = 0; i < n; i++) {
+        cdf[i] = (uint32_t)(run * scale) + (uint32_t)i;
+        run += (double)counts[i] / total;
+    }
+    cdf[n] = 1u << 24;
+    return 0;
+}
+
+/* Pushes sym[n-1], ..., sym[0] (so a decoder pops them in order 0..n-1)
+ * onto the coder (state, words[0..*n_words)).  Returns -1 when cap words
+ * would be exceeded. */
+int or_ans_push_reverse(uint64_t* state, uint32_t* words, int64_t* n_words, int64_t cap, const uint16_t* sym,
+                        int64_t n, const uint32_t* cdf, int n_symbols) {
+    uint64_t s = *state;
+    int64_t w = *n_words;
+    for (int64_t i = n - 1; i >= 0; i--) {
+        int c = sym[i];
+        if (c < 0 || c >= n_symbols) return -2;
+        uint64_t lo = cdf[c], p = (uint64_t)cdf[c + 1] - lo;
+        if ((s >> 40) >= p) {
+            if (w >= cap) return -1;
+            words[w++] = (uint32_t)s;
+            s >>= 32;
+        }
+        s = ((s / p) << 24) | (s % p + lo);
+    }
+    *state = s;
+    *n_words = w;
+    return 0;
+}
+
+/* Final state onto the stack, low word first (the top word is never zero). */
+int or_ans_flush(uint64_t* state, uint32_t* words, int64_t* n_words, int64_t cap) {
+    uint64_t s = *state;
+    int64_t w = *n_words;
+    while (s) {
+        if (w >= cap) return -1;
+        words[w++] = (uint32_t)s;
+        s >>= 32;
+    }
+    *state = 0;
+    *n_words = w;
+    return 0;
+}
+
+/* Decoder with a caller-held position: *top words are still on the stack.
+ * or_ans_open returns -1 for a zero top word. */
+int or_ans_open(const uint32_t* words, int64_t* top, uint64_t* state) {
+    *state = 0;
+    if (*top == 0) return 0;
+    uint32_t first = words[--*top];
+    if (first == 0) return -1;
+    uint64_t s = first;
+    while (*top > 0 && s < ((uint64_t)1 << 32)) s = (s << 32) | words[--*top];
+    *state = s;
+    return 0;
+}
+
+void or_ans_pop(const uint32_t* words, int64_t* top, uint64_t* state, const uint32_t* cdf, int n_symbols,
+                uint16_t* out, int64_t n) {
+    uint64_t s = *state;
+    int64_t t = *top;
+    for (int64_t i = 0; i < n; i++) {
+        uint32_t q = (uint32_t)(s & 0xFFFFFF);
+        int c = 0;
+        while (c + 1 < n_symbols && cdf[c + 1] <= q) c++;
+        s = (s >> 24) * (uint64_t)(cdf[c + 1] - cdf[c]) + (q - cdf[c]);
+        if (s < ((uint64_t)1 << 32) && t > 0) s = (s << 32) | words[--t];
+        out[i] = (uint16_t)c;
+    }
+    *state = s;
+    *top = t;
+}

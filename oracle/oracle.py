@@ -65,6 +65,11 @@ def lib() -> ctypes.CDLL:
             "or_tdt_decode_batch": (None, [_P, _P, _P, _I, _P, _P, _I]),
             "or_mel": (_I, [_P, ctypes.c_int64, _P, _P, _P]),
             "or_subsample": (_I, [_P, _I, _I] + [_P] * 11),
+            "or_ans_cdf": (_I, [_P, _I, _P]),
+            "or_ans_push_reverse": (_I, [_P, _P, _P, ctypes.c_int64, _P, ctypes.c_int64, _P, _I]),
+            "or_ans_flush": (_I, [_P, _P, _P, ctypes.c_int64]),
+            "or_ans_open": (_I, [_P, _P, _P]),
+            "or_ans_pop": (None, [_P, _P, _P, _P, _I, _P, ctypes.c_int64]),
         }
         for name, (res, args) in sig.items():
             f = getattr(L, name)
