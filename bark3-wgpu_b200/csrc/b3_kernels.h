@@ -1,5 +1,6 @@
 // b3_kernels.h — host launchers of the non-GEMM kernels.
 #pragma once
+#include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -63,15 +64,43 @@ struct DecState {
     uint32_t* tokens;        // [B][max_tokens][3] (id, frame, duration)
 };
 
-int dec_max_parts();   // most split-K parts the decoder kernels add
+// One GEMM of the persistent decoder: out[B][N] (+)= A[B][K] . W[N][K]^T,
+// where A holds [hi | lo] f16 halves per 640-wide segment and W matches them
+// ([W_seg | W_seg]), so the logical K is half the stored one.  128 x bn tiles
+// (bn 128 or 256), the logical K cut into `ks` parts of `nkb` 64-wide
+// k-blocks; part p lands at rows [p * prow, p * prow + B), part 0 adds `bias`.
+struct DecGemm {
+    int m_tiles, n_tiles, bn, ks, nkb;
+    float* out;
+    int ldo;
+    const float* bias;
+};
+
+// Maps of the persistent decoder's GEMMs, indexed like DecPersist::g:
+// A over the activation rows, B over the f16 weights (box 64 x 128 / 64 x 64),
+// C over the f32 split-K parts (box 32 x 32, 128-byte swizzle).
+struct alignas(64) DecMaps {
+    CUtensorMap a[4];
+    CUtensorMap b[4];
+    CUtensorMap c[4];
+};
+
+// The whole greedy decode of one batch in one cooperative launch.
+struct DecPersist {
+    DecState s;
+    DecGemm g[4];        // kDecHead, kDecLstm0, kDecLstm1, kDecProj
+    unsigned int* sync;  // [0] barrier arrivals, [1] abort flag, [2..3] active-row counts (host-zeroed)
+    int max_steps;       // lock steps at most (every row is bounded on its own as well)
+};
+constexpr int kDecHead = 0, kDecLstm0 = 1, kDecLstm1 = 2, kDecProj = 3;
+
+// CTAs of the persistent decoder that fit on the device at once (0 if none).
+int dec_persistent_grid(int device);
+int dec_launch_persistent(const DecMaps& maps, const DecPersist& p, int grid, cudaStream_t st);
+// Tile widths and splits of the four GEMMs for `grid` CTAs (DecPersist::g order).
+void dec_plan_persistent(int B, int npad, int grid, int bn[4], int ks[4]);
 int dec_launch_init(const DecState& s, cudaStream_t st);
-int dec_launch_joint_in(const DecState& s, cudaStream_t st);
-int dec_launch_argmax(const DecState& s, cudaStream_t st);
-int dec_launch_lstm_update(const DecState& s, int layer, cudaStream_t st);
-int dec_launch_any_active(const DecState& s, int* out, cudaStream_t st);
 int dec_launch_split(const float* src, __half* hi, __half* lo, int64_t n, cudaStream_t st);
-// Scatters the group's tokens / counts to rows out_row[b] of the batch outputs.
-int dec_launch_gather(const DecState& s, const int* out_row, uint32_t* out_tokens, int* out_count, cudaStream_t st);
 
 // Mel front end (frontend.cu).
 struct MelParams {

@@ -146,6 +146,61 @@ __device__ __forceinline__ void fence_async_shared() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// Generic-proxy global-memory writes (made visible to this thread) become
+// visible to its later async-proxy (TMA) reads after this fence.
+__device__ __forceinline__ void fence_async_global() {
+    asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+__device__ __forceinline__ unsigned int ld_acquire_gpu(const unsigned int* p) {
+    unsigned int v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Grid-wide barrier for a kernel whose CTAs are all resident (cooperative
+// launch).  `ctr` counts arrivals over the kernel's life; `target` is this
+// CTA's running total (nblocks more per barrier); `abort_flag` set by any CTA
+// ends every wait.  Bounded like mbar_wait: on time-out it records the error,
+// raises the abort flag and returns false.  Call with all threads of the CTA;
+// `ok_smem` is a shared int that carries thread 0's verdict to the others.
+__device__ __forceinline__ bool grid_barrier(unsigned int* ctr, unsigned int* abort_flag, unsigned int nblocks,
+                                             unsigned int& target, bool fail, int* ok_smem,
+                                             unsigned int site) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        target += nblocks;
+        int ok = 1;
+        if (fail) {
+            atomicExch(abort_flag, 1u);
+            ok = 0;
+        }
+        __threadfence();
+        atomicAdd(ctr, 1u);
+        unsigned long long t0 = 0;
+        while (ok) {
+            const unsigned int v = ld_acquire_gpu(ctr);
+            if (static_cast<int>(v - target) >= 0) break;
+            if (*reinterpret_cast<volatile unsigned int*>(abort_flag)) {
+                ok = 0;
+                break;
+            }
+            const unsigned long long t = globaltimer();
+            if (t0 == 0) {
+                t0 = t;
+            } else if (t - t0 > kWaitLimitNs) {
+                record_error(B3_ERR_TIMEOUT | site);
+                atomicExch(abort_flag, 1u);
+                ok = 0;
+            }
+        }
+        __threadfence();
+        *reinterpret_cast<volatile int*>(ok_smem) = ok;
+    }
+    __syncthreads();
+    return *reinterpret_cast<volatile int*>(ok_smem) != 0;
+}
+
 // ────────────────────────────── tcgen05 ──────────────────────────────
 
 template <uint32_t kCols>

@@ -201,22 +201,8 @@ struct b3_ctx {
         Linear proj;                           // [640][1280]  = W_p | W_p
         Linear head;                           // [npad][1280] = W_head | W_head (zero rows past vocab+5)
         DevBuf bias;                           // f32: lstm0 [2560] (unused) | lstm1 [2560] | proj [640] | head [npad]
-        DevBuf tokens, counts, pooler;         // batch outputs in utterance order; staged pooler
-        // The batch is decoded as independent groups of utterances, each a
-        // lock-step chain on its own stream with its own captured chunk graph:
-        // one chain's step is a sequence of small latency-bound kernels, so
-        // two chains share the GPU almost for free.
-        struct Group {
-            int B = 0;
-            DevBuf a0, a1, ap, aj, gates, cstate, dec, scores, ints, tokens, rows, flag;
-            cudaStream_t stream = nullptr;
-            cudaEvent_t done = nullptr;
-            cudaGraphExec_t exec = nullptr;    // captured decode chunk
-            std::vector<int64_t> key;          // buffers and shape the graph was captured with
-            int64_t launches[B3_K_COUNT] = {};
-        };
-        Group groups[2];
-        cudaEvent_t ready = nullptr;
+        // lock-step state (DecState), split-K parts, outputs, barrier words
+        DevBuf a0, a1, ap, aj, gates, cstate, dec, scores, ints, tokens, rows, sync, pooler;
     } dec;
     // mel front end + conv subsampling (optional: built when the conv
     // subsampling tensors are loaded)
@@ -240,22 +226,14 @@ struct b3_ctx {
         for (DevBuf* b : {&fe.tables, &fe.conv, &fe.pw_bias, &fe.wave, &fe.wave_off, &fe.frame_off, &fe.mel, &fe.x2,
                           &fe.x3, &fe.x4, &fe.ints, &fe.work})
             b->release();
-        for (auto& gr : dec.groups) {
-            if (gr.exec) cudaGraphExecDestroy(gr.exec);
-            if (gr.stream) cudaStreamSynchronize(gr.stream);
-            for (DevBuf* b : {&gr.a0, &gr.a1, &gr.ap, &gr.aj, &gr.gates, &gr.cstate, &gr.dec, &gr.scores, &gr.ints,
-                              &gr.tokens, &gr.rows, &gr.flag})
-                b->release();
-            if (gr.done) cudaEventDestroy(gr.done);
-            if (gr.stream) cudaStreamDestroy(gr.stream);
-        }
-        if (dec.ready) cudaEventDestroy(dec.ready);
         for (cudaEvent_t e : prof.pool) cudaEventDestroy(e);
         for (Linear* l : {&dec.lstm[0], &dec.lstm[1], &dec.proj, &dec.head}) {
             l->w.release();
             l->lut16.release();
         }
-        for (DevBuf* b : {&dec.e0, &dec.bias, &dec.tokens, &dec.counts, &dec.pooler}) b->release();
+        for (DevBuf* b : {&dec.e0, &dec.bias, &dec.a0, &dec.a1, &dec.ap, &dec.aj, &dec.gates, &dec.cstate, &dec.dec,
+                          &dec.scores, &dec.ints, &dec.tokens, &dec.rows, &dec.sync, &dec.pooler})
+            b->release();
         auto rel = [](Linear& l) { l.w.release(); l.lut16.release(); };
         rel(sub_w);
         rel(proj_w);
@@ -830,245 +808,103 @@ int build_decoder(b3_ctx* c) {
     return 0;
 }
 
-// Split-K plans of the four decoder GEMMs for a batch of B rows.
-struct DecPlan {
-    int tiles[4], ks[4];   // layer 0, layer 1, projector, head
-};
-
-// sms: the SMs this group's GEMMs should spread over.
-DecPlan dec_plan(b3_ctx* c, int B, int sms) {
-    auto& D = c->dec;
-    DecPlan pl;
-    const Linear* w[4] = {&D.lstm[0], &D.lstm[1], &D.proj, &D.head};
-    for (int i = 0; i < 4; ++i) gemm_plan_split(B, w[i]->N, w[i]->K, false, sms, dec_max_parts(), &pl.tiles[i], &pl.ks[i]);
-    return pl;
-}
-
-int dec_ensure(b3_ctx* c, b3_ctx::Decoder::Group& g, int B, int max_tokens, const DecPlan& pl) {
-    auto& D = c->dec;
-    const size_t b = static_cast<size_t>(B);
-    const size_t prow = static_cast<size_t>(gemm_split_rows(B));
-    const int ksg = std::max(pl.ks[0], pl.ks[1]);
-    B3_TRY(g.a0.ensure(b * 1280 * 2));
-    B3_TRY(g.a1.ensure(b * 2560 * 2));
-    B3_TRY(g.ap.ensure(b * 1280 * 2));
-    B3_TRY(g.aj.ensure(b * 1280 * 2));
-    B3_TRY(g.gates.ensure(ksg * prow * 2560 * 4));
-    B3_TRY(g.cstate.ensure(b * 2 * 640 * 4));
-    B3_TRY(g.dec.ensure(pl.ks[2] * prow * 640 * 4));
-    B3_TRY(g.scores.ensure(pl.ks[3] * prow * D.npad * 4));
-    B3_TRY(g.ints.ensure(b * 6 * 4));
-    B3_TRY(g.tokens.ensure(b * static_cast<size_t>(max_tokens) * 12));
-    B3_TRY(g.rows.ensure(b * 3 * 4));
-    B3_TRY(g.flag.ensure(16));
-    if (!g.stream) B3_CUDA(cudaStreamCreateWithFlags(&g.stream, cudaStreamNonBlocking));
-    if (!g.done) B3_CUDA(cudaEventCreateWithFlags(&g.done, cudaEventDisableTiming));
-    return 0;
-}
-
-GemmParams dec_params(float* out, int ldo, const float* bias, const DecPlan& pl, int i) {
-    GemmParams p = params_f32(out, ldo, bias);
-    p.ksplit = pl.ks[i];
-    p.tiles = pl.tiles[i];
-    p.pdl = 1;
-    return p;
-}
-
-int dec_lstm_step(b3_ctx* c, const DecState& s, const DecPlan& pl) {
-    auto& D = c->dec;
-    const float* bias = D.bias.as<float>();
-    B3_TRY(run_gemm(c, D.lstm[0], s.a0, s.B, 1280, EPI_F32, dec_params(s.gates, 2560, nullptr, pl, 0)));
-    {
-        ProfScope ps(c, B3_K_DECODER, 0.0, 0.0);
-        B3_TRY(dec_launch_lstm_update(s, 0, c->stream));
-    }
-    B3_TRY(run_gemm(c, D.lstm[1], s.a1, s.B, 2560, EPI_F32, dec_params(s.gates, 2560, bias + 2560, pl, 1)));
-    {
-        ProfScope ps(c, B3_K_DECODER, 0.0, 0.0);
-        B3_TRY(dec_launch_lstm_update(s, 1, c->stream));
-    }
-    return run_gemm(c, D.proj, s.ap, s.B, 1280, EPI_F32, dec_params(s.dec, 640, bias + 5120, pl, 2));
-}
-
-// Makes a decoder group's work go to its stream for the scope (every launch
-// helper uses c->stream).
-struct StreamSwap {
-    b3_ctx* c;
-    cudaStream_t saved;
-    StreamSwap(b3_ctx* c_, cudaStream_t st) : c(c_), saved(c_->stream) { c->stream = st; }
-    ~StreamSwap() { c->stream = saved; }
-};
-
-// Greedy-decodes n_utt utterances of a device pooler [total][640]; the
-// tokens and counts are left in the decoder's output buffers in utterance
-// order, ordered on the context stream.
-
+// Greedy-decodes n_utt utterances of a device pooler [total][640] with one
+// cooperative launch of the persistent decoder; the tokens and counts are
+// left in the decoder's buffers (row b = utterance b).
 int decode_device(b3_ctx* c, const float* pooler, const int32_t* cu, int n_utt, int max_tokens) {
     auto& D = c->dec;
     if (!D.present) return set_error(B3_ESTATE, "no decoder weights were loaded");
     if (n_utt <= 0 || max_tokens <= 0) return set_error(B3_EINVAL, "bad decode batch");
-    std::vector<int> len(n_utt);
-    for (int i = 0; i < n_utt; ++i) {
-        len[i] = cu[i + 1] - cu[i];
-        if (len[i] < 0) return set_error(B3_EINVAL, "cu_seqlens must be non-decreasing");
+    const int B = n_utt;
+    std::vector<int32_t> rows(2 * B);
+    int tmax = 0;
+    for (int b = 0; b < B; ++b) {
+        rows[b] = cu[b];
+        rows[B + b] = cu[b + 1] - cu[b];
+        if (rows[B + b] < 0) return set_error(B3_EINVAL, "cu_seqlens must be non-decreasing");
+        tmax = std::max(tmax, rows[B + b]);
     }
-    // Groups: one below 64 utterances, else two, dealt longest-first in a
-    // snake order so both get similar lengths (a chain runs as long as its
-    // longest utterance).
-    const int G = n_utt >= 64 ? 2 : 1;
-    std::vector<int> order(n_utt);
-    for (int i = 0; i < n_utt; ++i) order[i] = i;
-    std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return len[a] > len[b]; });
-    std::vector<std::vector<int>> members(G);
-    for (int k = 0; k < n_utt; ++k) members[G == 1 ? 0 : ((k & 3) == 0 || (k & 3) == 3 ? 0 : 1)].push_back(order[k]);
-    int sms = 0;
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, c->device);
-    if (sms <= 0) sms = 148;
+    const int grid = dec_persistent_grid(c->device);
+    if (grid <= 0) return set_error(B3_ECUDA, "the persistent decoder does not fit on this device");
+    int bn[4], ks[4];
+    dec_plan_persistent(B, D.npad, grid, bn, ks);
+    const size_t b = static_cast<size_t>(B);
+    const size_t prow = static_cast<size_t>(gemm_split_rows(B));
+    B3_TRY(D.a0.ensure(b * 1280 * 2));
+    B3_TRY(D.a1.ensure(b * 2560 * 2));
+    B3_TRY(D.ap.ensure(b * 1280 * 2));
+    B3_TRY(D.aj.ensure(b * 1280 * 2));
+    B3_TRY(D.gates.ensure(std::max(ks[kDecLstm0], ks[kDecLstm1]) * prow * 2560 * 4));
+    B3_TRY(D.cstate.ensure(b * 2 * 640 * 4));
+    B3_TRY(D.dec.ensure(ks[kDecProj] * prow * 640 * 4));
+    B3_TRY(D.scores.ensure(ks[kDecHead] * prow * D.npad * 4));
+    B3_TRY(D.ints.ensure(b * 6 * 4));
+    B3_TRY(D.tokens.ensure(b * static_cast<size_t>(max_tokens) * 12));
+    B3_TRY(D.rows.ensure(b * 2 * 4));
+    B3_TRY(D.sync.ensure(16));
+    ProfScope ps(c, B3_K_DECODER, 0.0, 0.0);
+    c->prof.launches[B3_K_DECODER]++;   // init + the persistent kernel
+    B3_CUDA(cudaMemcpyAsync(D.rows.p, rows.data(), rows.size() * 4, cudaMemcpyHostToDevice, c->stream));
+    B3_CUDA(cudaMemsetAsync(D.sync.p, 0, 16, c->stream));
 
-    B3_TRY(D.tokens.ensure(static_cast<size_t>(n_utt) * max_tokens * 12));
-    B3_TRY(D.counts.ensure(static_cast<size_t>(n_utt) * 4));
-    if (!D.ready) B3_CUDA(cudaEventCreateWithFlags(&D.ready, cudaEventDisableTiming));
-    // the whole decode is one profiled record on the context stream
-    ProfScope ps_all(c, B3_K_DECODER, 0.0, 0.0);
-    c->prof.launches[B3_K_DECODER]--;
-    const bool prof_on = c->prof.on;
-    c->prof.on = false;
-    struct Restore {
-        b3_ctx* c;
-        bool on;
-        ~Restore() { c->prof.on = on; }
-    } restore{c, prof_on};
-    B3_CUDA(cudaEventRecord(D.ready, c->stream));   // the pooler is ready
-
-    DecState st[2];
-    long max_steps[2];
-    const float* head_bias = D.bias.as<float>() + 5120 + 640;
-    constexpr int kChunk = 16;
-    for (int gi = 0; gi < G; ++gi) {
-        auto& g = D.groups[gi];
-        const std::vector<int>& mem = members[gi];
-        const int B = static_cast<int>(mem.size());
-        const DecPlan pl = dec_plan(c, B, sms / G);
-        B3_TRY(dec_ensure(c, g, B, max_tokens, pl));
-        std::vector<int32_t> rows(3 * B);
-        int tmax = 0;
-        for (int b = 0; b < B; ++b) {
-            rows[b] = cu[mem[b]];
-            rows[B + b] = len[mem[b]];
-            rows[2 * B + b] = mem[b];
-            tmax = std::max(tmax, len[mem[b]]);
-        }
-        max_steps[gi] = static_cast<long>(tmax) * 14 + 64;
-        B3_CUDA(cudaStreamWaitEvent(g.stream, D.ready, 0));
-        B3_CUDA(cudaMemcpyAsync(g.rows.p, rows.data(), rows.size() * 4, cudaMemcpyHostToDevice, g.stream));
-        DecState& s = st[gi];
-        s.B = B;
-        s.vocab = D.vocab;
-        s.blank = D.vocab - 1;
-        s.max_tokens = max_tokens;
-        s.row0 = g.rows.as<int>();
-        s.len = g.rows.as<int>() + B;
-        s.pooler = pooler;
-        s.e0 = D.e0.as<float>();
-        s.a0 = g.a0.as<__half>();
-        s.a1 = g.a1.as<__half>();
-        s.ap = g.ap.as<__half>();
-        s.aj = g.aj.as<__half>();
-        s.gates = g.gates.as<float>();
-        s.c = g.cstate.as<float>();
-        s.dec = g.dec.as<float>();
-        s.scores = g.scores.as<float>();
-        s.ld_scores = D.npad;
-        s.prow = gemm_split_rows(B);
-        s.ks_g0 = pl.ks[0];
-        s.ks_g1 = pl.ks[1];
-        s.ks_p = pl.ks[2];
-        s.ks_h = pl.ks[3];
-        int* ints = g.ints.as<int>();
-        s.frame = ints;
-        s.count = ints + B;
-        s.guard = ints + 2 * B;
-        s.emit = ints + 3 * B;
-        s.active = ints + 4 * B;
-        s.tok = ints + 5 * B;
-        s.tokens = g.tokens.as<uint32_t>();
-
-        StreamSwap sw(c, g.stream);
-        c->prof.launches[B3_K_DECODER]++;
-        B3_TRY(dec_launch_init(s, c->stream));
-        B3_TRY(dec_lstm_step(c, s, pl));
-        // One chunk = kChunk lock steps + the "any row still active" reduction,
-        // captured once as a CUDA graph and replayed until every row is done.
-        auto chunk = [&]() -> int {
-            for (int k = 0; k < kChunk; ++k) {
-                B3_TRY(dec_launch_joint_in(s, c->stream));
-                B3_TRY(run_gemm(c, D.head, s.aj, s.B, 1280, EPI_F32, dec_params(s.scores, D.npad, head_bias, pl, 3)));
-                B3_TRY(dec_launch_argmax(s, c->stream));
-                B3_TRY(dec_lstm_step(c, s, pl));
-            }
-            return dec_launch_any_active(s, g.flag.as<int>(), c->stream);
-        };
-        const std::vector<int64_t> key = {reinterpret_cast<int64_t>(s.pooler), reinterpret_cast<int64_t>(s.a0),
-                                          reinterpret_cast<int64_t>(s.tokens), reinterpret_cast<int64_t>(s.scores),
-                                          reinterpret_cast<int64_t>(s.gates), reinterpret_cast<int64_t>(s.row0),
-                                          static_cast<int64_t>(B) << 20 | max_tokens};
-        if (!g.exec || key != g.key) {
-            if (g.exec) cudaGraphExecDestroy(g.exec);
-            g.exec = nullptr;
-            int64_t pre[B3_K_COUNT];
-            memcpy(pre, c->prof.launches, sizeof(pre));
-            B3_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
-            const int rc = chunk();
-            cudaGraph_t graph = nullptr;
-            const cudaError_t ec = cudaStreamEndCapture(c->stream, &graph);
-            if (rc) {
-                if (graph) cudaGraphDestroy(graph);
-                return rc;
-            }
-            if (ec != cudaSuccess) return set_cuda_error("capturing the decoder chunk", ec);
-            const cudaError_t ei = cudaGraphInstantiate(&g.exec, graph, 0);
-            cudaGraphDestroy(graph);
-            if (ei != cudaSuccess) {
-                g.exec = nullptr;
-                return set_cuda_error("instantiating the decoder chunk", ei);
-            }
-            for (int k = 0; k < B3_K_COUNT; ++k) {
-                g.launches[k] = c->prof.launches[k] - pre[k];
-                c->prof.launches[k] = pre[k];
-            }
-            g.key = key;
-        }
+    DecPersist p{};
+    DecState& s = p.s;
+    s.B = B;
+    s.vocab = D.vocab;
+    s.blank = D.vocab - 1;
+    s.max_tokens = max_tokens;
+    s.row0 = D.rows.as<int>();
+    s.len = D.rows.as<int>() + B;
+    s.pooler = pooler;
+    s.e0 = D.e0.as<float>();
+    s.a0 = D.a0.as<__half>();
+    s.a1 = D.a1.as<__half>();
+    s.ap = D.ap.as<__half>();
+    s.aj = D.aj.as<__half>();
+    s.gates = D.gates.as<float>();
+    s.c = D.cstate.as<float>();
+    s.dec = D.dec.as<float>();
+    s.scores = D.scores.as<float>();
+    s.ld_scores = D.npad;
+    s.prow = static_cast<int>(prow);
+    s.ks_g0 = ks[kDecLstm0];
+    s.ks_g1 = ks[kDecLstm1];
+    s.ks_p = ks[kDecProj];
+    s.ks_h = ks[kDecHead];
+    int* ints = D.ints.as<int>();
+    s.frame = ints;
+    s.count = ints + B;
+    s.guard = ints + 2 * B;
+    s.emit = ints + 3 * B;
+    s.active = ints + 4 * B;
+    s.tok = ints + 5 * B;
+    s.tokens = D.tokens.as<uint32_t>();
+    const float* bias = D.bias.as<float>();
+    const Linear* w[4] = {&D.head, &D.lstm[0], &D.lstm[1], &D.proj};
+    __half* acts[4] = {s.aj, s.a0, s.a1, s.ap};
+    float* outs[4] = {s.scores, s.gates, s.gates, s.dec};
+    const int ldos[4] = {D.npad, 2560, 2560, 640};
+    const float* biases[4] = {bias + 5120 + 640, nullptr, bias + 2560, bias + 5120};
+    DecMaps maps;
+    for (int i = 0; i < 4; ++i) {
+        B3_TRY(gemm_make_a_map(&maps.a[i], acts[i], B, w[i]->K, w[i]->K));
+        maps.b[i] = w[i]->map_b;
+        B3_TRY(make_map_2d(&maps.c[i], outs[i], kMapF32, static_cast<uint64_t>(ldos[i]),
+                           static_cast<uint64_t>(ks[i]) * prow, static_cast<uint64_t>(ldos[i]) * 4, 32, 32, true));
+        DecGemm& g = p.g[i];
+        g.m_tiles = (B + 127) / 128;
+        g.bn = bn[i];
+        g.n_tiles = w[i]->N / bn[i];
+        g.ks = ks[i];
+        g.nkb = w[i]->K / 2 / 64 / ks[i];
+        g.out = outs[i];
+        g.ldo = ldos[i];
+        g.bias = biases[i];
     }
-    // replay every group's chunk, then read every group's "still active" flag
-    int any[2] = {1, G > 1 ? 1 : 0};
-    for (long step = 0; any[0] || any[1]; step += kChunk) {
-        for (int gi = 0; gi < G; ++gi) {
-            auto& g = D.groups[gi];
-            if (!any[gi]) continue;
-            if (step >= max_steps[gi]) {
-                any[gi] = 0;
-                continue;
-            }
-            B3_CUDA(cudaGraphLaunch(g.exec, g.stream));
-            for (int k = 0; k < B3_K_COUNT; ++k) c->prof.launches[k] += g.launches[k];
-        }
-        for (int gi = 0; gi < G; ++gi) {
-            if (!any[gi]) continue;
-            auto& g = D.groups[gi];
-            B3_CUDA(cudaMemcpyAsync(&any[gi], g.flag.p, sizeof(int), cudaMemcpyDeviceToHost, g.stream));
-        }
-        for (int gi = 0; gi < G; ++gi) B3_CUDA(cudaStreamSynchronize(D.groups[gi].stream));
-    }
-    // tokens back in utterance order, on the context stream
-    for (int gi = 0; gi < G; ++gi) {
-        auto& g = D.groups[gi];
-        c->prof.launches[B3_K_DECODER]++;
-        B3_TRY(dec_launch_gather(st[gi], g.rows.as<int>() + 2 * st[gi].B, D.tokens.as<uint32_t>(), D.counts.as<int>(),
-                                 g.stream));
-        B3_CUDA(cudaEventRecord(g.done, g.stream));
-        B3_CUDA(cudaStreamWaitEvent(c->stream, g.done, 0));
-    }
-    return 0;
+    p.sync = D.sync.as<unsigned int>();
+    p.max_steps = tmax * 14 + 64;
+    B3_TRY(dec_launch_init(s, c->stream));
+    return dec_launch_persistent(maps, p, grid, c->stream);
 }
 
 // Copies the decoder's tokens / counts out (device or host destination).
@@ -1077,7 +913,7 @@ int decode_collect(b3_ctx* c, int n_utt, b3_token* tokens, int32_t* counts, int 
     const cudaMemcpyKind k = dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost;
     B3_CUDA(cudaMemcpyAsync(tokens, D.tokens.p, static_cast<size_t>(n_utt) * max_tokens * sizeof(b3_token), k,
                             c->stream));
-    B3_CUDA(cudaMemcpyAsync(counts, D.counts.p, n_utt * sizeof(int32_t), k, c->stream));
+    B3_CUDA(cudaMemcpyAsync(counts, D.ints.as<int>() + n_utt, n_utt * sizeof(int32_t), k, c->stream));
     return 0;
 }
 

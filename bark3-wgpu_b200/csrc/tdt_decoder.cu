@@ -3,21 +3,22 @@
 // workgroup set per step, src/tdt_gpu.rs).
 //
 // All utterances of a batch advance in lock step: one step is
-//   joint input   x_b = ReLU(enc_b[frame_b] + dec_b)                 (this file)
-//   joint GEMM    scores = x . head^T + bias          (K1, tensor cores)
+//   joint input   x_b = ReLU(enc_b[frame_b] + dec_b)
+//   joint GEMM    scores = x . head^T + bias                    (tensor cores)
 //   argmax/update first-max token over the vocabulary, first-max duration
 //                 over the 5 duration rows; blank advances >= 1 frame, a
-//                 token is recorded and advances `duration` frames   (this file)
-//   LSTM layer 0  gates = E0[token] + h0 . W_hh^T             (K1) + update
-//   LSTM layer 1  gates = [h0 | h1] . [W_ih | W_hh]^T + b     (K1) + update
-//   projector     dec = h1 . W_p^T + b                        (K1)
+//                 token is recorded and advances `duration` frames
+//   LSTM layer 0  gates = E0[token] + h0 . W_hh^T          (tensor cores) + cell
+//   LSTM layer 1  gates = [h0 | h1] . [W_ih | W_hh]^T + b  (tensor cores) + cell
+//   projector     dec = h1 . W_p^T + b                     (tensor cores)
 // E0[v] = W_ih0 . emb(v) + b_ih0 + b_hh0 is computed once per vocabulary
 // entry at load, so layer 0's GEMM only carries the recurrent half.  Rows
 // that did not emit keep their LSTM state (their gates are computed and
-// dropped), so recomputing dec for them reproduces the same value.
+// dropped), so recomputing dec for them reproduces the same value.  The whole
+// decode is one cooperative launch of k_dec_persist (below).
 //
-// The GEMMs have M = batch rows only, so K1 runs them split-K over all SMs;
-// every consumer below adds the K parts in a fixed order (deterministic).
+// The GEMMs have M = batch rows only, so they run split-K over all SMs; every
+// consumer adds the K parts in a fixed order (deterministic).
 //
 // Precision: each GEMM input x is split into f16 hi = f16(x) and
 // lo = f16(x - hi) and the weight is repeated along K ([W | W]), so the
@@ -26,6 +27,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+
+#include <vector>
 
 #include "b3_internal.h"
 #include "b3_kernels.h"
@@ -124,25 +127,6 @@ __global__ void k_dec_init(DecState s) {
     }
 }
 
-// x_b = ReLU(enc[frame_b] + dec_b), split into hi | lo (zeros for finished
-// rows).  One block of 160 threads per row, 4 columns per thread.
-__global__ void __launch_bounds__(160) k_dec_joint_in(DecState s) {
-    pdl_wait();
-    pdl_launch_dependents();
-    const int b = blockIdx.x;
-    if (b >= s.B) return;
-    const int j = 4 * threadIdx.x;
-    const bool act = s.active[b] != 0;
-    __half* aj = s.aj + static_cast<size_t>(b) * 2 * kH;
-    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (act) {
-        const float4 e = __ldg(reinterpret_cast<const float4*>(s.pooler + static_cast<size_t>(s.row0[b] + s.frame[b]) * kH + j));
-        const float4 d = parts_sum4(s.dec, s.ks_p, s.prow, kH, b, j);
-        v = make_float4(fmaxf(e.x + d.x, 0.f), fmaxf(e.y + d.y, 0.f), fmaxf(e.z + d.z, 0.f), fmaxf(e.w + d.w, 0.f));
-    }
-    split_store4(aj + j, aj + kH + j, v);
-}
-
 // (value, index) pair that wins under the reference's strict `>` scan:
 // larger value, or the lower index on a tie.
 __device__ __forceinline__ bool wins(float v, int i, float bv, int bi) {
@@ -161,112 +145,247 @@ __device__ __forceinline__ void warp_argmax(float& v, int& i) {
     }
 }
 
-// Argmax over one row of scores and the step's state update.  One block of
-// 256 threads per utterance; each thread scans 4 consecutive vocabulary
-// entries per 1024-wide chunk; ties keep the lowest index.
-__global__ void __launch_bounds__(256) k_dec_argmax(DecState s) {
-    pdl_wait();
-    pdl_launch_dependents();
-    const int b = blockIdx.x;
-    if (b >= s.B) return;
-    __shared__ float wv[8];
-    __shared__ int wi[8];
-    __shared__ int wdur;
-    if (!s.active[b]) {
-        if (threadIdx.x == 0) s.emit[b] = 0;
-        return;
-    }
-    const int ld = s.ld_scores;
-    float best = -INFINITY;
-    int bidx = 0x7fffffff;
-    for (int base = 4 * threadIdx.x; base < s.vocab; base += 1024) {
-        const float4 v = parts_sum4(s.scores, s.ks_h, s.prow, ld, b, base);
-        const float e[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-            if (base + q < s.vocab && e[q] > best) {   // increasing index: strict > keeps the first max
-                best = e[q];
-                bidx = base + q;
-            }
-    }
-    warp_argmax(best, bidx);
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (lane == 0) {
-        wv[warp] = best;
-        wi[warp] = bidx;
-    }
-    if (warp == 0) {
-        // durations: the 5 rows after the vocabulary, first max
-        float dv = -INFINITY;
-        int di = 0x7fffffff;
-        if (lane < 5) {
-            dv = parts_sum1(s.scores, s.ks_h, s.prow, ld, b, s.vocab + lane);
-            di = lane;
-        }
-        warp_argmax(dv, di);
-        if (lane == 0) wdur = di;
-    }
-    __syncthreads();
-    if (threadIdx.x != 0) return;
-    float tv = wv[0];
-    int tok = wi[0];
-    for (int w = 1; w < 8; ++w)
-        if (wins(wv[w], wi[w], tv, tok)) {
-            tv = wv[w];
-            tok = wi[w];
-        }
-    int dur = wdur;
-    if (tok == 0x7fffffff) tok = 0;   // every score NaN: mirrors the reference's initial index
-    if (dur == 0x7fffffff) dur = 0;
-    const int T = s.len[b];
-    const bool emit = tok != s.blank;
-    const int frame = s.frame[b];
-    if (emit) {
-        const int n = s.count[b];
-        if (n < s.max_tokens) {
-            uint32_t* t = s.tokens + (static_cast<size_t>(b) * s.max_tokens + n) * 3;
-            t[0] = static_cast<uint32_t>(tok);
-            t[1] = static_cast<uint32_t>(frame);
-            t[2] = static_cast<uint32_t>(dur);
-        }
-        s.count[b] = n + 1;
-        s.frame[b] = frame + dur;
-        s.tok[b] = tok;
-    } else {
-        s.frame[b] = frame + (dur > 0 ? dur : 1);
-    }
-    const int g = s.guard[b] + 1;
-    s.guard[b] = g;
-    s.emit[b] = emit ? 1 : 0;
-    const long max_steps = static_cast<long>(T) * (10 + 4) + 64;
-    s.active[b] = (s.frame[b] < T && g < max_steps) ? 1 : 0;
+// Embedding rows as f16 hi | lo (load time).
+__global__ void k_split_rows(const float* __restrict__ src, __half* hi, __half* lo, int64_t n) {
+    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+        split_store(hi + i, lo + i, src[i]);
 }
 
-// LSTM cell update for rows that emitted: gates [B][2560] (i, f, g, o).
-// One block of 160 threads per row, 4 columns per thread.
-__global__ void __launch_bounds__(160) k_dec_lstm_update(DecState s, int layer) {
-    pdl_wait();
-    pdl_launch_dependents();
-    const int b = blockIdx.x;
-    if (b >= s.B || !s.emit[b]) return;
-    const int j = 4 * threadIdx.x;
-    const int parts = layer == 0 ? s.ks_g0 : s.ks_g1;
-    float4 g[4];
+// ─────────────────────── persistent decoder (one launch) ───────────────────────
+//
+// The lock step above as ONE cooperative launch: every CTA stays resident
+// (one per SM) and the step's six dependent phases are separated by grid
+// barriers instead of kernel boundaries:
+//   A  joint head GEMM  +  layer-0 recurrent GEMM (h0 is not changed by the
+//      argmax, so both read inputs that are ready)
+//   B  argmax + state update, then the layer-0 cell for the rows that emitted
+//   C  layer-1 GEMM        D  layer-1 cell
+//   E  projector GEMM      F  joint input x = ReLU(enc[frame] + dec)
+// The first pass runs C..F after a layer-0 step on the blank token (A without
+// the head, B without the argmax), as the reference starts (src/tdt.rs:424-428).
+//
+// GEMM phases are warp-specialised like K1: warp 0 issues TMA loads, warp 1
+// issues tcgen05.mma (M 128, N = 128 or 256, f32 accumulators in TMEM, two
+// buffers), warps 4..7 drain the accumulators to the split-K parts.  A work
+// item is (GEMM, 128-row tile, BN-column tile, K part); items are dealt
+// round-robin to the CTAs.  Activations are [hi | lo] f16 halves per 640-wide
+// segment and the weights are stored doubled to match ([W | W]); a stage holds
+// one 64-wide logical k-block: the hi and lo A boxes and ONE weight tile, and
+// the MMAs of both halves read that tile, so every weight byte crosses L2 once
+// per item.  The batch is small (M = rows), so these GEMMs are bound by the
+// bytes each SM pulls from L2, not by the tensor cores.
+// Row phases give each row to one half of a CTA (128 threads) and issue the
+// loads a phase needs together, so a phase costs one or two L2 round trips.
+// Activations written by the row phases are read by the next GEMM phase
+// through TMA (async proxy): writers and the TMA issuer fence the proxies
+// around the grid barrier.
+constexpr int kPThreads = 256;
+constexpr int kPStages = 3;
+constexpr uint32_t kPABytes = 128 * 64 * 2;             // one A box (hi or lo)
+constexpr uint32_t kPBBytes = 256 * 64 * 2;             // weight tile, up to 256 rows
+constexpr uint32_t kPStageBytes = 2 * kPABytes + kPBBytes;
+constexpr uint32_t kPSlabOff = kPStages * kPStageBytes;  // [4 warps][2] 32 x 32 f32 output slabs
+constexpr uint32_t kPBarOff = kPSlabOff + 8 * 4096;
+constexpr uint32_t kPBiasOff = kPBarOff + 256;           // [256] f32 item bias
+constexpr uint32_t kPSmem = kPBiasOff + 1024 + 1024;    // + alignment slack
+static_assert(kPSmem <= 232448, "shared memory budget");
+constexpr uint32_t kPTmemCols = 512;                    // two 256-column accumulators
+constexpr int kPSegK = 640;                             // logical K of one [hi | lo] segment
+
+struct PItem {
+    int g, m0, n0, bn, kb0, nkb, part;
+};
+
+// Item j of a phase's GEMM list (GEMMs in order, each part-major then m, n).
+__device__ __forceinline__ PItem p_item(const DecPersist& p, int g0, int g1, int j) {
+    for (int i = 0; i < 2; ++i) {
+        const int gi = i == 0 ? g0 : g1;
+        if (gi < 0) continue;
+        const DecGemm& G = p.g[gi];
+        const int mn = G.m_tiles * G.n_tiles;
+        if (j < mn * G.ks) {
+            const int part = j / mn, t = j % mn;
+            return PItem{gi, (t / G.n_tiles) * 128, (t % G.n_tiles) * G.bn, G.bn, part * G.nkb, G.nkb, part};
+        }
+        j -= mn * G.ks;
+    }
+    return PItem{-1, 0, 0, 0, 0, 0, 0};
+}
+
+__device__ __forceinline__ int p_items(const DecPersist& p, int g0, int g1) {
+    int n = 0;
+    if (g0 >= 0) n += p.g[g0].m_tiles * p.g[g0].n_tiles * p.g[g0].ks;
+    if (g1 >= 0) n += p.g[g1].m_tiles * p.g[g1].n_tiles * p.g[g1].ks;
+    return n;
+}
+
+struct PRing {
+    uint8_t* ring;
+    uint8_t* slabs;
+    float* bias;   // [256] the epilogue's current item bias
+    uint64_t* full;
+    uint64_t* empty;
+    uint64_t* tfull;
+    uint64_t* tempty;
+    uint32_t tmem;
+};
+
+// One GEMM phase on this CTA.  The role counters (`pit` ring slot of the
+// producer, `mit` of the MMA issuer, `acc` accumulator uses of the MMA issuer
+// and of the epilogue) persist across phases.  Returns false on a timed-out
+// wait.
+__device__ __forceinline__ bool p_gemm_phase(const DecMaps& maps, const DecPersist& p, const PRing& r, int g0,
+                                             int g1, int& pit, int& mit, int& acc) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n_items = p_items(p, g0, g1);
+    bool ok = true;
+    if (warp == 0) {
+        if (lane == 0) {
+            fence_async_global();   // row-phase writes -> the TMA reads below
+            for (int j = blockIdx.x; j < n_items && ok; j += gridDim.x) {
+                const PItem it = p_item(p, g0, g1, j);
+                for (int kb = 0; kb < it.nkb; ++kb, ++pit) {
+                    const int s = pit % kPStages;
+                    if (pit >= kPStages && !(ok = mbar_wait(smem_u32(&r.empty[s]), ((pit / kPStages) & 1) ^ 1, 0x61)))
+                        break;
+                    const int k = (it.kb0 + kb) * 64;                       // logical k
+                    const int x = (k / kPSegK) * 2 * kPSegK + k % kPSegK;  // its hi column
+                    const uint32_t fb = smem_u32(&r.full[s]);
+                    uint8_t* st = r.ring + s * kPStageBytes;
+                    mbar_arrive_expect_tx(fb, 2 * kPABytes + it.bn * 128);
+                    tma_load_2d(smem_u32(st), &maps.a[it.g], fb, x, it.m0);
+                    tma_load_2d(smem_u32(st + kPABytes), &maps.a[it.g], fb, x + kPSegK, it.m0);
+                    for (int q = 0; q < it.bn / 64; ++q)
+                        tma_load_2d(smem_u32(st + 2 * kPABytes + q * 8192), &maps.b[it.g], fb, x, it.n0 + 64 * q);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        if (lane == 0) {
+            for (int j = blockIdx.x; j < n_items && ok; j += gridDim.x, ++acc) {
+                const PItem it = p_item(p, g0, g1, j);
+                const uint32_t idesc = (1u << 4) | (static_cast<uint32_t>(it.bn >> 3) << 17) | ((128u >> 4) << 24);
+                const int b = acc & 1, use = acc >> 1;
+                if (use > 0 && !(ok = mbar_wait(smem_u32(&r.tempty[b]), (use - 1) & 1, 0x62))) break;
+                tc_fence_after();
+                const uint32_t d = r.tmem + b * 256;
+                for (int kb = 0; kb < it.nkb; ++kb, ++mit) {
+                    const int s = mit % kPStages;
+                    if (!(ok = mbar_wait(smem_u32(&r.full[s]), (mit / kPStages) & 1, 0x63))) break;
+                    tc_fence_after();
+                    const uint32_t a0 = smem_u32(r.ring + s * kPStageBytes);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) g[q] = parts_sum4(s.gates, parts, s.prow, 4 * kH, b, q * kH + j);
-    if (layer == 0) {
-        const float* e0 = s.e0 + static_cast<size_t>(s.tok[b]) * 4 * kH + j;
+                    for (int kk = 0; kk < 4; ++kk) {
+                        const uint64_t bd = smem_desc_sw128(a0 + 2 * kPABytes + kk * 32);
+                        mma_f16_ss(d, smem_desc_sw128(a0 + kk * 32), bd, idesc, (kb | kk) != 0);
+                        mma_f16_ss(d, smem_desc_sw128(a0 + kPABytes + kk * 32), bd, idesc, 1u);
+                    }
+                    mma_commit(smem_u32(&r.empty[s]));
+                }
+                if (ok) mma_commit(smem_u32(&r.tfull[b]));
+            }
+        }
+    } else if (warp >= 4) {
+        int slab = 0;
+        // The four epilogue warps meet at named barrier 3 twice per item
+        // whatever happens (a timed-out wait skips the work, not the
+        // barriers), so the barrier count always matches.
+        const int q = warp & 3;
+        for (int j = blockIdx.x; j < n_items; j += gridDim.x, ++acc) {
+            const PItem it = p_item(p, g0, g1, j);
+            const int b = acc & 1;
+            const DecGemm& G = p.g[it.g];
+            const bool bias = it.part == 0 && G.bias;
+            // the item's bias into shared memory while its MMAs run (one
+            // load per thread instead of a dependent load per column chunk)
+            if (bias) {
+                const int e = threadIdx.x - 128;
+                if (e < it.bn / 2)
+                    reinterpret_cast<float2*>(r.bias)[e] = __ldg(reinterpret_cast<const float2*>(G.bias + it.n0) + e);
+            }
+            asm volatile("bar.sync 3, 128;" ::: "memory");
+            bool got = ok && mbar_wait(smem_u32(&r.tfull[b]), (acc >> 1) & 1, 0x64);
+            got = __all_sync(0xffffffffu, got);
+            if (!got) ok = false;
+            if (got) {
+                tc_fence_after();
+                // 32 x 32 f32 slabs (128-byte swizzle: 16-byte chunk i of row
+                // r at chunk i ^ (r & 7), conflict-free) leave by TMA tile
+                // stores, two slabs per warp in turn; rows past the batch are
+                // written too (they stay inside the part's rows, never read)
+                const int y = it.part * p.s.prow + it.m0 + q * 32;
+                const uint32_t tq = r.tmem + (static_cast<uint32_t>(q * 32) << 16) + b * 256;
+                for (int c = 0; c < it.bn / 32; ++c, ++slab) {
+                    uint32_t v[32];
+                    tmem_ld_32x32b_x32(tq + c * 32, v);
+                    tmem_wait_ld();
+                    if (c == it.bn / 32 - 1) {
+                        tc_fence_before();
+                        mbar_arrive(smem_u32(&r.tempty[b]));
+                    }
+                    if (bias) {
+                        const float4* b4 = reinterpret_cast<const float4*>(r.bias + c * 32);
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const float4 t = b4[i];
+                            v[4 * i] = __float_as_uint(__uint_as_float(v[4 * i]) + t.x);
+                            v[4 * i + 1] = __float_as_uint(__uint_as_float(v[4 * i + 1]) + t.y);
+                            v[4 * i + 2] = __float_as_uint(__uint_as_float(v[4 * i + 2]) + t.z);
+                            v[4 * i + 3] = __float_as_uint(__uint_as_float(v[4 * i + 3]) + t.w);
+                        }
+                    }
+                    uint8_t* sl = r.slabs + ((q * 2 + (slab & 1)) << 12);
+                    if (lane == 0) bulk_wait_read<1>();   // the store that last read this slab is done reading
+                    __syncwarp();
+#pragma unroll
+                    for (int i = 0; i < 8; ++i)
+                        *reinterpret_cast<uint4*>(sl + lane * 128 + ((i ^ (lane & 7)) << 4)) =
+                            make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+                    fence_async_shared();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tma_store_2d(&maps.c[it.g], smem_u32(sl), it.n0 + c * 32, y);
+                        bulk_commit();
+                    }
+                }
+            }
+            asm volatile("bar.sync 3, 128;" ::: "memory");   // bias slot free for the next item
+        }
+        // the phase's parts are complete in global memory before the grid barrier
+        if (lane == 0) {
+            bulk_wait_all();
+            fence_async_global();
+        }
+        __syncwarp();
+    }
+    return ok;
+}
+
+__device__ __forceinline__ void half_sync(int h) { asm volatile("bar.sync %0, 128;" ::"r"(1 + h) : "memory"); }
+
+__device__ __forceinline__ int ldcg_i(const int* p) { return __ldcg(p); }
+
+// The four gate pre-activations (summed over the split-K parts) of columns
+// [4 j4, 4 j4 + 4) of row b.
+__device__ __forceinline__ void p_gates(const DecState& s, int parts, int b, int j4, float4 (&g)[4]) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) g[q] = parts_sum4(s.gates, parts, s.prow, 4 * kH, b, q * kH + 4 * j4);
+}
+
+// LSTM cell from summed gates (+ E0[tok] for layer 0) and the old cell state.
+__device__ __forceinline__ void p_cell_apply(const DecState& s, int layer, int b, int j4, float4 (&g)[4],
+                                             const float4* e0, float4 c4) {
+    const int j = 4 * j4;
+    if (e0) {
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-            const float4 e = __ldg(reinterpret_cast<const float4*>(e0 + q * kH));
-            g[q].x += e.x;
-            g[q].y += e.y;
-            g[q].z += e.z;
-            g[q].w += e.w;
+            g[q].x += e0[q].x;
+            g[q].y += e0[q].y;
+            g[q].z += e0[q].z;
+            g[q].w += e0[q].w;
         }
     }
-    float* cp = s.c + (static_cast<size_t>(b) * 2 + layer) * kH + j;
-    const float4 c4 = *reinterpret_cast<const float4*>(cp);
     const float gi[4] = {g[0].x, g[0].y, g[0].z, g[0].w}, gf[4] = {g[1].x, g[1].y, g[1].z, g[1].w};
     const float gg[4] = {g[2].x, g[2].y, g[2].z, g[2].w}, go[4] = {g[3].x, g[3].y, g[3].z, g[3].w};
     const float cold[4] = {c4.x, c4.y, c4.z, c4.w};
@@ -279,8 +398,8 @@ __global__ void __launch_bounds__(160) k_dec_lstm_update(DecState s, int layer) 
         cn[e] = fg * cold[e] + in * cand;
         h[e] = sigm(go[e]) * tanhf(cn[e]);
     }
+    float* cp = s.c + (static_cast<size_t>(b) * 2 + layer) * kH + j;
     *reinterpret_cast<float4*>(cp) = make_float4(cn[0], cn[1], cn[2], cn[3]);
-    // this layer's recurrent input and the next GEMM's input (hi | lo)
     __half* self = layer == 0 ? s.a0 + static_cast<size_t>(b) * 2 * kH : s.a1 + static_cast<size_t>(b) * 4 * kH + 2 * kH;
     __half* next = layer == 0 ? s.a1 + static_cast<size_t>(b) * 4 * kH : s.ap + static_cast<size_t>(b) * 2 * kH;
     const float4 h4 = make_float4(h[0], h[1], h[2], h[3]);
@@ -288,38 +407,263 @@ __global__ void __launch_bounds__(160) k_dec_lstm_update(DecState s, int layer) 
     split_store4(next + j, next + kH + j, h4);
 }
 
-__global__ void k_dec_any_active(const int* active, int B, int* out) {
-    pdl_wait();
-    pdl_launch_dependents();
-    __shared__ int any;
-    if (threadIdx.x == 0) any = 0;
-    __syncthreads();
-    for (int b = threadIdx.x; b < B; b += blockDim.x)
-        if (active[b]) any = 1;
-    __syncthreads();
-    if (threadIdx.x == 0) *out = any;
+__device__ __forceinline__ float4 ldcg4(const float* p) { return __ldcg(reinterpret_cast<const float4*>(p)); }
+
+// Row b's phase B on the 128 threads of half h: argmax (first max over the
+// vocabulary and over the 5 durations, blank moves >= 1 frame; the rule of
+// k_dec_argmax), state update, then the layer-0 cell if the row emitted.  The
+// scores, this thread's gates and the row's state are loaded together.
+__device__ __forceinline__ void p_row_b(const DecPersist& p, int b, int h, int t, bool first, float* wv, int* wi,
+                                        int* wdur, int* sx, unsigned int* act_cnt) {
+    const DecState& s = p.s;
+    const int warp = t >> 5, lane = t & 31;
+    const int ld = s.ld_scores;
+    // gates of column groups j4 = t and (t < 32) t + 128
+    float4 g1[4], g2[4];
+    p_gates(s, s.ks_g0, b, t, g1);
+    const bool two = t < kH / 4 - 128;
+    if (two) p_gates(s, s.ks_g0, b, t + 128, g2);
+    const float4 c1 = ldcg4(s.c + static_cast<size_t>(b) * 2 * kH + 4 * t);
+    float4 c2 = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (two) c2 = ldcg4(s.c + static_cast<size_t>(b) * 2 * kH + 4 * (t + 128));
+    int tok = s.blank, emit = 1;
+    if (!first) {
+        int st_act = 0, st_frame = 0, st_count = 0, st_guard = 0, st_len = 0;
+        if (t == 0) {
+            st_len = s.len[b];
+            st_act = ldcg_i(s.active + b);
+            st_frame = ldcg_i(s.frame + b);
+            st_count = ldcg_i(s.count + b);
+            st_guard = ldcg_i(s.guard + b);
+        }
+        float best = -INFINITY;
+        int bidx = 0x7fffffff;
+        float dv = -INFINITY;
+        int di = 0x7fffffff;
+        if (warp == 0 && lane < 5) {
+            dv = parts_sum1(s.scores, s.ks_h, s.prow, ld, b, s.vocab + lane);
+            di = lane;
+        }
+        // the row in chunks of 1536 columns, three 4-column loads per thread
+        // in flight (one chunk covers a 1025-entry vocabulary)
+        for (int base0 = 0; base0 < s.vocab; base0 += 1536) {
+            float4 sc[3];
+#pragma unroll
+            for (int i = 0; i < 3; ++i) {
+                const int base = base0 + 4 * t + 512 * i;
+                sc[i] = base < s.vocab ? parts_sum4(s.scores, s.ks_h, s.prow, ld, b, base)
+                                       : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int i = 0; i < 3; ++i) {
+                const int base = base0 + 4 * t + 512 * i;
+                const float e[4] = {sc[i].x, sc[i].y, sc[i].z, sc[i].w};
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                    if (base + q < s.vocab && e[q] > best) {   // increasing index: strict > keeps the first max
+                        best = e[q];
+                        bidx = base + q;
+                    }
+            }
+        }
+        warp_argmax(best, bidx);
+        if (lane == 0) {
+            wv[h * 4 + warp] = best;
+            wi[h * 4 + warp] = bidx;
+        }
+        if (warp == 0) {
+            warp_argmax(dv, di);
+            if (lane == 0) wdur[h] = di;
+        }
+        half_sync(h);
+        if (t == 0) {
+            int e = 0, tk = 0;
+            if (st_act) {
+                float tv = wv[h * 4];
+                tk = wi[h * 4];
+                for (int w = 1; w < 4; ++w)
+                    if (wins(wv[h * 4 + w], wi[h * 4 + w], tv, tk)) {
+                        tv = wv[h * 4 + w];
+                        tk = wi[h * 4 + w];
+                    }
+                int dur = wdur[h];
+                if (tk == 0x7fffffff) tk = 0;
+                if (dur == 0x7fffffff) dur = 0;
+                const int T = st_len;
+                e = tk != s.blank;
+                int nf;
+                if (e) {
+                    if (st_count < s.max_tokens) {
+                        uint32_t* tw = s.tokens + (static_cast<size_t>(b) * s.max_tokens + st_count) * 3;
+                        tw[0] = static_cast<uint32_t>(tk);
+                        tw[1] = static_cast<uint32_t>(st_frame);
+                        tw[2] = static_cast<uint32_t>(dur);
+                    }
+                    s.count[b] = st_count + 1;
+                    nf = st_frame + dur;
+                    s.tok[b] = tk;
+                } else {
+                    nf = st_frame + (dur > 0 ? dur : 1);
+                }
+                s.frame[b] = nf;
+                s.guard[b] = st_guard + 1;
+                const long max_steps = static_cast<long>(T) * (10 + 4) + 64;
+                const bool act = nf < T && st_guard + 1 < max_steps;
+                s.active[b] = act ? 1 : 0;
+                if (act) atomicAdd(act_cnt, 1u);
+            }
+            s.emit[b] = e;
+            sx[2 * h] = e;
+            sx[2 * h + 1] = tk;
+        }
+        half_sync(h);
+        emit = sx[2 * h];
+        tok = sx[2 * h + 1];
+    }
+    if (!emit) return;
+    const float* e0 = s.e0 + static_cast<size_t>(tok) * 4 * kH;
+    float4 e1[4], e2[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) e1[q] = __ldg(reinterpret_cast<const float4*>(e0 + q * kH + 4 * t));
+    if (two) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) e2[q] = __ldg(reinterpret_cast<const float4*>(e0 + q * kH + 4 * (t + 128)));
+    }
+    p_cell_apply(s, 0, b, t, g1, e1, c1);
+    if (two) p_cell_apply(s, 0, b, t + 128, g2, e2, c2);
 }
 
-// Embedding rows as f16 hi | lo (load time).
-__global__ void k_split_rows(const float* __restrict__ src, __half* hi, __half* lo, int64_t n) {
-    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x)
-        split_store(hi + i, lo + i, src[i]);
+// Phase D for row b: the layer-1 cell if the row emitted.
+__device__ __forceinline__ void p_row_d(const DecState& s, int b, int t) {
+    const int emit = ldcg_i(s.emit + b);
+    float4 g1[4], g2[4];
+    p_gates(s, s.ks_g1, b, t, g1);
+    const bool two = t < kH / 4 - 128;
+    if (two) p_gates(s, s.ks_g1, b, t + 128, g2);
+    const float* cb = s.c + (static_cast<size_t>(b) * 2 + 1) * kH;
+    const float4 c1 = ldcg4(cb + 4 * t);
+    float4 c2 = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (two) c2 = ldcg4(cb + 4 * (t + 128));
+    if (!emit) return;
+    p_cell_apply(s, 1, b, t, g1, nullptr, c1);
+    if (two) p_cell_apply(s, 1, b, t + 128, g2, nullptr, c2);
 }
 
-// Row b of a decoder group -> utterance out_row[b] of the batch outputs.
-__global__ void __launch_bounds__(256) k_dec_gather(const uint32_t* __restrict__ tokens, const int* __restrict__ count,
-                                                    const int* __restrict__ out_row, int B, int max_tokens,
-                                                    uint32_t* __restrict__ out_tokens, int* __restrict__ out_count) {
-    const int b = blockIdx.x;
-    if (b >= B) return;
-    const int u = out_row[b];
-    const int n = count[b];
-    if (threadIdx.x == 0) out_count[u] = n;
-    const int words = 3 * (n < max_tokens ? n : max_tokens);
-    const uint32_t* src = tokens + static_cast<size_t>(b) * max_tokens * 3;
-    uint32_t* dst = out_tokens + static_cast<size_t>(u) * max_tokens * 3;
-    for (int i = threadIdx.x; i < words; i += blockDim.x) dst[i] = src[i];
+// Phase F for row b: joint input x = ReLU(enc[frame] + dec) as hi | lo
+// (zeros for finished rows).
+__device__ __forceinline__ void p_row_f(const DecState& s, int b, int t) {
+    const int act = ldcg_i(s.active + b);
+    const int fr = ldcg_i(s.frame + b);
+    const int r0 = s.row0[b];
+    float4 d1 = parts_sum4(s.dec, s.ks_p, s.prow, kH, b, 4 * t), d2 = make_float4(0.f, 0.f, 0.f, 0.f);
+    const bool two = t < kH / 4 - 128;
+    if (two) d2 = parts_sum4(s.dec, s.ks_p, s.prow, kH, b, 4 * (t + 128));
+    __half* aj = s.aj + static_cast<size_t>(b) * 2 * kH;
+    for (int u = 0; u < (two ? 2 : 1); ++u) {
+        const int j = 4 * (t + 128 * u);
+        const float4 d = u ? d2 : d1;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (act) {
+            const float4 e = __ldg(reinterpret_cast<const float4*>(s.pooler + static_cast<size_t>(r0 + fr) * kH + j));
+            v = make_float4(fmaxf(e.x + d.x, 0.f), fmaxf(e.y + d.y, 0.f), fmaxf(e.z + d.z, 0.f), fmaxf(e.w + d.w, 0.f));
+        }
+        split_store4(aj + j, aj + kH + j, v);
+    }
+}
+
+__global__ void __launch_bounds__(kPThreads, 1)
+    k_dec_persist(const __grid_constant__ DecMaps maps, const DecPersist p) {
+    extern __shared__ __align__(1024) uint8_t p_smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(p_smem_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kPBarOff);
+    PRing r;
+    r.ring = smem;
+    r.slabs = smem + kPSlabOff;
+    r.bias = reinterpret_cast<float*>(smem + kPBiasOff);
+    r.full = bars;
+    r.empty = bars + kPStages;
+    r.tfull = bars + 2 * kPStages;
+    r.tempty = bars + 2 * kPStages + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kPStages + 4);
+    int* ok_smem = reinterpret_cast<int*>(tmem_slot + 1);
+    float* wv = reinterpret_cast<float*>(tmem_slot + 2);   // [2][4]
+    int* wi = reinterpret_cast<int*>(wv + 8);              // [2][4]
+    int* wdur = wi + 8;                                    // [2]
+    int* sx = wdur + 2;                                    // [2][emit, token]
+    int* sdone = sx + 4;
+
+    const int warp = threadIdx.x >> 5;
+    const int t = threadIdx.x & 127, h = threadIdx.x >> 7;
+    if (threadIdx.x == 0) {
+        for (int i = 0; i < 4; ++i) {
+            tma_prefetch_desc(&maps.a[i]);
+            tma_prefetch_desc(&maps.b[i]);
+        }
+        for (int i = 0; i < kPStages; ++i) {
+            mbar_init(smem_u32(&r.full[i]), 1);
+            mbar_init(smem_u32(&r.empty[i]), 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(smem_u32(&r.tfull[i]), 1);
+            mbar_init(smem_u32(&r.tempty[i]), 128);
+        }
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc<kPTmemCols>(smem_u32(tmem_slot));
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    r.tmem = *tmem_slot;
+
+    const DecState& s = p.s;
+    unsigned int* sync = p.sync;
+    const unsigned int nb = gridDim.x;
+    unsigned int target = 0;
+    int pit = 0, mit = 0, acc = 0;
+    const int row_stride = 2 * gridDim.x;
+    for (int step = -1; step < p.max_steps; ++step) {
+        const bool first = step < 0;
+        // A: joint head (not on the first pass) + layer-0 recurrent GEMM
+        bool fail = __syncthreads_or(!p_gemm_phase(maps, p, r, first ? -1 : kDecHead, kDecLstm0, pit, mit, acc));
+        if (!grid_barrier(sync, sync + 1, nb, target, fail, ok_smem, 0x65)) break;
+        // B: argmax + update, layer-0 cell
+        if (threadIdx.x == 0 && blockIdx.x == 0 && !first) sync[2 + ((step + 1) & 1)] = 0;
+        for (int b = blockIdx.x * 2 + h; b < s.B; b += row_stride) {
+            p_row_b(p, b, h, t, first, wv, wi, wdur, sx, sync + 2 + (step & 1));
+            half_sync(h);
+        }
+        fence_async_global();
+        if (!grid_barrier(sync, sync + 1, nb, target, false, ok_smem, 0x66)) break;
+        if (!first) {
+            if (threadIdx.x == 0) *sdone = ld_acquire_gpu(sync + 2 + (step & 1)) == 0;
+            __syncthreads();
+            if (*reinterpret_cast<volatile int*>(sdone)) break;
+        }
+        // C: layer-1 GEMM
+        fail = __syncthreads_or(!p_gemm_phase(maps, p, r, kDecLstm1, -1, pit, mit, acc));
+        if (!grid_barrier(sync, sync + 1, nb, target, fail, ok_smem, 0x67)) break;
+        // D: layer-1 cell
+        for (int b = blockIdx.x * 2 + h; b < s.B; b += row_stride) p_row_d(s, b, t);
+        fence_async_global();
+        if (!grid_barrier(sync, sync + 1, nb, target, false, ok_smem, 0x68)) break;
+        // E: projector GEMM
+        fail = __syncthreads_or(!p_gemm_phase(maps, p, r, kDecProj, -1, pit, mit, acc));
+        if (!grid_barrier(sync, sync + 1, nb, target, fail, ok_smem, 0x69)) break;
+        // F: joint input
+        for (int b = blockIdx.x * 2 + h; b < s.B; b += row_stride) p_row_f(s, b, t);
+        fence_async_global();
+        if (!grid_barrier(sync, sync + 1, nb, target, false, ok_smem, 0x6A)) break;
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc<kPTmemCols>(r.tmem);
+    }
 }
 
 int check_launch(const char* what) {
@@ -329,10 +673,8 @@ int check_launch(const char* what) {
 
 }  // namespace
 
-int dec_max_parts() { return kMaxParts; }
-
-// The step kernels are launched with programmatic stream serialization: each
-// one's CTAs are scheduled while its predecessor drains and wait in pdl_wait()
+// The init kernel is launched with programmatic stream serialization: its CTAs
+// are scheduled while the producer of the pooler drains and wait in pdl_wait()
 // for its results.
 template <typename... Args>
 int launch_pdl(void (*kern)(Args...), dim3 grid, dim3 block, cudaStream_t st, const char* what, Args... args) {
@@ -353,22 +695,86 @@ int launch_pdl(void (*kern)(Args...), dim3 grid, dim3 block, cudaStream_t st, co
 int dec_launch_init(const DecState& s, cudaStream_t st) {
     return launch_pdl(k_dec_init, dim3(s.B), dim3(128), st, "k_dec_init", s);
 }
-int dec_launch_joint_in(const DecState& s, cudaStream_t st) {
-    return launch_pdl(k_dec_joint_in, dim3(s.B), dim3(kH / 4), st, "k_dec_joint_in", s);
+
+int dec_persistent_grid(int device) {
+    static int cached = -1, cached_dev = -1;
+    if (cached >= 0 && cached_dev == device) return cached;
+    if (cudaFuncSetAttribute(k_dec_persist, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmem) != cudaSuccess)
+        return 0;
+    int per_sm = 0, sms = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_dec_persist, kPThreads, kPSmem) != cudaSuccess) return 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    cached = per_sm >= 1 ? sms : 0;   // one CTA per SM (TMEM and the ring are sized for it)
+    cached_dev = device;
+    return cached;
 }
-int dec_launch_argmax(const DecState& s, cudaStream_t st) {
-    return launch_pdl(k_dec_argmax, dim3(s.B), dim3(256), st, "k_dec_argmax", s);
+
+// Tile widths and split-K parts for the persistent decoder.  The GEMMs are
+// bound by the bytes each SM pulls from L2, so the model is bytes: per item,
+// its k-blocks (two 16 KB A boxes + a bn x 64 weight tile each) plus its
+// partial-output write; items are dealt round-robin, and per GEMM phase the
+// plan with the smallest busiest CTA wins (ties keep fewer parts).
+void dec_plan_persistent(int B, int npad, int grid, int bn[4], int ks[4]) {
+    const int m_tiles = (B + 127) / 128;
+    const int n[4] = {npad, 2560, 2560, 640};
+    const int nk[4] = {640 / 64, 640 / 64, 1280 / 64, 640 / 64};   // logical k-blocks
+    for (int i = 0; i < 4; ++i) bn[i] = n[i] % 256 == 0 ? 256 : 128;
+    auto cost = [&](const int* gs, const int* kss, int ng) {
+        std::vector<double> load(grid, 0.0);
+        long j = 0;
+        for (int i = 0; i < ng; ++i) {
+            const int g = gs[i];
+            const long items = static_cast<long>(m_tiles) * (n[g] / bn[g]) * kss[i];
+            const double c = (nk[g] / kss[i]) * (32768.0 + bn[g] * 128.0) + 128.0 * bn[g] * 4.0 + 16384.0;
+            for (long u = 0; u < items; ++u, ++j) load[j % grid] += c;
+        }
+        double mx = 0;
+        for (double v : load) mx = v > mx ? v : mx;
+        return mx;
+    };
+    auto ok_ks = [&](int g, int k) { return k >= 1 && k <= kMaxParts && nk[g] % k == 0; };
+    double best = -1;
+    for (int a = 1; a <= kMaxParts; ++a) {
+        if (!ok_ks(kDecHead, a)) continue;
+        for (int b = 1; b <= kMaxParts; ++b) {
+            if (!ok_ks(kDecLstm0, b)) continue;
+            const int gs[2] = {kDecHead, kDecLstm0}, kss[2] = {a, b};
+            const double c = cost(gs, kss, 2);
+            if (best < 0 || c < best * 0.999) {
+                best = c;
+                ks[kDecHead] = a;
+                ks[kDecLstm0] = b;
+            }
+        }
+    }
+    for (int g : {kDecLstm1, kDecProj}) {
+        best = -1;
+        for (int k = 1; k <= kMaxParts; ++k) {
+            if (!ok_ks(g, k)) continue;
+            const int gs[1] = {g}, kss[1] = {k};
+            const double c = cost(gs, kss, 1);
+            if (best < 0 || c < best * 0.999) {
+                best = c;
+                ks[g] = k;
+            }
+        }
+    }
 }
-int dec_launch_lstm_update(const DecState& s, int layer, cudaStream_t st) {
-    return launch_pdl(k_dec_lstm_update, dim3(s.B), dim3(kH / 4), st, "k_dec_lstm_update", s, layer);
-}
-int dec_launch_any_active(const DecState& s, int* out, cudaStream_t st) {
-    return launch_pdl(k_dec_any_active, dim3(1), dim3(256), st, "k_dec_any_active", static_cast<const int*>(s.active),
-                      s.B, out);
-}
-int dec_launch_gather(const DecState& s, const int* out_row, uint32_t* out_tokens, int* out_count, cudaStream_t st) {
-    k_dec_gather<<<s.B, 256, 0, st>>>(s.tokens, s.count, out_row, s.B, s.max_tokens, out_tokens, out_count);
-    return check_launch("k_dec_gather");
+
+int dec_launch_persistent(const DecMaps& maps, const DecPersist& p, int grid, cudaStream_t st) {
+    if (grid <= 0) return set_error(B3_ECUDA, "the persistent decoder does not fit on this device");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kPThreads);
+    cfg.dynamicSmemBytes = kPSmem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, k_dec_persist, maps, p);
+    return e == cudaSuccess ? 0 : set_cuda_error("k_dec_persist", e);
 }
 
 int dec_launch_split(const float* src, __half* hi, __half* lo, int64_t n, cudaStream_t st) {
