@@ -89,7 +89,8 @@ struct alignas(64) DecMaps {
 struct DecPersist {
     DecState s;
     DecGemm g[4];        // kDecHead, kDecLstm0, kDecLstm1, kDecProj
-    unsigned int* sync;  // [0] barrier arrivals, [1] abort flag, [2..3] active-row counts (host-zeroed)
+    unsigned int* sync;  // [0] barrier arrivals, [1] abort flag,
+                         // [4..5] active-row counts of even / odd steps (8 words, host-zeroed)
     int max_steps;       // lock steps at most (every row is bounded on its own as well)
 };
 constexpr int kDecHead = 0, kDecLstm0 = 1, kDecLstm1 = 2, kDecProj = 3;

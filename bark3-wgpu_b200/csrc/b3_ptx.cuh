@@ -159,29 +159,28 @@ __device__ __forceinline__ unsigned int ld_acquire_gpu(const unsigned int* p) {
 }
 
 // Grid-wide barrier for a kernel whose CTAs are all resident (cooperative
-// launch).  `ctr` counts arrivals over the kernel's life; `target` is this
-// CTA's running total (nblocks more per barrier); `abort_flag` set by any CTA
-// ends every wait.  Bounded like mbar_wait: on time-out it records the error,
-// raises the abort flag and returns false.  Call with all threads of the CTA;
+// launch).  sync[0] counts arrivals over the kernel's life (each arrival is a
+// fire-and-forget reduction, so no CTA waits for its own atomic), sync[1] is
+// the abort flag.  `target` is this CTA's running total (nblocks more per
+// barrier).  Bounded like mbar_wait: on time-out it records the error, raises
+// the abort flag and returns false.  Call with all threads of the CTA;
 // `ok_smem` is a shared int that carries thread 0's verdict to the others.
-__device__ __forceinline__ bool grid_barrier(unsigned int* ctr, unsigned int* abort_flag, unsigned int nblocks,
-                                             unsigned int& target, bool fail, int* ok_smem,
-                                             unsigned int site) {
+__device__ __forceinline__ bool grid_barrier(unsigned int* sync, unsigned int nblocks, unsigned int& target,
+                                             bool fail, int* ok_smem, unsigned int site) {
     __syncthreads();
     if (threadIdx.x == 0) {
         target += nblocks;
         int ok = 1;
         if (fail) {
-            atomicExch(abort_flag, 1u);
+            atomicExch(sync + 1, 1u);
             ok = 0;
         }
         __threadfence();
-        atomicAdd(ctr, 1u);
+        atomicAdd(sync, 1u);
         unsigned long long t0 = 0;
         while (ok) {
-            const unsigned int v = ld_acquire_gpu(ctr);
-            if (static_cast<int>(v - target) >= 0) break;
-            if (*reinterpret_cast<volatile unsigned int*>(abort_flag)) {
+            if (static_cast<int>(ld_acquire_gpu(sync) - target) >= 0) break;
+            if (*reinterpret_cast<volatile unsigned int*>(sync + 1)) {
                 ok = 0;
                 break;
             }
@@ -190,7 +189,7 @@ __device__ __forceinline__ bool grid_barrier(unsigned int* ctr, unsigned int* ab
                 t0 = t;
             } else if (t - t0 > kWaitLimitNs) {
                 record_error(B3_ERR_TIMEOUT | site);
-                atomicExch(abort_flag, 1u);
+                atomicExch(sync + 1, 1u);
                 ok = 0;
             }
         }

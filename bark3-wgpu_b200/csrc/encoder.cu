@@ -841,11 +841,11 @@ int decode_device(b3_ctx* c, const float* pooler, const int32_t* cu, int n_utt, 
     B3_TRY(D.ints.ensure(b * 6 * 4));
     B3_TRY(D.tokens.ensure(b * static_cast<size_t>(max_tokens) * 12));
     B3_TRY(D.rows.ensure(b * 2 * 4));
-    B3_TRY(D.sync.ensure(16));
+    B3_TRY(D.sync.ensure(32));
     ProfScope ps(c, B3_K_DECODER, 0.0, 0.0);
     c->prof.launches[B3_K_DECODER]++;   // init + the persistent kernel
     B3_CUDA(cudaMemcpyAsync(D.rows.p, rows.data(), rows.size() * 4, cudaMemcpyHostToDevice, c->stream));
-    B3_CUDA(cudaMemsetAsync(D.sync.p, 0, 16, c->stream));
+    B3_CUDA(cudaMemsetAsync(D.sync.p, 0, 32, c->stream));
 
     DecPersist p{};
     DecState& s = p.s;

@@ -316,14 +316,9 @@ __device__ __forceinline__ bool p_gemm_phase(const DecMaps& maps, const DecPersi
                 // written too (they stay inside the part's rows, never read)
                 const int y = it.part * p.s.prow + it.m0 + q * 32;
                 const uint32_t tq = r.tmem + (static_cast<uint32_t>(q * 32) << 16) + b * 256;
-                for (int c = 0; c < it.bn / 32; ++c, ++slab) {
-                    uint32_t v[32];
-                    tmem_ld_32x32b_x32(tq + c * 32, v);
-                    tmem_wait_ld();
-                    if (c == it.bn / 32 - 1) {
-                        tc_fence_before();
-                        mbar_arrive(smem_u32(&r.tempty[b]));
-                    }
+                const int nc = it.bn / 32;   // 4 or 8
+                // one 32-column chunk in registers -> bias -> slab -> TMA store
+                auto put = [&](uint32_t (&v)[32], int c) {
                     if (bias) {
                         const float4* b4 = reinterpret_cast<const float4*>(r.bias + c * 32);
 #pragma unroll
@@ -336,6 +331,7 @@ __device__ __forceinline__ bool p_gemm_phase(const DecMaps& maps, const DecPersi
                         }
                     }
                     uint8_t* sl = r.slabs + ((q * 2 + (slab & 1)) << 12);
+                    ++slab;
                     if (lane == 0) bulk_wait_read<1>();   // the store that last read this slab is done reading
                     __syncwarp();
 #pragma unroll
@@ -348,7 +344,22 @@ __device__ __forceinline__ bool p_gemm_phase(const DecMaps& maps, const DecPersi
                         tma_store_2d(&maps.c[it.g], smem_u32(sl), it.n0 + c * 32, y);
                         bulk_commit();
                     }
+                };
+                // two register sets: the next chunk loads from TMEM while the
+                // current one is stored
+                uint32_t va[32], vb[32];
+                tmem_ld_32x32b_x32(tq, va);
+                tmem_wait_ld();
+                for (int c = 0; c < nc; c += 2) {
+                    tmem_ld_32x32b_x32(tq + (c + 1) * 32, vb);
+                    put(va, c);
+                    tmem_wait_ld();
+                    if (c + 2 < nc) tmem_ld_32x32b_x32(tq + (c + 2) * 32, va);
+                    put(vb, c + 1);
+                    tmem_wait_ld();
                 }
+                tc_fence_before();
+                mbar_arrive(smem_u32(&r.tempty[b]));
             }
             asm volatile("bar.sync 3, 128;" ::: "memory");   // bias slot free for the next item
         }
@@ -629,34 +640,36 @@ __global__ void __launch_bounds__(kPThreads, 1)
         const bool first = step < 0;
         // A: joint head (not on the first pass) + layer-0 recurrent GEMM
         bool fail = __syncthreads_or(!p_gemm_phase(maps, p, r, first ? -1 : kDecHead, kDecLstm0, pit, mit, acc));
-        if (!grid_barrier(sync, sync + 1, nb, target, fail, ok_smem, 0x65)) break;
+        if (!grid_barrier(sync, nb, target, fail, ok_smem, 0x65)) break;
         // B: argmax + update, layer-0 cell
-        if (threadIdx.x == 0 && blockIdx.x == 0 && !first) sync[2 + ((step + 1) & 1)] = 0;
+        if (threadIdx.x == 0 && blockIdx.x == 0 && !first) sync[4 + ((step + 1) & 1)] = 0;
         for (int b = blockIdx.x * 2 + h; b < s.B; b += row_stride) {
-            p_row_b(p, b, h, t, first, wv, wi, wdur, sx, sync + 2 + (step & 1));
+            p_row_b(p, b, h, t, first, wv, wi, wdur, sx, sync + 4 + (step & 1));
             half_sync(h);
         }
         fence_async_global();
-        if (!grid_barrier(sync, sync + 1, nb, target, false, ok_smem, 0x66)) break;
+        if (!grid_barrier(sync, nb, target, false, ok_smem, 0x66)) break;
+        // C: layer-1 GEMM
+        fail = __syncthreads_or(!p_gemm_phase(maps, p, r, kDecLstm1, -1, pit, mit, acc));
+        if (!grid_barrier(sync, nb, target, fail, ok_smem, 0x67)) break;
+        // every row finished at this step's argmax (the count is final since
+        // the barrier after B; read here so that phase C starts at once)
         if (!first) {
-            if (threadIdx.x == 0) *sdone = ld_acquire_gpu(sync + 2 + (step & 1)) == 0;
+            if (threadIdx.x == 0) *sdone = ld_acquire_gpu(sync + 4 + (step & 1)) == 0;
             __syncthreads();
             if (*reinterpret_cast<volatile int*>(sdone)) break;
         }
-        // C: layer-1 GEMM
-        fail = __syncthreads_or(!p_gemm_phase(maps, p, r, kDecLstm1, -1, pit, mit, acc));
-        if (!grid_barrier(sync, sync + 1, nb, target, fail, ok_smem, 0x67)) break;
         // D: layer-1 cell
         for (int b = blockIdx.x * 2 + h; b < s.B; b += row_stride) p_row_d(s, b, t);
         fence_async_global();
-        if (!grid_barrier(sync, sync + 1, nb, target, false, ok_smem, 0x68)) break;
+        if (!grid_barrier(sync, nb, target, false, ok_smem, 0x68)) break;
         // E: projector GEMM
         fail = __syncthreads_or(!p_gemm_phase(maps, p, r, kDecProj, -1, pit, mit, acc));
-        if (!grid_barrier(sync, sync + 1, nb, target, fail, ok_smem, 0x69)) break;
+        if (!grid_barrier(sync, nb, target, fail, ok_smem, 0x69)) break;
         // F: joint input
         for (int b = blockIdx.x * 2 + h; b < s.B; b += row_stride) p_row_f(s, b, t);
         fence_async_global();
-        if (!grid_barrier(sync, sync + 1, nb, target, false, ok_smem, 0x6A)) break;
+        if (!grid_barrier(sync, nb, target, false, ok_smem, 0x6A)) break;
     }
     tc_fence_before();
     __syncthreads();
