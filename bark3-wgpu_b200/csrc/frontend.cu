@@ -176,9 +176,12 @@ __global__ void __launch_bounds__(256) k_mel_norm(MelParams p) {
 // tile needs with even and odd columns split (conv0's stride-2 taps are then
 // unit-stride across lanes) and the conv0 output tile [kT1][kC][65] (column
 // -1 is the zero pad; the odd row stride keeps the channel-per-lane reads of
-// the depthwise conv free of bank conflicts).  conv0: a warp owns 4 channels
-// with their 9 taps in registers, lanes walk the 64 columns; conv1: a lane
-// owns a channel, warps walk (row, 16-column run) with a sliding window.
+// the depthwise conv free of bank conflicts).  conv0: a warp owns 8 channels
+// (4 pairs, one packed f32x2 FMA per pair and tap) with their 9 taps in
+// registers over 32 of the 64 columns, so each mel value loaded feeds 8
+// channels; conv1: a lane owns a channel, warps walk (row, 16-column run) with
+// a sliding window, two output columns per packed FMA.  Every output keeps the
+// scalar accumulation order (bias, then taps row by row, left to right).
 constexpr int kT2 = 4;
 constexpr int kC = 32;
 constexpr int kT1 = 2 * kT2 + 1;   // conv0 rows needed (9)
@@ -215,46 +218,52 @@ __global__ void __launch_bounds__(256, 2) k_sub_conv0_dw1(SubParams p) {
     for (int i = threadIdx.x; i < kT1 * kC; i += blockDim.x) c0[i * kC0S] = 0.f;  // col -1
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     {
-        const int cb = cg + warp * 4;
-        float w[4][9], bias[4];
+        // conv0: warp w owns channels 8 (w & 3) .. +8 as 4 channel pairs (one
+        // packed f32x2 FMA per pair and tap) over columns 32 (w >> 2) + lane
+        const int cq = (warp & 3) * 8;
+        const int j = (warp >> 2) * 32 + lane;
+        float2 w[4][9], bias[4];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-            bias[q] = __ldg(p.b0 + cb + q);
+            bias[q] = make_float2(__ldg(p.b0 + cg + cq + 2 * q), __ldg(p.b0 + cg + cq + 2 * q + 1));
 #pragma unroll
-            for (int t = 0; t < 9; ++t) w[q][t] = __ldg(p.w0 + (cb + q) * 9 + t);
+            for (int t = 0; t < 9; ++t)
+                w[q][t] = make_float2(__ldg(p.w0 + (cg + cq + 2 * q) * 9 + t), __ldg(p.w0 + (cg + cq + 2 * q + 1) * 9 + t));
         }
         __syncthreads();
         for (int r = 0; r < kT1; ++r) {
             const int t1 = t1_0 + r;
             const bool live = t1 >= 0 && t1 < F1 && t1 < v1;
             const float* m0 = mel + 2 * r * kMelS;   // mel rows 2 t1 - 1 + ki
-            float* out = c0 + (r * kC + warp * 4) * kC0S + 1;
+            float* out = c0 + (r * kC + cq) * kC0S + 1 + j;
+            float2 acc[4];
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int j = lane + 32 * h;
-                float acc[4];
+            for (int q = 0; q < 4; ++q) acc[q] = bias[q];
+            if (live) {
 #pragma unroll
-                for (int q = 0; q < 4; ++q) acc[q] = bias[q];
-                if (live) {
+                for (int ki = 0; ki < 3; ++ki) {
+                    const float* row = m0 + ki * kMelS;
+                    const float a = row[65 + j], b = row[j], c = row[66 + j];  // cols 2j-1, 2j, 2j+1
+                    const float2 a2 = make_float2(a, a), b2 = make_float2(b, b), c2 = make_float2(c, c);
 #pragma unroll
-                    for (int ki = 0; ki < 3; ++ki) {
-                        const float* row = m0 + ki * kMelS;
-                        const float a = row[65 + j], b = row[j], c = row[66 + j];  // cols 2j-1, 2j, 2j+1
-#pragma unroll
-                        for (int q = 0; q < 4; ++q) {
-                            acc[q] += w[q][ki * 3] * a;
-                            acc[q] += w[q][ki * 3 + 1] * b;
-                            acc[q] += w[q][ki * 3 + 2] * c;
-                        }
+                    for (int q = 0; q < 4; ++q) {
+                        acc[q] = __ffma2_rn(w[q][ki * 3], a2, acc[q]);
+                        acc[q] = __ffma2_rn(w[q][ki * 3 + 1], b2, acc[q]);
+                        acc[q] = __ffma2_rn(w[q][ki * 3 + 2], c2, acc[q]);
                     }
                 }
+            }
 #pragma unroll
-                for (int q = 0; q < 4; ++q) out[q * kC0S + j] = live ? fmaxf(acc[q], 0.f) : 0.f;
+            for (int q = 0; q < 4; ++q) {
+                out[(2 * q) * kC0S] = live ? fmaxf(acc[q].x, 0.f) : 0.f;
+                out[(2 * q + 1) * kC0S] = live ? fmaxf(acc[q].y, 0.f) : 0.f;
             }
         }
     }
     __syncthreads();
     {
+        // depthwise conv: a lane per channel, warps walk (row, 16-column run)
+        // two output columns at a time as one packed f32x2 FMA per tap
         const int c = lane;
         float w[9];
 #pragma unroll
@@ -264,26 +273,27 @@ __global__ void __launch_bounds__(256, 2) k_sub_conv0_dw1(SubParams p) {
         const int t2 = t2_0 + r2;
         if (t2 >= F2) return;
         const bool live = t2 < v2;
-        // conv0 local rows 2 r2 + ki hold t1 = 2 t2 - 1 + ki
+        // conv0 local rows 2 r2 + ki hold t1 = 2 t2 - 1 + ki; index 1 + col
         const float* base = c0 + (2 * r2 * kC + c) * kC0S;
         __half* out = p.x2 + static_cast<size_t>(p.x2_off[u] + t2) * 32 * 256 + cg + c;
         float prev[3];
 #pragma unroll
         for (int ki = 0; ki < 3; ++ki) prev[ki] = base[ki * kC0Row + 2 * jb];   // col 2 jb - 1
-#pragma unroll 4
-        for (int jj = 0; jj < 16; ++jj) {
-            const int j2 = jb + jj;
-            float s = bias;
+#pragma unroll 2
+        for (int jj = 0; jj < 16; jj += 2) {
+            const int j2 = jb + jj;   // outputs j2 (cols 2j2-1..2j2+1) and j2+1 (cols 2j2+1..2j2+3)
+            float2 s = make_float2(bias, bias);
 #pragma unroll
             for (int ki = 0; ki < 3; ++ki) {
                 const float* row = base + ki * kC0Row;
-                const float x1 = row[2 * j2 + 1], x2 = row[2 * j2 + 2];   // cols 2 j2, 2 j2 + 1
-                s += w[ki * 3] * prev[ki];
-                s += w[ki * 3 + 1] * x1;
-                s += w[ki * 3 + 2] * x2;
-                prev[ki] = x2;
+                const float x0 = row[2 * j2 + 1], x1 = row[2 * j2 + 2], x2 = row[2 * j2 + 3], x3 = row[2 * j2 + 4];
+                s = __ffma2_rn(make_float2(w[ki * 3], w[ki * 3]), make_float2(prev[ki], x1), s);
+                s = __ffma2_rn(make_float2(w[ki * 3 + 1], w[ki * 3 + 1]), make_float2(x0, x2), s);
+                s = __ffma2_rn(make_float2(w[ki * 3 + 2], w[ki * 3 + 2]), make_float2(x1, x3), s);
+                prev[ki] = x3;
             }
-            out[j2 * 256] = __float2half_rn(live ? s : 0.f);
+            out[j2 * 256] = __float2half_rn(live ? s.x : 0.f);
+            out[(j2 + 1) * 256] = __float2half_rn(live ? s.y : 0.f);
         }
     }
 }
