@@ -106,7 +106,8 @@ int dec_launch_split(const float* src, __half* hi, __half* lo, int64_t n, cudaSt
 // Mel front end (frontend.cu).
 struct MelParams {
     int n_utt;
-    const float* wave;        // padded waves, concatenated
+    int lead;                 // zero samples before each utterance (not stored)
+    const float* wave;        // waves, concatenated
     const int64_t* wave_off;  // [n_utt + 1] sample offsets
     const int* frame_off;     // [n_utt + 1] frame offsets (1 + len/160 frames each)
     const float* window;      // [512] Hann(400) centred
@@ -132,9 +133,12 @@ struct SubParams {
     const int* x4_off;        // [n_utt + 1] row offsets of x4 (= encoder frames)
 };
 
-int launch_mel(const MelParams& p, int n_frames, cudaStream_t st);
-int launch_sub_conv0_dw1(const SubParams& p, int n_work, cudaStream_t st);
-int launch_sub_dw2(const SubParams& p, int rows, cudaStream_t st);
+// The front-end kernels over a range of the batch: mel frames [f0, f1) and
+// the normalisation of utterances [u0, u1); conv work items [w0, w1); second
+// depthwise-conv rows [r0, r1).
+int launch_mel(const MelParams& p, int f0, int f1, int u0, int u1, cudaStream_t st);
+int launch_sub_conv0_dw1(const SubParams& p, int w0, int w1, cudaStream_t st);
+int launch_sub_dw2(const SubParams& p, int r0, int r1, cudaStream_t st);
 int launch_sub_to_ref(const __half* src, float* dst, int rows, cudaStream_t st);
 int sub_work_rows();
 int sub_work_channels();

@@ -146,8 +146,13 @@ struct Plan {
 
 // Frame bookkeeping of a front-end batch: frame / depthwise-1 / encoder row
 // offsets per utterance and the subsampling CTA work list.
+// Zero samples the audio front end puts before every utterance: the
+// reference's 0.25 s of leading silence at 16 kHz (src/transcription.rs:48-52).
+constexpr int kLeadSamples = 4000;
+
 struct FeShape {
     std::vector<int32_t> foff, nvalid, x2off, x4off;
+    std::vector<int32_t> woff;   // first conv work item of each utterance (n + 1)
     std::vector<int4> work;
 };
 
@@ -217,15 +222,26 @@ struct b3_ctx {
         std::vector<int32_t> sub_key;   // batch shape whose tables are on the device
         std::vector<int64_t> mel_key;   // padded wave offsets of the cached shape
         FeShape mel_shape;
+        // host-pointer input: the waves go up in utterance chunks on their own
+        // stream, each chunk's front end waiting only for its own copies
+        cudaStream_t copy_st = nullptr;
+        cudaEvent_t wave_free = nullptr;
+        std::vector<cudaEvent_t> chunk_ev;
+        std::vector<int> chunk_u;   // chunk c = utterances [chunk_u[c], chunk_u[c + 1])
+        bool chunk_wait = false;    // chunk_ev holds this call's copies
     } fe;
     ~b3_ctx() {
         for (Linear* l : {&fe.pw1, &fe.pw2, &fe.sub_w_perm}) {
             l->w.release();
             l->lut16.release();
         }
+        if (fe.copy_st) cudaStreamSynchronize(fe.copy_st);
         for (DevBuf* b : {&fe.tables, &fe.conv, &fe.pw_bias, &fe.wave, &fe.wave_off, &fe.frame_off, &fe.mel, &fe.x2,
                           &fe.x3, &fe.x4, &fe.ints, &fe.work})
             b->release();
+        for (cudaEvent_t e : fe.chunk_ev) cudaEventDestroy(e);
+        if (fe.wave_free) cudaEventDestroy(fe.wave_free);
+        if (fe.copy_st) cudaStreamDestroy(fe.copy_st);
         for (cudaEvent_t e : prof.pool) cudaEventDestroy(e);
         for (Linear* l : {&dec.lstm[0], &dec.lstm[1], &dec.proj, &dec.head}) {
             l->w.release();
@@ -1043,6 +1059,7 @@ void fe_shape_from_frames(FeShape& s, const std::vector<int32_t>& frames, const 
     s.x4off.assign(n + 1, 0);
     s.nvalid = nvalid;
     s.work.clear();
+    s.woff.assign(n + 1, 0);
     const int rows = sub_work_rows(), groups = 256 / sub_work_channels();
     for (int u = 0; u < n; ++u) {
         const int f2 = conv_len_h(conv_len_h(frames[u]));
@@ -1052,12 +1069,15 @@ void fe_shape_from_frames(FeShape& s, const std::vector<int32_t>& frames, const 
         s.x4off[u + 1] = s.x4off[u] + t;
         for (int t2 = 0; t2 < f2; t2 += rows)
             for (int g = 0; g < groups; ++g) s.work.push_back(make_int4(u, t2, g, 0));
+        s.woff[u + 1] = static_cast<int32_t>(s.work.size());
     }
 }
 
 // mel [frames][128] (device, in c->fe.mel) -> c->sub16 [sum T][4096] in
-// (freq, channel) column order; sets up the encoder plan for the T offsets.
-int fe_subsample(b3_ctx* c, const FeShape& s) {
+// (freq, channel) column order.  fe_sub_setup sizes the buffers, uploads the
+// batch tables and sets up the encoder plan for the T offsets; fe_sub_run
+// subsamples utterances [u0, u1).
+int fe_sub_setup(b3_ctx* c, const FeShape& s, SubParams& sp) {
     auto& F = c->fe;
     const int n = static_cast<int>(s.nvalid.size());
     const int rows2 = s.x2off[n], T = s.x4off[n];
@@ -1080,7 +1100,6 @@ int fe_subsample(b3_ctx* c, const FeShape& s) {
         F.sub_key = key;
     }
     ints = F.ints.as<int32_t>();
-    SubParams sp;
     sp.n_utt = n;
     sp.mel = F.mel.as<float>();
     sp.mel_off = F.frame_off.as<int>();
@@ -1098,33 +1117,54 @@ int fe_subsample(b3_ctx* c, const FeShape& s) {
     sp.x4 = F.x4.as<__half>();
     sp.x2_off = ints + n;
     sp.x4_off = ints + 2 * n + 1;
-    {
-        ProfScope ps(c, B3_K_FRONTEND, 0.0, 0.0);
-        B3_TRY(launch_sub_conv0_dw1(sp, static_cast<int>(s.work.size()), c->stream));
-    }
-    GemmParams p1 = params_f16(F.x3.as<__half>(), 256);
-    p1.bias = F.pw_bias.as<float>();
-    B3_TRY(run_gemm(c, F.pw1, F.x2.as<__half>(), rows2 * 32, 256, EPI_RELU_F16, p1));
-    {
-        ProfScope ps(c, B3_K_FRONTEND, 0.0, 0.0);
-        B3_TRY(launch_sub_dw2(sp, T, c->stream));
-    }
-    GemmParams p2 = params_f16(c->sub16.as<__half>(), 256);
-    p2.bias = F.pw_bias.as<float>() + 256;
-    return run_gemm(c, F.pw2, F.x4.as<__half>(), T * 16, 256, EPI_RELU_F16, p2);
+    return 0;
 }
 
-// Padded waves (device, concatenated at woff) -> c->fe.mel; fills s.
-int fe_mel(b3_ctx* c, const float* wave, const std::vector<int64_t>& woff, FeShape& s) {
+int fe_sub_run(b3_ctx* c, const FeShape& s, const SubParams& sp, int u0, int u1) {
+    auto& F = c->fe;
+    {
+        ProfScope ps(c, B3_K_FRONTEND, 0.0, 0.0);
+        B3_TRY(launch_sub_conv0_dw1(sp, s.woff[u0], s.woff[u1], c->stream));
+    }
+    const size_t r2 = static_cast<size_t>(s.x2off[u0]) * 32, n2 = static_cast<size_t>(s.x2off[u1]) * 32 - r2;
+    if (n2 > 0) {
+        GemmParams p1 = params_f16(F.x3.as<__half>() + r2 * 256, 256);
+        p1.bias = F.pw_bias.as<float>();
+        B3_TRY(run_gemm(c, F.pw1, F.x2.as<__half>() + r2 * 256, static_cast<int>(n2), 256, EPI_RELU_F16, p1));
+    }
+    {
+        ProfScope ps(c, B3_K_FRONTEND, 0.0, 0.0);
+        B3_TRY(launch_sub_dw2(sp, s.x4off[u0], s.x4off[u1], c->stream));
+    }
+    const size_t r4 = static_cast<size_t>(s.x4off[u0]) * 16, n4 = static_cast<size_t>(s.x4off[u1]) * 16 - r4;
+    if (n4 == 0) return 0;
+    GemmParams p2 = params_f16(c->sub16.as<__half>() + r4 * 256, 256);
+    p2.bias = F.pw_bias.as<float>() + 256;
+    return run_gemm(c, F.pw2, F.x4.as<__half>() + r4 * 256, static_cast<int>(n4), 256, EPI_RELU_F16, p2);
+}
+
+int fe_subsample(b3_ctx* c, const FeShape& s) {
+    SubParams sp;
+    B3_TRY(fe_sub_setup(c, s, sp));
+    return fe_sub_run(c, s, sp, 0, static_cast<int>(s.nvalid.size()));
+}
+
+// Padded waves (device, concatenated at woff) -> c->fe.mel: fe_mel_setup
+// fills s, uploads the batch's offset tables (once per shape) and the kernel
+// parameters; fe_mel_run computes a range of utterances.
+int fe_mel_setup(b3_ctx* c, const float* wave, const std::vector<int64_t>& woff, int lead, FeShape& s,
+                 MelParams& mp) {
     auto& F = c->fe;
     const int n = static_cast<int>(woff.size()) - 1;
-    if (woff == F.mel_key) {
+    std::vector<int64_t> key(woff);
+    key.push_back(lead);
+    if (key == F.mel_key) {
         s = F.mel_shape;  // same batch shape as the previous call: tables are on the device
     } else {
         std::vector<int32_t> frames(n), nvalid(n);
         for (int u = 0; u < n; ++u) {
-            const int64_t len = woff[u + 1] - woff[u];
-            if (len < 0) return set_error(B3_EINVAL, "sample offsets must be non-decreasing");
+            const int64_t len = woff[u + 1] - woff[u] + lead;
+            if (len < lead) return set_error(B3_EINVAL, "sample offsets must be non-decreasing");
             frames[u] = static_cast<int32_t>(1 + len / 160);
             nvalid[u] = static_cast<int32_t>(len / 160);
         }
@@ -1134,13 +1174,12 @@ int fe_mel(b3_ctx* c, const float* wave, const std::vector<int64_t>& woff, FeSha
         B3_TRY(F.mel.ensure(static_cast<size_t>(s.foff[n]) * 128 * 4 + 16));
         B3_CUDA(cudaMemcpyAsync(F.wave_off.p, woff.data(), (n + 1) * 8, cudaMemcpyHostToDevice, c->stream));
         B3_CUDA(cudaMemcpyAsync(F.frame_off.p, s.foff.data(), (n + 1) * 4, cudaMemcpyHostToDevice, c->stream));
-        F.mel_key = woff;
+        F.mel_key = key;
         F.mel_shape = s;
     }
-    const int nf = s.foff[n];
     const float* t = F.tables.as<float>();
-    MelParams mp;
     mp.n_utt = n;
+    mp.lead = lead;
     mp.wave = wave;
     mp.wave_off = F.wave_off.as<int64_t>();
     mp.frame_off = F.frame_off.as<int>();
@@ -1150,31 +1189,94 @@ int fe_mel(b3_ctx* c, const float* wave, const std::vector<int64_t>& woff, FeSha
     mp.fb_lo = reinterpret_cast<const int*>(t + 1024 + 128 * 257);
     mp.fb_hi = mp.fb_lo + 128;
     mp.mel = F.mel.as<float>();
-    ProfScope ps(c, B3_K_FRONTEND, 0.0, nf * (160.0 * 4 + 512.0));
-    return launch_mel(mp, nf, c->stream);
+    return 0;
 }
 
-// Samples (host or device, one utterance per offset range) -> padded waves
-// in c->fe.wave with the reference's 0.25 s of leading silence
-// (src/transcription.rs:48-52).  Returns the padded offsets.
-int fe_pad(b3_ctx* c, const float* samples, const int64_t* off, int n, bool dev, std::vector<int64_t>& woff) {
+// Mel of utterances [u0, u1) (frames and per-utterance normalisation).
+int fe_mel_run(b3_ctx* c, const FeShape& s, const MelParams& mp, int u0, int u1) {
+    const int f0 = s.foff[u0], f1 = s.foff[u1];
+    ProfScope ps(c, B3_K_FRONTEND, 0.0, (f1 - f0) * (160.0 * 4 + 512.0));
+    return launch_mel(mp, f0, f1, u0, u1, c->stream);
+}
+
+int fe_mel(b3_ctx* c, const float* wave, const std::vector<int64_t>& woff, FeShape& s) {
+    MelParams mp;
+    B3_TRY(fe_mel_setup(c, wave, woff, 0, s, mp));
+    return fe_mel_run(c, s, mp, 0, static_cast<int>(woff.size()) - 1);
+}
+
+// The whole front end of an audio batch (device waves at woff, each
+// utterance behind the reference's 0.25 s of silence -> c->sub16), chunk by
+// chunk: with host input each chunk starts as soon as its own waves are on the
+// device, so the upload of later chunks overlaps the mel and subsampling of
+// earlier ones.  max_rows < 0: no limit on the subsampled rows; else a batch
+// with more rows is an error before any launch.
+int fe_front(b3_ctx* c, const float* wave, const std::vector<int64_t>& woff, FeShape& s, int64_t max_rows) {
     auto& F = c->fe;
-    constexpr int64_t kPad = 4000;
-    woff.assign(n + 1, 0);
-    for (int u = 0; u < n; ++u) {
-        const int64_t len = off[u + 1] - off[u];
-        if (len < 0) return set_error(B3_EINVAL, "sample offsets must be non-decreasing");
-        woff[u + 1] = woff[u] + kPad + len;
+    const int n = static_cast<int>(woff.size()) - 1;
+    MelParams mp;
+    B3_TRY(fe_mel_setup(c, wave, woff, kLeadSamples, s, mp));
+    if (max_rows >= 0 && s.x4off[n] > max_rows)
+        return set_error(B3_EINVAL, "pooler needs %d rows, capacity is %lld", s.x4off[n], static_cast<long long>(max_rows));
+    SubParams sp;
+    B3_TRY(fe_sub_setup(c, s, sp));
+    const bool chunked = F.chunk_wait && F.chunk_u.size() >= 2 && F.chunk_u.back() == n;
+    const std::vector<int> one = {0, n};
+    const std::vector<int>& cu = chunked ? F.chunk_u : one;
+    for (size_t k = 0; k + 1 < cu.size(); ++k) {
+        if (chunked) B3_CUDA(cudaStreamWaitEvent(c->stream, F.chunk_ev[k], 0));
+        B3_TRY(fe_mel_run(c, s, mp, cu[k], cu[k + 1]));
+        B3_TRY(fe_sub_run(c, s, sp, cu[k], cu[k + 1]));
     }
-    B3_TRY(F.wave.ensure(static_cast<size_t>(woff[n]) * 4 + 16));
+    F.chunk_wait = false;
+    return 0;
+}
+
+// Samples (host or device, one utterance per offset range) for the audio
+// front end.  Device samples are read where they are.  Host samples go up
+// into c->fe.wave (same offsets) as about kChunks chunks of similar size, one
+// copy each, on the front end's copy stream, which first waits for every
+// earlier use of that buffer; fe_front waits for each chunk only.  The
+// reference's 0.25 s of leading silence (src/transcription.rs:48-52) is never
+// stored: the mel reads it as zeros.
+int fe_upload(b3_ctx* c, const float* samples, const int64_t* off, int n, bool dev, std::vector<int64_t>& woff,
+              const float** wave) {
+    auto& F = c->fe;
+    woff.assign(off, off + n + 1);
+    for (int u = 0; u < n; ++u)
+        if (off[u + 1] < off[u]) return set_error(B3_EINVAL, "sample offsets must be non-decreasing");
+    F.chunk_wait = false;
+    if (dev) {
+        *wave = samples;
+        return 0;
+    }
+    B3_TRY(F.wave.ensure(static_cast<size_t>(off[n]) * 4 + 16));
     float* w = F.wave.as<float>();
-    const cudaMemcpyKind k = dev ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
-    for (int u = 0; u < n; ++u) {
-        B3_CUDA(cudaMemsetAsync(w + woff[u], 0, kPad * 4, c->stream));
-        const int64_t len = off[u + 1] - off[u];
-        if (len > 0)
-            B3_CUDA(cudaMemcpyAsync(w + woff[u] + kPad, samples + off[u], static_cast<size_t>(len) * 4, k, c->stream));
+    *wave = w;
+    constexpr int kChunks = 8;
+    if (!F.copy_st) B3_CUDA(cudaStreamCreateWithFlags(&F.copy_st, cudaStreamNonBlocking));
+    if (!F.wave_free) B3_CUDA(cudaEventCreateWithFlags(&F.wave_free, cudaEventDisableTiming));
+    while (F.chunk_ev.size() < static_cast<size_t>(kChunks)) {
+        cudaEvent_t e;
+        B3_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+        F.chunk_ev.push_back(e);
     }
+    B3_CUDA(cudaEventRecord(F.wave_free, c->stream));
+    B3_CUDA(cudaStreamWaitEvent(F.copy_st, F.wave_free, 0));
+    F.chunk_u.assign(1, 0);
+    const int64_t total = off[n];
+    for (int u = 0; u < n; ++u) {
+        const int k = static_cast<int>(F.chunk_u.size()) - 1;
+        if (u + 1 == n || (off[u + 1] * kChunks >= total * (k + 1) && k + 1 < kChunks)) {
+            const int64_t a = off[F.chunk_u.back()], b = off[u + 1];
+            if (b > a)
+                B3_CUDA(cudaMemcpyAsync(w + a, samples + a, static_cast<size_t>(b - a) * 4, cudaMemcpyHostToDevice,
+                                        F.copy_st));
+            B3_CUDA(cudaEventRecord(F.chunk_ev[k], F.copy_st));
+            F.chunk_u.push_back(u + 1);
+        }
+    }
+    F.chunk_wait = true;
     return 0;
 }
 
@@ -1550,10 +1652,10 @@ int b3_transcribe_audio(b3_ctx* ctx, const float* samples, const int64_t* offset
     DeviceGuard g(ctx->device);
     const bool dev = flags & B3_DEVICE_PTRS;
     std::vector<int64_t> woff;
-    B3_TRY(fe_pad(ctx, samples, offsets, n_utt, dev, woff));
+    const float* wave = nullptr;
+    B3_TRY(fe_upload(ctx, samples, offsets, n_utt, dev, woff, &wave));
     FeShape s;
-    B3_TRY(fe_mel(ctx, ctx->fe.wave.as<float>(), woff, s));
-    B3_TRY(fe_subsample(ctx, s));
+    B3_TRY(fe_front(ctx, wave, woff, s, -1));
     const int M = s.x4off[n_utt];
     B3_TRY(forward_blocks(ctx, M, ctx->n_layers, &ctx->fe.sub_w_perm));
     B3_TRY(ctx->dec.pooler.ensure(static_cast<size_t>(M) * 640 * 4));
@@ -1574,12 +1676,11 @@ int b3_encode_audio(b3_ctx* ctx, const float* samples, const int64_t* offsets, i
     DeviceGuard g(ctx->device);
     const bool dev = flags & B3_DEVICE_PTRS;
     std::vector<int64_t> woff;
-    B3_TRY(fe_pad(ctx, samples, offsets, n_utt, dev, woff));
+    const float* wave = nullptr;
+    B3_TRY(fe_upload(ctx, samples, offsets, n_utt, dev, woff, &wave));
     FeShape s;
-    B3_TRY(fe_mel(ctx, ctx->fe.wave.as<float>(), woff, s));
+    B3_TRY(fe_front(ctx, wave, woff, s, max_rows));
     const int M = s.x4off[n_utt];
-    if (M > max_rows) return set_error(B3_EINVAL, "pooler needs %d rows, capacity is %lld", M, static_cast<long long>(max_rows));
-    B3_TRY(fe_subsample(ctx, s));
     B3_TRY(forward_blocks(ctx, M, ctx->n_layers, &ctx->fe.sub_w_perm));
     float* dst = dev ? pooler : nullptr;
     if (!dev) {

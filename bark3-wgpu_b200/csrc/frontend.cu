@@ -42,20 +42,24 @@ __device__ __forceinline__ int conv_len_d(int l) { return (l - 1) / 2 + 1; }
 //   X[k] = (Z[k] + conj Z[256-k]) / 2 + W512^k (Z[k] - conj Z[256-k]) / 2i.
 constexpr int kMelWarps = 8;
 
-__device__ __forceinline__ float mel_sample(const float* x, int64_t len, int64_t s, float w) {
+// Sample s of an utterance whose first `lead` samples are zeros (the leading
+// silence, never stored) followed by x[0 .. len - lead): pre-emphasised and
+// windowed.
+__device__ __forceinline__ float mel_sample(const float* x, int64_t len, int lead, int64_t s, float w) {
     if (s < 0 || s >= len) return 0.f;
-    const float cur = __ldg(x + s);
-    return (s == 0 ? cur : cur - 0.97f * __ldg(x + s - 1)) * w;
+    const float cur = s >= lead ? __ldg(x + (s - lead)) : 0.f;
+    const float prev = s - 1 >= lead ? __ldg(x + (s - 1 - lead)) : 0.f;
+    return (s == 0 ? cur : cur - 0.97f * prev) * w;
 }
 
-__global__ void __launch_bounds__(256) k_mel_frames(MelParams p, int n_frames) {
+__global__ void __launch_bounds__(256) k_mel_frames(MelParams p, int f0, int f1) {
     __shared__ float zre[kMelWarps][256], zim[kMelWarps][256], pwr[kMelWarps][260];
     __shared__ float2 tw[256];
     tw[threadIdx.x] = p.twiddle[threadIdx.x];
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int f = blockIdx.x * kMelWarps + warp;
-    if (f >= n_frames) return;
+    const int f = f0 + blockIdx.x * kMelWarps + warp;
+    if (f >= f1) return;
     int lo = 0, hi = p.n_utt;
     while (hi - lo > 1) {
         const int mid = (lo + hi) >> 1;
@@ -64,7 +68,7 @@ __global__ void __launch_bounds__(256) k_mel_frames(MelParams p, int n_frames) {
     const int u = lo;
     const int t = f - p.frame_off[u];
     const float* x = p.wave + p.wave_off[u];
-    const int64_t len = p.wave_off[u + 1] - p.wave_off[u];
+    const int64_t len = p.wave_off[u + 1] - p.wave_off[u] + p.lead;
     const int64_t start = static_cast<int64_t>(t) * kHop - kNfft / 2;
     float* re = zre[warp];
     float* im = zim[warp];
@@ -72,8 +76,8 @@ __global__ void __launch_bounds__(256) k_mel_frames(MelParams p, int n_frames) {
     for (int q = 0; q < 8; ++q) {
         const int m = lane + 32 * q;
         const int r = __brev(m) >> 24;  // 8-bit reversal
-        re[r] = mel_sample(x, len, start + 2 * m, __ldg(p.window + 2 * m));
-        im[r] = mel_sample(x, len, start + 2 * m + 1, __ldg(p.window + 2 * m + 1));
+        re[r] = mel_sample(x, len, p.lead, start + 2 * m, __ldg(p.window + 2 * m));
+        im[r] = mel_sample(x, len, p.lead, start + 2 * m + 1, __ldg(p.window + 2 * m + 1));
     }
     __syncwarp();
 #pragma unroll
@@ -125,15 +129,15 @@ __global__ void __launch_bounds__(256) k_mel_frames(MelParams p, int n_frames) {
 // Per-utterance normalisation over the valid frames (src/mel.rs:103-136):
 // one CTA per (utterance, 32 mel bins); 8 frame lanes per bin, reduced in
 // shared memory; two passes (mean, then squared deviations) as the reference.
-__global__ void __launch_bounds__(256) k_mel_norm(MelParams p) {
+__global__ void __launch_bounds__(256) k_mel_norm(MelParams p, int u0) {
     __shared__ float red[8][33];
     __shared__ float stat[32];
-    const int u = blockIdx.x;
+    const int u = u0 + blockIdx.x;
     const int b = threadIdx.x & 31, fl = threadIdx.x >> 5;
     const int m = blockIdx.y * 32 + b;
     const int f0 = p.frame_off[u];
     const int nf = p.frame_off[u + 1] - f0;
-    const int nvalid = static_cast<int>((p.wave_off[u + 1] - p.wave_off[u]) / kHop);
+    const int nvalid = static_cast<int>((p.wave_off[u + 1] - p.wave_off[u] + p.lead) / kHop);
     const int nv = nvalid > 1 ? nvalid : 1;
     float* mel = p.mel + static_cast<size_t>(f0) * kMel + m;
     float s = 0.f;
@@ -191,11 +195,11 @@ constexpr int kC0S = 65;           // conv0 row of one channel: cols -1..63
 constexpr int kC0Row = kC * kC0S;  // one conv0 row of all kC channels
 constexpr int kSubSmem = (kTm * kMelS + kT1 * kC0Row) * 4;
 
-__global__ void __launch_bounds__(256, 2) k_sub_conv0_dw1(SubParams p) {
+__global__ void __launch_bounds__(256, 2) k_sub_conv0_dw1(SubParams p, int w0) {
     extern __shared__ float sub_smem[];
     float* mel = sub_smem;                 // [kTm][kMelS]
     float* c0 = sub_smem + kTm * kMelS;    // [kT1][kC][kC0S]
-    const int4 wk = p.work[blockIdx.x];    // (utterance, t2_0, channel group)
+    const int4 wk = p.work[w0 + blockIdx.x];   // (utterance, t2_0, channel group)
     const int u = wk.x, t2_0 = wk.y, cg = wk.z * kC;
     const int F = p.mel_off[u + 1] - p.mel_off[u];
     const int F1 = conv_len_d(F), F2 = conv_len_d(F1);
@@ -299,8 +303,8 @@ __global__ void __launch_bounds__(256, 2) k_sub_conv0_dw1(SubParams p) {
 }
 
 // Second depthwise conv (+ bias, + mask): x3 [t2][32][256] -> x4 [t3][16][256].
-__global__ void __launch_bounds__(256) k_sub_dw2(SubParams p) {
-    const int row = blockIdx.x;  // global t3 row
+__global__ void __launch_bounds__(256) k_sub_dw2(SubParams p, int r0) {
+    const int row = r0 + blockIdx.x;  // global t3 row
     int lo = 0, hi = p.n_utt;
     while (hi - lo > 1) {
         const int mid = (lo + hi) >> 1;
@@ -358,16 +362,17 @@ int check_launch(const char* what) {
 
 }  // namespace
 
-int launch_mel(const MelParams& p, int n_frames, cudaStream_t st) {
-    if (n_frames <= 0) return 0;
-    k_mel_frames<<<(n_frames + kMelWarps - 1) / kMelWarps, 256, 0, st>>>(p, n_frames);
+int launch_mel(const MelParams& p, int f0, int f1, int u0, int u1, cudaStream_t st) {
+    if (f1 <= f0 || u1 <= u0) return 0;
+    k_mel_frames<<<(f1 - f0 + kMelWarps - 1) / kMelWarps, 256, 0, st>>>(p, f0, f1);
     const int rc = check_launch("k_mel_frames");
     if (rc) return rc;
-    k_mel_norm<<<dim3(p.n_utt, kMel / 32), 256, 0, st>>>(p);
+    k_mel_norm<<<dim3(u1 - u0, kMel / 32), 256, 0, st>>>(p, u0);
     return check_launch("k_mel_norm");
 }
 
-int launch_sub_conv0_dw1(const SubParams& p, int n_work, cudaStream_t st) {
+int launch_sub_conv0_dw1(const SubParams& p, int w0, int w1, cudaStream_t st) {
+    const int n_work = w1 - w0;
     if (n_work <= 0) return 0;
     static bool attr_done = false;
     if (!attr_done) {
@@ -375,13 +380,13 @@ int launch_sub_conv0_dw1(const SubParams& p, int n_work, cudaStream_t st) {
         if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(k_sub_conv0_dw1)", e);
         attr_done = true;
     }
-    k_sub_conv0_dw1<<<n_work, 256, kSubSmem, st>>>(p);
+    k_sub_conv0_dw1<<<n_work, 256, kSubSmem, st>>>(p, w0);
     return check_launch("k_sub_conv0_dw1");
 }
 
-int launch_sub_dw2(const SubParams& p, int rows, cudaStream_t st) {
-    if (rows <= 0) return 0;
-    k_sub_dw2<<<rows, 256, 0, st>>>(p);
+int launch_sub_dw2(const SubParams& p, int r0, int r1, cudaStream_t st) {
+    if (r1 <= r0) return 0;
+    k_sub_dw2<<<r1 - r0, 256, 0, st>>>(p, r0);
     return check_launch("k_sub_dw2");
 }
 
