@@ -1234,9 +1234,11 @@ int fe_front(b3_ctx* c, const float* wave, const std::vector<int64_t>& woff, FeS
 
 // Samples (host or device, one utterance per offset range) for the audio
 // front end.  Device samples are read where they are.  Host samples go up
-// into c->fe.wave (same offsets) as about kChunks chunks of similar size, one
-// copy each, on the front end's copy stream, which first waits for every
-// earlier use of that buffer; fe_front waits for each chunk only.  The
+// into c->fe.wave (same offsets) in up to kChunks chunks, one copy each, on
+// the front end's copy stream, which first waits for every earlier use of that
+// buffer; fe_front waits for each chunk only.  The first chunk is small (1/32
+// of the samples) so the front end starts early; the front end then consumes
+// samples more slowly than the copies deliver them.  The
 // reference's 0.25 s of leading silence (src/transcription.rs:48-52) is never
 // stored: the mel reads it as zeros.
 int fe_upload(b3_ctx* c, const float* samples, const int64_t* off, int n, bool dev, std::vector<int64_t>& woff,
@@ -1265,9 +1267,11 @@ int fe_upload(b3_ctx* c, const float* samples, const int64_t* off, int n, bool d
     B3_CUDA(cudaStreamWaitEvent(F.copy_st, F.wave_free, 0));
     F.chunk_u.assign(1, 0);
     const int64_t total = off[n];
+    // cumulative sample fractions (in 32nds) at which chunks 0 .. kChunks-2 end
+    static constexpr int kEnd32[kChunks - 1] = {1, 4, 8, 12, 16, 20, 24};
     for (int u = 0; u < n; ++u) {
         const int k = static_cast<int>(F.chunk_u.size()) - 1;
-        if (u + 1 == n || (off[u + 1] * kChunks >= total * (k + 1) && k + 1 < kChunks)) {
+        if (u + 1 == n || (k + 1 < kChunks && off[u + 1] * 32 >= total * kEnd32[k])) {
             const int64_t a = off[F.chunk_u.back()], b = off[u + 1];
             if (b > a)
                 B3_CUDA(cudaMemcpyAsync(w + a, samples + a, static_cast<size_t>(b - a) * 4, cudaMemcpyHostToDevice,
