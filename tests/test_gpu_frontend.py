@@ -86,3 +86,42 @@ def test_audio_to_tokens(fe_model, syn, oracle, pkg):
     print(f"audio -> tokens vs oracle decoder on the GPU pooler: match {m:.4f}, identical streams {exact:.2f}; "
           f"vs the whole oracle pipeline {token_match(got, full)[0]:.4f}")
     assert m >= 0.99
+
+
+def test_audio_host_and_device_inputs_agree(fe_model, syn, pkg):
+    """The host-pointer call uploads the samples in utterance chunks on a side
+    stream and runs the front end chunk by chunk; the device-pointer call reads
+    the samples in place in one pass.  Both must give bit-identical poolers and
+    identical token streams, on a batch large enough for every chunk (and with
+    an empty utterance)."""
+    import torch
+
+    w, enc = fe_model
+    rng = np.random.default_rng(17)
+    secs = [1.3, 0.0, 4.0, 0.7, 2.2, 0.1, 3.1, 0.9, 1.6, 2.7, 0.4, 5.0]
+    waves = [syn.synth_audio(rng, s) if s > 0 else np.zeros(0, np.float32) for s in secs]
+    host_pooler, host_roff = enc.encode_audio(waves)
+    host_tokens = enc.transcribe_audio(waves)
+
+    L = pkg.lib()
+    off = np.concatenate([[0], np.cumsum([len(x) for x in waves])]).astype(np.int64)
+    samples = torch.from_numpy(np.concatenate(waves).astype(np.float32)).cuda()
+    n = len(waves)
+    rows = int(host_roff[-1])
+    pooler = torch.zeros(rows + 8, 640, dtype=torch.float32, device="cuda")
+    roff = np.zeros(n + 1, dtype=np.int32)
+    pkg.check(L.b3_encode_audio(enc.ctx, samples.data_ptr(), off.ctypes.data, n, pooler.data_ptr(), roff.ctypes.data,
+                                rows + 8, pkg.B3_DEVICE_PTRS))
+    enc.sync()
+    assert np.array_equal(roff, host_roff)
+    assert np.array_equal(pooler[:rows].cpu().numpy(), host_pooler)
+
+    max_tokens = 4096
+    tok = torch.zeros(n, max_tokens, 3, dtype=torch.int32, device="cuda")
+    cnt = torch.zeros(n, dtype=torch.int32, device="cuda")
+    pkg.check(L.b3_transcribe_audio(enc.ctx, samples.data_ptr(), off.ctypes.data, n, tok.data_ptr(), cnt.data_ptr(),
+                                    max_tokens, pkg.B3_DEVICE_PTRS))
+    enc.sync()
+    tok, cnt = tok.cpu().numpy().view(np.uint32), cnt.cpu().numpy()
+    for i in range(n):
+        assert np.array_equal(tok[i, : min(int(cnt[i]), max_tokens)], host_tokens[i]), f"utterance {i}"
