@@ -52,6 +52,25 @@ def test_decoder_matches_oracle(dec_model, syn, oracle):
     assert m >= MATCH
 
 
+def test_large_batch_rows_per_cta(dec_model, oracle):
+    """333 utterances: more rows than the persistent decoder has half-CTAs
+    (2 per SM), so each walks several rows per phase; 3 row tiles of 128, the
+    last partial; lengths 0..40 frames (an empty utterance finishes at once)."""
+    w, enc = dec_model
+    rng = np.random.default_rng(9)
+    lens = rng.integers(0, 41, size=333)
+    lens[5] = 0
+    pooler = rng.normal(0, 1, size=(int(lens.sum()), 640)).astype(np.float32)
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    got = enc.decode_batch(pooler, cu)
+    want = oracle.OracleTdt(w).decode_batch(pooler, cu)
+    m, exact = token_match(got, want)
+    print(f"333-utterance batch: token match {m:.4f}, identical streams {exact:.2f}, "
+          f"tokens {sum(len(x) for x in want)}")
+    assert len(got[5]) == 0
+    assert m >= MATCH
+
+
 def test_reference_vocab_size(syn, oracle, pkg):
     """The released model's joint: 8192 tokens + blank, 5 durations."""
     w = syn.encoder_weights(seed=9, n_layers=1, layout="lut4")
