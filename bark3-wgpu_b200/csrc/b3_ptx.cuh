@@ -279,6 +279,15 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
     return d;
 }
 
+// The descriptor of the same layout `bytes` further on: only the start
+// address field (address >> 4, bits [0,14)) moves.  Shared-memory addresses
+// stay below 2^18, so the field cannot carry into the next one; adding to
+// the low word alone keeps the issuing thread's integer work to one add per
+// MMA, which matters while the expander warps load the integer pipe.
+__device__ __forceinline__ uint64_t desc_advance(uint64_t desc, uint32_t bytes) {
+    return (desc & 0xFFFFFFFF00000000ull) | static_cast<uint32_t>(static_cast<uint32_t>(desc) + (bytes >> 4));
+}
+
 // Instruction descriptor, kind::f16: D f32, A and B f16, both K-major.
 // Bits: [4,6) D fmt (1 = f32), [7,10) A fmt (0 = f16), [10,13) B fmt,
 // [15] A major, [16] B major, [17,23) N>>3, [24,29) M>>4.

@@ -366,15 +366,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (ok && LUT) ok = mbar_wait(smem_u32(&bready[s]), ph, 0x03);
                     if (!ok) break;
                     tc_fence_after();
-                    const uint32_t b0 = smem_u32(sB + s * Cfg::kBBytes);
+                    const uint64_t db = smem_desc_sw128(smem_u32(sB + s * Cfg::kBBytes));
+                    const uint64_t da = smem_desc_sw128(smem_u32(sA + s * SUB * Cfg::kABytes));
 #pragma unroll
                     for (int kk = 0; kk < kBK / 16; ++kk) {
-                        const uint64_t bd = smem_desc_sw128(b0 + kk * 32);
 #pragma unroll
-                        for (int sub = 0; sub < SUB; ++sub) {
-                            const uint32_t a0 = smem_u32(sA + (s * SUB + sub) * Cfg::kABytes);
-                            mma_f16_ss(acc + sub * BN, smem_desc_sw128(a0 + kk * 32), bd, idesc, (kb | kk) != 0);
-                        }
+                        for (int sub = 0; sub < SUB; ++sub)
+                            mma_f16_ss(acc + sub * BN, desc_advance(da, sub * Cfg::kABytes + kk * 32),
+                                       desc_advance(db, kk * 32), idesc, kk != 0 || kb != 0);
                     }
                     mma_commit(smem_u32(&empty[s]));
                 }
@@ -619,12 +618,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     if (ok && LUT) ok = mbar_wait(smem_u32(&bready[s]), ph, 0x13);
                     if (!ok) break;
                     tc_fence_after();
-                    const uint32_t a0 = smem_u32(sA + s * pair::kABytes);
-                    const uint32_t b0 = smem_u32(sB + s * pair::kBBytes);
+                    const uint64_t da = smem_desc_sw128(smem_u32(sA + s * pair::kABytes));
+                    const uint64_t db = smem_desc_sw128(smem_u32(sB + s * pair::kBBytes));
 #pragma unroll
                     for (int kk = 0; kk < kBK / 16; ++kk)
-                        mma_f16_ss_pair(acc, smem_desc_sw128(a0 + kk * 32), smem_desc_sw128(b0 + kk * 32), idesc,
-                                        (kb | kk) != 0);
+                        mma_f16_ss_pair(acc, desc_advance(da, kk * 32), desc_advance(db, kk * 32), idesc,
+                                        kk != 0 || kb != 0);
                     mma_commit_pair_mc(smem_u32(&empty[s]), 0x3);
                 }
                 if (ok) mma_commit_pair_mc(smem_u32(&tfull[b]), 0x3);
