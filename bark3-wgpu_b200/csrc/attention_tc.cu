@@ -380,14 +380,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // 31 - lane + j; across a warp the word index moves by 65 per lane: no conflicts
                 const float* dg = sh + 31 - lane;
                 const int kvalid = it.T - kb * kBK - 32 * hf;
+                const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
+#pragma unroll
+                for (int j = 0; j < 32; j += 2) {
+                    const float2 v = __fmul2_rn(__fadd2_rn(make_float2(s[j], s[j + 1]), make_float2(dg[j], dg[j + 1])), sc2);
+                    s[j] = v.x;
+                    s[j + 1] = v.y;
+                }
+                if (kvalid < 32) {   // warp-uniform: only an utterance's last key block has keys past its end
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        if (j >= kvalid) s[j] = -INFINITY;
+                }
                 float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-                for (int j = 0; j < 32; ++j) {
-                    float v = (s[j] + dg[j]) * p.scale_log2;
-                    if (j >= kvalid) v = -INFINITY;
-                    s[j] = v;
-                    mx[j & 3] = fmaxf(mx[j & 3], v);
-                }
+                for (int j = 0; j < 32; ++j) mx[j & 3] = fmaxf(mx[j & 3], s[j]);
                 const float mloc = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
                 const int xs = 64 + (x & 1);   // exchange slot, by exchange parity
                 sh[xs] = mloc;
@@ -419,15 +426,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                         tmem_st_32x32b_x32(tmem + lrow + kTO + 64 * hf + 32, o1);
                     }
                 }
-                float ls[4] = {0.f, 0.f, 0.f, 0.f};
+                float2 ls[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
                 uint32_t pk[16];
+                const float2 mneg = make_float2(-m_use, -m_use);
 #pragma unroll
                 for (int j = 0; j < 32; j += 2) {
-                    const float a = exp2f(s[j] - m_use), b = exp2f(s[j + 1] - m_use);
-                    ls[(j >> 1) & 3] += a + b;
-                    pk[j >> 1] = h2u(a, b);
+                    const float2 x = __fadd2_rn(make_float2(s[j], s[j + 1]), mneg);
+                    const float2 e = make_float2(exp2f(x.x), exp2f(x.y));
+                    ls[(j >> 1) & 1] = __fadd2_rn(ls[(j >> 1) & 1], e);
+                    pk[j >> 1] = h2u(e.x, e.y);
                 }
-                l_half = l_half * corr + ((ls[0] + ls[1]) + (ls[2] + ls[3]));
+                l_half = l_half * corr + ((ls[0].x + ls[0].y) + (ls[1].x + ls[1].y));
                 tmem_st_32x32b_x16(tmem + lrow + kTS + 64 * st + 16 * hf, pk);   // P over this block's S columns
                 tmem_wait_st();
                 tc_fence_before();

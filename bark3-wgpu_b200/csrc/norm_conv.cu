@@ -101,41 +101,50 @@ __global__ void __launch_bounds__(256) k4_layernorm(const float* __restrict__ x,
     }
 }
 
-// Depthwise conv k=9 + BN(a, b) + SiLU.  Block: 256 threads x 4 channels =
-// all 1024 channels of kDwRows consecutive frames.  The (kDwRows + 8)-frame
-// input tile is staged in shared memory with cp.async in two groups, so the
-// first rows are convolved while the rest are still arriving; each thread
-// slides a 9-frame register window (pairs of channels, packed f32x2 FMAs)
-// over it.  Frame t reads t-4 .. t+4 inside its own utterance [seg.x,
-// seg.y); anything outside is zero.
+// Depthwise conv k=9 + BN(a, b) + SiLU.  Persistent: one CTA per SM walks
+// tiles of kDwRows consecutive frames x all 1024 channels.  A tile's
+// (kDwRows + 8)-frame input (with the +-4 halo) is staged in shared memory by
+// cp.async into one of two buffers while the CTA convolves the previous tile
+// from the other, so the loads of tile i+1 overlap the arithmetic and stores
+// of tile i.  512 threads: thread (c4, half) owns channels 4 c4 .. 4 c4 + 3
+// of rows [half * kDwHalf, half * kDwHalf + kDwHalf) and slides a 9-frame
+// register window (pairs of channels, packed f32x2 FMAs) over them.  Frame t
+// reads t-4 .. t+4 inside its own utterance [seg.x, seg.y); anything outside
+// is zero.  Rows whose whole window lies inside the utterance take a path
+// without per-tap tests; the taps are summed in the same order either way.
+// A row's utterance bounds come from a per-frame [start, end) table.
 constexpr int kDwRows = 40;
+constexpr int kDwHalf = kDwRows / 2;
 constexpr int kDwTile = kDwRows + 8;
-constexpr int kDwSplit = 24;                 // tile rows in the first cp.async group
-constexpr int kDwSmem = kDwTile * 1024 * 2;
+constexpr int kDwTileBytes = kDwTile * 1024 * 2;
+constexpr int kDwSmem = 2 * kDwTileBytes;
+constexpr int kDwThreads = 512;
 
-__global__ void __launch_bounds__(256, 2) k3_dwconv_bn_silu(const __half* __restrict__ src,
-                                                            const int2* __restrict__ seg, int rows,
-                                                            const float* __restrict__ dw_t,  // [9][1024]
-                                                            const float* __restrict__ bn_a,
-                                                            const float* __restrict__ bn_b,
-                                                            __half* __restrict__ dst) {
-    extern __shared__ __align__(16) uint8_t tile[];  // [kDwTile][1024] f16, frame t0-4+i in row i
-    const int c0 = threadIdx.x * 4;
-    const int t0 = blockIdx.x * kDwRows;
-    {
-        const uint32_t base = static_cast<uint32_t>(__cvta_generic_to_shared(tile));
-        for (int c = threadIdx.x; c < kDwTile * 128; c += 256) {
+__global__ void __launch_bounds__(kDwThreads, 1) k3_dwconv_bn_silu(const __half* __restrict__ src,
+                                                                   const int2* __restrict__ seg, int rows,
+                                                                   const float* __restrict__ dw_t,  // [9][1024]
+                                                                   const float* __restrict__ bn_a,
+                                                                   const float* __restrict__ bn_b,
+                                                                   __half* __restrict__ dst) {
+    extern __shared__ __align__(16) uint8_t tiles[];  // 2 x [kDwTile][1024] f16, frame t0-4+i in row i
+    const int c4 = threadIdx.x & 255;
+    const int c0 = c4 * 4;
+    const int rbeg = (threadIdx.x >> 8) * kDwHalf;
+    const int n_tiles = (rows + kDwRows - 1) / kDwRows;
+    const uint32_t sbase = static_cast<uint32_t>(__cvta_generic_to_shared(tiles));
+    // rows past the end of the input are zero-filled (cp.async with 0 source bytes)
+    auto stage = [&](int tile, int buf) {
+        const int t0 = tile * kDwRows;
+        for (int c = threadIdx.x; c < kDwTile * 128; c += kDwThreads) {
             const int r = c >> 7, ch = c & 127;
             const int t = t0 - 4 + r;
             const bool ok = t >= 0 && t < rows;
             const __half* g = src + static_cast<size_t>(ok ? t : 0) * 1024 + ch * 8;
-            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(base + r * 2048 + ch * 16), "l"(g),
-                         "r"(ok ? 16 : 0)
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(sbase + buf * kDwTileBytes + r * 2048 + ch * 16),
+                         "l"(g), "r"(ok ? 16 : 0)
                          : "memory");
-            if (c + 256 >= kDwSplit * 128 && c < kDwSplit * 128) asm volatile("cp.async.commit_group;" ::: "memory");
         }
-        asm volatile("cp.async.commit_group;" ::: "memory");
-    }
+    };
     float2 w[9][2];
 #pragma unroll
     for (int i = 0; i < 9; ++i) {
@@ -152,53 +161,78 @@ __global__ void __launch_bounds__(256, 2) k3_dwconv_bn_silu(const __half* __rest
         bb[0] = make_float2(b.x, b.y);
         bb[1] = make_float2(b.z, b.w);
     }
-    auto load = [&](int r, float2 (&d)[2]) {
-        const uint2 u = *reinterpret_cast<const uint2*>(tile + r * 2048 + c0 * 2);
-        d[0] = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
-        d[1] = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
-    };
-    asm volatile("cp.async.wait_group 1;" ::: "memory");
-    __syncthreads();
-    // circular 9-frame window: tile row r lives in slot r % 9.  The row loop
-    // is unrolled by 9 so every slot index is a compile-time constant.
-    float2 win[9][2];
+    if (static_cast<int>(blockIdx.x) < n_tiles) stage(blockIdx.x, 0);
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    int buf = 0;
+    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, buf ^= 1) {
+        const int next = tile + gridDim.x;
+        const int t0 = tile * kDwRows;
+        // utterance bounds of this thread's first and last row, fetched before
+        // the wait: with at most one utterance boundary inside its rows (the
+        // first row's utterance ends where the last row's begins, or both rows
+        // share one) every row's bounds are one of the two, and no row needs a
+        // dependent load of its own
+        const int ta = t0 + rbeg < rows ? t0 + rbeg : rows - 1;
+        const int tz = t0 + rbeg + kDwHalf - 1 < rows ? t0 + rbeg + kDwHalf - 1 : rows - 1;
+        const int2 sga = __ldg(seg + ta), sgz = __ldg(seg + tz);
+        const bool two_segs = sga.y >= sgz.x;
+        if (next < n_tiles) stage(next, buf ^ 1);
+        asm volatile("cp.async.commit_group;" ::: "memory");   // possibly empty: keeps the group count fixed
+        asm volatile("cp.async.wait_group 1;" ::: "memory");   // this tile's group has landed
+        __syncthreads();
+        const uint8_t* tb = tiles + buf * kDwTileBytes;
+        auto load = [&](int r, float2 (&d)[2]) {
+            const uint2 u = *reinterpret_cast<const uint2*>(tb + r * 2048 + c0 * 2);
+            d[0] = __half22float2(*reinterpret_cast<const __half2*>(&u.x));
+            d[1] = __half22float2(*reinterpret_cast<const __half2*>(&u.y));
+        };
+        // circular 9-frame window: tile row r lives in slot (r - rbeg) % 9; the
+        // row loop is unrolled by 9 so every slot index is a compile-time constant
+        float2 win[9][2];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) load(i, win[i]);
+        for (int i = 0; i < 8; ++i) load(rbeg + i, win[i]);
 #pragma unroll 1
-    for (int r0 = 0; r0 < kDwRows; r0 += 9) {
-        if (r0 + 8 + 8 >= kDwSplit && r0 < kDwSplit) {   // rows up to r0 + 16 may come from the second group
-            asm volatile("cp.async.wait_group 0;" ::: "memory");
-            __syncthreads();
-        }
+        for (int r0 = 0; r0 < kDwHalf; r0 += 9) {
 #pragma unroll
-        for (int u = 0; u < 9; ++u) {
-            const int r = r0 + u;
-            const int t = t0 + r;
-            if (r < kDwRows && t < rows) {
-                load(r + 8, win[(u + 8) % 9]);
-                const int2 sg = __ldg(seg + t);
-                const int lo = max(sg.x - (t - 4), 0);
-                const int hi = min(sg.y - (t - 4), 9);
-                float2 acc[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+            for (int u = 0; u < 9; ++u) {
+                const int r = rbeg + r0 + u;
+                const int t = t0 + r;
+                if (r0 + u < kDwHalf && t < rows) {
+                    load(r + 8, win[(u + 8) % 9]);
+                    const int2 sg = two_segs ? (t < sga.y ? sga : sgz) : __ldg(seg + t);
+                    const int lo = max(sg.x - (t - 4), 0);
+                    const int hi = min(sg.y - (t - 4), 9);
+                    float2 acc[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+                    if (lo == 0 && hi == 9) {
 #pragma unroll
-                for (int i = 0; i < 9; ++i) {
-                    if (i < lo || i >= hi) continue;
-                    acc[0] = __ffma2_rn(win[(u + i) % 9][0], w[i][0], acc[0]);
-                    acc[1] = __ffma2_rn(win[(u + i) % 9][1], w[i][1], acc[1]);
+                        for (int i = 0; i < 9; ++i) {
+                            acc[0] = __ffma2_rn(win[(u + i) % 9][0], w[i][0], acc[0]);
+                            acc[1] = __ffma2_rn(win[(u + i) % 9][1], w[i][1], acc[1]);
+                        }
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 9; ++i) {
+                            if (i < lo || i >= hi) continue;
+                            acc[0] = __ffma2_rn(win[(u + i) % 9][0], w[i][0], acc[0]);
+                            acc[1] = __ffma2_rn(win[(u + i) % 9][1], w[i][1], acc[1]);
+                        }
+                    }
+                    uint32_t o[2];
+#pragma unroll
+                    for (int j = 0; j < 2; ++j) {
+                        const float2 y = __ffma2_rn(acc[j], ba[j], bb[j]);
+                        const float y0 = __fdividef(y.x, 1.0f + __expf(-y.x));
+                        const float y1 = __fdividef(y.y, 1.0f + __expf(-y.y));
+                        __half2 h = __floats2half2_rn(y0, y1);
+                        o[j] = *reinterpret_cast<uint32_t*>(&h);
+                    }
+                    *reinterpret_cast<uint2*>(dst + static_cast<size_t>(t) * 1024 + c0) = make_uint2(o[0], o[1]);
                 }
-                uint32_t o[2];
-#pragma unroll
-                for (int j = 0; j < 2; ++j) {
-                    const float2 y = __ffma2_rn(acc[j], ba[j], bb[j]);
-                    const float y0 = __fdividef(y.x, 1.0f + __expf(-y.x));
-                    const float y1 = __fdividef(y.y, 1.0f + __expf(-y.y));
-                    __half2 h = __floats2half2_rn(y0, y1);
-                    o[j] = *reinterpret_cast<uint32_t*>(&h);
-                }
-                *reinterpret_cast<uint2*>(dst + static_cast<size_t>(t) * 1024 + c0) = make_uint2(o[0], o[1]);
             }
         }
+        __syncthreads();   // every thread is done with this buffer before it is restaged
     }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
 __global__ void k_f32_to_f16(const float4* __restrict__ src, uint2* __restrict__ dst, int64_t n4) {
@@ -243,7 +277,15 @@ int launch_dwconv(const __half* src, const int2* seg, int rows, const float* dw_
         if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(k3)", e);
         attr_done = true;
     }
-    k3_dwconv_bn_silu<<<(rows + kDwRows - 1) / kDwRows, 256, kDwSmem, st>>>(src, seg, rows, dw_t, bn_a, bn_b, dst);
+    static int n_sms = 0;
+    if (!n_sms) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n_sms, cudaDevAttrMultiProcessorCount, dev);
+        if (n_sms <= 0) n_sms = 148;
+    }
+    const int tiles = (rows + kDwRows - 1) / kDwRows;
+    k3_dwconv_bn_silu<<<tiles < n_sms ? tiles : n_sms, kDwThreads, kDwSmem, st>>>(src, seg, rows, dw_t, bn_a, bn_b, dst);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? 0 : set_cuda_error("k3_dwconv_bn_silu", e);
 }
