@@ -209,11 +209,16 @@ __global__ void __launch_bounds__(256, 2) k_sub_conv0_dw1(SubParams p, int w0) {
     const float* melu = p.mel + static_cast<size_t>(p.mel_off[u]) * kMel;
     const int t1_0 = 2 * t2_0 - 1;      // first conv0 row
     const int tm_0 = 2 * t1_0 - 1;      // first mel row
-    for (int i = threadIdx.x; i < kTm * kMel; i += blockDim.x) {
-        const int r = i >> 7, col = i & 127;
+    // 16-byte loads of mel columns 4 c .. 4 c + 3: the even pair goes to even
+    // slots 2 c, 2 c + 1 and the odd pair to odd slots 66 + 2 c, 67 + 2 c
+    for (int i = threadIdx.x; i < kTm * (kMel / 4); i += blockDim.x) {
+        const int r = i >> 5, c = i & 31;
         const int tm = tm_0 + r;
-        const float v = (tm >= 0 && tm < F) ? melu[static_cast<size_t>(tm) * kMel + col] : 0.f;
-        mel[r * kMelS + ((col & 1) ? 65 + ((col + 1) >> 1) : (col >> 1))] = v;
+        const float4 v = (tm >= 0 && tm < F)
+                             ? __ldg(reinterpret_cast<const float4*>(melu + static_cast<size_t>(tm) * kMel) + c)
+                             : make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float2*>(mel + r * kMelS + 2 * c) = make_float2(v.x, v.z);
+        *reinterpret_cast<float2*>(mel + r * kMelS + 66 + 2 * c) = make_float2(v.y, v.w);
     }
     if (threadIdx.x < kTm) {
         mel[threadIdx.x * kMelS + 64] = 0.f;   // even col 128 (never read)

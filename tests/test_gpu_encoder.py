@@ -98,6 +98,23 @@ def test_attn_conv_section(lut_model, syn):
     assert e <= LAYER_TOL
 
 
+@pytest.mark.parametrize("t", [2001, 7500])
+def test_attn_conv_long_sequence(lut_model, t):
+    """BASELINE config 3's sequence length (T = 7500, ten minutes of audio):
+    59 query blocks x 118 key blocks per head, the 256-row R ring wrapping many
+    times, a ragged last block; the same section through the CPU oracle."""
+    w, enc, ref, n_layers = lut_model
+    x = np.random.default_rng(t).normal(0, 1, size=(t, 1024)).astype(np.float32)
+    got = x.copy()
+    enc.attn_conv(1, got)
+    want = ref.attn_conv(1, x)
+    assert np.isfinite(got).all()
+    e = rel_err(got - x, want - x)
+    mean = float(np.mean(np.abs((got - x) - (want - x))) / np.mean(np.abs(want - x)))
+    print(f"T={t} attn+conv delta err max {e:.2e} mean {mean:.2e}")
+    assert e <= LAYER_TOL
+
+
 def test_errors(pkg, syn):
     enc = pkg.Encoder(0)
     sub = np.zeros((4, 4096), dtype=np.float32)
