@@ -127,10 +127,13 @@ __global__ void __launch_bounds__(256) k_mel_frames(MelParams p, int f0, int f1)
 }
 
 // Per-utterance normalisation over the valid frames (src/mel.rs:103-136):
-// one CTA per (utterance, 32 mel bins); 8 frame lanes per bin, reduced in
-// shared memory; two passes (mean, then squared deviations) as the reference.
-__global__ void __launch_bounds__(256) k_mel_norm(MelParams p, int u0) {
-    __shared__ float red[8][33];
+// one CTA per (utterance, 32 mel bins); kNormLanes frame lanes per bin
+// (1024 threads, so a CTA keeps 32 rows of loads in flight per pass),
+// reduced in shared memory; two passes (mean, then squared deviations) as
+// the reference.
+constexpr int kNormLanes = 32;
+__global__ void __launch_bounds__(32 * kNormLanes) k_mel_norm(MelParams p, int u0) {
+    __shared__ float red[kNormLanes][33];
     __shared__ float stat[32];
     const int u = u0 + blockIdx.x;
     const int b = threadIdx.x & 31, fl = threadIdx.x >> 5;
@@ -142,20 +145,20 @@ __global__ void __launch_bounds__(256) k_mel_norm(MelParams p, int u0) {
     float* mel = p.mel + static_cast<size_t>(f0) * kMel + m;
     float s = 0.f;
 #pragma unroll 4
-    for (int t = fl; t < nvalid; t += 8) s += mel[static_cast<size_t>(t) * kMel];
+    for (int t = fl; t < nvalid; t += kNormLanes) s += mel[static_cast<size_t>(t) * kMel];
     red[fl][b] = s;
     __syncthreads();
     if (fl == 0) {
         float tot = 0.f;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) tot += red[i][b];
+        for (int i = 0; i < kNormLanes; ++i) tot += red[i][b];
         stat[b] = tot / static_cast<float>(nv);
     }
     __syncthreads();
     const float mean = stat[b];
     float q = 0.f;
 #pragma unroll 4
-    for (int t = fl; t < nvalid; t += 8) {
+    for (int t = fl; t < nvalid; t += kNormLanes) {
         const float d = mel[static_cast<size_t>(t) * kMel] - mean;
         q += d * d;
     }
@@ -164,12 +167,12 @@ __global__ void __launch_bounds__(256) k_mel_norm(MelParams p, int u0) {
     if (fl == 0) {
         float tot = 0.f;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) tot += red[i][b];
+        for (int i = 0; i < kNormLanes; ++i) tot += red[i][b];
         stat[b] = sqrtf(tot / static_cast<float>(nv - 1 > 1 ? nv - 1 : 1)) + 1e-5f;
     }
     __syncthreads();
     const float den = stat[b];
-    for (int t = fl; t < nf; t += 8) {
+    for (int t = fl; t < nf; t += kNormLanes) {
         float& v = mel[static_cast<size_t>(t) * kMel];
         v = t < nvalid ? (v - mean) / den : 0.f;
     }
@@ -372,7 +375,7 @@ int launch_mel(const MelParams& p, int f0, int f1, int u0, int u1, cudaStream_t 
     k_mel_frames<<<(f1 - f0 + kMelWarps - 1) / kMelWarps, 256, 0, st>>>(p, f0, f1);
     const int rc = check_launch("k_mel_frames");
     if (rc) return rc;
-    k_mel_norm<<<dim3(u1 - u0, kMel / 32), 256, 0, st>>>(p, u0);
+    k_mel_norm<<<dim3(u1 - u0, kMel / 32), 32 * kNormLanes, 0, st>>>(p, u0);
     return check_launch("k_mel_norm");
 }
 
