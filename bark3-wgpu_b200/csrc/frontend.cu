@@ -311,8 +311,15 @@ __global__ void __launch_bounds__(256, 2) k_sub_conv0_dw1(SubParams p, int w0) {
 }
 
 // Second depthwise conv (+ bias, + mask): x3 [t2][32][256] -> x4 [t3][16][256].
-__global__ void __launch_bounds__(256) k_sub_dw2(SubParams p, int r0) {
-    const int row = r0 + blockIdx.x;  // global t3 row
+// 64 threads per t3 row (4 rows per CTA), a thread owns 4 channels: it walks
+// the 16 output columns left to right, loading each input column (3 rows x
+// 4 channels, 8-byte loads) once and carrying the shared column to the next
+// output.  Every output keeps the scalar accumulation order (bias, then taps
+// row by row, left to right).
+constexpr int kDw2Rows = 4;
+__global__ void __launch_bounds__(64 * kDw2Rows) k_sub_dw2(SubParams p, int r0, int r1) {
+    const int row = r0 + blockIdx.x * kDw2Rows + (threadIdx.x >> 6);  // global t3 row
+    if (row >= r1) return;
     int lo = 0, hi = p.n_utt;
     while (hi - lo > 1) {
         const int mid = (lo + hi) >> 1;
@@ -325,30 +332,70 @@ __global__ void __launch_bounds__(256) k_sub_dw2(SubParams p, int r0) {
     const int nvalid = p.n_valid[u];
     const int v3 = conv_len_d(conv_len_d(conv_len_d(nvalid > 1 ? nvalid : 1)));
     const __half* x3 = p.x3 + static_cast<size_t>(p.x2_off[u]) * 32 * 256;
-    const int c = threadIdx.x;   // blockDim.x == 256: one channel per thread
-    float w[9];
+    const int c0 = (threadIdx.x & 63) * 4;
+    float w[9][4], bias[4];
 #pragma unroll
-    for (int t = 0; t < 9; ++t) w[t] = __ldg(p.w5 + c * 9 + t);
-    const float bias = __ldg(p.b5 + c);
+    for (int e = 0; e < 4; ++e) {
+        bias[e] = __ldg(p.b5 + c0 + e);
+#pragma unroll
+        for (int t = 0; t < 9; ++t) w[t][e] = __ldg(p.w5 + (c0 + e) * 9 + t);
+    }
     const bool live = t3 < v3;
+    bool rok[3];
+#pragma unroll
+    for (int ki = 0; ki < 3; ++ki) {
+        const int t2 = 2 * t3 + ki - 1;
+        rok[ki] = t2 >= 0 && t2 < F2;
+    }
+    // column j2 of the 3 input rows, 4 channels
+    auto col = [&](int j2, float (&v)[3][4]) {
+#pragma unroll
+        for (int ki = 0; ki < 3; ++ki) {
+            uint2 raw = make_uint2(0u, 0u);
+            if (rok[ki]) {
+                const int t2 = 2 * t3 + ki - 1;
+                raw = __ldg(reinterpret_cast<const uint2*>(x3 + (static_cast<size_t>(t2) * 32 + j2) * 256 + c0));
+            }
+            const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+            const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+            v[ki][0] = a.x;
+            v[ki][1] = a.y;
+            v[ki][2] = b.x;
+            v[ki][3] = b.y;
+        }
+    };
+    float cl[3][4];   // column 2 j3 - 1 (the previous output's right column)
+#pragma unroll
+    for (int ki = 0; ki < 3; ++ki)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) cl[ki][e] = 0.f;
+    __half* out = p.x4 + static_cast<size_t>(row) * 16 * 256 + c0;
 #pragma unroll 2
     for (int j3 = 0; j3 < 16; ++j3) {
-        float s = 0.f;
+        float cm[3][4], cr[3][4];
+        col(2 * j3, cm);
+        col(2 * j3 + 1, cr);
+        float s[4] = {0.f, 0.f, 0.f, 0.f};
         if (live) {
-            s = bias;
 #pragma unroll
-            for (int ki = 0; ki < 3; ++ki) {
-                const int t2 = 2 * t3 + ki - 1;
-                if (t2 < 0 || t2 >= F2) continue;
+            for (int e = 0; e < 4; ++e) {
+                s[e] = bias[e];
 #pragma unroll
-                for (int kj = 0; kj < 3; ++kj) {
-                    const int j2 = 2 * j3 + kj - 1;
-                    if (j2 < 0) continue;   // j2 <= 31 always
-                    s += w[ki * 3 + kj] * __half2float(x3[(static_cast<size_t>(t2) * 32 + j2) * 256 + c]);
+                for (int ki = 0; ki < 3; ++ki) {
+                    if (!rok[ki]) continue;
+                    if (j3 > 0) s[e] += w[ki * 3][e] * cl[ki][e];   // column 2 j3 - 1 exists
+                    s[e] += w[ki * 3 + 1][e] * cm[ki][e];
+                    s[e] += w[ki * 3 + 2][e] * cr[ki][e];
                 }
             }
         }
-        p.x4[(static_cast<size_t>(row) * 16 + j3) * 256 + c] = __float2half_rn(s);
+        __half2 h0 = __floats2half2_rn(s[0], s[1]), h1 = __floats2half2_rn(s[2], s[3]);
+        *reinterpret_cast<uint2*>(out + j3 * 256) =
+            make_uint2(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1));
+#pragma unroll
+        for (int ki = 0; ki < 3; ++ki)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) cl[ki][e] = cr[ki][e];
     }
 }
 
@@ -394,7 +441,7 @@ int launch_sub_conv0_dw1(const SubParams& p, int w0, int w1, cudaStream_t st) {
 
 int launch_sub_dw2(const SubParams& p, int r0, int r1, cudaStream_t st) {
     if (r1 <= r0) return 0;
-    k_sub_dw2<<<r1 - r0, 256, 0, st>>>(p, r0);
+    k_sub_dw2<<<(r1 - r0 + kDw2Rows - 1) / kDw2Rows, 64 * kDw2Rows, 0, st>>>(p, r0, r1);
     return check_launch("k_sub_dw2");
 }
 
