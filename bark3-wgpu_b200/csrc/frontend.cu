@@ -80,22 +80,42 @@ __global__ void __launch_bounds__(256) k_mel_frames(MelParams p, int f0, int f1)
         im[r] = mel_sample(x, len, p.lead, start + 2 * m + 1, __ldg(p.window + 2 * m + 1));
     }
     __syncwarp();
+    // radix-2 stages taken two at a time: the 4 points i0 + {0, h, 2h, 3h}
+    // of a group of 4h pass through stage lh (butterflies (i0, i1), (i2, i3))
+    // and stage lh + 1 ((i0, i2), (i1, i3)) in registers, which halves the
+    // shared-memory traffic; the arithmetic is that of the stages one by one
+    auto bfly = [](float& ar, float& ai, float& br, float& bi, float2 w) {
+        const float vr = br * w.x - bi * w.y;
+        const float vi = br * w.y + bi * w.x;
+        const float ur = ar, ui = ai;
+        ar = ur + vr;
+        ai = ui + vi;
+        br = ur - vr;
+        bi = ui - vi;
+    };
 #pragma unroll
-    for (int lh = 0; lh < 8; ++lh) {
-        const int half = 1 << lh;
+    for (int lh = 0; lh < 8; lh += 2) {
+        const int h = 1 << lh;
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const int b = lane + 32 * q;
-            const int k = b & (half - 1);
-            const int i0 = ((b - k) << 1) + k, i1 = i0 + half;
-            const float2 w = tw[k << (8 - lh)];  // W256^(k * 128 / half) = W512^(k * 256 / half)
-            const float vr = re[i1] * w.x - im[i1] * w.y;
-            const float vi = re[i1] * w.y + im[i1] * w.x;
-            const float ur = re[i0], ui = im[i0];
-            re[i0] = ur + vr;
-            im[i0] = ui + vi;
-            re[i1] = ur - vr;
-            im[i1] = ui - vi;
+        for (int q = 0; q < 2; ++q) {
+            const int b = lane + 32 * q;   // group-of-4 index, 0..63
+            const int k = b & (h - 1);
+            const int i0 = ((b - k) << 2) + k, i1 = i0 + h, i2 = i0 + 2 * h, i3 = i0 + 3 * h;
+            float r0 = re[i0], m0 = im[i0], r1 = re[i1], m1 = im[i1];
+            float r2 = re[i2], m2 = im[i2], r3 = re[i3], m3 = im[i3];
+            const float2 wa = tw[k << (8 - lh)];   // W256^(k * 128 / h) = W512^(k * 256 / h)
+            bfly(r0, m0, r1, m1, wa);
+            bfly(r2, m2, r3, m3, wa);
+            bfly(r0, m0, r2, m2, tw[k << (7 - lh)]);
+            bfly(r1, m1, r3, m3, tw[(k + h) << (7 - lh)]);
+            re[i0] = r0;
+            im[i0] = m0;
+            re[i1] = r1;
+            im[i1] = m1;
+            re[i2] = r2;
+            im[i2] = m2;
+            re[i3] = r3;
+            im[i3] = m3;
         }
         __syncwarp();
     }
