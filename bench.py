@@ -238,6 +238,15 @@ def make_weights(args, syn):
     return weights
 
 
+def host_threads() -> int:
+    """Every host core this process may run on (the reference's CPU path
+    runs on all of them, rayon's default)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
 def run_reference(args, rank, world):
     """--impl reference: the reference's CPU encoder path (restated in C) on
     the host cores, one utterance of the batch per step."""
@@ -246,6 +255,7 @@ def run_reference(args, rank, world):
     pkg = load_package()
     import bark3_b200.synthetic as syn
     oracle = load_oracle()
+    oracle.set_threads(host_threads())   # torchrun sets OMP_NUM_THREADS=1 for every rank
     secs, frames = batch_for_rank(args, 0, 1, pkg, syn)
     weights = make_weights(args, syn)
     one = make_cpu_pipeline(oracle, syn, pkg, weights, args.workload)
@@ -439,6 +449,7 @@ def main():
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         oracle = load_oracle()
+        oracle.set_threads(host_threads())
         v, n, a_s, used = cpu_baseline_sample(oracle, syn, pkg, weights, secs, frames, args.cpu_seconds, args.seed,
                                               args.workload)
         cpu = {"value": round(v, 3), "unit": "audio-s/s", "cores": oracle.threads(), "kind": "port",
