@@ -34,9 +34,11 @@
 //
 // The diagonal read: row i of the tile needs band column 127 - i + j for key
 // j, a window whose start moves by one column per row.  TMEM loads address
-// the same columns for all lanes of a warp, so each softmax thread parks its
-// lane's loaded band columns in a private shared-memory row and reads the 32
-// it needs back at its own offset.
+// the same columns for all lanes of a warp, so the rows' band columns are
+// parked in shared memory and each thread reads the 32 it needs back at its
+// own offset.  The two warps of a lane quarter share one parked row per query
+// (the 96 band columns the pair spans, 48 loaded and parked by each) and meet
+// on their mbarrier between parking and reading.
 #include <cuda.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
@@ -55,21 +57,21 @@ constexpr int kBK = 64;           // keys per block
 constexpr int kThreads = 320;     // warp 0 TMA, warp 1 MMA, warps 2..9 softmax
 constexpr int kSoftThreads = 256;
 constexpr int kRing = 256;        // R ring rows
-constexpr int kShStride = 66;     // floats per softmax thread's diagonal row: 64 band columns + 2 exchange
-                                  // slots; 8-byte stores and lane-shifted scalar reads are both conflict-free
+constexpr int kShRows = 128;      // one parked row per query, shared by the pair of warps
+constexpr int kShStride = 130;    // floats per row: 96 band columns + 2 x 2 exchange slots (+ pad); a stride
+                                  // of 2 mod 32 words keeps 8-byte stores and lane-shifted reads conflict-free
 
 // shared memory (offsets from a 1024-aligned base)
 constexpr uint32_t kQuOff = 0;                   // Qu: 2 dim-halves x (128 rows x 128 B)
 constexpr uint32_t kKOff = 32768;                // K: 2 stages x 2 halves x (64 rows x 128 B)
 constexpr uint32_t kVOff = kKOff + 32768;        // V: same
 constexpr uint32_t kROff = kVOff + 32768;        // R ring: 2 halves x (256 rows x 128 B)
-constexpr uint32_t kShOff = kROff + 65536;       // diagonal rows 256 x 65 f32 (Qv staging first)
-constexpr uint32_t kBarOff = kShOff + kSoftThreads * kShStride * 4;
+constexpr uint32_t kShOff = kROff + 65536;       // parked band rows 128 x 130 f32
+constexpr uint32_t kBarOff = kShOff + kShRows * kShStride * 4;
 constexpr uint32_t kBarBytes = 160;                   // 19 mbarriers + the TMEM address
 constexpr uint32_t kSmemMax = 232448;
 constexpr uint32_t kSmem = kSmemMax;
 constexpr uint32_t kAlignSlack = kSmemMax - kBarOff - kBarBytes;   // room to align the base to 1024 B
-static_assert(kSoftThreads * kShStride * 4 >= 32768, "Qv staging fits the diagonal rows");
 static_assert(kBarOff + kBarBytes + 256 <= kSmemMax, "shared memory budget");
 
 // TMEM columns
@@ -300,11 +302,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int q = warp & 3;
         const int hf = (warp - 2) >> 2;
         const int i = q * 32 + lane;                   // query row / TMEM lane
-        const int t = (warp - 2) * 32 + lane;          // diagonal row
-        const int tp = t ^ 128;                        // the pair partner's diagonal row
         const uint32_t lrow = static_cast<uint32_t>(q * 32) << 16;
-        float* sh = sSh + t * kShStride;
-        const float* shp = sSh + tp * kShStride;
+        float* sh = sSh + i * kShStride;               // this query's parked row (both warps of the pair)
+        float* xmine = sh + 96 + 2 * hf;               // exchange slots, by exchange parity
+        const float* xpeer = sh + 96 + 2 * (hf ^ 1);
         // Qv row i, dim half hf of an item, from global memory (rows past the
         // utterance read its last row: their results are never stored)
         auto load_qv = [&](const Item& it, uint32_t (&r)[32]) {
@@ -357,28 +358,34 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (handoff) store_qv(qn);
                 float s[32];
                 {
-                    // S columns [32 hf, 32 hf + 32) and band columns [96 - 32q + 32hf, +64): one wait
-                    uint32_t r0[32], g0r[32], g1r[32];
+                    // S columns [32 hf, 32 hf + 32); the pair's band window is columns
+                    // [96 - 32q, 192 - 32q), of which this warp loads [48 hf, 48 hf + 48)
+                    uint32_t r0[32], g0r[32], g1r[16];
                     tmem_ld_32x32b_x32(tmem + lrow + kTS + 64 * st + 32 * hf, r0);
-                    tmem_ld_32x32b_x32(tmem + lrow + kTG + 96 - 32 * q + 32 * hf, g0r);
-                    tmem_ld_32x32b_x32(tmem + lrow + kTG + 128 - 32 * q + 32 * hf, g1r);
+                    tmem_ld_32x32b_x32(tmem + lrow + kTG + 96 - 32 * q + 48 * hf, g0r);
+                    tmem_ld_32x32b_x16(tmem + lrow + kTG + 128 - 32 * q + 48 * hf, g1r);
                     tmem_wait_ld();
                     tc_fence_before();
                     __syncwarp();
                     if (lane == 0) mbar_arrive(smem_u32(g_free));
 #pragma unroll
                     for (int e = 0; e < 32; ++e) s[e] = __uint_as_float(r0[e]);
-                    // window columns 0..63 (0..62 are used) as 8-byte stores: with the
-                    // row stride of 66 words a half-warp's stores cover all 32 banks
+                    // window columns [48 hf, 48 hf + 48) as 8-byte stores: with the row
+                    // stride of 2 mod 32 words a half-warp's stores cover all 32 banks
+                    float* wp = sh + 48 * hf;
 #pragma unroll
-                    for (int e = 0; e < 32; e += 2) {
-                        *reinterpret_cast<uint2*>(sh + e) = make_uint2(g0r[e], g0r[e + 1]);
-                        *reinterpret_cast<uint2*>(sh + 32 + e) = make_uint2(g1r[e], g1r[e + 1]);
-                    }
+                    for (int e = 0; e < 32; e += 2) *reinterpret_cast<uint2*>(wp + e) = make_uint2(g0r[e], g0r[e + 1]);
+#pragma unroll
+                    for (int e = 0; e < 16; e += 2)
+                        *reinterpret_cast<uint2*>(wp + 32 + e) = make_uint2(g1r[e], g1r[e + 1]);
                 }
+                // the partner's half of the window is parked too
+                if (!(ok = pair_exchange(&xchg[q], lane, x & 1, 0x27))) break;
+                ++x;
                 // row i, key 32 hf + j: band column 127 - i + 32 hf + j = window column
-                // 31 - lane + j; across a warp the word index moves by 65 per lane: no conflicts
-                const float* dg = sh + 31 - lane;
+                // 32 hf + 31 - lane + j; across a warp the word index moves by 129 per
+                // lane: no conflicts
+                const float* dg = sh + 32 * hf + 31 - lane;
                 const int kvalid = it.T - kb * kBK - 32 * hf;
                 const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
 #pragma unroll
@@ -396,11 +403,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int j = 0; j < 32; ++j) mx[j & 3] = fmaxf(mx[j & 3], s[j]);
                 const float mloc = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
-                const int xs = 64 + (x & 1);   // exchange slot, by exchange parity
-                sh[xs] = mloc;
+                xmine[x & 1] = mloc;
                 if (!(ok = pair_exchange(&xchg[q], lane, x & 1, 0x2B))) break;
+                const float m_blk = fmaxf(mloc, xpeer[x & 1]);
                 ++x;
-                const float m_blk = fmaxf(mloc, shp[xs]);
                 const bool grow = m_blk > m_use + kRescale;
                 float corr = 1.f;
                 if (__any_sync(0xffffffffu, grow)) {
@@ -446,11 +452,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             // ── O / l -> f16 row, columns [64 hf, 64 hf + 64) ──
             if (ok && mbar_wait(smem_u32(o_final), n & 1, 0x2A)) {
                 tc_fence_after();
-                const int xs = 64 + (x & 1);
-                sh[xs] = l_half;
+                xmine[x & 1] = l_half;
                 const bool xok = pair_exchange(&xchg[q], lane, x & 1, 0x2C);
+                const float inv = 1.0f / (l_half + xpeer[x & 1]);
                 ++x;
-                const float inv = 1.0f / (l_half + shp[xs]);
                 const bool store = xok && it.q0 + i < it.T;
                 __half* dst = p.out + static_cast<size_t>(it.seg0 + it.q0 + i) * 1024 + it.head * 128 + 64 * hf;
                 uint32_t o0[32], o1[32];
