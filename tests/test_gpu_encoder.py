@@ -51,6 +51,36 @@ def test_bf16_layout_parity(syn, oracle, gpu_encoder_factory):
         assert e <= LAYER_TOL
 
 
+def test_bf16_layout_long_utterance(syn, oracle, gpu_encoder_factory):
+    """BASELINE config 2's length: 150 s of audio (T = 1875 encoder frames) in
+    the bf16 Pro layout, 15 query blocks per head and the f16-weight K1 path at
+    M = 1875."""
+    n_layers = 2
+    w = syn.encoder_weights(seed=2, n_layers=n_layers, layout="bf16")
+    enc = gpu_encoder_factory(w, n_layers)
+    ref = oracle.OracleEncoder(w, n_layers)
+    sub = syn.sub_features(np.random.default_rng(5), 1875)
+    for layers in (1, 2):
+        e = rel_err(enc.encode(sub, layers=layers), ref.encode(sub, layers=layers))
+        print(f"bf16 T=1875 layers={layers} err {e:.2e}")
+        assert e <= LAYER_TOL
+
+
+def test_long_and_short_utterances_batch_exactly(lut_model, syn):
+    """A varlen batch mixing a ten-minute utterance with tiny ones equals the
+    utterances encoded one by one, bit for bit (the persistent attention walks
+    items of every utterance in one launch)."""
+    w, enc, ref, n_layers = lut_model
+    rng = np.random.default_rng(19)
+    lens = [3, 7500, 1, 640, 129]
+    subs = [syn.sub_features(rng, t) for t in lens]
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    got = enc.encode_batch(np.concatenate(subs), cu)
+    assert np.isfinite(got).all()
+    for i, s in enumerate(subs):
+        assert np.array_equal(got[cu[i]:cu[i + 1]], enc.encode(s)), f"utterance {i} (T={lens[i]})"
+
+
 def test_batch_equals_single(lut_model, syn):
     """Varlen batching is exact: every kernel is row- or segment-local."""
     w, enc, ref, n_layers = lut_model
