@@ -56,6 +56,27 @@ def test_subsample_matches_oracle(fe_model, syn, oracle):
         assert e < 1e-2
 
 
+def test_long_audio_pooler(fe_model, syn, oracle, pkg):
+    """Ten minutes of audio beside a short clip, through the host-pointer path
+    (chunked upload, chunked front end): the pooler of each utterance against
+    the oracle pipeline (mel, subsampling, encoder) within the per-layer
+    tolerance; the 600 s utterance gives T = 7504 encoder frames."""
+    w, enc = fe_model
+    rng = np.random.default_rng(23)
+    waves = [syn.synth_audio(rng, 600.0), syn.synth_audio(rng, 2.0)]
+    pooler, roff = enc.encode_audio(waves)
+    fb = pkg.mel_filters()
+    oenc = oracle.OracleEncoder(w, 2)
+    for i, wv in enumerate(waves):
+        mel, nv = oracle.mel(np.concatenate([np.zeros(4000, np.float32), wv]), fb)
+        ref = oenc.encode(oracle.subsample(mel, nv, w))
+        g = pooler[roff[i]:roff[i + 1]]
+        assert g.shape == ref.shape
+        e = np.max(np.abs(g - ref)) / np.max(np.abs(ref))
+        print(f"utterance {i} ({len(wv) / 16000:.0f} s, T={g.shape[0]}): pooler err {e:.2e}")
+        assert e <= 2e-2
+
+
 def test_audio_to_tokens(fe_model, syn, oracle, pkg):
     """transcribe_samples end to end (pad, mel, subsampling, encoder, greedy
     TDT), stage by stage on identical inputs: the GPU pooler from audio
