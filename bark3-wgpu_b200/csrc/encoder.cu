@@ -196,6 +196,24 @@ struct b3_ctx {
     DevBuf io_in, io_out;   // device staging for host-pointer calls
     DevBuf scratch16;       // f16 copy of A for the single-linear entry points
     Plan plan;
+    uint64_t plan_gen = 0;  // bumped whenever a plan, the arena or the weights change
+    // A repeated small-batch encode (same rows, buffers and block count)
+    // replays a CUDA graph of its launches: the 24 blocks are ~350 launches,
+    // which at a few hundred rows cost more than the kernels.
+    struct EncGraph {
+        cudaGraphExec_t exec = nullptr;
+        const float* sub = nullptr;
+        float* out = nullptr;
+        int M = 0, layers = -1;
+        uint64_t gen = 0;
+        bool seen = false;     // the key ran eagerly once (first-call set-up done)
+        bool no_graph = false; // capture failed for this key: stay eager
+        void reset() {
+            if (exec) cudaGraphExecDestroy(exec);
+            exec = nullptr;
+            seen = no_graph = false;
+        }
+    } enc_graph;
     Prof prof;
     // greedy TDT decoder (optional: built when its tensors are loaded)
     struct Decoder {
@@ -231,6 +249,7 @@ struct b3_ctx {
         bool chunk_wait = false;    // chunk_ev holds this call's copies
     } fe;
     ~b3_ctx() {
+        enc_graph.reset();
         for (Linear* l : {&fe.pw1, &fe.pw2, &fe.sub_w_perm}) {
             l->w.release();
             l->lut16.release();
@@ -540,6 +559,7 @@ int make_plan(b3_ctx* c, const int32_t* cu, int n_utt) {
     const int M = cu[n_utt];
     std::vector<int32_t> key(cu, cu + n_utt + 1);
     if (key == c->plan.cu && c->mcap >= M && c->tcap >= tmax) return 0;
+    ++c->plan_gen;
     B3_TRY(ensure_arena(c, M));
     B3_TRY(ensure_pos(c, tmax));
     const int bq = attention_tc_block_rows();
@@ -688,6 +708,53 @@ int encode_device(b3_ctx* c, const float* sub, int M, int layers, float* out) {
     return 0;
 }
 
+// Rows up to which a repeated encode replays a graph (above it the kernels
+// outweigh the launches by far).
+constexpr int kGraphRows = 8192;
+
+// encode_device, replayed from a CUDA graph when the same call (rows, input
+// and output buffers, block count, plan) comes again.  The first call of a
+// key runs eagerly (it also does the kernels' one-time set-up), the second
+// captures and replays, later ones replay.  Off while profiling (the
+// per-launch events are host-side bookkeeping) and for large batches.
+int encode_rows(b3_ctx* c, const float* sub, int M, int layers, float* out) {
+    auto& G = c->enc_graph;
+    if (c->prof.on || M > kGraphRows) return encode_device(c, sub, M, layers, out);
+    const bool same = G.sub == sub && G.out == out && G.M == M && G.layers == layers && G.gen == c->plan_gen;
+    if (!same) {
+        G.reset();
+        G.sub = sub;
+        G.out = out;
+        G.M = M;
+        G.layers = layers;
+        G.gen = c->plan_gen;
+    }
+    if (G.exec) {
+        B3_CUDA(cudaGraphLaunch(G.exec, c->stream));
+        return 0;
+    }
+    if (!G.seen || G.no_graph) {
+        G.seen = true;
+        return encode_device(c, sub, M, layers, out);
+    }
+    cudaGraph_t graph = nullptr;
+    B3_CUDA(cudaStreamBeginCapture(c->stream, cudaStreamCaptureModeThreadLocal));
+    const int rc = encode_device(c, sub, M, layers, out);
+    cudaError_t e = cudaStreamEndCapture(c->stream, &graph);
+    if (rc == 0 && e == cudaSuccess) e = cudaGraphInstantiate(&G.exec, graph, 0);
+    if (graph) cudaGraphDestroy(graph);
+    if (rc != 0 || e != cudaSuccess) {
+        // nothing was launched while capturing: run the call eagerly, and keep
+        // this key eager from now on
+        cudaGetLastError();
+        G.exec = nullptr;
+        G.no_graph = true;
+        return encode_device(c, sub, M, layers, out);
+    }
+    B3_CUDA(cudaGraphLaunch(G.exec, c->stream));
+    return 0;
+}
+
 int encode_any(b3_ctx* c, const float* sub, const int32_t* cu, int n_utt, int layers, float* out,
                unsigned flags) {
     B3_TRY(check_finalized(c));
@@ -696,13 +763,13 @@ int encode_any(b3_ctx* c, const float* sub, const int32_t* cu, int n_utt, int la
     B3_TRY(make_plan(c, cu, n_utt));
     const int M = c->plan.M;
     const int out_cols = layers >= c->n_layers ? kProj : kHidden;
-    if (flags & B3_DEVICE_PTRS) return encode_device(c, sub, M, layers, out);
+    if (flags & B3_DEVICE_PTRS) return encode_rows(c, sub, M, layers, out);
     const size_t in_bytes = static_cast<size_t>(M) * kSubIn * 4;
     const size_t out_bytes = static_cast<size_t>(M) * out_cols * 4;
     B3_TRY(c->io_in.ensure(in_bytes));
     B3_TRY(c->io_out.ensure(out_bytes));
     B3_CUDA(cudaMemcpyAsync(c->io_in.p, sub, in_bytes, cudaMemcpyHostToDevice, c->stream));
-    B3_TRY(encode_device(c, c->io_in.as<float>(), M, layers, c->io_out.as<float>()));
+    B3_TRY(encode_rows(c, c->io_in.as<float>(), M, layers, c->io_out.as<float>()));
     B3_CUDA(cudaMemcpyAsync(out, c->io_out.p, out_bytes, cudaMemcpyDeviceToHost, c->stream));
     return sync_and_check(c);
 }
@@ -1530,6 +1597,7 @@ int b3_finalize(b3_ctx* ctx, int n_layers) {
     B3_TRY(build_frontend(ctx));
     ctx->n_layers = n_layers;
     ctx->finalized = true;
+    ++ctx->plan_gen;
     ctx->staged.clear();
     return 0;
 }
