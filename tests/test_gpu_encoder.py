@@ -81,6 +81,30 @@ def test_long_and_short_utterances_batch_exactly(lut_model, syn):
         assert np.array_equal(got[cu[i]:cu[i + 1]], enc.encode(s)), f"utterance {i} (T={lens[i]})"
 
 
+def test_repeated_encode_replays_identically(lut_model, syn):
+    """A small batch encoded again with the same buffers is replayed from a
+    CUDA graph (the first call runs eagerly, the second captures, later calls
+    replay): every call gives the eager result bit for bit, on the device-
+    pointer and the host-pointer paths."""
+    import torch
+
+    w, enc, ref, n_layers = lut_model
+    rng = np.random.default_rng(29)
+    lens = [120, 57]
+    host = np.concatenate([syn.sub_features(rng, t) for t in lens])
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    dev = torch.from_numpy(host).cuda()
+    out = torch.empty(int(cu[-1]), 640, device="cuda")
+    runs = []
+    for _ in range(4):
+        enc.encode_batch(dev, cu, out=out)
+        enc.sync()
+        runs.append(out.cpu().numpy().copy())
+    host_runs = [enc.encode_batch(host, cu) for _ in range(4)]
+    for r in runs[1:] + host_runs:
+        assert np.array_equal(r, runs[0])
+
+
 def test_batch_equals_single(lut_model, syn):
     """Varlen batching is exact: every kernel is row- or segment-local."""
     w, enc, ref, n_layers = lut_model
