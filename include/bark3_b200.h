@@ -113,7 +113,10 @@ int b3_encode(b3_ctx* ctx, const float* sub, int t, int layers, float* out, unsi
 /* Varlen batch: utterance i occupies rows cu_seqlens[i] .. cu_seqlens[i+1]
  * of sub [total][4096] and pooler [total][640].  Attention and the depthwise
  * conv stay inside each utterance; linears run over the concatenation.
- * cu_seqlens is always host memory (n_utt + 1 entries, starting at 0). */
+ * cu_seqlens is always host memory (n_utt + 1 entries, starting at 0).
+ * Both encode calls, at up to 8192 rows, replay a CUDA graph of their launches
+ * when the same call (rows, buffers, block count) is repeated: the second such
+ * call captures it on the context's stream, later ones replay it. */
 int b3_encode_batch(b3_ctx* ctx, const float* sub, const int32_t* cu_seqlens, int n_utt,
                     float* pooler, unsigned flags);
 
