@@ -103,6 +103,13 @@ def test_repeated_encode_replays_identically(lut_model, syn):
     host_runs = [enc.encode_batch(host, cu) for _ in range(4)]
     for r in runs[1:] + host_runs:
         assert np.array_equal(r, runs[0])
+    # another shape in between (a new plan) invalidates the replay; coming
+    # back to the first shape rebuilds it and still gives the same rows
+    other = syn.sub_features(rng, 33)
+    one = [enc.encode(other) for _ in range(3)]
+    assert all(np.array_equal(x, one[0]) for x in one)
+    for _ in range(3):
+        assert np.array_equal(enc.encode_batch(host, cu), runs[0])
 
 
 def test_batch_equals_single(lut_model, syn):
