@@ -75,6 +75,7 @@ def lib() -> ctypes.CDLL:
         "b3_destroy": (None, [c_p]),
         "b3_sync": (c_i, [c_p]),
         "b3_stream": (c_p, [c_p]),
+        "b3_set_wait_limit": (c_i, [c_p, ctypes.c_int64]),
         "b3_load_tensor": (c_i, [c_p, ctypes.c_char_p, c_i, c_p, c_i, c_p]),
         "b3_load_lowbit": (c_i, [c_p, ctypes.c_char_p, c_p, c_p, c_i, c_i]),
         "b3_load_lowbit_levels": (c_i, [c_p, ctypes.c_char_p, c_p, c_p, c_i, c_i, c_i]),

@@ -503,26 +503,16 @@ int check_launch(const char* what) {
 
 int launch_attention_tc(const AttnParams& p, int M, int n_work, cudaStream_t st) {
     if (n_work <= 0) return 0;
-    static bool attr_done = false;
-    if (!attr_done) {
-        cudaError_t e = cudaFuncSetAttribute(k2_relpos_attention_tc, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(kSmem));
-        if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(k2 tc)", e);
-        attr_done = true;
-    }
+    static PerDeviceOnce attr;
+    int rc0 = set_smem_limit_once(attr, k2_relpos_attention_tc, static_cast<int>(kSmem), "cudaFuncSetAttribute(k2 tc)");
+    if (rc0) return rc0;
     CUtensorMap tq, tkv, tr;
     int rc = make_map_2d(&tq, p.qkv, kMapF16, 4096, static_cast<uint64_t>(M), 8192, 64, kBQ, true);
     if (!rc) rc = make_map_2d(&tkv, p.qkv, kMapF16, 4096, static_cast<uint64_t>(M), 8192, 64, kBK, true);
     if (!rc) rc = make_map_2d(&tr, p.R, kMapF16, 1024, static_cast<uint64_t>(p.r_rows), 2048, 64, 64, true);
     if (rc) return rc;
     // persistent: one CTA per SM walks the (work entry, head) items
-    static int sms = 0;
-    if (!sms) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-        if (sms <= 0) sms = 148;
-    }
+    const int sms = device_sms();
     const int n_items = n_work * 8;
     k2_relpos_attention_tc<<<n_items < sms ? n_items : sms, kThreads, kSmem, st>>>(tq, tkv, tr, p, n_items);
     return check_launch("k2_relpos_attention_tc");

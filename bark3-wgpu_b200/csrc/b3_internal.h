@@ -5,9 +5,16 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+#include <mutex>
+
 #include "../../include/bark3_b200.h"
 
 namespace b3 {
+
+// Default wall-time bound of a device-side wait (2 s: orders of magnitude
+// above any legitimate wait in these kernels).
+constexpr unsigned long long kDefaultWaitNs = 2000000000ull;
 
 // ── errors: every ABI call returns 0 or a negative B3_E* code and leaves a
 // message in the calling thread's last-error slot.
@@ -15,8 +22,45 @@ int set_error(int code, const char* fmt, ...);
 int set_cuda_error(const char* what, cudaError_t e);
 void clear_error();
 
-// Reads and clears the device error word (bounded waits that ran out).
-int check_device_error(cudaStream_t st);
+// Runs a set-up step once per device (the device current at the call) for
+// one call site.  Kernel attributes such as the dynamic shared-memory limit
+// belong to a device, so a process that drives several GPUs (one host thread
+// per context) must set them on each; concurrent first calls from several
+// threads run the step once per device.  Returns 0 or the step's error.
+class PerDeviceOnce {
+public:
+    template <typename F>
+    int run(F&& step) {
+        int dev = 0;
+        const cudaError_t e = cudaGetDevice(&dev);
+        if (e != cudaSuccess) return set_cuda_error("cudaGetDevice", e);
+        if (dev < 0 || dev >= 64) return set_error(B3_EINVAL, "device ordinal %d is beyond 63", dev);
+        const uint64_t bit = 1ull << dev;
+        if (done_.load(std::memory_order_acquire) & bit) return 0;
+        std::lock_guard<std::mutex> lock(mu_);
+        if (done_.load(std::memory_order_relaxed) & bit) return 0;
+        const int rc = step();
+        if (rc == 0) done_.fetch_or(bit, std::memory_order_release);
+        return rc;
+    }
+
+private:
+    std::atomic<uint64_t> done_{0};
+    std::mutex mu_;
+};
+
+// cudaFuncSetAttribute(kernel, MaxDynamicSharedMemorySize, bytes) once per
+// device for the given call site's PerDeviceOnce.
+template <typename K>
+int set_smem_limit_once(PerDeviceOnce& once, K kernel, int bytes, const char* what) {
+    return once.run([&]() {
+        const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+        return e == cudaSuccess ? 0 : set_cuda_error(what, e);
+    });
+}
+
+// Streaming multiprocessors of the current device (cached per device).
+int device_sms();
 
 // ── K1 GEMM ──
 enum GemmEpi {

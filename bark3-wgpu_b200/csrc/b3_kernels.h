@@ -92,6 +92,7 @@ struct DecPersist {
     unsigned int* sync;  // [0] barrier arrivals, [1] abort flag,
                          // [4..5] active-row counts of even / odd steps (8 words, host-zeroed)
     int max_steps;       // lock steps at most (every row is bounded on its own as well)
+    unsigned long long grid_wait_ns;   // wall-time bound of each grid-barrier wait
 };
 constexpr int kDecHead = 0, kDecLstm0 = 1, kDecLstm1 = 2, kDecProj = 3;
 
@@ -102,6 +103,8 @@ int dec_launch_persistent(const DecMaps& maps, const DecPersist& p, int grid, cu
 void dec_plan_persistent(int B, int npad, int grid, int bn[4], int ks[4]);
 int dec_launch_init(const DecState& s, cudaStream_t st);
 int dec_launch_split(const float* src, __half* hi, __half* lo, int64_t n, cudaStream_t st);
+// Reads and clears the decoder's device error word (stream-ordered).
+int decoder_take_dev_error(cudaStream_t st, unsigned int* out);
 
 // Mel front end (frontend.cu).
 struct MelParams {

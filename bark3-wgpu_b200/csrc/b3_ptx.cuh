@@ -162,11 +162,13 @@ __device__ __forceinline__ unsigned int ld_acquire_gpu(const unsigned int* p) {
 // launch).  sync[0] counts arrivals over the kernel's life (each arrival is a
 // fire-and-forget reduction, so no CTA waits for its own atomic), sync[1] is
 // the abort flag.  `target` is this CTA's running total (nblocks more per
-// barrier).  Bounded like mbar_wait: on time-out it records the error, raises
-// the abort flag and returns false.  Call with all threads of the CTA;
+// barrier).  Bounded like mbar_wait, by `limit_ns` of wall time (a kernel
+// parameter, so a host can shorten it): on time-out it records the error,
+// raises the abort flag and returns false.  Call with all threads of the CTA;
 // `ok_smem` is a shared int that carries thread 0's verdict to the others.
 __device__ __forceinline__ bool grid_barrier(unsigned int* sync, unsigned int nblocks, unsigned int& target,
-                                             bool fail, int* ok_smem, unsigned int site) {
+                                             bool fail, int* ok_smem, unsigned int site,
+                                             unsigned long long limit_ns) {
     __syncthreads();
     if (threadIdx.x == 0) {
         target += nblocks;
@@ -187,7 +189,7 @@ __device__ __forceinline__ bool grid_barrier(unsigned int* sync, unsigned int nb
             const unsigned long long t = globaltimer();
             if (t0 == 0) {
                 t0 = t;
-            } else if (t - t0 > kWaitLimitNs) {
+            } else if (t - t0 > limit_ns) {
                 record_error(B3_ERR_TIMEOUT | site);
                 atomicExch(sync + 1, 1u);
                 ok = 0;

@@ -55,6 +55,17 @@ int set_cuda_error(const char* what, cudaError_t e) {
 
 void clear_error() { g_last_error[0] = 0; }
 
+int device_sms() {
+    static std::atomic<int> cached[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+    int n = cached[dev].load(std::memory_order_relaxed);
+    if (n > 0) return n;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cached[dev].store(n, std::memory_order_relaxed);
+    return n;
+}
+
 }  // namespace b3
 
 using namespace b3;
@@ -215,6 +226,8 @@ struct b3_ctx {
         }
     } enc_graph;
     Prof prof;
+    // wall-time bound of the decoder's grid-barrier waits (b3_set_wait_limit)
+    uint64_t grid_wait_ns = kDefaultWaitNs;
     // greedy TDT decoder (optional: built when its tensors are loaded)
     struct Decoder {
         bool present = false;
@@ -686,12 +699,18 @@ int check_finalized(b3_ctx* c) {
     return 0;
 }
 
+// Waits for the context stream, then reads and clears the device error words
+// of every module with bounded waits (K1 GEMM, attention, decoder): any set
+// bit means a wait ran out and the call's results are not valid.
 int sync_and_check(b3_ctx* c) {
     B3_CUDA(cudaStreamSynchronize(c->stream));
-    unsigned int flag = 0, aflag = 0;
+    unsigned int flag = 0, aflag = 0, dflag = 0;
     B3_TRY(gemm_take_dev_error(c->stream, &flag));
     B3_TRY(attention_take_dev_error(c->stream, &aflag));
-    if (flag | aflag) return set_error(B3_ETIMEOUT, "device wait ran out (code 0x%x)", flag | aflag);
+    B3_TRY(decoder_take_dev_error(c->stream, &dflag));
+    if (flag | aflag | dflag)
+        return set_error(B3_ETIMEOUT, "device wait ran out (gemm 0x%x, attention 0x%x, decoder 0x%x)", flag, aflag,
+                         dflag);
     return 0;
 }
 
@@ -986,6 +1005,7 @@ int decode_device(b3_ctx* c, const float* pooler, const int32_t* cu, int n_utt, 
     }
     p.sync = D.sync.as<unsigned int>();
     p.max_steps = tmax * 14 + 64;
+    p.grid_wait_ns = c->grid_wait_ns;
     B3_TRY(dec_launch_init(s, c->stream));
     return dec_launch_persistent(maps, p, grid, c->stream);
 }
@@ -1470,6 +1490,12 @@ int b3_sync(b3_ctx* ctx) {
 }
 
 void* b3_stream(b3_ctx* ctx) { return ctx ? static_cast<void*>(ctx->stream) : nullptr; }
+
+int b3_set_wait_limit(b3_ctx* ctx, int64_t grid_barrier_ns) {
+    if (!ctx) return set_error(B3_EINVAL, "null context");
+    ctx->grid_wait_ns = grid_barrier_ns > 0 ? static_cast<uint64_t>(grid_barrier_ns) : kDefaultWaitNs;
+    return 0;
+}
 
 int b3_load_tensor(b3_ctx* ctx, const char* name, int dtype, const int64_t* shape, int ndim,
                    const void* data) {

@@ -449,12 +449,9 @@ int launch_mel(const MelParams& p, int f0, int f1, int u0, int u1, cudaStream_t 
 int launch_sub_conv0_dw1(const SubParams& p, int w0, int w1, cudaStream_t st) {
     const int n_work = w1 - w0;
     if (n_work <= 0) return 0;
-    static bool attr_done = false;
-    if (!attr_done) {
-        cudaError_t e = cudaFuncSetAttribute(k_sub_conv0_dw1, cudaFuncAttributeMaxDynamicSharedMemorySize, kSubSmem);
-        if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(k_sub_conv0_dw1)", e);
-        attr_done = true;
-    }
+    static PerDeviceOnce attr;
+    const int rc = set_smem_limit_once(attr, k_sub_conv0_dw1, kSubSmem, "cudaFuncSetAttribute(k_sub_conv0_dw1)");
+    if (rc) return rc;
     k_sub_conv0_dw1<<<n_work, 256, kSubSmem, st>>>(p, w0);
     return check_launch("k_sub_conv0_dw1");
 }

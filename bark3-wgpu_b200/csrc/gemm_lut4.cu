@@ -722,8 +722,6 @@ int make_out_map(CUtensorMap* tc, const GemmParams& p, int ksplit) {
     return make_map_2d(tc, p.out_f16, kMapF16, p.N, p.M, static_cast<uint64_t>(p.ldo) * 2, 64, 32, true);
 }
 
-int g_num_sms = 0;
-
 template <bool LUT, int EPI>
 int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t st);
 
@@ -731,19 +729,10 @@ template <int BN, int SUB, bool LUT, int EPI>
 int launch_one(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t st) {
     using Cfg = GemmCfg<BN, SUB, LUT>;
     auto kern = k1_gemm<BN, SUB, LUT, EPI>;
-    static bool attr_done = false;  // per template instance
-    if (!attr_done) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(Cfg::kSmemBytes));
-        if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(k1_gemm)", e);
-        attr_done = true;
-    }
-    if (!g_num_sms) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-        if (g_num_sms <= 0) g_num_sms = 148;
-    }
+    static PerDeviceOnce smem_once;  // per template instance
+    const int rc0 = set_smem_limit_once(smem_once, kern, static_cast<int>(Cfg::kSmemBytes), "cudaFuncSetAttribute(k1_gemm)");
+    if (rc0) return rc0;
+    const int g_num_sms = device_sms();
     // output map: 32-row boxes of 128-byte rows (64-byte rows for the GLU
     // output of a 64-column tile), matching the epilogue's slab layout
     CUtensorMap tc;
@@ -789,17 +778,15 @@ template <bool LUT, int EPI>
 int launch_pair(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t st) {
     using Cfg = pair::Cfg<LUT>;
     auto kern = k1_gemm_pair<LUT, EPI>;
-    static bool attr_done = false;  // per template instance
-    if (!attr_done) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             static_cast<int>(Cfg::kSmemBytes));
-        if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(k1_gemm_pair)", e);
-        attr_done = true;
-    }
+    static PerDeviceOnce smem_once;  // per template instance
+    const int rc0 = set_smem_limit_once(smem_once, kern, static_cast<int>(Cfg::kSmemBytes),
+                                        "cudaFuncSetAttribute(k1_gemm_pair)");
+    if (rc0) return rc0;
     CUtensorMap tc;
     int rc = make_out_map<EPI>(&tc, p, 1);
     if (rc) return rc;
     const int tiles = (p.N / pair::kBN) * ((p.M + 2 * kBM - 1) / (2 * kBM));
+    const int g_num_sms = device_sms();
     const int pairs = tiles < g_num_sms / 2 ? tiles : g_num_sms / 2;
     kern<<<2 * pairs, kThreads, Cfg::kSmemBytes, st>>>(ta, tb, tc, p);
     cudaError_t e = cudaGetLastError();
@@ -886,12 +873,7 @@ int gemm_launch(const GemmOp& op, cudaStream_t st) {
     const bool big = p.tiles ? p.tiles == 2 : big_tiles >= 148;
     if (p.ksplit > 1 && op.epi != EPI_F32) return set_error(B3_EINVAL, "GEMM split-K needs the f32 epilogue");
     // CTA pairs with 256 x 256 tiles once they fill every SM pair once
-    if (!g_num_sms) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-        if (g_num_sms <= 0) g_num_sms = 148;
-    }
+    const int g_num_sms = device_sms();
     const long pair_tiles = static_cast<long>(p.N / 256) * ((p.M + 255) / 256);
     const bool use_pair = p.tiles ? p.tiles == 3 : (p.N % 256 == 0 && p.ksplit <= 1 && pair_tiles >= g_num_sms / 2);
     if (use_pair) {

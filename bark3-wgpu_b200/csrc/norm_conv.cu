@@ -271,19 +271,10 @@ int launch_layernorm(const float* x, int rows, const float* w1, const float* b1,
 int launch_dwconv(const __half* src, const int2* seg, int rows, const float* dw_t, const float* bn_a,
                   const float* bn_b, __half* dst, cudaStream_t st) {
     if (rows <= 0) return 0;
-    static bool attr_done = false;
-    if (!attr_done) {
-        cudaError_t e = cudaFuncSetAttribute(k3_dwconv_bn_silu, cudaFuncAttributeMaxDynamicSharedMemorySize, kDwSmem);
-        if (e != cudaSuccess) return set_cuda_error("cudaFuncSetAttribute(k3)", e);
-        attr_done = true;
-    }
-    static int n_sms = 0;
-    if (!n_sms) {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&n_sms, cudaDevAttrMultiProcessorCount, dev);
-        if (n_sms <= 0) n_sms = 148;
-    }
+    static PerDeviceOnce attr;
+    const int rc0 = set_smem_limit_once(attr, k3_dwconv_bn_silu, kDwSmem, "cudaFuncSetAttribute(k3)");
+    if (rc0) return rc0;
+    const int n_sms = device_sms();
     const int tiles = (rows + kDwRows - 1) / kDwRows;
     k3_dwconv_bn_silu<<<tiles < n_sms ? tiles : n_sms, kDwThreads, kDwSmem, st>>>(src, seg, rows, dw_t, bn_a, bn_b, dst);
     cudaError_t e = cudaGetLastError();

@@ -640,7 +640,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
         const bool first = step < 0;
         // A: joint head (not on the first pass) + layer-0 recurrent GEMM
         bool fail = __syncthreads_or(!p_gemm_phase(maps, p, r, first ? -1 : kDecHead, kDecLstm0, pit, mit, acc));
-        if (!grid_barrier(sync, nb, target, fail, ok_smem, 0x65)) break;
+        if (!grid_barrier(sync, nb, target, fail, ok_smem, 0x65, p.grid_wait_ns)) break;
         // B: argmax + update, layer-0 cell
         if (threadIdx.x == 0 && blockIdx.x == 0 && !first) sync[4 + ((step + 1) & 1)] = 0;
         for (int b = blockIdx.x * 2 + h; b < s.B; b += row_stride) {
@@ -648,10 +648,10 @@ __global__ void __launch_bounds__(kPThreads, 1)
             half_sync(h);
         }
         fence_async_global();
-        if (!grid_barrier(sync, nb, target, false, ok_smem, 0x66)) break;
+        if (!grid_barrier(sync, nb, target, false, ok_smem, 0x66, p.grid_wait_ns)) break;
         // C: layer-1 GEMM
         fail = __syncthreads_or(!p_gemm_phase(maps, p, r, kDecLstm1, -1, pit, mit, acc));
-        if (!grid_barrier(sync, nb, target, fail, ok_smem, 0x67)) break;
+        if (!grid_barrier(sync, nb, target, fail, ok_smem, 0x67, p.grid_wait_ns)) break;
         // every row finished at this step's argmax (the count is final since
         // the barrier after B; read here so that phase C starts at once)
         if (!first) {
@@ -662,14 +662,14 @@ __global__ void __launch_bounds__(kPThreads, 1)
         // D: layer-1 cell
         for (int b = blockIdx.x * 2 + h; b < s.B; b += row_stride) p_row_d(s, b, t);
         fence_async_global();
-        if (!grid_barrier(sync, nb, target, false, ok_smem, 0x68)) break;
+        if (!grid_barrier(sync, nb, target, false, ok_smem, 0x68, p.grid_wait_ns)) break;
         // E: projector GEMM
         fail = __syncthreads_or(!p_gemm_phase(maps, p, r, kDecProj, -1, pit, mit, acc));
-        if (!grid_barrier(sync, nb, target, fail, ok_smem, 0x69)) break;
+        if (!grid_barrier(sync, nb, target, fail, ok_smem, 0x69, p.grid_wait_ns)) break;
         // F: joint input
         for (int b = blockIdx.x * 2 + h; b < s.B; b += row_stride) p_row_f(s, b, t);
         fence_async_global();
-        if (!grid_barrier(sync, nb, target, false, ok_smem, 0x6A)) break;
+        if (!grid_barrier(sync, nb, target, false, ok_smem, 0x6A, p.grid_wait_ns)) break;
     }
     tc_fence_before();
     __syncthreads();
@@ -710,16 +710,18 @@ int dec_launch_init(const DecState& s, cudaStream_t st) {
 }
 
 int dec_persistent_grid(int device) {
-    static int cached = -1, cached_dev = -1;
-    if (cached >= 0 && cached_dev == device) return cached;
-    if (cudaFuncSetAttribute(k_dec_persist, cudaFuncAttributeMaxDynamicSharedMemorySize, kPSmem) != cudaSuccess)
-        return 0;
-    int per_sm = 0, sms = 0;
+    // per device: the shared-memory attribute and the occupancy check
+    static std::atomic<int> cached[64];
+    static PerDeviceOnce attr;
+    if (device < 0 || device >= 64) return 0;
+    const int known = cached[device].load(std::memory_order_acquire);
+    if (known > 0) return known;
+    if (set_smem_limit_once(attr, k_dec_persist, kPSmem, "cudaFuncSetAttribute(k_dec_persist)")) return 0;
+    int per_sm = 0;
     if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_dec_persist, kPThreads, kPSmem) != cudaSuccess) return 0;
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
-    cached = per_sm >= 1 ? sms : 0;   // one CTA per SM (TMEM and the ring are sized for it)
-    cached_dev = device;
-    return cached;
+    const int grid = per_sm >= 1 ? device_sms() : 0;   // one CTA per SM (TMEM and the ring are sized for it)
+    cached[device].store(grid, std::memory_order_release);
+    return grid;
 }
 
 // Tile widths and split-K parts for the persistent decoder.  The GEMMs are
@@ -788,6 +790,19 @@ int dec_launch_persistent(const DecMaps& maps, const DecPersist& p, int grid, cu
     cfg.numAttrs = 1;
     const cudaError_t e = cudaLaunchKernelEx(&cfg, k_dec_persist, maps, p);
     return e == cudaSuccess ? 0 : set_cuda_error("k_dec_persist", e);
+}
+
+// Reads and clears this translation unit's device error word (stream-ordered):
+// the decoder's bounded waits (grid barriers and its GEMM phases) write it.
+int decoder_take_dev_error(cudaStream_t st, unsigned int* out) {
+    static const unsigned int zero = 0;
+    cudaError_t e = cudaMemcpyFromSymbolAsync(out, g_b3_dev_error, sizeof(unsigned int), 0,
+                                              cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    if (e == cudaSuccess)
+        e = cudaMemcpyToSymbolAsync(g_b3_dev_error, &zero, sizeof(unsigned int), 0, cudaMemcpyHostToDevice, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    return e == cudaSuccess ? 0 : set_cuda_error("reading the decoder device error word", e);
 }
 
 int dec_launch_split(const float* src, __half* hi, __half* lo, int64_t n, cudaStream_t st) {

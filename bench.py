@@ -1,22 +1,25 @@
 #!/usr/bin/env python3
 """Benchmark of the B200 encoder hot path (bark3-wgpu's Conformer encoder).
 
-Default workload (BASELINE config 5's batch, encoder stage): per rank a batch
-of 256 seeded utterances with lengths uniform in 10-60 s, encoded by the
-24-block 4-bit (LUT) Conformer encoder: sub linear -> 24 blocks -> projector.
-The encoder input is the conv-subsampled feature matrix (T_i, 4096) per
-utterance, synthetic (seeded ReLU'd normals; the mel / subsampling front end
-and the TDT decoder are outside this hot path).  One step = one encode of the
-whole batch.  Metric: RTFx = audio seconds encoded per second.
+Default workload: BASELINE config 5 as written -- ONE batch of 256 seeded
+utterances, lengths uniform in 10-60 s, transcribed from 16 kHz audio (mel,
+conv subsampling, the 24-block 4-bit LUT encoder, greedy TDT).  Under
+torchrun the batch is sharded across the ranks by longest-processing-time
+over the encoder cost (b3_shard_lpt), one process per GPU, no collective on
+the data path ("scaling": "strong").  --scaling weak gives every rank its own
+256-utterance batch instead.  One step = the whole batch once.  Metric: RTFx =
+audio seconds transcribed per second, whole job.
 
   value  device-resident inputs (HBM), CUDA events on the library's stream,
-         max over ranks; the batch (1.8 GB of f32 input) is far larger than
-         L2, so no flush is needed between steps.
-  e2e    the same through the host-pointer C ABI call: pinned host input
-         copied in and the pooler copied out inside every timed step.
+         max over ranks; the per-step working set (GBs of activations) is far
+         larger than L2, so no flush is needed between steps.
+  e2e    the same through the host-pointer C ABI call: pinned host audio
+         copied in and the token buffers copied out inside every timed step.
 
---impl reference times the reference's CPU encoder (the C restatement of
-src/cpu/*, all host cores) on utterances of the same batch.
+--impl reference times the reference's CPU pipeline (the C restatement of
+src/mel.rs, src/sub.rs, src/cpu/* and src/tdt.rs in oracle/, all host cores)
+on utterances of the same batch.  It loads only the oracle library, never
+the product's.
 """
 from __future__ import annotations
 
@@ -50,8 +53,11 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--utterances", type=int, default=256)
-    ap.add_argument("--strong", action="store_true",
-                    help="shard one batch of --utterances across ranks (LPT) instead of one batch per rank")
+    ap.add_argument("--scaling", default="strong", choices=["strong", "weak"],
+                    help="strong: one batch of --utterances sharded across the ranks (LPT; BASELINE config 5); "
+                         "weak: every rank its own batch of --utterances")
+    ap.add_argument("--ref-utterances", type=int, default=16,
+                    help="--impl reference: utterances of the batch its steps cycle through")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--seed", type=int, default=5)
@@ -127,16 +133,54 @@ def peaks():
     return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
 
 
+def job_batch(args, world, syn):
+    """(seconds, frames) of every utterance of the whole job, in batch order;
+    pure Python (loads no library)."""
+    import bark3_b200 as pkg
+
+    if args.scaling == "strong":
+        secs = [float(x) for x in syn.batch_lengths(args.seed, args.utterances)]
+    else:
+        secs = [float(x) for r in range(world) for x in syn.batch_lengths(args.seed + 1000 * r, args.utterances)]
+    return secs, [pkg.frames_for_seconds(x) for x in secs]
+
+
 def batch_for_rank(args, rank, world, pkg, syn):
-    """(seconds per utterance, frames per utterance) of this rank's batch."""
-    if args.strong:
-        secs = syn.batch_lengths(args.seed, args.utterances)
-        frames = [pkg.frames_for_seconds(s) for s in secs]
+    """(seconds per utterance, frames per utterance) of this rank's share."""
+    if args.scaling == "strong":
+        secs, frames = job_batch(args, 1, syn)
+        if world == 1:
+            return secs, frames
         rank_of = pkg.shard_lpt(frames, world)
         mine = [i for i in range(len(frames)) if rank_of[i] == rank]
-        return [float(secs[i]) for i in mine], [frames[i] for i in mine]
+        return [secs[i] for i in mine], [frames[i] for i in mine]
     secs = syn.batch_lengths(args.seed + 1000 * rank, args.utterances)
     return [float(s) for s in secs], [pkg.frames_for_seconds(s) for s in secs]
+
+
+def job_config(args, world, syn):
+    """The `config` object of the JSON line: the whole job's workload (both
+    arms print the same one)."""
+    secs, frames = job_batch(args, world, syn)
+    decode = args.workload in ("audio", "transcribe")
+    return {
+        "workload": {"audio": "config 5: batched transcription, 16 kHz audio -> tokens (mel, conv subsampling, "
+                              "24-block 4-bit LUT encoder, greedy TDT)",
+                     "transcribe": "config-5 batch from subsampled features: 4-bit encoder + greedy TDT",
+                     "encoder": "config-5 batch through the 24-block 4-bit LUT encoder"}[args.workload],
+        "utterances": len(secs), "audio_s": round(sum(secs), 1), "frames": int(sum(frames)),
+        "lengths_s": "U(10,60) seeded", "seed": args.seed, "layers": N_LAYERS,
+        "d_model": 1024, "heads": 8, "ffn": 4096, "conv_kernel": 9,
+        "weights": "random-init 4-bit codes + 16-entry f16 LUT per row (levels N(0,0.02) sorted, row-centred)",
+        "input": ("synthetic audio: white noise U(-0.1,0.1) + 3 sines of amplitude 0.1, 16 kHz f32"
+                  if args.workload == "audio" else "synthetic (T,4096) subsampled features, f32"),
+        "decoder": (f"2-layer LSTM 640, joint 640, vocab {VOCAB - 1}+blank, durations 0..4, random-init"
+                    if decode else None),
+        "l2": "per-step working set (%.2f GB of encoder activations per GPU) > L2, no flush"
+              % (sum(frames) / world * 4096 * 2 * 3 / 1e9),
+        "parallelism": (f"one batch LPT-sharded over {world} GPU(s), no collective" if args.scaling == "strong"
+                        else f"one batch per GPU x{world}, no collective"),
+    }
 
 
 class ClockSampler:
@@ -194,7 +238,7 @@ def make_cpu_pipeline(oracle, syn, pkg, weights, workload):
     (or the pooler) out, every stage on all host cores."""
     enc = oracle.OracleEncoder(weights, N_LAYERS)
     dec = oracle.OracleTdt(weights) if workload in ("audio", "transcribe") else None
-    fb = pkg.mel_filters() if workload == "audio" else None
+    fb = oracle.mel_filters() if workload == "audio" else None
 
     def run(x):
         if workload == "audio":
@@ -248,19 +292,21 @@ def host_threads() -> int:
 
 
 def run_reference(args, rank, world):
-    """--impl reference: the reference's CPU encoder path (restated in C) on
-    the host cores, one utterance of the batch per step."""
+    """--impl reference: the reference's CPU pipeline (restated in C, all host
+    cores) on the utterances of the same batch, one utterance per step,
+    cycling through the first --ref-utterances of the batch.  Only rank 0
+    runs; the oracle library is the only native code it loads."""
     if rank != 0:
         return
-    pkg = load_package()
+    pkg = load_package()          # the package's pure-Python helpers; its CUDA library is never loaded here
     import bark3_b200.synthetic as syn
     oracle = load_oracle()
     oracle.set_threads(host_threads())   # torchrun sets OMP_NUM_THREADS=1 for every rank
-    secs, frames = batch_for_rank(args, 0, 1, pkg, syn)
+    secs, frames = job_batch(args, world, syn)
     weights = make_weights(args, syn)
     one = make_cpu_pipeline(oracle, syn, pkg, weights, args.workload)
     rng = np.random.default_rng(args.seed)
-    k = max(1, min(len(frames), 4))
+    k = max(1, min(len(frames), args.ref_utterances))
     subs = [cpu_input(syn, rng, args.workload, secs[i], frames[i]) for i in range(k)]
 
     for w in range(args.warmup):
@@ -274,19 +320,21 @@ def run_reference(args, rank, world):
         audio += secs[i]
     v = audio / wall
     cores = oracle.threads()
+    sample = (f"{args.steps} utterances, cycling the first {len(subs)} of the batch "
+              f"({sum(secs[:len(subs)]):.1f} audio-s, {min(secs[:len(subs)]):.1f}-{max(secs[:len(subs)]):.1f} s), "
+              f"one per step, {args.workload} pipeline on {cores} host threads")
     line = {
         "impl": "reference", "metric": METRIC, "value": round(v, 3), "unit": "audio-s/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1000 * wall / args.steps, 3),
-        "higher_is_better": True, "scaling": "weak" if not args.strong else "strong", "vs_baseline": None,
+        "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
         "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "reference CPU path (" + {"audio": "src/mel.rs + src/sub.rs + src/cpu/* encoder + "
-                   "src/tdt.rs greedy TDT", "transcribe": "src/cpu/* encoder + src/tdt.rs greedy TDT",
-                   "encoder": "src/cpu/* encoder"}[args.workload]
-                   + ", restated in C, AVX2/F16C FMA), one utterance of the config-5 batch per step",
-                   "utterances_sampled": len(subs),
-                   "frames": frames[: len(subs)], "layers": N_LAYERS, "weights": "random-init 4-bit LUT"},
+        "config": job_config(args, world, syn),
+        "reference_path": {"audio": "src/mel.rs + src/sub.rs + src/cpu/* encoder + src/tdt.rs greedy TDT",
+                           "transcribe": "src/cpu/* encoder + src/tdt.rs greedy TDT",
+                           "encoder": "src/cpu/* encoder"}[args.workload]
+                          + ", restated in C (oracle/), AVX2/F16C FMA",
         "cpu_baseline": {"value": round(v, 3), "unit": "audio-s/s", "cores": cores, "kind": "port",
-                         "sample": f"{args.steps} utterances (cycling {frames[:len(subs)]} frames), {args.workload}"},
+                         "sample": sample},
         "e2e": {"value": round(v, 3), "unit": "audio-s/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -414,12 +462,23 @@ def main():
     L.b3_profile(enc.ctx, 0)
     launches = int(sum(p["launches"] for p in prof.values()))
     ms_max = max_over_ranks(ms)
-    value = world * audio * args.steps / (ms_max / 1000.0) if not args.strong else None
-    if args.strong:
-        tot = torch.tensor([audio], dtype=torch.float64, device="cuda")
-        if world > 1:
-            dist.all_reduce(tot)
-        value = float(tot.item()) * args.steps / (ms_max / 1000.0)
+    # whole-job audio: every rank's share (strong: the one batch; weak: N batches)
+    tot = torch.tensor([audio], dtype=torch.float64, device="cuda")
+    if world > 1:
+        dist.all_reduce(tot)
+    job_audio = float(tot.item())
+    value = job_audio * args.steps / (ms_max / 1000.0)
+    # per-rank attribution: step time, clocks and the per-kind split of every rank
+    mine = {"rank": rank, "utterances": n_utt, "frames": M, "audio_s": round(audio, 1),
+            "longest_frames": int(max(frames)) if frames else 0,
+            "ms_per_step": round(ms / args.steps, 3), "sm_mhz": clocks.get("sm_mhz"),
+            "reasons": clocks.get("reasons"),
+            "kernels_ms_per_step": {k: round(v["ms"] / args.steps, 3) for k, v in prof.items() if v["launches"]}}
+    ranks = [None] * world
+    if world > 1:
+        dist.all_gather_object(ranks, mine)
+    else:
+        ranks = [mine]
 
     # ── e2e: host buffers through the host-pointer ABI call ──
     barrier()
@@ -434,10 +493,7 @@ def main():
     e1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
-    if args.strong:
-        e2e_value = value * ms_max / e2e_ms
-    else:
-        e2e_value = world * audio * args.steps / (e2e_ms / 1000.0)
+    e2e_value = job_audio * args.steps / (e2e_ms / 1000.0)
 
     pk, pk_kind = peaks()
     g = prof["gemm_lut4"]
@@ -460,22 +516,9 @@ def main():
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "audio-s/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3),
-            "higher_is_better": True, "scaling": "strong" if args.strong else "weak", "vs_baseline": None,
+            "higher_is_better": True, "scaling": args.scaling, "vs_baseline": None,
             "dtype": "f16", "data": "synthetic",
-            "config": {"workload": {"audio": "config 5: batched transcription, 16 kHz audio -> tokens (mel, conv "
-                                             "subsampling, 24-block 4-bit LUT encoder, greedy TDT)",
-                                    "transcribe": "config-5 batch from subsampled features: 4-bit encoder + greedy TDT",
-                                    "encoder": "config-5 batch through the 24-block 4-bit LUT encoder"}[args.workload],
-                       "utterances_per_rank": len(frames), "audio_s_per_rank": round(audio, 1),
-                       "frames_per_rank": M, "lengths_s": "U(10,60) seeded", "layers": N_LAYERS,
-                       "d_model": 1024, "heads": 8, "ffn": 4096, "conv_kernel": 9,
-                       "weights": "random-init 4-bit codes + 16-entry f16 LUT per row",
-                       "input": ("synthetic audio: white noise U(-0.1,0.1) + 3 sines of amplitude 0.1, "
-                                 "16 kHz f32" if audio_in else "synthetic (T,4096) subsampled features, f32"),
-                       "decoder": (f"2-layer LSTM 640, joint 640, vocab {VOCAB - 1}+blank, durations 0..4, "
-                                   "random-init" if decode else None),
-                       "l2": "per-step working set (%.2f GB of encoder activations) > L2, no flush" % (M * 4096 * 2 * 3 / 1e9),
-                       "parallelism": f"utterance-sharded x{world}, no collective"},
+            "config": job_config(args, world, syn),
             "roofline": {"kernel": "k1_gemm (LUT4, tcgen05)", "bound": "tensor",
                          "achieved": round(achieved, 1) if achieved else None,
                          "peak": peak, "unit": "TFLOP/s",
@@ -489,9 +532,11 @@ def main():
                             "launches": v["launches"]} for k, v in prof.items() if v["launches"]},
             "gpu_launches": launches,
             "clocks": clocks,
+            "ranks": ranks,
             "e2e": {"value": round(e2e_value, 2), "unit": "audio-s/s",
                     "h2d_bytes_per_step": int(host_in.numel() * 4),
-                    "d2h_bytes_per_step": int(n_utt * (MAX_TOKENS * 12 + 4)) if decode else int(M * 640 * 4)},
+                    "d2h_bytes_per_step": int(n_utt * (MAX_TOKENS * 12 + 4)) if decode else int(M * 640 * 4),
+                    "bytes_are": "rank 0's per step"},
             "cpu_baseline": cpu,
         }
         print(json.dumps(line), flush=True)

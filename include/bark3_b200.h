@@ -68,6 +68,16 @@ int b3_sync(b3_ctx* ctx);
  * B3_DEVICE_PTRS calls. */
 void* b3_stream(b3_ctx* ctx);
 
+/* Wall-time bound, in nanoseconds, of each grid-barrier wait of the greedy
+ * decoder's persistent kernel (default 2 s; grid_barrier_ns <= 0 restores
+ * it).  A wait that runs out raises the kernel's abort flag, every CTA leaves
+ * at its next barrier with its own copies and MMAs complete, and the call
+ * returns B3_ETIMEOUT; the context stays usable.  This is the device-side
+ * counterpart of the reference GPU decoder's exit code and step guard
+ * (src/tdt_gpu.rs:62-70, src/tdt.rs:422-424); a short bound lets a test make
+ * the wait run out without faulting anything. */
+int b3_set_wait_limit(b3_ctx* ctx, int64_t grid_barrier_ns);
+
 /* ───────────────────────── weight loading ─────────────────────────
  * Tensors are pushed by the reference checkpoint's names, the way
  * Encoder::load_with pulls them from a WeightSource (src/weights.rs:22-36,

@@ -814,9 +814,11 @@ static void layer_forward(const OrLayer* L, float* x, Scratch* s, const PackW* p
 
 /* `CpuEncoder::encode` (src/cpu/mod.rs:156-189).  Returns the (t, 640)
  * pooler when layers >= n_layers, else the last block's pre-norm residual
- * (t, 1024).  `out` must hold the matching size. */
-int or_encode(void* enc, const float* sub, int t, int layers, float* out) {
-    OrEncoder* e = (OrEncoder*)enc;
+ * (t, 1024).  `out` must hold the matching size.  When `dump` is given and
+ * every block runs, it receives the pre-norm_out residual after each block
+ * (n_layers x t x 1024 floats) from the same single pass: block l's entry
+ * equals what a call with layers = l + 1 returns. */
+static int encode_impl(OrEncoder* e, const float* sub, int t, int layers, float* out, float* dump) {
     if (t <= 0) return -1;
     Scratch s;
     scratch_init(&s, t);
@@ -832,6 +834,7 @@ int or_encode(void* enc, const float* sub, int t, int layers, float* out) {
     int upto = layers < e->n_layers ? layers : e->n_layers;
     for (int i = 0; i < upto; i++) {
         layer_forward(&e->layers[i], x, &s, &pos);
+        if (dump) memcpy(dump + (size_t)i * t * HIDDEN, x, (size_t)t * HIDDEN * 4);
         if (i + 1 < upto || upto == e->n_layers) memcpy(x, s.normed, (size_t)t * HIDDEN * 4);
     }
     if (upto == e->n_layers) {
@@ -844,6 +847,17 @@ int or_encode(void* enc, const float* sub, int t, int layers, float* out) {
     packw_free(&pos);
     scratch_free(&s);
     return 0;
+}
+
+int or_encode(void* enc, const float* sub, int t, int layers, float* out) {
+    return encode_impl((OrEncoder*)enc, sub, t, layers, out, NULL);
+}
+
+/* Every block's pre-norm_out residual (dump: n_layers x t x 1024) and the
+ * pooler (out: t x 640) in one pass over all blocks. */
+int or_encode_layers(void* enc, const float* sub, int t, float* dump, float* out) {
+    OrEncoder* e = (OrEncoder*)enc;
+    return encode_impl(e, sub, t, e->n_layers, out, dump);
 }
 
 /* Attention + conv sections of one block in isolation:
@@ -1081,34 +1095,46 @@ static void project(const OrTdt* d, const float* x, float* out) {
     for (int r = 0; r < DEC_H; r++) out[r] = d->proj_b[r] + dot16(d->proj_w + (size_t)r * DEC_H, x, DEC_H);
 }
 
-/* joint (src/tdt.rs:217-290): first maximum wins on ties. */
-static void joint(const OrTdt* d, const float* enc, const float* dec, uint32_t* tok, uint32_t* dur) {
+/* joint (src/tdt.rs:217-290): first maximum wins on ties.  When `gap` is
+ * given it receives the decision margins of this step: gap[0] = best token
+ * score - runner-up token score, gap[1] = the same over the durations. */
+static void joint(const OrTdt* d, const float* enc, const float* dec, uint32_t* tok, uint32_t* dur, float* gap) {
     float s[DEC_H];
     for (int i = 0; i < DEC_H; i++) {
         float v = enc[i] + dec[i];
         s[i] = v > 0.0f ? v : 0.0f;
     }
-    float bt = -INFINITY, bd = -INFINITY;
+    float bt = -INFINITY, bd = -INFINITY, st = -INFINITY, sd = -INFINITY;
     uint32_t it = 0, id = (uint32_t)d->vocab;
     int rows = d->vocab + N_DUR;
     for (int r = 0; r < rows; r++) {
         float score = d->head_b[r] + dot16(d->head_w + (size_t)r * DEC_H, s, DEC_H);
         if (r < d->vocab) {
-            if (score > bt) { bt = score; it = (uint32_t)r; }
+            if (score > bt) { st = bt; bt = score; it = (uint32_t)r; }
+            else if (score > st) st = score;
         } else if (score > bd) {
+            sd = bd;
             bd = score;
             id = (uint32_t)r;
+        } else if (score > sd) {
+            sd = score;
         }
     }
     *tok = it;
     *dur = id - (uint32_t)d->vocab;
+    if (gap) {
+        gap[0] = bt - st;
+        gap[1] = bd - sd;
+    }
 }
 
 /* Greedy decode of one utterance (decode_rayon, src/tdt.rs:416-467).  out
  * receives (id, frame, dur) triples; returns the token count (capped at
- * max_tokens; the loop still runs to the end). */
-int or_tdt_decode(const void* p, const float* pooler, int t_len, uint32_t* out, int max_tokens) {
-    const OrTdt* d = (const OrTdt*)p;
+ * max_tokens; the loop still runs to the end).  When `gaps` is given, step s
+ * (s < max_gaps) writes its two decision margins to gaps[2s], gaps[2s+1] and
+ * *n_steps receives the number of steps taken. */
+static int tdt_decode_impl(const OrTdt* d, const float* pooler, int t_len, uint32_t* out, int max_tokens,
+                           float* gaps, long max_gaps, long* n_steps) {
     const uint32_t blank = (uint32_t)d->vocab - 1;
     float h[2][DEC_H] = {{0}}, c[2][DEC_H] = {{0}}, dec[DEC_H];
     lstm_step(d, d->embed + (size_t)blank * DEC_H, h, c);
@@ -1120,7 +1146,8 @@ int or_tdt_decode(const void* p, const float* pooler, int t_len, uint32_t* out, 
         if (frame >= t_len) break;
         if (++guard > max_steps) break;
         uint32_t tok, dur;
-        joint(d, pooler + (size_t)frame * DEC_H, dec, &tok, &dur);
+        float* g = (gaps && guard <= max_gaps) ? gaps + 2 * (guard - 1) : NULL;
+        joint(d, pooler + (size_t)frame * DEC_H, dec, &tok, &dur, g);
         if (tok == blank) {
             frame += dur > 0 ? (int)dur : 1;
         } else {
@@ -1135,7 +1162,20 @@ int or_tdt_decode(const void* p, const float* pooler, int t_len, uint32_t* out, 
             frame += (int)dur;
         }
     }
+    if (n_steps) *n_steps = guard > max_steps ? max_steps : guard;
     return n;
+}
+
+int or_tdt_decode(const void* p, const float* pooler, int t_len, uint32_t* out, int max_tokens) {
+    return tdt_decode_impl((const OrTdt*)p, pooler, t_len, out, max_tokens, NULL, 0, NULL);
+}
+
+/* The same decode, also recording each step's token and duration margins
+ * (test statistics: how far every greedy decision is from a tie).  Returns
+ * the token count; *n_steps receives the step count. */
+int or_tdt_decode_margins(const void* p, const float* pooler, int t_len, uint32_t* out, int max_tokens,
+                          float* gaps, long max_gaps, long* n_steps) {
+    return tdt_decode_impl((const OrTdt*)p, pooler, t_len, out, max_tokens, gaps, max_gaps, n_steps);
 }
 
 /* Decodes n_utt utterances of a varlen pooler [total][640] (cu offsets), one

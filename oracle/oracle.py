@@ -57,11 +57,13 @@ def lib() -> ctypes.CDLL:
             "or_encoder_set_layer": (_I, [_P, _I] + [_P] * 20),
             "or_encoder_free": (None, [_P]),
             "or_encode": (_I, [_P, _P, _I, _I, _P]),
+            "or_encode_layers": (_I, [_P, _P, _I, _P, _P]),
             "or_attn_conv": (_I, [_P, _I, _P, _I]),
             "or_attention_core": (_I, [_P, _P, _P, _P, _P, _I, _P]),
             "or_tdt_new": (_P, [_I] + [_P] * 9),
             "or_tdt_free": (None, [_P]),
             "or_tdt_decode": (_I, [_P, _P, _I, _P, _I]),
+            "or_tdt_decode_margins": (_I, [_P, _P, _I, _P, _I, _P, ctypes.c_long, _P]),
             "or_tdt_decode_batch": (None, [_P, _P, _P, _I, _P, _P, _I]),
             "or_mel": (_I, [_P, ctypes.c_int64, _P, _P, _P]),
             "or_subsample": (_I, [_P, _I, _I] + [_P] * 11),
@@ -169,6 +171,44 @@ def pos_embed(t: int) -> np.ndarray:
     return out
 
 
+def mel_filters(n_mels: int = 128, n_fft: int = 512, sr: int = 16000) -> np.ndarray:
+    """The (128, 257) slaney mel filterbank the reference bundles as
+    data/mel_filters.f32 and hands to `MelFrontend::new` (src/mel.rs:10-40),
+    restated from Slaney's Auditory Toolbox construction (as published in
+    librosa.filters.mel with htk=False, norm="slaney"): a mel scale linear
+    below 1 kHz (200/3 Hz per mel) and logarithmic above it (27 mels per
+    factor 6.4), n_mels + 2 equally spaced mel points between 0 Hz and sr/2,
+    triangular filters over the linearly spaced FFT bin frequencies, each
+    scaled by 2 / (its upper edge - its lower edge) so it has unit area.
+    Computed in float64 and rounded once to float32.  Pure numpy: loads no
+    shared library."""
+    f_sp = 200.0 / 3.0
+    min_log_hz = 1000.0
+    min_log_mel = min_log_hz / f_sp
+    logstep = np.log(6.4) / 27.0
+
+    def hz_to_mel(f):
+        f = np.asarray(f, dtype=np.float64)
+        m = f / f_sp
+        return np.where(f >= min_log_hz, min_log_mel + np.log(np.maximum(f, 1e-300) / min_log_hz) / logstep, m)
+
+    def mel_to_hz(m):
+        m = np.asarray(m, dtype=np.float64)
+        return np.where(m >= min_log_mel, min_log_hz * np.exp(logstep * (m - min_log_mel)), f_sp * m)
+
+    bins = np.linspace(0.0, sr / 2.0, 1 + n_fft // 2)
+    edges = mel_to_hz(np.linspace(hz_to_mel(0.0), hz_to_mel(sr / 2.0), n_mels + 2))
+    width = np.diff(edges)
+    dist = edges[:, None] - bins[None, :]
+    fb = np.zeros((n_mels, len(bins)), dtype=np.float64)
+    for i in range(n_mels):
+        rise = -dist[i] / width[i]
+        fall = dist[i + 2] / width[i + 1]
+        fb[i] = np.maximum(0.0, np.minimum(rise, fall))
+    fb *= (2.0 / (edges[2 : n_mels + 2] - edges[:n_mels]))[:, None]
+    return fb.astype(np.float32)
+
+
 def mel(wave: np.ndarray, filters: np.ndarray):
     """MelFrontend::compute restated: padded wave -> ((frames, 128), n_valid)."""
     wave = f32(wave)
@@ -257,6 +297,17 @@ class OracleEncoder:
         assert lib().or_encode(self.h, _p(sub), t, layers, _p(out)) == 0
         return out
 
+    def encode_layers(self, sub: np.ndarray):
+        """One pass over every block: (per-block pre-norm_out residuals
+        [n_layers, t, 1024], pooler [t, 640]); entry l equals
+        encode(sub, layers=l + 1)."""
+        sub = f32(sub)
+        t = sub.shape[0]
+        dump = np.empty((self.n_layers, t, 1024), dtype=np.float32)
+        out = np.empty((t, 640), dtype=np.float32)
+        assert lib().or_encode_layers(self.h, _p(sub), t, _p(dump), _p(out)) == 0
+        return dump, out
+
     def attn_conv(self, layer: int, x: np.ndarray) -> np.ndarray:
         x = f32(x).copy()
         assert lib().or_attn_conv(self.h, layer, _p(x), x.shape[0]) == 0
@@ -301,6 +352,20 @@ class OracleTdt:
         out = np.zeros((max_tokens, 3), dtype=np.uint32)
         n = lib().or_tdt_decode(self.h, _p(pooler), pooler.shape[0], _p(out), max_tokens)
         return out[: min(n, max_tokens)]
+
+    def decode_margins(self, pooler: np.ndarray, max_tokens: int = 1 << 16):
+        """decode() plus every step's decision margins: (tokens, gaps [steps, 2])
+        with gaps[:, 0] = best - runner-up token score and gaps[:, 1] the same
+        over the five durations."""
+        pooler = f32(pooler)
+        t = pooler.shape[0]
+        cap = t * 14 + 64
+        out = np.zeros((max_tokens, 3), dtype=np.uint32)
+        gaps = np.zeros((cap, 2), dtype=np.float32)
+        steps = ctypes.c_long()
+        n = lib().or_tdt_decode_margins(self.h, _p(pooler), t, _p(out), max_tokens, _p(gaps), cap,
+                                        ctypes.byref(steps))
+        return out[: min(n, max_tokens)], gaps[: min(steps.value, cap)]
 
     def decode_batch(self, pooler: np.ndarray, cu, max_tokens: int = 4096) -> list:
         pooler = f32(pooler)

@@ -56,3 +56,17 @@ def rel_err(got, ref):
     got = np.asarray(got, dtype=np.float64)
     ref = np.asarray(ref, dtype=np.float64)
     return float(np.max(np.abs(got - ref)) / max(np.max(np.abs(ref)), 1e-30))
+
+
+def centred_err(got, ref):
+    """Frame-centred normwise error: max |(got - mean frame of got) - (ref -
+    mean frame of ref)| / max |ref - mean frame of ref|, the mean frame being
+    the per-column mean over rows (frames).  Measures the part of a
+    (frames, channels) result that differs between frames on its own scale."""
+    import numpy as np
+
+    got = np.asarray(got, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    g = got - got.mean(axis=0, keepdims=True)
+    r = ref - ref.mean(axis=0, keepdims=True)
+    return float(np.max(np.abs(g - r)) / max(np.max(np.abs(r)), 1e-30))

@@ -38,6 +38,37 @@ def dec_model(syn, oracle, pkg):
     enc.close()
 
 
+def test_grid_barrier_timeout_is_reported_and_context_recovers(dec_model, pkg):
+    """The persistent decoder's grid-barrier waits are bounded in wall time
+    (the device-side counterpart of the reference GPU decoder's exit code,
+    src/tdt_gpu.rs:62-70).  With the bound cut to 1 ns a CTA that reaches a
+    barrier before the others gives up: it raises the kernel's abort flag,
+    every CTA leaves at its next barrier with its own copies and MMAs
+    complete, and the call returns B3_ETIMEOUT naming the decoder.  Nothing
+    faults: the failing call cleared the device error words (b3_sync then
+    returns 0), and with the default bound restored the same decode on the
+    same context gives the same tokens bit for bit."""
+    w, enc = dec_model
+    L = pkg.lib()
+    rng = np.random.default_rng(71)
+    lens = [300, 120, 41, 7]
+    pooler = rng.normal(0, 1, size=(sum(lens), 640)).astype(np.float32)
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    ref = enc.decode_batch(pooler, cu)
+    pkg.check(L.b3_set_wait_limit(enc.ctx, 1))
+    try:
+        with pytest.raises(pkg.B3Error) as err:
+            enc.decode_batch(pooler, cu)
+    finally:
+        pkg.check(L.b3_set_wait_limit(enc.ctx, 0))
+    assert err.value.code == pkg.B3_ETIMEOUT
+    assert "decoder 0x10" in str(err.value)
+    enc.sync()
+    again = enc.decode_batch(pooler, cu)
+    assert len(again) == len(ref)
+    assert all(np.array_equal(a, b) for a, b in zip(again, ref))
+
+
 def test_decoder_matches_oracle(dec_model, syn, oracle):
     w, enc = dec_model
     rng = np.random.default_rng(5)

@@ -274,3 +274,40 @@ def test_golden_fixtures(oracle, syn):
     assert set(fixtures.files) == set(current)
     for name in fixtures.files:
         np.testing.assert_allclose(current[name], fixtures[name], rtol=1e-6, atol=1e-7, err_msg=name)
+
+
+def test_encode_layers_matches_truncated_encodes(oracle, syn):
+    """The one-pass per-block dump equals encode(layers=l + 1) for every
+    block, bit for bit, and its pooler equals the full-depth encode."""
+    n = 3
+    w = syn.encoder_weights(seed=41, n_layers=n, layout="lut4")
+    enc = oracle.OracleEncoder(w, n)
+    sub = syn.sub_features(np.random.default_rng(41), 37)
+    dump, pool = enc.encode_layers(sub)
+    for l in range(n - 1):
+        assert np.array_equal(dump[l], enc.encode(sub, layers=l + 1))
+    assert np.array_equal(pool, enc.encode(sub))
+
+
+def test_decode_margins_same_tokens(oracle, syn):
+    """decode_margins takes the same greedy path as decode and reports one
+    non-negative (token, duration) margin pair per step."""
+    w = syn.decoder_weights(seed=42, vocab=1025)
+    dec = oracle.OracleTdt(w)
+    pooler = np.random.default_rng(42).normal(size=(120, 640)).astype(np.float32)
+    toks, gaps = dec.decode_margins(pooler)
+    assert np.array_equal(toks, dec.decode(pooler))
+    assert len(gaps) >= len(toks) and (gaps >= 0).all()
+
+
+def test_centred_levels_are_zero_mean(syn):
+    """The encoder model's 4-bit rows are centred (each row's 16 levels sum
+    to ~0 before f16 rounding); BASELINE config 1's linear keeps uncentred
+    sorted N(0, 0.02) levels."""
+    rng = np.random.default_rng(43)
+    _, lut = syn.make_lut4(rng, 64, 32, centre=True)
+    lv = lut.view(np.float16).astype(np.float64)
+    assert np.all(np.abs(lv.mean(axis=1)) < 1e-4)
+    assert np.all(np.diff(lv, axis=1) >= 0)
+    _, lut1 = syn.make_lut4(rng, 64, 32)
+    assert np.abs(lut1.view(np.float16).astype(np.float64).mean(axis=1)).max() > 1e-3
