@@ -56,6 +56,13 @@ def parse():
     ap.add_argument("--scaling", default="strong", choices=["strong", "weak"],
                     help="strong: one batch of --utterances sharded across the ranks (LPT; BASELINE config 5); "
                          "weak: every rank its own batch of --utterances")
+    ap.add_argument("--seconds", type=float, default=0.0,
+                    help="every utterance this many seconds long instead of U(10, 60) (e.g. --utterances 1 "
+                         "--seconds 30: BASELINE config 2's single 30 s clip)")
+    ap.add_argument("--shard", default="",
+                    help="R:N -- on one GPU, time the share rank R of an N-GPU strong-scaling job would get "
+                         "(diagnostic; the line says so)")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the K1 M-sweep recorded in the N=1 line")
     ap.add_argument("--ref-utterances", type=int, default=16,
                     help="--impl reference: utterances of the batch its steps cycle through")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="budget of the CPU-baseline sample")
@@ -68,24 +75,25 @@ def parse():
     return ap.parse_args()
 
 
-def run_linear_sweep(args):
-    """BASELINE config 1 (M=1875, K=1024, N=4096, f32 activations, bias) and the
-    M >= 2048 sweep of the north-star GEMM target, through b3_linear_lut4 with
-    device pointers.  One JSON line per shape; the GEMM kernel is timed alone
-    (the f32 -> f16 conversion of A is a separate, separately timed kernel)."""
+SWEEP_SHAPES = [(1875, 4096, 1024), (2048, 4096, 1024), (4096, 4096, 1024), (8192, 4096, 1024),
+                (16384, 4096, 1024), (8192, 1024, 4096), (8192, 3072, 1024), (110894, 4096, 1024)]
+
+
+def k1_sweep(pkg, syn, enc, shapes, warmup, steps, seed):
+    """BASELINE config 1 (M=1875, K=1024, N=4096, f32 activations, bias) and
+    the M >= 2048 shapes of the north-star GEMM target, through
+    b3_linear_lut4 with device pointers (config 1's uncentred level tables).
+    The K1 launch is timed alone with CUDA events on the library's stream
+    (the f32 -> f16 conversion of A is a separate, separately timed kernel);
+    TFLOP/s against the burst bf16 peak (a kernel timed in isolation)."""
     import ctypes
 
     import torch
 
-    pkg = load_package()
-    import bark3_b200.synthetic as syn
-
-    enc = pkg.Encoder(0)
     L = pkg.lib()
     pk, pk_kind = peaks()
-    rng = np.random.default_rng(args.seed)
-    shapes = [(1875, 4096, 1024), (2048, 4096, 1024), (4096, 4096, 1024), (8192, 4096, 1024),
-              (16384, 4096, 1024), (8192, 1024, 4096), (8192, 3072, 1024), (110894, 4096, 1024)]
+    rng = np.random.default_rng(seed)
+    rows = []
     for m, n, k in shapes:
         codes, lut16 = syn.make_lut4(rng, n, k)
         a = torch.randn(m, k, device="cuda")
@@ -94,27 +102,39 @@ def run_linear_sweep(args):
         tl = torch.from_numpy(lut16.view(np.int16)).cuda()
         out = torch.empty(m, n, device="cuda")
         torch.cuda.synchronize()
-        for _ in range(args.warmup):
+        for _ in range(warmup):
             enc.linear_lut4(a, tc, tl, bias, out=out)
         enc.sync()
         L.b3_profile(enc.ctx, 1)
-        for _ in range(args.steps):
+        for _ in range(steps):
             enc.linear_lut4(a, tc, tl, bias, out=out)
         vals = {}
         for kind in (pkg_kind("gemm_lut4"), pkg_kind("convert")):
             t, f, b, nl = ctypes.c_double(), ctypes.c_double(), ctypes.c_double(), ctypes.c_int64()
-            pkg.check(L.b3_profile_read(enc.ctx, kind, ctypes.byref(t), ctypes.byref(f), ctypes.byref(b), ctypes.byref(nl)))
+            pkg.check(L.b3_profile_read(enc.ctx, kind, ctypes.byref(t), ctypes.byref(f), ctypes.byref(b),
+                                        ctypes.byref(nl)))
             vals[kind] = (t.value, f.value, b.value, nl.value)
         L.b3_profile(enc.ctx, 0)
         t, f, b, nl = vals[pkg_kind("gemm_lut4")]
         tflops = f / (t / 1000.0) / 1e12
         peak = pk.get("bf16_tflops")
-        print(json.dumps({"workload": "k1 LUT4 linear", "m": m, "n": n, "k": k, "us_per_launch": round(1000 * t / nl, 2),
-                          "TFLOP/s": round(tflops, 1), "frac_of_burst_peak": round(tflops / peak, 4),
-                          "peak": f"bf16_tflops (burst) of {pk_kind}", "alg_GB/s": round(b / t / 1e6, 1),
-                          "convert_us": round(1000 * vals[pkg_kind('convert')][0] / max(1, vals[pkg_kind('convert')][3]), 2)}),
-              flush=True)
+        ct = vals[pkg_kind("convert")]
+        rows.append({"m": m, "n": n, "k": k, "us_per_launch": round(1000 * t / nl, 2),
+                     "TFLOP/s": round(tflops, 1), "frac_of_burst_peak": round(tflops / peak, 4),
+                     "alg_GB/s": round(b / t / 1e6, 1), "convert_us": round(1000 * ct[0] / max(1, ct[3]), 2)})
         del a, out, tc, tl
+    return rows, f"bf16_tflops (burst) of {pk_kind}"
+
+
+def run_linear_sweep(args):
+    """--workload linear: one JSON line per K1 shape (see k1_sweep)."""
+    pkg = load_package()
+    import bark3_b200.synthetic as syn
+
+    enc = pkg.Encoder(0)
+    rows, peak_src = k1_sweep(pkg, syn, enc, SWEEP_SHAPES, args.warmup, args.steps, args.seed)
+    for r in rows:
+        print(json.dumps({"workload": "k1 LUT4 linear", **r, "peak": peak_src}), flush=True)
     enc.close()
 
 
@@ -138,15 +158,22 @@ def job_batch(args, world, syn):
     pure Python (loads no library)."""
     import bark3_b200 as pkg
 
+    def lengths(seed):
+        if args.seconds > 0:
+            return [args.seconds] * args.utterances
+        return [float(x) for x in syn.batch_lengths(seed, args.utterances)]
+
     if args.scaling == "strong":
-        secs = [float(x) for x in syn.batch_lengths(args.seed, args.utterances)]
+        secs = lengths(args.seed)
     else:
-        secs = [float(x) for r in range(world) for x in syn.batch_lengths(args.seed + 1000 * r, args.utterances)]
+        secs = [x for r in range(world) for x in lengths(args.seed + 1000 * r)]
     return secs, [pkg.frames_for_seconds(x) for x in secs]
 
 
 def batch_for_rank(args, rank, world, pkg, syn):
     """(seconds per utterance, frames per utterance) of this rank's share."""
+    if args.shard:   # one GPU standing in for rank R of an N-GPU strong job
+        rank, world = (int(v) for v in args.shard.split(":"))
     if args.scaling == "strong":
         secs, frames = job_batch(args, 1, syn)
         if world == 1:
@@ -154,8 +181,10 @@ def batch_for_rank(args, rank, world, pkg, syn):
         rank_of = pkg.shard_lpt(frames, world)
         mine = [i for i in range(len(frames)) if rank_of[i] == rank]
         return [secs[i] for i in mine], [frames[i] for i in mine]
-    secs = syn.batch_lengths(args.seed + 1000 * rank, args.utterances)
-    return [float(s) for s in secs], [pkg.frames_for_seconds(s) for s in secs]
+    if args.seconds > 0:
+        return job_batch(args, 1, syn)
+    secs = [float(x) for x in syn.batch_lengths(args.seed + 1000 * rank, args.utterances)]
+    return secs, [pkg.frames_for_seconds(x) for x in secs]
 
 
 def job_config(args, world, syn):
@@ -169,7 +198,8 @@ def job_config(args, world, syn):
                      "transcribe": "config-5 batch from subsampled features: 4-bit encoder + greedy TDT",
                      "encoder": "config-5 batch through the 24-block 4-bit LUT encoder"}[args.workload],
         "utterances": len(secs), "audio_s": round(sum(secs), 1), "frames": int(sum(frames)),
-        "lengths_s": "U(10,60) seeded", "seed": args.seed, "layers": N_LAYERS,
+        "lengths_s": f"{args.seconds:g} each" if args.seconds > 0 else "U(10,60) seeded", "seed": args.seed,
+        "layers": N_LAYERS,
         "d_model": 1024, "heads": 8, "ffn": 4096, "conv_kernel": 9,
         "weights": "random-init 4-bit codes + 16-entry f16 LUT per row (levels N(0,0.02) sorted, row-centred)",
         "input": ("synthetic audio: white noise U(-0.1,0.1) + 3 sines of amplitude 0.1, 16 kHz f32"
@@ -502,6 +532,12 @@ def main():
     traffic_file = ROOT / "profiles" / "k1_gemm_lut4_traffic.json"
     traffic = json.loads(traffic_file.read_text()).get("bytes_per_launch") if traffic_file.exists() else None
 
+    sweep = None
+    if rank == 0 and world == 1 and not args.no_sweep:
+        rows, peak_src = k1_sweep(pkg, syn, enc, SWEEP_SHAPES[:5], 3, 10, args.seed)
+        sweep = {"kernel": "k1 LUT4 linear alone (b3_linear_lut4, device pointers)", "peak": peak_src,
+                 "shapes": rows}
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         oracle = load_oracle()
@@ -538,7 +574,12 @@ def main():
                     "d2h_bytes_per_step": int(n_utt * (MAX_TOKENS * 12 + 4)) if decode else int(M * 640 * 4),
                     "bytes_are": "rank 0's per step"},
             "cpu_baseline": cpu,
+            "k1_sweep": sweep,
         }
+        if args.shard:
+            line["emulated_shard"] = (f"rank {args.shard.split(':')[0]} of a {args.shard.split(':')[1]}-GPU "
+                                      "strong-scaling job, timed alone on one GPU: value is that share's "
+                                      "throughput, not a whole-job number")
         print(json.dumps(line), flush=True)
     enc.close()
     if world > 1:
