@@ -37,6 +37,7 @@ B3_ETIMEOUT = -4
 B3_ESTATE = -5
 B3_ENOTFOUND = -6
 B3_DEVICE_PTRS = 1
+B3_DECODER_AUTO, B3_DECODER_SPLIT_K = 0, 1
 DTYPE_F32, DTYPE_F16, DTYPE_BF16 = 0, 1, 2
 
 N_LAYERS = 24
@@ -76,6 +77,7 @@ def lib() -> ctypes.CDLL:
         "b3_sync": (c_i, [c_p]),
         "b3_stream": (c_p, [c_p]),
         "b3_set_wait_limit": (c_i, [c_p, ctypes.c_int64]),
+        "b3_set_decoder": (c_i, [c_p, c_i]),
         "b3_load_tensor": (c_i, [c_p, ctypes.c_char_p, c_i, c_p, c_i, c_p]),
         "b3_load_lowbit": (c_i, [c_p, ctypes.c_char_p, c_p, c_p, c_i, c_i]),
         "b3_load_lowbit_levels": (c_i, [c_p, ctypes.c_char_p, c_p, c_p, c_i, c_i, c_i]),

@@ -105,6 +105,10 @@ struct GemmOp {
 constexpr int kMapU8 = 0, kMapF16 = 1, kMapF32 = 2;
 int make_map_2d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, uint64_t outer,
                 uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer, bool swizzle128);
+// TMA 3D map: dims[0] innermost (contiguous), stride_bytes[i] between
+// consecutive indices of dims[i + 1].
+int make_map_3d(CUtensorMap* map, const void* base, int dtype, const uint64_t dims[3], const uint64_t stride_bytes[2],
+                const uint32_t box[3], bool swizzle128);
 int gemm_make_a_map(CUtensorMap* map, const __half* a, int M, int K, int lda);
 int gemm_make_b_map(CUtensorMap* map, const void* w, bool lut, int N, int K);
 int gemm_validate(const GemmParams& p, bool lut);

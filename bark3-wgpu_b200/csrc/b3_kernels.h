@@ -106,6 +106,42 @@ int dec_launch_split(const float* src, __half* hi, __half* lo, int64_t n, cudaSt
 // Reads and clears the decoder's device error word (stream-ordered).
 int decoder_take_dev_error(cudaStream_t st, unsigned int* out);
 
+// Weight-stationary lock-step decoder (batches up to 2 x 128 rows).  Every
+// CTA owns one 128-row tile of one weight matrix for the whole decode, kept
+// in shared memory; tiles are numbered head (head_tiles), layer-0 recurrent
+// (20), layer-1 recurrent (20), layer-1 input (20), projector (5).  The LSTM
+// tiles hold 32 channels x 4 gates (rows i | f | g | o of channels
+// [32 t, 32 t + 32)), so a tile's owner applies the cell to its channels.
+// With nsplit = 2 the batch rows are cut in two halves of `ntile` rows and
+// every tile has one CTA per half.
+constexpr int kWsLstmTiles = 20;
+constexpr int kWsProjTiles = 5;
+struct DecWs {
+    int B, vocab, blank, max_tokens;
+    int head_tiles, n_roles, ntile, bpad, kc, max_steps;   // kc: k-blocks per TMA box
+    const int* row0;         // [B] first pooler row of each utterance
+    const int* len;          // [B] encoder frames of each utterance
+    const float* pooler;     // [total][640]
+    const float* e0;         // [vocab][2560] W_ih0 . emb(token) + b_ih0 + b_hh0 (gate order i | f | g | o)
+    const float* bias;       // head [head_tiles * 128] | layer 1 [2560] (b_ih1 + b_hh1) | projector [640]
+    __half *act0, *act1, *aj;   // h0, h1 and the joint input as f16 hi | lo: [10 k-blocks][hi, lo][bpad][64]
+    float* c;                // [B][2][640] cell states
+    float* g1p;              // [bpad][2560] recurrent half of the layer-1 gates (W_hh1 . h1)
+    unsigned long long* keys;   // [2 step parities][2: token, duration][B] argmax keys
+    int *frame, *count, *guard;  // [B] each
+    int* alive;              // [2 step parities][B]
+    uint32_t* tokens;        // [B][max_tokens][3] (id, frame, duration)
+    unsigned int* sync;      // [0] barrier arrivals, [1] abort flag, [4..5] alive counts by step parity
+    unsigned long long grid_wait_ns;
+};
+struct alignas(64) DecWsMaps {
+    CUtensorMap w;                 // [n_roles * 128][640] f16 weight tiles, box 64 x 128
+    CUtensorMap act0, act1, aj;    // 3D (64, bpad, 20 panels) f16, box 64 x ntile x 2 kc
+};
+// CTAs of one weight-stationary decode (0 if it does not fit this device).
+int dec_ws_grid(int device, int n_roles, int nsplit);
+int dec_ws_launch(const DecWsMaps& maps, const DecWs& p, int grid, cudaStream_t st);
+
 // Mel front end (frontend.cu).
 struct MelParams {
     int n_utt;

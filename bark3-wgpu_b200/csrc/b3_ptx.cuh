@@ -111,6 +111,18 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map
         : "memory");
 }
 
+// 3D tiled load into this CTA's shared memory (box laid out with dimension 0
+// fastest); completion is counted on `bar`.  x must be a multiple of 16
+// bytes; callers guarantee it.
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int32_t x, int32_t y,
+                                            int32_t z) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y), "r"(z)
+        : "memory");
+}
+
 // 2D tiled store from shared memory (bulk-group completion).
 __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int32_t x, int32_t y) {
     asm volatile(
@@ -152,6 +164,12 @@ __device__ __forceinline__ void fence_async_global() {
     asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 
+__device__ __forceinline__ unsigned long long ld_acquire_gpu_u64(const unsigned int* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
 __device__ __forceinline__ unsigned int ld_acquire_gpu(const unsigned int* p) {
     unsigned int v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
@@ -161,7 +179,8 @@ __device__ __forceinline__ unsigned int ld_acquire_gpu(const unsigned int* p) {
 // Grid-wide barrier for a kernel whose CTAs are all resident (cooperative
 // launch).  sync[0] counts arrivals over the kernel's life (each arrival is a
 // fire-and-forget reduction, so no CTA waits for its own atomic), sync[1] is
-// the abort flag.  `target` is this CTA's running total (nblocks more per
+// the abort flag (sync must be 8-byte aligned: both words are polled with one
+// load).  `target` is this CTA's running total (nblocks more per
 // barrier).  Bounded like mbar_wait, by `limit_ns` of wall time (a kernel
 // parameter, so a host can shorten it): on time-out it records the error,
 // raises the abort flag and returns false.  Call with all threads of the CTA;
@@ -181,8 +200,10 @@ __device__ __forceinline__ bool grid_barrier(unsigned int* sync, unsigned int nb
         atomicAdd(sync, 1u);
         unsigned long long t0 = 0;
         while (ok) {
-            if (static_cast<int>(ld_acquire_gpu(sync) - target) >= 0) break;
-            if (*reinterpret_cast<volatile unsigned int*>(sync + 1)) {
+            // arrivals and the abort flag in one load (sync is 8-byte aligned)
+            const unsigned long long both = ld_acquire_gpu_u64(sync);
+            if (static_cast<int>(static_cast<unsigned int>(both) - target) >= 0) break;
+            if (both >> 32) {
                 ok = 0;
                 break;
             }

@@ -228,6 +228,8 @@ struct b3_ctx {
     Prof prof;
     // wall-time bound of the decoder's grid-barrier waits (b3_set_wait_limit)
     uint64_t grid_wait_ns = kDefaultWaitNs;
+    // decode every batch with the split-K persistent kernel (b3_set_decoder)
+    bool dec_split_k_only = false;
     // greedy TDT decoder (optional: built when its tensors are loaded)
     struct Decoder {
         bool present = false;
@@ -239,6 +241,10 @@ struct b3_ctx {
         DevBuf bias;                           // f32: lstm0 [2560] (unused) | lstm1 [2560] | proj [640] | head [npad]
         // lock-step state (DecState), split-K parts, outputs, barrier words
         DevBuf a0, a1, ap, aj, gates, cstate, dec, scores, ints, tokens, rows, sync, pooler;
+        // weight-stationary decoder (DecWs): 128-row weight tiles, their biases, argmax keys
+        int ws_ht = 0;
+        DevBuf ws_w, ws_bias, ws_keys;
+        CUtensorMap ws_wmap;
     } dec;
     // mel front end + conv subsampling (optional: built when the conv
     // subsampling tensors are loaded)
@@ -905,9 +911,120 @@ int build_decoder(b3_ctx* c) {
     B3_TRY(get_vec(c, "joint.head.bias", V + 5, v1));
     memcpy(&bias[2 * G + H], v1.data(), (V + 5) * 4);
     B3_TRY(upload(D.bias, bias.data(), bias.size() * 4, c->stream));
+    {
+        // weight-stationary tiles (DecWs): head rows, then the three LSTM
+        // matrices with 32 channels x 4 gates per tile, then the projector
+        const int ht = (V + 5 + 127) / 128;
+        const int n_roles = ht + 3 * kWsLstmTiles + kWsProjTiles;
+        std::vector<uint16_t> wt(static_cast<size_t>(n_roles) * 128 * H, 0);
+        auto put = [&](int dst_row, const std::vector<uint16_t>& src, int src_row) {
+            memcpy(&wt[static_cast<size_t>(dst_row) * H], &src[static_cast<size_t>(src_row) * H], H * 2);
+        };
+        for (int r = 0; r < V + 5; ++r) put(r, *wh, r);
+        const std::vector<uint16_t>*whh0, *whh1, *wih1;
+        B3_TRY(dec_matrix(c, "decoder.lstm.weight_hh_l0", G, &whh0));
+        B3_TRY(dec_matrix(c, "decoder.lstm.weight_hh_l1", G, &whh1));
+        B3_TRY(dec_matrix(c, "decoder.lstm.weight_ih_l1", G, &wih1));
+        const std::vector<uint16_t>* lstm[3] = {whh0, whh1, wih1};
+        for (int m = 0; m < 3; ++m)
+            for (int t = 0; t < kWsLstmTiles; ++t)
+                for (int q = 0; q < 4; ++q)
+                    for (int ch = 0; ch < 32; ++ch)
+                        put((ht + m * kWsLstmTiles + t) * 128 + q * 32 + ch, *lstm[m], q * H + 32 * t + ch);
+        for (int r = 0; r < H; ++r) put((ht + 3 * kWsLstmTiles) * 128 + r, *wp, r);
+        std::vector<float> wb(static_cast<size_t>(ht) * 128 + G + H, 0.f);
+        memcpy(wb.data(), v1.data(), (V + 5) * 4);                  // head bias
+        memcpy(wb.data() + ht * 128, &bias[G], G * 4);               // b_ih1 + b_hh1
+        memcpy(wb.data() + ht * 128 + G, &bias[2 * G], H * 4);       // projector bias
+        B3_TRY(upload(D.ws_w, wt.data(), wt.size() * 2, c->stream));
+        B3_TRY(upload(D.ws_bias, wb.data(), wb.size() * 4, c->stream));
+        B3_TRY(make_map_2d(&D.ws_wmap, D.ws_w.p, kMapF16, H, static_cast<uint64_t>(n_roles) * 128, 2 * H, 64, 128,
+                           true));
+        D.ws_ht = ht;
+    }
     B3_CUDA(cudaStreamSynchronize(c->stream));
     D.present = true;
     return 0;
+}
+
+// Greedy decode with the weight-stationary kernel (DecWs): batches of up to
+// 2 x 128 rows on n_roles x nsplit CTAs.  Tokens and counts land where
+// decode_collect reads them.
+int decode_ws(b3_ctx* c, const float* pooler, const std::vector<int32_t>& rows, int B, int tmax, int max_tokens,
+              int nsplit, int grid) {
+    auto& D = c->dec;
+    const int ntile = ((B + nsplit - 1) / nsplit + 31) / 32 * 32;
+    const int bpad = ntile * nsplit;
+    const size_t act_bytes = static_cast<size_t>(bpad) * 1280 * 2;
+    B3_TRY(D.a0.ensure(act_bytes));
+    B3_TRY(D.ap.ensure(act_bytes));
+    B3_TRY(D.aj.ensure(act_bytes));
+    B3_TRY(D.cstate.ensure(static_cast<size_t>(B) * 2 * 640 * 4));
+    B3_TRY(D.gates.ensure(static_cast<size_t>(bpad) * 2560 * 4));
+    B3_TRY(D.ws_keys.ensure(static_cast<size_t>(B) * 4 * 8));
+    B3_TRY(D.ints.ensure(static_cast<size_t>(B) * 6 * 4));
+    B3_TRY(D.tokens.ensure(static_cast<size_t>(B) * max_tokens * 12));
+    B3_TRY(D.rows.ensure(static_cast<size_t>(B) * 2 * 4));
+    B3_TRY(D.sync.ensure(32));
+    ProfScope ps(c, B3_K_DECODER, 0.0, 0.0);
+    c->prof.launches[B3_K_DECODER]++;
+    // frame | count | guard (0) | alive of steps 0 and -1 (utterances with frames)
+    std::vector<int32_t> ints(static_cast<size_t>(B) * 5, 0);
+    for (int b = 0; b < B; ++b) ints[3 * B + b] = ints[4 * B + b] = rows[B + b] > 0 ? 1 : 0;
+    B3_CUDA(cudaMemcpyAsync(D.rows.p, rows.data(), rows.size() * 4, cudaMemcpyHostToDevice, c->stream));
+    B3_CUDA(cudaMemcpyAsync(D.ints.p, ints.data(), ints.size() * 4, cudaMemcpyHostToDevice, c->stream));
+    B3_CUDA(cudaMemsetAsync(D.a0.p, 0, act_bytes, c->stream));
+    B3_CUDA(cudaMemsetAsync(D.ap.p, 0, act_bytes, c->stream));
+    B3_CUDA(cudaMemsetAsync(D.aj.p, 0, act_bytes, c->stream));
+    B3_CUDA(cudaMemsetAsync(D.cstate.p, 0, static_cast<size_t>(B) * 2 * 640 * 4, c->stream));
+    B3_CUDA(cudaMemsetAsync(D.ws_keys.p, 0, static_cast<size_t>(B) * 4 * 8, c->stream));
+    B3_CUDA(cudaMemsetAsync(D.sync.p, 0, 32, c->stream));
+    DecWs p{};
+    p.B = B;
+    p.vocab = D.vocab;
+    p.blank = D.vocab - 1;
+    p.max_tokens = max_tokens;
+    p.head_tiles = D.ws_ht;
+    p.n_roles = D.ws_ht + 3 * kWsLstmTiles + kWsProjTiles;
+    p.ntile = ntile;
+    p.bpad = bpad;
+    // k-blocks per TMA box: the largest divisor of the 10 k-blocks that keeps
+    // two ring stages in the 64 KB ring (so no box reaches past the panels)
+    p.kc = 1;
+    for (int d : {10, 5, 2})
+        if (d * 2 * ntile * 128 <= 32768) {
+            p.kc = d;
+            break;
+        }
+    p.max_steps = tmax * 14 + 64;
+    p.row0 = D.rows.as<int>();
+    p.len = D.rows.as<int>() + B;
+    p.pooler = pooler;
+    p.e0 = D.e0.as<float>();
+    p.bias = D.ws_bias.as<float>();
+    p.act0 = D.a0.as<__half>();
+    p.act1 = D.ap.as<__half>();
+    p.aj = D.aj.as<__half>();
+    p.c = D.cstate.as<float>();
+    p.g1p = D.gates.as<float>();
+    p.keys = D.ws_keys.as<unsigned long long>();
+    int* ip = D.ints.as<int>();
+    p.frame = ip;
+    p.count = ip + B;
+    p.guard = ip + 2 * B;
+    p.alive = ip + 3 * B;   // [0] step-0 parity, [1] the first pass (step -1)
+    p.tokens = D.tokens.as<uint32_t>();
+    p.sync = D.sync.as<unsigned int>();
+    p.grid_wait_ns = c->grid_wait_ns;
+    DecWsMaps maps;
+    maps.w = D.ws_wmap;
+    const uint64_t dims[3] = {64, static_cast<uint64_t>(bpad), 20};
+    const uint64_t strides[2] = {128, static_cast<uint64_t>(bpad) * 128};
+    const uint32_t box[3] = {64, static_cast<uint32_t>(ntile), static_cast<uint32_t>(2 * p.kc)};
+    B3_TRY(make_map_3d(&maps.act0, D.a0.p, kMapF16, dims, strides, box, true));
+    B3_TRY(make_map_3d(&maps.act1, D.ap.p, kMapF16, dims, strides, box, true));
+    B3_TRY(make_map_3d(&maps.aj, D.aj.p, kMapF16, dims, strides, box, true));
+    return dec_ws_launch(maps, p, grid, c->stream);
 }
 
 // Greedy-decodes n_utt utterances of a device pooler [total][640] with one
@@ -925,6 +1042,16 @@ int decode_device(b3_ctx* c, const float* pooler, const int32_t* cu, int n_utt, 
         rows[B + b] = cu[b + 1] - cu[b];
         if (rows[B + b] < 0) return set_error(B3_EINVAL, "cu_seqlens must be non-decreasing");
         tmax = std::max(tmax, rows[B + b]);
+    }
+    // up to 128 rows: the weight-stationary kernel (two halves of at most 64
+    // columns above 64 rows), when its CTAs fit; its epilogues do per-column
+    // work, so wider halves run slower than the split-K kernel
+    {
+        const int n_roles = D.ws_ht + 3 * kWsLstmTiles + kWsProjTiles;
+        int nsplit = B <= 64 ? 1 : (B <= 128 ? 2 : 0);
+        if (nsplit == 1 && B > 32 && 2 * n_roles <= device_sms()) nsplit = 2;
+        const int ws_grid = nsplit ? dec_ws_grid(c->device, n_roles, nsplit) : 0;
+        if (ws_grid > 0 && !c->dec_split_k_only) return decode_ws(c, pooler, rows, B, tmax, max_tokens, nsplit, ws_grid);
     }
     const int grid = dec_persistent_grid(c->device);
     if (grid <= 0) return set_error(B3_ECUDA, "the persistent decoder does not fit on this device");
@@ -1490,6 +1617,13 @@ int b3_sync(b3_ctx* ctx) {
 }
 
 void* b3_stream(b3_ctx* ctx) { return ctx ? static_cast<void*>(ctx->stream) : nullptr; }
+
+int b3_set_decoder(b3_ctx* ctx, int kind) {
+    if (!ctx) return set_error(B3_EINVAL, "null context");
+    if (kind != B3_DECODER_AUTO && kind != B3_DECODER_SPLIT_K) return set_error(B3_EINVAL, "unknown decoder kind %d", kind);
+    ctx->dec_split_k_only = kind == B3_DECODER_SPLIT_K;
+    return 0;
+}
 
 int b3_set_wait_limit(b3_ctx* ctx, int64_t grid_barrier_ns) {
     if (!ctx) return set_error(B3_EINVAL, "null context");

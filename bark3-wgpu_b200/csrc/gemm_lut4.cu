@@ -931,6 +931,26 @@ int make_map_2d(CUtensorMap* map, const void* base, int dtype, uint64_t inner, u
     return 0;
 }
 
+int make_map_3d(CUtensorMap* map, const void* base, int dtype, const uint64_t dims[3], const uint64_t stride_bytes[2],
+                const uint32_t box[3], bool swizzle128) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn) return set_error(B3_ECUDA, "cuTensorMapEncodeTiled is unavailable");
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (stride_bytes[0] & 15) || (stride_bytes[1] & 15))
+        return set_error(B3_EINVAL, "TMA base/stride must be 16-byte aligned");
+    cuuint64_t d[3] = {dims[0], dims[1], dims[2]};
+    cuuint64_t st[2] = {stride_bytes[0], stride_bytes[1]};
+    cuuint32_t bx[3] = {box[0], box[1], box[2]};
+    cuuint32_t estr[3] = {1, 1, 1};
+    const CUtensorMapDataType dt = dtype == kMapF32   ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                   : dtype == kMapF16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16
+                                                      : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+    CUresult r = fn(map, dt, 3, const_cast<void*>(base), d, st, bx, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(B3_ECUDA, "cuTensorMapEncodeTiled (3D) failed (%d)", static_cast<int>(r));
+    return 0;
+}
+
 int gemm_make_a_map(CUtensorMap* map, const __half* a, int M, int K, int lda) {
     return make_map_2d(map, a, true, static_cast<uint64_t>(K), static_cast<uint64_t>(M),
                        static_cast<uint64_t>(lda) * 2, kBK, kBM, true);

@@ -679,6 +679,549 @@ __global__ void __launch_bounds__(kPThreads, 1)
     }
 }
 
+// ───────────────── weight-stationary decoder (batches up to 2 x 128 rows) ─────────────────
+//
+// The same lock step as k_dec_persist with the weights held still: every CTA
+// owns one 128-row weight tile (DecWs) for the whole decode and keeps it in
+// shared memory (160 KB: 10 k-blocks of 128 rows x 64 f16, 128-byte swizzle),
+// so a step streams only activations.  The GEMMs are transposed, D = W . A^T:
+// the tile's 128 weight rows are the MMA's M, the batch rows (the CTA's half)
+// its N, and the f16 hi and lo halves of the activation rows are stacked as
+// 2 x ntile B rows of one MMA (N = 2 ntile), the epilogue adding the two
+// column halves.  An LSTM tile covers whole channels (its four gate rows), so
+// its owner applies the cell in its own epilogue and no split-K parts exist.
+// A step is four phases behind grid barriers (one fewer per step than the
+// split-K kernel's six, and a quarter of the CTAs at up to 128 rows):
+//   1  head GEMM -> per-row argmax as 64-bit atomicMax keys (first maximum
+//      wins: the low word is ~index); layer-0 recurrent GEMM (kept in TMEM);
+//      layer-1 recurrent GEMM -> g1p
+//   2  row state update (head tile 0 of each half); layer-0 cell with E0[token]
+//   3  layer-1 input GEMM + g1p + bias -> layer-1 cell
+//   4  projector GEMM -> joint input ReLU(enc[frame] + dec) as hi | lo
+// Rows that do not emit keep their state; finished rows keep being computed
+// (their results are never read), the loop ends when no row is alive.  The
+// first pass (step -1) is phases 1-4 without the head, on the blank token, as
+// the reference starts (src/tdt.rs:424-428).
+constexpr int kWsThreads = 256;                 // warp 0 TMA, warp 1 MMA, warps 4..7 epilogue
+constexpr int kWsKB = 10;                       // 640 / 64 k-blocks
+constexpr uint32_t kWsWBytes = 128u * 640 * 2;  // one weight tile
+constexpr uint32_t kWsRingOff = kWsWBytes;
+constexpr uint32_t kWsRingBytes = 65536;        // activation ring, reused as the epilogue's exchange area
+constexpr uint32_t kWsMetaOff = kWsRingOff + kWsRingBytes;
+constexpr uint32_t kWsMetaBytes = 1536;
+constexpr uint32_t kWsSmem = kWsMetaOff + kWsMetaBytes + 1024;   // + alignment slack
+static_assert(kWsSmem <= 232448, "shared memory budget");
+constexpr int kWsMaxStages = 10;
+constexpr uint32_t kWsTmemCols = 256;
+
+enum { kWsHead = 0, kWsL0 = 1, kWsL1hh = 2, kWsL1ih = 3, kWsProj = 4 };
+
+__device__ __forceinline__ unsigned long long ws_key(float v, int idx) {
+    uint32_t u = __float_as_uint(v);
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);   // order-preserving map of f32 onto u32
+    return (static_cast<unsigned long long>(u) << 32) | (0xFFFFFFFFu - static_cast<uint32_t>(idx));
+}
+__device__ __forceinline__ int ws_key_index(unsigned long long k) {
+    return static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(k));
+}
+
+// 32 lanes x 32 columns (v[j], ix[j] of column j) -> lane l holds the winner
+// of column l over the 32 lanes (31 exchanges; halves of the columns travel
+// at each step).
+__device__ __forceinline__ void ws_transpose_argmax(float (&v)[32], int (&ix)[32], int lane) {
+#pragma unroll
+    for (int s = 16; s >= 1; s >>= 1) {
+        const bool up = (lane & s) != 0;
+#pragma unroll
+        for (int k = 0; k < s; ++k) {
+            const float sv = up ? v[k] : v[k + s];
+            const int si = up ? ix[k] : ix[k + s];
+            float kv = up ? v[k + s] : v[k];
+            int ki = up ? ix[k + s] : ix[k];
+            const float rv = __shfl_xor_sync(0xffffffffu, sv, s);
+            const int ri = __shfl_xor_sync(0xffffffffu, si, s);
+            if (wins(rv, ri, kv, ki)) {
+                kv = rv;
+                ki = ri;
+            }
+            v[k] = kv;
+            ix[k] = ki;
+        }
+    }
+}
+
+// Activation layout of the weight-stationary kernel: 20 panels [k-block][hi, lo]
+// of [bpad rows][64 f16], so one 3D TMA box (64 x rows x 2 kc panels) brings kc
+// k-blocks with each k-block's hi rows and lo rows stacked as the MMA's B.
+__device__ __forceinline__ __half* ws_panel(__half* base, int bpad, int col, int n, int h) {
+    return base + (static_cast<size_t>(2 * (col >> 6) + h) * bpad + n) * 64 + (col & 63);
+}
+
+// Named barriers that leave out warps 0 and 1 (the TMA and MMA issuers,
+// which return from a GEMM only once its last stage has landed): the four
+// epilogue warps (id 5), and warps 2..7, which share the LSTM cell math (id 6).
+__device__ __forceinline__ void ws_sync_epi() { asm volatile("bar.sync 5, 128;" ::: "memory"); }
+__device__ __forceinline__ bool ws_sync_math_and(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.and.pred q, 6, 192, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"(static_cast<uint32_t>(v))
+        : "memory");
+    return r != 0;
+}
+
+// Named barrier of the four epilogue warps that also ANDs a predicate over them.
+__device__ __forceinline__ bool __syncthreads_and_epi(bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.and.pred q, 5, 128, p;\n\t"
+        "selp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"(static_cast<uint32_t>(v))
+        : "memory");
+    return r != 0;
+}
+
+__global__ void __launch_bounds__(kWsThreads, 1)
+    k_dec_ws(const __grid_constant__ DecWsMaps maps, const DecWs p) {
+    extern __shared__ __align__(1024) uint8_t ws_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(ws_raw) + 1023) &
+                                               ~static_cast<uintptr_t>(1023));
+    uint8_t* sW = smem;
+    uint8_t* ring = smem + kWsRingOff;
+    float* xc = reinterpret_cast<float*>(ring);               // epilogue exchange (ring idle then)
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kWsMetaOff);
+    uint64_t* empty = full + kWsMaxStages;
+    uint64_t* wfull = full + 2 * kWsMaxStages;
+    uint64_t* tfull = wfull + 1;
+    uint32_t* tslot = reinterpret_cast<uint32_t*>(tfull + 1);
+    int* ok_smem = reinterpret_cast<int*>(tslot + 1);
+    int* sdone = ok_smem + 1;
+    int* em = reinterpret_cast<int*>(smem + kWsMetaOff + 512);   // [128] per-column flag
+    int* tk = em + 128;                                          // [128] per-column token / pooler row
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int tile = blockIdx.x % p.n_roles, half = blockIdx.x / p.n_roles;
+    const int n0 = half * p.ntile;
+    const int ht = p.head_tiles;
+    int role, t;
+    if (tile < ht) {
+        role = kWsHead, t = tile;
+    } else if (tile < ht + kWsLstmTiles) {
+        role = kWsL0, t = tile - ht;
+    } else if (tile < ht + 2 * kWsLstmTiles) {
+        role = kWsL1hh, t = tile - ht - kWsLstmTiles;
+    } else if (tile < ht + 3 * kWsLstmTiles) {
+        role = kWsL1ih, t = tile - ht - 2 * kWsLstmTiles;
+    } else {
+        role = kWsProj, t = tile - ht - 3 * kWsLstmTiles;
+    }
+    const CUtensorMap* amap = role == kWsHead ? &maps.aj : (role == kWsL0 || role == kWsL1ih) ? &maps.act0 : &maps.act1;
+    const int nt = p.ntile;
+    const int kc = p.kc;                                   // k-blocks per TMA box / ring stage
+    const int nloads = (kWsKB + kc - 1) / kc;
+    const uint32_t kb_bytes = 2u * nt * 128u;              // one k-block: hi rows then lo rows
+    const uint32_t stage_bytes = kc * kb_bytes;
+    const int stages = min(kWsMaxStages, static_cast<int>(kWsRingBytes / stage_bytes));
+    const uint32_t idesc = (1u << 4) | (static_cast<uint32_t>((2 * nt) >> 3) << 17) | ((128u >> 4) << 24);
+
+    if (threadIdx.x == 0) {
+        tma_prefetch_desc(&maps.w);
+        tma_prefetch_desc(amap);
+        for (int i = 0; i < stages; ++i) {
+            mbar_init(smem_u32(&full[i]), 1);
+            mbar_init(smem_u32(&empty[i]), 1);
+        }
+        mbar_init(smem_u32(wfull), 1);
+        mbar_init(smem_u32(tfull), 1);
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        tmem_alloc<kWsTmemCols>(smem_u32(tslot));
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+    if (threadIdx.x == 0) {   // the tile's weights, once
+        mbar_arrive_expect_tx(smem_u32(wfull), kWsWBytes);
+        for (int kb = 0; kb < kWsKB; ++kb)
+            tma_load_2d(smem_u32(sW + kb * 16384), &maps.w, smem_u32(wfull), 64 * kb, 128 * tile);
+    }
+
+    int pit = 0, mit = 0, ng_mma = 0, ng_epi = 0;
+    bool wready = false;
+    // One GEMM of this CTA: D[128][2 nt] = W . [hi rows | lo rows]^T.  The
+    // producer and the MMA issuer return after issuing; the epilogue waits
+    // for the accumulator (ws_acc).
+    auto gemm = [&]() -> bool {
+        bool ok = true;
+        if (warp == 0 && lane == 0) {
+            fence_async_global();   // activations other CTAs wrote before the barrier
+            // one TMA instruction per kc k-blocks (kc divides the 10): issuing
+            // TMA instructions, not their bytes, is what a phase waits for at
+            // small batches
+            for (int i = 0; i < nloads; ++i, ++pit) {
+                const int st = pit % stages;
+                if (pit >= stages && !(ok = mbar_wait(smem_u32(&empty[st]), ((pit / stages) - 1) & 1, 0x70))) break;
+                const uint32_t fb = smem_u32(&full[st]);
+                mbar_arrive_expect_tx(fb, stage_bytes);
+                tma_load_3d(smem_u32(ring + st * stage_bytes), amap, fb, 0, n0, 2 * kc * i);
+            }
+        } else if (warp == 1 && lane == 0) {
+            if (!wready) {
+                if (!(ok = mbar_wait(smem_u32(wfull), 0, 0x71))) return ok;
+                wready = true;
+            }
+            tc_fence_after();
+            for (int i = 0; i < nloads; ++i, ++mit) {
+                const int st = mit % stages;
+                if (!(ok = mbar_wait(smem_u32(&full[st]), (mit / stages) & 1, 0x72))) break;
+                tc_fence_after();
+                for (int j = 0; j < kc && i * kc + j < kWsKB; ++j) {
+                    const int kb = i * kc + j;
+                    const uint64_t a = smem_desc_sw128(smem_u32(sW + kb * 16384));
+                    const uint64_t b = smem_desc_sw128(smem_u32(ring + st * stage_bytes + j * kb_bytes));
+#pragma unroll
+                    for (int kk = 0; kk < 4; ++kk) mma_f16_ss(tmem, a + 2 * kk, b + 2 * kk, idesc, (kb | kk) != 0);
+                }
+                mma_commit(smem_u32(&empty[st]));
+            }
+            if (ok) {
+                mma_commit(smem_u32(tfull));
+                ++ng_mma;
+            }
+        }
+        return ok;
+    };
+    // Epilogue warps: wait for this CTA's latest accumulator.
+    auto ws_acc = [&]() -> bool {
+        bool got = mbar_wait(smem_u32(tfull), ng_epi & 1, 0x73);
+        ++ng_epi;
+        got = __all_sync(0xffffffffu, got);
+        tc_fence_after();
+        return got;
+    };
+    // Columns [c0, c0 + 32) of the accumulator as hi + lo (lane = weight row).
+    auto acc32 = [&](int q, int c0, float (&v)[32]) {
+        uint32_t h[32], l[32];
+        const uint32_t base = tmem + (static_cast<uint32_t>(q * 32) << 16);
+        tmem_ld_32x32b_x32(base + c0, h);
+        tmem_ld_32x32b_x32(base + nt + c0, l);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(h[j]) + __uint_as_float(l[j]);
+    };
+    // Per column of this half: emit flag and token of step `par` (epilogue threads).
+    auto load_emit = [&](int par, bool first) {
+        const int u = threadIdx.x - 128;
+        if (u < nt) {
+            const int n = n0 + u;
+            int e = 0, tkn = p.blank;
+            if (n < p.B) {   // both loads issued together
+                const int a = __ldcg(p.alive + par * p.B + n);
+                const unsigned long long key = __ldcg(p.keys + static_cast<size_t>(par * 2) * p.B + n);
+                if (first) {
+                    e = a;
+                } else {
+                    tkn = ws_key_index(key);
+                    e = a && tkn != p.blank;
+                }
+            }
+            em[u] = e;
+            tk[u] = tkn;
+        }
+    };
+    // LSTM cell of layer `layer` for this tile's 32 channels x this half's
+    // rows (ntile <= 64), run by warps 2..7 after load_emit and their named
+    // barrier.  Every global load (cell states, E0 row slices, the recurrent
+    // half of the layer-1 gates) is issued before the accumulator wait, so it
+    // overlaps this phase's GEMM; thread (channel ch, column group cg) of the
+    // six warps takes columns cg + 6 i.
+    auto cell = [&](int layer) -> bool {
+        const int mt = threadIdx.x - 64, ch = mt & 31, cg = mt >> 5;
+        constexpr int kCols = 11;   // ceil(64 / 6)
+        bool act[kCols];
+        float cold[kCols], e[kCols][4];
+#pragma unroll
+        for (int i = 0; i < kCols; ++i) {
+            const int col = cg + 6 * i;
+            act[i] = col < nt && n0 + col < p.B && em[col];
+            const int n = n0 + (act[i] ? col : 0);
+            cold[i] = act[i] ? __ldcg(p.c + (static_cast<size_t>(n) * 2 + layer) * 640 + 32 * t + ch) : 0.f;
+#pragma unroll
+            for (int g = 0; g < 4; ++g)
+                e[i][g] = (layer == 0 && act[i])
+                              ? __ldg(p.e0 + static_cast<size_t>(tk[col]) * 2560 + g * 640 + 32 * t + ch)
+                              : 0.f;
+        }
+        bool got = true;
+        if (warp >= 4) {
+            const int q = warp & 3;
+            const int gi = q * 640 + 32 * t + lane;   // gate row in the original i | f | g | o order
+            float r[64];
+#pragma unroll
+            for (int j = 0; j < 64; ++j) {
+                const int n = n0 + j;
+                r[j] = (layer == 1 && j < nt && n < p.B) ? __ldcg(p.g1p + static_cast<size_t>(n) * 2560 + gi) : 0.f;
+            }
+            const float b1 = layer == 1 ? __ldg(p.bias + ht * 128 + gi) : 0.f;
+            got = ws_acc();
+            if (got) {
+#pragma unroll
+                for (int c0 = 0; c0 < 64; c0 += 32) {
+                    if (c0 >= nt) break;
+                    float v[32];
+                    acc32(q, c0, v);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j)
+                        xc[(q * nt + c0 + j) * 32 + lane] = layer == 1 ? (b1 + v[j]) + r[c0 + j] : v[j];
+                }
+            }
+            tc_fence_before();
+        }
+        const bool all_got = ws_sync_math_and(got);
+#pragma unroll
+        for (int i = 0; i < kCols; ++i) {
+            if (!all_got || !act[i]) continue;
+            const int col = cg + 6 * i, n = n0 + col;
+            float gate[4];
+#pragma unroll
+            for (int g = 0; g < 4; ++g) gate[g] = xc[(g * nt + col) * 32 + ch] + e[i][g];
+            const float in = sigm(gate[0]);
+            const float fg = sigm(gate[1]);
+            const float cand = tanhf(gate[2]);
+            const float cn = fg * cold[i] + in * cand;
+            const float h = sigm(gate[3]) * tanhf(cn);
+            p.c[(static_cast<size_t>(n) * 2 + layer) * 640 + 32 * t + ch] = cn;
+            __half* a = layer == 0 ? p.act0 : p.act1;
+            split_store(ws_panel(a, p.bpad, 32 * t + ch, n, 0), ws_panel(a, p.bpad, 32 * t + ch, n, 1), h);
+        }
+        fence_async_shared();
+        return all_got;
+    };
+
+    const int epi = warp >= 4;
+    unsigned int* sync = p.sync;
+    const unsigned int nb = gridDim.x;
+    unsigned int target = 0;
+    for (int s = -1; s < p.max_steps; ++s) {
+        const int par = s & 1;
+        const bool first = s < 0;
+        bool ok = true;
+        // ── phase 1: head (argmax keys), layer-0 recurrent, layer-1 recurrent ──
+        if (role == kWsL0 || role == kWsL1hh || (role == kWsHead && !first)) ok = gemm();
+        if (ok && epi && role == kWsHead && !first) {
+            const int q = warp & 3;
+            const int wr = 128 * t + 32 * q + lane;   // head row: token < vocab <= duration < vocab + 5
+            const bool is_tok = wr < p.vocab, is_dur = wr >= p.vocab && wr < p.vocab + 5;
+            const bool has_dur = 128 * t < p.vocab + 5 && 128 * t + 127 >= p.vocab;
+            const float br = __ldg(p.bias + wr);
+            float* hx = xc;                                   // [2][4][128] (value, index) per warp
+            int* hi_ = reinterpret_cast<int*>(xc + 1024);
+            const bool got = ws_acc();
+            {
+                for (int c0 = 0; got && c0 < nt; c0 += 32) {
+                    float v[32], d[32];
+                    int ix[32], dx[32];
+                    acc32(q, c0, v);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const float sc = v[j] + br;
+                        v[j] = is_tok ? sc : -INFINITY;
+                        ix[j] = wr;
+                        d[j] = is_dur ? sc : -INFINITY;
+                        dx[j] = wr - p.vocab;
+                    }
+                    ws_transpose_argmax(v, ix, lane);
+                    hx[q * 128 + c0 + lane] = v[0];
+                    hi_[q * 128 + c0 + lane] = ix[0];
+                    if (has_dur) {
+                        ws_transpose_argmax(d, dx, lane);
+                        hx[512 + q * 128 + c0 + lane] = d[0];
+                        hi_[512 + q * 128 + c0 + lane] = dx[0];
+                    }
+                }
+                tc_fence_before();
+                ok = __syncthreads_and_epi(got);   // every epilogue warp meets here
+                const int col = threadIdx.x - 128;
+                const int n = n0 + col;
+                if (ok && col < nt && n < p.B) {
+                    for (int kind = 0; kind < (has_dur ? 2 : 1); ++kind) {
+                        float bv = hx[kind * 512 + col];
+                        int bi = hi_[kind * 512 + col];
+                        for (int w = 1; w < 4; ++w) {
+                            const float wv = hx[kind * 512 + w * 128 + col];
+                            const int wi = hi_[kind * 512 + w * 128 + col];
+                            if (wins(wv, wi, bv, bi)) {
+                                bv = wv;
+                                bi = wi;
+                            }
+                        }
+                        if (bv > -INFINITY)
+                            atomicMax(p.keys + static_cast<size_t>(par * 2 + kind) * p.B + n, ws_key(bv, bi));
+                    }
+                }
+                fence_async_shared();
+            }
+        }
+        if (ok && epi && role == kWsL1hh) {
+            const int q = warp & 3;
+            const int gi = q * 640 + 32 * t + lane;
+            if ((ok = ws_acc())) {
+                for (int c0 = 0; c0 < nt; c0 += 32) {
+                    float v[32];
+                    acc32(q, c0, v);
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const int n = n0 + c0 + j;
+                        if (n < p.B) p.g1p[static_cast<size_t>(n) * 2560 + gi] = v[j];
+                    }
+                }
+                tc_fence_before();
+            }
+        }
+        bool fail = __syncthreads_or(!ok);
+        if (!grid_barrier(sync, nb, target, fail, ok_smem, 0x74, p.grid_wait_ns)) break;
+
+        // ── phase 2: row state (head tile 0 of each half), layer-0 cell ──
+        if (epi && role == kWsHead && t == 0 && !first) {
+            const int u = threadIdx.x - 128, n = n0 + u;
+            if (u < nt && n < p.B) {
+                int act = 0;
+                // every load of the row issued together
+                const int alive = __ldcg(p.alive + par * p.B + n);
+                const int tkn = ws_key_index(__ldcg(p.keys + static_cast<size_t>(par * 2) * p.B + n));
+                const int dur = ws_key_index(__ldcg(p.keys + static_cast<size_t>(par * 2 + 1) * p.B + n));
+                const int T = p.len[n], fr = p.frame[n], cnt = p.count[n], gd = p.guard[n];
+                if (alive) {
+                    int nf;
+                    if (tkn != p.blank) {
+                        if (cnt < p.max_tokens) {
+                            uint32_t* tw = p.tokens + (static_cast<size_t>(n) * p.max_tokens + cnt) * 3;
+                            tw[0] = static_cast<uint32_t>(tkn);
+                            tw[1] = static_cast<uint32_t>(fr);
+                            tw[2] = static_cast<uint32_t>(dur);
+                        }
+                        p.count[n] = cnt + 1;
+                        nf = fr + dur;
+                    } else {
+                        nf = fr + (dur > 0 ? dur : 1);
+                    }
+                    p.frame[n] = nf;
+                    p.guard[n] = gd + 1;
+                    const long max_steps = static_cast<long>(T) * (10 + 4) + 64;
+                    act = nf < T && gd + 1 < max_steps;
+                    if (act) atomicAdd(sync + 4 + par, 1u);
+                }
+                p.alive[(par ^ 1) * p.B + n] = act;
+            }
+        }
+        if (role == kWsL0 && warp >= 2) {
+            if (epi) load_emit(par, first);
+            ws_sync_math_and(true);
+            ok = cell(0);
+        }
+        fence_async_global();
+        fail = __syncthreads_or(!ok);
+        if (!grid_barrier(sync, nb, target, fail, ok_smem, 0x75, p.grid_wait_ns)) break;
+        if (!first) {   // every row finished at this step's argmax
+            if (threadIdx.x == 0) *sdone = ld_acquire_gpu(sync + 4 + par) == 0;
+            __syncthreads();
+            if (*reinterpret_cast<volatile int*>(sdone)) break;
+        }
+
+        // ── phase 3: layer-1 input GEMM + cell; the next step's keys and count cleared ──
+        if (blockIdx.x == 0) {
+            for (int i = threadIdx.x; i < 2 * p.B; i += blockDim.x)
+                p.keys[static_cast<size_t>((par ^ 1) * 2) * p.B + i] = 0ull;
+            if (threadIdx.x == 0) sync[4 + (par ^ 1)] = 0u;
+        }
+        if (role == kWsL1ih) {
+            ok = gemm();
+            if (warp >= 2) {
+                if (epi) load_emit(par, first);
+                ws_sync_math_and(true);
+                ok = cell(1);
+            }
+        }
+        fence_async_global();
+        fail = __syncthreads_or(!ok);
+        if (!grid_barrier(sync, nb, target, fail, ok_smem, 0x76, p.grid_wait_ns)) break;
+
+        // ── phase 4: projector GEMM -> joint input ──
+        if (role == kWsProj) {
+            ok = gemm();
+            if (epi) {
+                const int u = threadIdx.x - 128;
+                if (u < nt) {   // pooler row of each alive column of the next step
+                    const int n = n0 + u;
+                    int pr = -1;
+                    if (n < p.B) {
+                        const int a = __ldcg(p.alive + (par ^ 1) * p.B + n), fr = __ldcg(p.frame + n), r0 = p.row0[n];
+                        if (a) pr = r0 + fr;
+                    }
+                    tk[u] = pr;
+                }
+                ws_sync_epi();
+            }
+            if (ok && epi) {
+                const int q = warp & 3;
+                const int j = 128 * t + 32 * q + lane;   // joint-input column
+                const float bj = __ldg(p.bias + ht * 128 + 2560 + j);
+                // every encoder-frame load before the accumulator wait (they
+                // overlap the GEMM) and before any store
+                float e[64];
+#pragma unroll
+                for (int jj = 0; jj < 64; ++jj) {
+                    const int pr = jj < nt ? tk[jj] : -1;
+                    e[jj] = pr >= 0 ? __ldg(p.pooler + static_cast<size_t>(pr) * 640 + j) : 0.f;
+                }
+                if ((ok = ws_acc())) {
+#pragma unroll
+                    for (int c0 = 0; c0 < 64; c0 += 32) {
+                        if (c0 >= nt) break;
+                        float v[32];
+                        acc32(q, c0, v);
+#pragma unroll
+                        for (int jj = 0; jj < 32; ++jj) {
+                            const int n = n0 + c0 + jj;
+                            if (n >= p.B) continue;
+                            const float x = tk[c0 + jj] >= 0 ? fmaxf(e[c0 + jj] + (bj + v[jj]), 0.f) : 0.f;
+                            split_store(ws_panel(p.aj, p.bpad, j, n, 0), ws_panel(p.aj, p.bpad, j, n, 1), x);
+                        }
+                    }
+                    tc_fence_before();
+                }
+            }
+        }
+        fence_async_global();
+        fail = __syncthreads_or(!ok);
+        if (!grid_barrier(sync, nb, target, fail, ok_smem, 0x77, p.grid_wait_ns)) break;
+    }
+    // Leaving (normally or on an abort between phases): the weight load and
+    // the last accumulator this CTA issued (a layer-0 tile's MMAs may still
+    // run when a barrier after phase 1 gave up) are waited for, bounded,
+    // before TMEM is freed.
+    if (warp == 1 && lane == 0) {
+        if (!wready) mbar_wait(smem_u32(wfull), 0, 0x78);
+        if (ng_mma > 0) mbar_wait(smem_u32(tfull), (ng_mma - 1) & 1, 0x79);
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc<kWsTmemCols>(tmem);
+    }
+}
+
 int check_launch(const char* what) {
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? 0 : set_cuda_error(what, e);
@@ -803,6 +1346,41 @@ int decoder_take_dev_error(cudaStream_t st, unsigned int* out) {
         e = cudaMemcpyToSymbolAsync(g_b3_dev_error, &zero, sizeof(unsigned int), 0, cudaMemcpyHostToDevice, st);
     if (e == cudaSuccess) e = cudaStreamSynchronize(st);
     return e == cudaSuccess ? 0 : set_cuda_error("reading the decoder device error word", e);
+}
+
+
+int dec_ws_grid(int device, int n_roles, int nsplit) {
+    static std::atomic<int> fits[64];   // 0 unknown, 1 yes, -1 no
+    static PerDeviceOnce attr;
+    if (device < 0 || device >= 64 || n_roles <= 0 || nsplit <= 0) return 0;
+    int f = fits[device].load(std::memory_order_acquire);
+    if (f == 0) {
+        int per_sm = 0;
+        f = -1;
+        if (!set_smem_limit_once(attr, k_dec_ws, static_cast<int>(kWsSmem), "cudaFuncSetAttribute(k_dec_ws)") &&
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_dec_ws, kWsThreads, kWsSmem) == cudaSuccess &&
+            per_sm >= 1)
+            f = 1;
+        fits[device].store(f, std::memory_order_release);
+    }
+    const int grid = n_roles * nsplit;
+    return f > 0 && grid <= device_sms() ? grid : 0;
+}
+
+int dec_ws_launch(const DecWsMaps& maps, const DecWs& p, int grid, cudaStream_t st) {
+    if (grid <= 0) return set_error(B3_ECUDA, "the weight-stationary decoder does not fit on this device");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kWsThreads);
+    cfg.dynamicSmemBytes = kWsSmem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const cudaError_t e = cudaLaunchKernelEx(&cfg, k_dec_ws, maps, p);
+    return e == cudaSuccess ? 0 : set_cuda_error("k_dec_ws", e);
 }
 
 int dec_launch_split(const float* src, __half* hi, __half* lo, int64_t n, cudaStream_t st) {

@@ -78,6 +78,18 @@ void* b3_stream(b3_ctx* ctx);
  * the wait run out without faulting anything. */
 int b3_set_wait_limit(b3_ctx* ctx, int64_t grid_barrier_ns);
 
+/* Which greedy-decoder kernel decodes a batch.  B3_DECODER_AUTO (the
+ * default): batches of up to 256 utterances run on the weight-stationary
+ * kernel (every CTA keeps one 128-row weight tile in shared memory for the
+ * whole decode; four grid barriers per lock step), larger ones on the
+ * split-K kernel.  B3_DECODER_SPLIT_K: every batch on the split-K kernel
+ * (weights streamed from L2 each step, six barriers per step).  Both follow
+ * the reference's greedy rule (src/tdt.rs:416-467); the choice changes speed,
+ * not the decoding rule. */
+#define B3_DECODER_AUTO 0
+#define B3_DECODER_SPLIT_K 1
+int b3_set_decoder(b3_ctx* ctx, int kind);
+
 /* ───────────────────────── weight loading ─────────────────────────
  * Tensors are pushed by the reference checkpoint's names, the way
  * Encoder::load_with pulls them from a WeightSource (src/weights.rs:22-36,

@@ -83,6 +83,36 @@ def test_decoder_matches_oracle(dec_model, syn, oracle):
     assert m >= MATCH
 
 
+@pytest.mark.parametrize("n_utt", [1, 100, 128, 129, 256])
+def test_weight_stationary_and_split_k_kernels_agree(dec_model, oracle, pkg, n_utt):
+    """Batches of up to 256 utterances decode on the weight-stationary kernel
+    (one 128-row weight tile resident per CTA, transposed GEMMs, argmax as
+    64-bit atomicMax keys; one half of CTAs up to 128 rows, two halves above);
+    b3_set_decoder(B3_DECODER_SPLIT_K) sends the same batch through the
+    split-K kernel.  Both against the oracle decoder on the same poolers,
+    and against each other."""
+    w, enc = dec_model
+    L = pkg.lib()
+    rng = np.random.default_rng(100 + n_utt)
+    lens = rng.integers(0, 61, size=n_utt)
+    lens[0] = 60
+    pooler = rng.normal(0, 1, size=(int(lens.sum()), 640)).astype(np.float32)
+    cu = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    ws = enc.decode_batch(pooler, cu)
+    pkg.check(L.b3_set_decoder(enc.ctx, pkg.B3_DECODER_SPLIT_K))
+    try:
+        sk = enc.decode_batch(pooler, cu)
+    finally:
+        pkg.check(L.b3_set_decoder(enc.ctx, pkg.B3_DECODER_AUTO))
+    want = oracle.OracleTdt(w).decode_batch(pooler, cu)
+    m_ws, ex_ws = token_match(ws, want)
+    m_sk, ex_sk = token_match(sk, want)
+    m_x, ex_x = token_match(ws, sk)
+    print(f"{n_utt} utterances, {sum(len(x) for x in want)} tokens: weight-stationary {m_ws:.4f} ({ex_ws:.2f} "
+          f"identical), split-K {m_sk:.4f} ({ex_sk:.2f}), between the two {m_x:.4f}")
+    assert m_ws >= MATCH and m_sk >= MATCH and m_x >= MATCH
+
+
 def test_large_batch_rows_per_cta(dec_model, oracle):
     """333 utterances: more rows than the persistent decoder has half-CTAs
     (2 per SM), so each walks several rows per phase; 3 row tiles of 128, the
