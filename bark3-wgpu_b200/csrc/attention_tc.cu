@@ -12,32 +12,39 @@
 // src/cpu/layer.rs:234-247); scores, softmax and O accumulate in f32.
 //
 // One CTA per (utterance, 128-query block, head); key blocks of 64.
-//   warp 0      TMA: Qu and Qv (staging) once; per key block K, V and the
-//               new rows of the R band into a 2-stage ring;
+//   warp 0      TMA: Qu and Qv once per item; per key block K, the new band
+//               chunk's 64 R rows and V, each in its own 2-stage ring;
 //   warp 1      TMEM owner; one thread issues the MMAs:
-//                 S  = Qu K^T      M128 N64  K128  (A: Qu in shared memory)
-//                 G  = Qv R_band^T M128 N192 K128  (three N64 pieces, A: Qv in TMEM)
-//                 O += P V         M128 N128 K64   (A: P in TMEM, B: V MN-major)
-//   warps 2..9  softmax, two warps per TMEM lane quarter: one query row per
-//               lane, each warp of a pair owns 32 of the block's 64 keys (and
-//               64 of O's 128 columns).  A thread reads its S columns and the
-//               band columns its warp spans, adds the row's diagonal of the
-//               band, and the pair exchanges row maxima through shared memory;
+//                 S  = Qu K^T       M128 N64  K128 (A: Qu in shared memory)
+//                 Gc = Qv R_chunk^T M128 N64  K128 (A: Qv in shared memory)
+//                 O += P V          M128 N128 K64  (A: P in TMEM, B: V MN-major)
+//   warps 2..17 softmax, four warps per TMEM lane quarter: one query row per
+//               lane, each warp of a quad owns 16 of the block's 64 keys (and
+//               32 of O's 128 columns).  A thread reads its S columns and the
+//               band columns its warp parks, adds the row's diagonal of the
+//               band, and the quad exchanges row maxima through shared memory;
 //               online softmax in f32 with a lazily moved reference max (O and
 //               l are rescaled only when the block max exceeds it by 2^8);
-//               P (f16) is written over the block's S columns.
+//               P (f16) is written over the block's S columns.  Four warps
+//               per quarter (not two) keep the dependent chain of each
+//               thread short enough that the special-function, shared-memory
+//               and tensor work of consecutive blocks overlap.
 // The band of a 128 x 64 score tile covers offsets q0-k0-63 .. q0-k0+127 (191
-// R rows, loaded as 192).  Consecutive key blocks share all but 64 of them,
-// so R rows live in a 256-row ring and each key block loads one 64-row chunk.
-// S is double-buffered in TMEM, so the S and G MMAs of the next key block run
-// while the softmax of this one is still working.
+// R rows, taken as 192 = three 64-row chunks).  Consecutive key blocks share
+// two of their three chunks, so the band lives in TMEM as a ring of four
+// 64-column chunk slots: block 0 of an item computes chunks 0, 1 and 2, every
+// later block only the one new chunk kb + 2 (each band product once, a third
+// of the band MMAs of computing all 192 columns per block).  With S double-
+// buffered and the fourth slot spare, the MMAs of block kb + 1 need only the
+// softmax of block kb - 1 to have read its columns, so the tensor pipe runs a
+// block ahead of the softmax instead of waiting for it every block.
 //
 // The diagonal read: row i of the tile needs band column 127 - i + j for key
 // j, a window whose start moves by one column per row.  TMEM loads address
 // the same columns for all lanes of a warp, so the rows' band columns are
-// parked in shared memory and each thread reads the 32 it needs back at its
-// own offset.  The two warps of a lane quarter share one parked row per query
-// (the 96 band columns the pair spans, 48 loaded and parked by each) and meet
+// parked in shared memory and each thread reads the 16 it needs back at its
+// own offset.  The four warps of a lane quarter share one parked row per query
+// (the 96 band columns the quad spans, 24 loaded and parked by each) and meet
 // on their mbarrier between parking and reading.
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -54,35 +61,31 @@ namespace {
 
 constexpr int kBQ = 128;          // queries per CTA
 constexpr int kBK = 64;           // keys per block
-constexpr int kThreads = 320;     // warp 0 TMA, warp 1 MMA, warps 2..9 softmax
-constexpr int kSoftThreads = 256;
-constexpr int kRing = 256;        // R ring rows
-constexpr int kShRows = 128;      // one parked row per query, shared by the pair of warps
-constexpr int kShStride = 130;    // floats per row: 96 band columns + 2 x 2 exchange slots (+ pad); a stride
+constexpr int kThreads = 576;     // warp 0 TMA, warp 1 MMA, warps 2..17 softmax
+constexpr int kShRows = 128;      // one parked row per query, shared by the quad of warps
+constexpr int kShStride = 130;    // floats per row: 96 band columns + 4 x 2 exchange slots (+ pad); a stride
                                   // of 2 mod 32 words keeps 8-byte stores and lane-shifted reads conflict-free
 
 // shared memory (offsets from a 1024-aligned base)
 constexpr uint32_t kQuOff = 0;                   // Qu: 2 dim-halves x (128 rows x 128 B)
-constexpr uint32_t kKOff = 32768;                // K: 2 stages x 2 halves x (64 rows x 128 B)
+constexpr uint32_t kQvOff = 32768;               // Qv: same (A operand of the band chunks)
+constexpr uint32_t kKOff = 65536;                // K: 2 stages x 2 halves x (64 rows x 128 B)
 constexpr uint32_t kVOff = kKOff + 32768;        // V: same
-constexpr uint32_t kROff = kVOff + 32768;        // R ring: 2 halves x (256 rows x 128 B)
-constexpr uint32_t kShOff = kROff + 65536;       // parked band rows 128 x 130 f32
+constexpr uint32_t kROff = kVOff + 32768;        // R chunks: same (64 R rows per chunk)
+constexpr uint32_t kShOff = kROff + 32768;       // parked band rows 128 x 130 f32
 constexpr uint32_t kBarOff = kShOff + kShRows * kShStride * 4;
-constexpr uint32_t kBarBytes = 160;                   // 19 mbarriers + the TMEM address
+constexpr uint32_t kBarBytes = 208;                   // 25 mbarriers + the TMEM address
 constexpr uint32_t kSmemMax = 232448;
 constexpr uint32_t kSmem = kSmemMax;
 constexpr uint32_t kAlignSlack = kSmemMax - kBarOff - kBarBytes;   // room to align the base to 1024 B
-static_assert(kBarOff + kBarBytes + 256 <= kSmemMax, "shared memory budget");
+static_assert(kBarOff + kBarBytes + 1024 <= kSmemMax, "shared memory budget");
 
 // TMEM columns
 constexpr uint32_t kTS = 0;       // S / P, 2 buffers x 64
-constexpr uint32_t kTG = 128;     // band, 192
-constexpr uint32_t kTO = 320;     // O, 128
-constexpr uint32_t kTQ = 448;     // Qv (A operand of the band GEMM), 64
+constexpr uint32_t kTG = 128;     // band ring: 4 chunks x 64 offsets (chunk c in slot c mod 4)
+constexpr uint32_t kTO = 384;     // O, 128
 
 constexpr uint32_t kIdescS = idesc_f16_f32_b<128, 64, 0>();
-constexpr uint32_t kIdescG192 = idesc_f16_f32_b<128, 192, 0>();
-constexpr uint32_t kIdescG128 = idesc_f16_f32_b<128, 128, 0>();
 constexpr uint32_t kIdescPV = idesc_f16_f32_b<128, 128, 1>();
 
 __device__ __forceinline__ uint32_t h2u(float a, float b) {
@@ -90,9 +93,9 @@ __device__ __forceinline__ uint32_t h2u(float a, float b) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// The two softmax warps of a lane quarter meet on their mbarrier (one arrival
-// per warp; a bounded wait, so a warp that left early ends its partner's wait
-// with an error instead of a hang).
+// The four softmax warps of a lane quarter meet on their mbarrier (one
+// arrival per warp; a bounded wait, so a warp that left early ends the
+// others' wait with an error instead of a hang).
 __device__ __forceinline__ bool pair_exchange(uint64_t* bar, int lane, uint32_t parity, unsigned int site) {
     __syncwarp();
     if (lane == 0) mbar_arrive(smem_u32(bar));
@@ -110,30 +113,36 @@ __global__ void __launch_bounds__(kThreads, 1)
         return;
     }
     uint8_t* sQu = smem + kQuOff;
+    uint8_t* sQv = smem + kQvOff;
     uint8_t* sK = smem + kKOff;
     uint8_t* sV = smem + kVOff;
     uint8_t* sR = smem + kROff;
     float* sSh = reinterpret_cast<float*>(smem + kShOff);
     uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kBarOff);
-    // K + R chunk and V have separate 2-stage rings: a K / R stage is free
-    // again once the S and band MMAs that read it are done, long before the
-    // P.V that frees its V stage, so the next loads start a softmax earlier.
-    // Every phase is counted over the CTA's whole run (g = key block, n =
-    // item, x = pair exchange), so the rings keep prefetching across items.
-    uint64_t* kr_full = bars;        // [2]
-    uint64_t* kr_empty = bars + 2;   // [2]
+    // K, R chunks and V have separate 2-stage rings: a K or R stage is free
+    // again once the MMA that read it is done, long before the P.V that frees
+    // its V stage.  Every phase is counted over the CTA's whole run (g = key
+    // block, rc = band chunk, n = item, x = quad exchange), so the rings keep
+    // prefetching across items.  sg_full, g_free and p_ready come in two
+    // copies (even and odd key blocks): the MMA issuer may run a block ahead
+    // of the slowest softmax warp and wait for a block two behind, and with
+    // one barrier per parity no barrier can complete twice before a waiter
+    // looks at it, so every parity wait is unambiguous.
+    uint64_t* k_full = bars;         // [2]
+    uint64_t* k_empty = bars + 2;    // [2]
     uint64_t* v_full = bars + 4;     // [2]
     uint64_t* v_empty = bars + 6;    // [2]
-    uint64_t* qld = bars + 8;        // Qu of item n in shared memory
-    uint64_t* q_tmem = bars + 9;     // Qv of item n in TMEM
-    uint64_t* sg_full = bars + 10;
-    uint64_t* g_free = bars + 11;
-    uint64_t* p_ready = bars + 12;
-    uint64_t* o_ready = bars + 13;   // every P.V (waited only when O is rescaled)
-    uint64_t* o_final = bars + 14;   // the last P.V of an item
-    uint64_t* xchg = bars + 15;      // [4] softmax warp pairs
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
-    static_assert(19 * 8 + 4 <= kBarBytes, "barrier area");
+    uint64_t* r_full = bars + 8;     // [2]
+    uint64_t* r_empty = bars + 10;   // [2]
+    uint64_t* qld = bars + 12;       // Qu and Qv of item n in shared memory
+    uint64_t* sg_full = bars + 13;   // [2] S and the band chunks of a block are in TMEM
+    uint64_t* g_free = bars + 15;    // [2] the softmax has read a block's S and band columns
+    uint64_t* p_ready = bars + 17;   // [2] a block's P is in TMEM
+    uint64_t* o_ready = bars + 19;   // every P.V (waited only when O is rescaled)
+    uint64_t* o_final = bars + 20;   // the last P.V of an item
+    uint64_t* xchg = bars + 21;      // [4] softmax warp quads (one per lane quarter)
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 25);
+    static_assert(25 * 8 + 4 <= kBarBytes, "barrier area");
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -143,19 +152,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_prefetch_desc(&tm_kv);
         tma_prefetch_desc(&tm_r);
         for (int s = 0; s < 2; ++s) {
-            mbar_init(smem_u32(&kr_full[s]), 1);
-            mbar_init(smem_u32(&kr_empty[s]), 1);
+            mbar_init(smem_u32(&k_full[s]), 1);
+            mbar_init(smem_u32(&k_empty[s]), 1);
             mbar_init(smem_u32(&v_full[s]), 1);
             mbar_init(smem_u32(&v_empty[s]), 1);
+            mbar_init(smem_u32(&r_full[s]), 1);
+            mbar_init(smem_u32(&r_empty[s]), 1);
+            mbar_init(smem_u32(&sg_full[s]), 1);
+            mbar_init(smem_u32(&g_free[s]), 16);
+            mbar_init(smem_u32(&p_ready[s]), 16);
         }
         mbar_init(smem_u32(qld), 1);
-        mbar_init(smem_u32(q_tmem), 8);
-        mbar_init(smem_u32(sg_full), 1);
-        mbar_init(smem_u32(g_free), 8);
-        mbar_init(smem_u32(p_ready), 8);
         mbar_init(smem_u32(o_ready), 1);
         mbar_init(smem_u32(o_final), 1);
-        for (int c = 0; c < 4; ++c) mbar_init(smem_u32(&xchg[c]), 2);
+        for (int c = 0; c < 4; ++c) mbar_init(smem_u32(&xchg[c]), 4);
         fence_mbar_init();
     }
     if (warp == 1) {
@@ -179,8 +189,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         it.T = p.cu[wk.x + 1] - it.seg0;
         it.q0 = wk.y;
         it.nkb = (it.T + kBK - 1) / kBK;
-        // band of key block kb: R rows [r_lo0 + 64 kb, r_lo0 + 64 kb + 191]; ring
-        // slot of R row r is (r - r_lo0) mod 256, so every 64-row chunk is contiguous
+        // band of key block kb: R rows [r_lo0 + 64 kb, r_lo0 + 64 kb + 191], the
+        // band chunks kb, kb + 1 and kb + 2 of 64 rows (chunk c = R rows
+        // [r_lo0 + 64 c, r_lo0 + 64 c + 64)); block 0 computes chunks 0..2,
+        // block kb >= 1 chunk kb + 2, so every band product is computed once
         it.r_lo0 = p.r_center - it.q0 - (kBQ - 1);
         return it;
     };
@@ -188,38 +200,41 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0) {
         // ── TMA producer ──
         if (lane == 0) {
-            int g0 = 0, n = 0;
+            int g0 = 0, rc = 0;
             bool ok = true;
-            for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++n) {
+            for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x) {
                 const Item it = item(i);
-                // Qu and the item's first R rows reuse shared memory that the previous
-                // item's last S / band MMAs read: wait for those (block g0 - 1)
-                if (g0 >= 1 && !(ok = mbar_wait(smem_u32(&kr_empty[(g0 - 1) & 1]), ((g0 - 1) >> 1) & 1, 0x20)))
+                // Qu and Qv are read by the previous item's last S and band MMAs,
+                // which complete before that block's K stage is released
+                if (g0 >= 1 && !(ok = mbar_wait(smem_u32(&k_empty[(g0 - 1) & 1]), ((g0 - 1) >> 1) & 1, 0x20)))
                     break;
                 const uint32_t qb = smem_u32(qld);
-                mbar_arrive_expect_tx(qb, 2 * 16384);
-                for (int h = 0; h < 2; ++h)
+                mbar_arrive_expect_tx(qb, 4 * 16384);
+                for (int h = 0; h < 2; ++h) {
                     tma_load_2d(smem_u32(sQu + h * 16384), &tm_q, qb, it.head * 128 + h * 64, it.seg0 + it.q0);
-                // in the order the MMAs need them: K / R of block kb, then V of kb - 1
-                for (int kb = 0; kb <= it.nkb; ++kb) {
+                    tma_load_2d(smem_u32(sQv + h * 16384), &tm_q, qb, 1024 + it.head * 128 + h * 64, it.seg0 + it.q0);
+                }
+                // in the order the MMAs need them: K of block kb, its band chunks, then V of kb - 1
+                for (int kb = 0; kb <= it.nkb && ok; ++kb) {
                     if (kb < it.nkb) {
                         const int g = g0 + kb, st = g & 1;
-                        if (g >= 2 && !(ok = mbar_wait(smem_u32(&kr_empty[st]), ((g >> 1) - 1) & 1, 0x21))) break;
-                        const int nchunks = kb == 0 ? 3 : 1;
-                        const uint32_t fb = smem_u32(&kr_full[st]);
-                        mbar_arrive_expect_tx(fb, 16384 + nchunks * 16384);
+                        if (g >= 2 && !(ok = mbar_wait(smem_u32(&k_empty[st]), ((g >> 1) - 1) & 1, 0x21))) break;
+                        const uint32_t fb = smem_u32(&k_full[st]);
+                        mbar_arrive_expect_tx(fb, 16384);
                         for (int h = 0; h < 2; ++h)
                             tma_load_2d(smem_u32(sK + st * 16384 + h * 8192), &tm_kv, fb,
                                         2048 + it.head * 128 + h * 64, it.seg0 + kb * kBK);
-                        for (int c = (kb == 0 ? 0 : 2); c < 3; ++c) {
-                            const int rel = kb * kBK + c * 64;            // band row - r_lo0
-                            const uint32_t slot = static_cast<uint32_t>(rel) & (kRing - 1);
+                        for (int c = (kb == 0 ? 0 : kb + 2); c <= kb + 2; ++c, ++rc) {
+                            const int rs = rc & 1;
+                            if (rc >= 2 && !(ok = mbar_wait(smem_u32(&r_empty[rs]), ((rc >> 1) - 1) & 1, 0x2E))) break;
+                            const uint32_t rb = smem_u32(&r_full[rs]);
+                            mbar_arrive_expect_tx(rb, 16384);
                             for (int h = 0; h < 2; ++h)
-                                tma_load_2d(smem_u32(sR + h * 32768 + slot * 128), &tm_r, fb, it.head * 128 + h * 64,
-                                            it.r_lo0 + rel);
+                                tma_load_2d(smem_u32(sR + rs * 16384 + h * 8192), &tm_r, rb, it.head * 128 + h * 64,
+                                            it.r_lo0 + c * 64);
                         }
                     }
-                    if (kb >= 1) {
+                    if (ok && kb >= 1) {
                         const int gv = g0 + kb - 1, st = gv & 1;
                         if (gv >= 2 && !(ok = mbar_wait(smem_u32(&v_empty[st]), ((gv >> 1) - 1) & 1, 0x2D))) break;
                         const uint32_t fb = smem_u32(&v_full[st]);
@@ -235,51 +250,54 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         // ── MMA issuer ──
         if (lane == 0) {
-            int g0 = 0, n = 0;
+            int g0 = 0, n = 0, rc = 0, cbase = 0;
             bool ok = true;
             for (int i = blockIdx.x; i < n_items && ok; i += gridDim.x, ++n) {
                 const Item it = item(i);
-                if (!(ok = mbar_wait(smem_u32(qld), n & 1, 0x22) && mbar_wait(smem_u32(q_tmem), n & 1, 0x23))) break;
+                if (!(ok = mbar_wait(smem_u32(qld), n & 1, 0x22))) break;
+                const uint64_t aq0 = smem_desc_sw128(smem_u32(sQu));
+                const uint64_t aq1 = smem_desc_sw128(smem_u32(sQu + 16384));
+                const uint64_t av0 = smem_desc_sw128(smem_u32(sQv));
+                const uint64_t av1 = smem_desc_sw128(smem_u32(sQv + 16384));
                 for (int kb = 0; kb <= it.nkb && ok; ++kb) {
                     if (kb < it.nkb) {
                         const int g = g0 + kb, st = g & 1;
-                        if (!(ok = mbar_wait(smem_u32(&kr_full[st]), (g >> 1) & 1, 0x24))) break;
-                        if (g >= 1 && !(ok = mbar_wait(smem_u32(g_free), (g - 1) & 1, 0x25))) break;
+                        if (!(ok = mbar_wait(smem_u32(&k_full[st]), (g >> 1) & 1, 0x24))) break;
+                        // TMEM this block writes is free: S buffer st held P of block g - 2
+                        // (its P.V was issued before, MMAs run in order); the band slot of
+                        // chunk c held chunk c - 4, last read by block g - 2 (block g - 1
+                        // too when this is an item's first block, which writes three)
+                        const int gw = kb == 0 ? g - 1 : g - 2;
+                        if (gw >= 0 && !(ok = mbar_wait(smem_u32(&g_free[gw & 1]), (gw >> 1) & 1, 0x25))) break;
                         tc_fence_after();
                         const uint32_t dS = tmem + kTS + 64 * st;
                         // descriptors advance by 32 bytes (2 in the start-address field) per k-step
-                        const uint64_t aq0 = smem_desc_sw128(smem_u32(sQu));
-                        const uint64_t aq1 = smem_desc_sw128(smem_u32(sQu + 16384));
                         const uint64_t bk0 = smem_desc_sw128(smem_u32(sK + st * 16384));
                         const uint64_t bk1 = smem_desc_sw128(smem_u32(sK + st * 16384 + 8192));
 #pragma unroll
                         for (int kk = 0; kk < 8; ++kk)
                             mma_f16_ss(dS, (kk < 4 ? aq0 : aq1) + 2 * (kk & 3), (kk < 4 ? bk0 : bk1) + 2 * (kk & 3),
                                        kIdescS, kk > 0);
-                        // band rows [64 kb, 64 kb + 192) of the ring: one N192 piece when contiguous,
-                        // else N128 + N64 or N64 + N128 around the wrap
-                        const uint32_t s0 = static_cast<uint32_t>(kb * kBK) & (kRing - 1);
-                        const int n1 = s0 <= kRing - 192 ? 192 : static_cast<int>(kRing - s0);
-                        const uint64_t br0 = smem_desc_sw128(smem_u32(sR + s0 * 128));
-                        const uint64_t br1 = smem_desc_sw128(smem_u32(sR + 32768 + s0 * 128));
-#pragma unroll
-                        for (int kk = 0; kk < 8; ++kk)
-                            mma_f16_ts(tmem + kTG, tmem + kTQ + 8 * kk, (kk < 4 ? br0 : br1) + 2 * (kk & 3),
-                                       n1 == 192 ? kIdescG192 : (n1 == 128 ? kIdescG128 : kIdescS), kk > 0);
-                        if (n1 < 192) {
-                            const uint64_t bw0 = smem_desc_sw128(smem_u32(sR));
-                            const uint64_t bw1 = smem_desc_sw128(smem_u32(sR + 32768));
+                        for (int c = (kb == 0 ? 0 : kb + 2); c <= kb + 2 && ok; ++c, ++rc) {
+                            const int rs = rc & 1;
+                            if (!(ok = mbar_wait(smem_u32(&r_full[rs]), (rc >> 1) & 1, 0x2F))) break;
+                            tc_fence_after();
+                            const uint32_t dG = tmem + kTG + 64 * ((cbase + c) & 3);
+                            const uint64_t br0 = smem_desc_sw128(smem_u32(sR + rs * 16384));
+                            const uint64_t br1 = smem_desc_sw128(smem_u32(sR + rs * 16384 + 8192));
 #pragma unroll
                             for (int kk = 0; kk < 8; ++kk)
-                                mma_f16_ts(tmem + kTG + n1, tmem + kTQ + 8 * kk, (kk < 4 ? bw0 : bw1) + 2 * (kk & 3),
-                                           n1 == 128 ? kIdescS : kIdescG128, kk > 0);
+                                mma_f16_ss(dG, (kk < 4 ? av0 : av1) + 2 * (kk & 3), (kk < 4 ? br0 : br1) + 2 * (kk & 3),
+                                           kIdescS, kk > 0);
+                            mma_commit(smem_u32(&r_empty[rs]));
                         }
-                        mma_commit(smem_u32(sg_full));
-                        mma_commit(smem_u32(&kr_empty[st]));
+                        if (!ok) break;
+                        mma_commit(smem_u32(&sg_full[st]));
+                        mma_commit(smem_u32(&k_empty[st]));
                     }
                     if (kb >= 1) {
                         const int j = kb - 1, gj = g0 + j, st = gj & 1;
-                        if (!(ok = mbar_wait(smem_u32(p_ready), gj & 1, 0x26))) break;
+                        if (!(ok = mbar_wait(smem_u32(&p_ready[gj & 1]), (gj >> 1) & 1, 0x26))) break;
                         if (!(ok = mbar_wait(smem_u32(&v_full[st]), (gj >> 1) & 1, 0x2E))) break;
                         tc_fence_after();
                         // V [64 keys][128 dims] as the MN-major B operand: 64-dim halves 8 KB
@@ -295,117 +313,91 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
                 g0 += it.nkb;
+                cbase += it.nkb + 2;
             }
         }
     } else {
-        // ── softmax: warps 2..9, pair (q, hf): lane quarter q, key half hf ──
+        // ── softmax: warps 2..17, quad (q, ks): lane quarter q, keys [16 ks, 16 ks + 16) ──
         const int q = warp & 3;
-        const int hf = (warp - 2) >> 2;
+        const int ks = (warp - 2) >> 2;
         const int i = q * 32 + lane;                   // query row / TMEM lane
         const uint32_t lrow = static_cast<uint32_t>(q * 32) << 16;
-        float* sh = sSh + i * kShStride;               // this query's parked row (both warps of the pair)
-        float* xmine = sh + 96 + 2 * hf;               // exchange slots, by exchange parity
-        const float* xpeer = sh + 96 + 2 * (hf ^ 1);
-        // Qv row i, dim half hf of an item, from global memory (rows past the
-        // utterance read its last row: their results are never stored)
-        auto load_qv = [&](const Item& it, uint32_t (&r)[32]) {
-            const int row = it.q0 + i < it.T ? it.q0 + i : it.T - 1;
-            const uint4* src = reinterpret_cast<const uint4*>(p.qkv + static_cast<size_t>(it.seg0 + row) * 4096 + 1024 +
-                                                              it.head * 128 + 64 * hf);
-#pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                const uint4 v = __ldg(src + c);
-                r[4 * c] = v.x;
-                r[4 * c + 1] = v.y;
-                r[4 * c + 2] = v.z;
-                r[4 * c + 3] = v.w;
-            }
+        float* sh = sSh + i * kShStride;               // this query's parked row (all four warps of the quad)
+        float* xslot = sh + 96;                        // exchange slots [4 warps][2 parities]
+        // the four warps of the quad meet: every slot of parity `par` written
+        auto quad_sum = [&](int par) {
+            return ((xslot[par] + xslot[2 + par]) + xslot[4 + par]) + xslot[6 + par];
         };
-        auto store_qv = [&](const uint32_t (&r)[32]) {
-            tmem_st_32x32b_x32(tmem + lrow + kTQ + 32 * hf, r);
-            tmem_wait_st();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(smem_u32(q_tmem));
+        auto quad_max = [&](int par) {
+            return fmaxf(fmaxf(xslot[par], xslot[2 + par]), fmaxf(xslot[4 + par], xslot[6 + par]));
         };
         bool ok = true;
-        int g0 = 0, n = 0, x = 0;
-        if (static_cast<int>(blockIdx.x) < n_items) {
-            uint32_t r[32];
-            load_qv(item(blockIdx.x), r);
-            store_qv(r);
-        }
+        int g0 = 0, n = 0, x = 0, cbase = 0;
         for (int ii = blockIdx.x; ii < n_items && ok; ii += gridDim.x, ++n) {
             const Item it = item(ii);
-            const bool has_next = ii + static_cast<int>(gridDim.x) < n_items;
             // m_use: the max the row's exponentials are taken against.  It moves
             // (and O, l are rescaled) only when a block's max exceeds it by more
-            // than kRescale (log2 units), for the pair of warps as a whole; in
+            // than kRescale (log2 units), for the quad of warps as a whole; in
             // between, probabilities up to 2^kRescale are exact in f32 l and in
             // the f16 P operand.
             constexpr float kRescale = 8.0f;
-            float m_use = -INFINITY, l_half = 0.f;
+            float m_use = -INFINITY, l_part = 0.f;
             for (int kb = 0; kb < it.nkb && ok; ++kb) {
                 const int g = g0 + kb, st = g & 1;
-                const bool handoff = kb == it.nkb - 1 && has_next;
-                uint32_t qn[32];   // the next item's Qv row (last block only)
-                if (handoff) load_qv(item(ii + gridDim.x), qn);
-                if (!(ok = mbar_wait(smem_u32(sg_full), g & 1, 0x28))) break;
+                if (!(ok = mbar_wait(smem_u32(&sg_full[g & 1]), (g >> 1) & 1, 0x28))) break;
                 tc_fence_after();
-                // every band MMA of this item is done (sg_full of its last block
-                // passed): the next item's Qv replaces this one in TMEM, so the
-                // next item's S / band MMAs run under this block's softmax
-                if (handoff) store_qv(qn);
-                float s[32];
+                float s[16];
                 {
-                    // S columns [32 hf, 32 hf + 32); the pair's band window is columns
-                    // [96 - 32q, 192 - 32q), of which this warp loads [48 hf, 48 hf + 48)
-                    uint32_t r0[32], g0r[32], g1r[16];
-                    tmem_ld_32x32b_x32(tmem + lrow + kTS + 64 * st + 32 * hf, r0);
-                    tmem_ld_32x32b_x32(tmem + lrow + kTG + 96 - 32 * q + 48 * hf, g0r);
-                    tmem_ld_32x32b_x16(tmem + lrow + kTG + 128 - 32 * q + 48 * hf, g1r);
+                    // S columns [16 ks, 16 ks + 16); the quad's band window is band
+                    // columns [96 - 32q, 192 - 32q) (chunks kb .. kb + 2), of which this
+                    // warp loads [24 ks, 24 ks + 24); band column w sits in ring column
+                    // (64 (cbase + kb) + w) mod 256, and an 8-column load never wraps
+                    uint32_t r0[16], gr[24];
+                    const int w0 = 96 - 32 * q + 24 * ks;
+                    auto ring = [&](int w) { return kTG + ((64 * (cbase + kb) + w) & 255); };
+                    tmem_ld_32x32b_x16(tmem + lrow + kTS + 64 * st + 16 * ks, r0);
+                    tmem_ld_32x32b_x8(tmem + lrow + ring(w0), *reinterpret_cast<uint32_t(*)[8]>(gr));
+                    tmem_ld_32x32b_x8(tmem + lrow + ring(w0 + 8), *reinterpret_cast<uint32_t(*)[8]>(gr + 8));
+                    tmem_ld_32x32b_x8(tmem + lrow + ring(w0 + 16), *reinterpret_cast<uint32_t(*)[8]>(gr + 16));
                     tmem_wait_ld();
                     tc_fence_before();
                     __syncwarp();
-                    if (lane == 0) mbar_arrive(smem_u32(g_free));
+                    if (lane == 0) mbar_arrive(smem_u32(&g_free[g & 1]));
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) s[e] = __uint_as_float(r0[e]);
-                    // window columns [48 hf, 48 hf + 48) as 8-byte stores: with the row
+                    for (int e = 0; e < 16; ++e) s[e] = __uint_as_float(r0[e]);
+                    // window columns [24 ks, 24 ks + 24) as 8-byte stores: with the row
                     // stride of 2 mod 32 words a half-warp's stores cover all 32 banks
-                    float* wp = sh + 48 * hf;
+                    float* wp = sh + 24 * ks;
 #pragma unroll
-                    for (int e = 0; e < 32; e += 2) *reinterpret_cast<uint2*>(wp + e) = make_uint2(g0r[e], g0r[e + 1]);
-#pragma unroll
-                    for (int e = 0; e < 16; e += 2)
-                        *reinterpret_cast<uint2*>(wp + 32 + e) = make_uint2(g1r[e], g1r[e + 1]);
+                    for (int e = 0; e < 24; e += 2) *reinterpret_cast<uint2*>(wp + e) = make_uint2(gr[e], gr[e + 1]);
                 }
-                // the partner's half of the window is parked too
+                // the other warps' parts of the window are parked too
                 if (!(ok = pair_exchange(&xchg[q], lane, x & 1, 0x27))) break;
                 ++x;
-                // row i, key 32 hf + j: band column 127 - i + 32 hf + j = window column
-                // 32 hf + 31 - lane + j; across a warp the word index moves by 129 per
+                // row i, key 16 ks + j: band column 127 - i + 16 ks + j = window column
+                // 16 ks + 31 - lane + j; across a warp the word index moves by 129 per
                 // lane: no conflicts
-                const float* dg = sh + 32 * hf + 31 - lane;
-                const int kvalid = it.T - kb * kBK - 32 * hf;
+                const float* dg = sh + 16 * ks + 31 - lane;
+                const int kvalid = it.T - kb * kBK - 16 * ks;
                 const float2 sc2 = make_float2(p.scale_log2, p.scale_log2);
 #pragma unroll
-                for (int j = 0; j < 32; j += 2) {
+                for (int j = 0; j < 16; j += 2) {
                     const float2 v = __fmul2_rn(__fadd2_rn(make_float2(s[j], s[j + 1]), make_float2(dg[j], dg[j + 1])), sc2);
                     s[j] = v.x;
                     s[j + 1] = v.y;
                 }
-                if (kvalid < 32) {   // warp-uniform: only an utterance's last key block has keys past its end
+                if (kvalid < 16) {   // warp-uniform: only an utterance's last key block has keys past its end
 #pragma unroll
-                    for (int j = 0; j < 32; ++j)
+                    for (int j = 0; j < 16; ++j)
                         if (j >= kvalid) s[j] = -INFINITY;
                 }
                 float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-                for (int j = 0; j < 32; ++j) mx[j & 3] = fmaxf(mx[j & 3], s[j]);
+                for (int j = 0; j < 16; ++j) mx[j & 3] = fmaxf(mx[j & 3], s[j]);
                 const float mloc = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
-                xmine[x & 1] = mloc;
+                xslot[2 * ks + (x & 1)] = mloc;
                 if (!(ok = pair_exchange(&xchg[q], lane, x & 1, 0x2B))) break;
-                const float m_blk = fmaxf(mloc, xpeer[x & 1]);
+                const float m_blk = quad_max(x & 1);
                 ++x;
                 const bool grow = m_blk > m_use + kRescale;
                 float corr = 1.f;
@@ -414,53 +406,47 @@ __global__ void __launch_bounds__(kThreads, 1)
                     corr = exp2f(m_use - m_new);   // 0 for the first block
                     m_use = m_new;
                     if (kb >= 1) {
-                        // O columns [64 hf, 64 hf + 64) (after P_{g-1} V) *= corr.
+                        // O columns [32 ks, 32 ks + 32) (after P_{g-1} V) *= corr.
                         // Passing sg_full(g) implies P_{g-2} V is done and P_g V is not
                         // issued yet, so o_ready is at phase g-1 or g: the parity is exact.
                         if (!(ok = mbar_wait(smem_u32(o_ready), (g - 1) & 1, 0x29))) break;
                         tc_fence_after();
-                        uint32_t o0[32], o1[32];
-                        tmem_ld_32x32b_x32(tmem + lrow + kTO + 64 * hf, o0);
-                        tmem_ld_32x32b_x32(tmem + lrow + kTO + 64 * hf + 32, o1);
+                        uint32_t o0[32];
+                        tmem_ld_32x32b_x32(tmem + lrow + kTO + 32 * ks, o0);
                         tmem_wait_ld();
 #pragma unroll
-                        for (int e = 0; e < 32; ++e) {
-                            o0[e] = __float_as_uint(__uint_as_float(o0[e]) * corr);
-                            o1[e] = __float_as_uint(__uint_as_float(o1[e]) * corr);
-                        }
-                        tmem_st_32x32b_x32(tmem + lrow + kTO + 64 * hf, o0);
-                        tmem_st_32x32b_x32(tmem + lrow + kTO + 64 * hf + 32, o1);
+                        for (int e = 0; e < 32; ++e) o0[e] = __float_as_uint(__uint_as_float(o0[e]) * corr);
+                        tmem_st_32x32b_x32(tmem + lrow + kTO + 32 * ks, o0);
                     }
                 }
                 float2 ls[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-                uint32_t pk[16];
+                uint32_t pk[8];
                 const float2 mneg = make_float2(-m_use, -m_use);
 #pragma unroll
-                for (int j = 0; j < 32; j += 2) {
-                    const float2 x = __fadd2_rn(make_float2(s[j], s[j + 1]), mneg);
-                    const float2 e = make_float2(exp2f(x.x), exp2f(x.y));
+                for (int j = 0; j < 16; j += 2) {
+                    const float2 xv = __fadd2_rn(make_float2(s[j], s[j + 1]), mneg);
+                    const float2 e = make_float2(exp2f(xv.x), exp2f(xv.y));
                     ls[(j >> 1) & 1] = __fadd2_rn(ls[(j >> 1) & 1], e);
                     pk[j >> 1] = h2u(e.x, e.y);
                 }
-                l_half = l_half * corr + ((ls[0].x + ls[0].y) + (ls[1].x + ls[1].y));
-                tmem_st_32x32b_x16(tmem + lrow + kTS + 64 * st + 16 * hf, pk);   // P over this block's S columns
+                l_part = l_part * corr + ((ls[0].x + ls[0].y) + (ls[1].x + ls[1].y));
+                tmem_st_32x32b_x8(tmem + lrow + kTS + 64 * st + 8 * ks, pk);   // P over this block's S columns
                 tmem_wait_st();
                 tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(smem_u32(p_ready));
+                if (lane == 0) mbar_arrive(smem_u32(&p_ready[g & 1]));
             }
-            // ── O / l -> f16 row, columns [64 hf, 64 hf + 64) ──
+            // ── O / l -> f16 row, columns [32 ks, 32 ks + 32) ──
             if (ok && mbar_wait(smem_u32(o_final), n & 1, 0x2A)) {
                 tc_fence_after();
-                xmine[x & 1] = l_half;
+                xslot[2 * ks + (x & 1)] = l_part;
                 const bool xok = pair_exchange(&xchg[q], lane, x & 1, 0x2C);
-                const float inv = 1.0f / (l_half + xpeer[x & 1]);
+                const float inv = 1.0f / quad_sum(x & 1);
                 ++x;
                 const bool store = xok && it.q0 + i < it.T;
-                __half* dst = p.out + static_cast<size_t>(it.seg0 + it.q0 + i) * 1024 + it.head * 128 + 64 * hf;
-                uint32_t o0[32], o1[32];
-                tmem_ld_32x32b_x32(tmem + lrow + kTO + 64 * hf, o0);
-                tmem_ld_32x32b_x32(tmem + lrow + kTO + 64 * hf + 32, o1);
+                __half* dst = p.out + static_cast<size_t>(it.seg0 + it.q0 + i) * 1024 + it.head * 128 + 32 * ks;
+                uint32_t o0[32];
+                tmem_ld_32x32b_x32(tmem + lrow + kTO + 32 * ks, o0);
                 tmem_wait_ld();
                 if (store) {
 #pragma unroll
@@ -470,11 +456,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                                        h2u(__uint_as_float(o0[e + 2]) * inv, __uint_as_float(o0[e + 3]) * inv),
                                        h2u(__uint_as_float(o0[e + 4]) * inv, __uint_as_float(o0[e + 5]) * inv),
                                        h2u(__uint_as_float(o0[e + 6]) * inv, __uint_as_float(o0[e + 7]) * inv));
-                        *reinterpret_cast<uint4*>(dst + 32 + e) =
-                            make_uint4(h2u(__uint_as_float(o1[e]) * inv, __uint_as_float(o1[e + 1]) * inv),
-                                       h2u(__uint_as_float(o1[e + 2]) * inv, __uint_as_float(o1[e + 3]) * inv),
-                                       h2u(__uint_as_float(o1[e + 4]) * inv, __uint_as_float(o1[e + 5]) * inv),
-                                       h2u(__uint_as_float(o1[e + 6]) * inv, __uint_as_float(o1[e + 7]) * inv));
                     }
                 }
                 tc_fence_before();
@@ -483,6 +464,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 ok = false;
             }
             g0 += it.nkb;
+            cbase += it.nkb + 2;
         }
     }
 
