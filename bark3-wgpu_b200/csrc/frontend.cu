@@ -218,51 +218,89 @@ constexpr int kC0S = 65;           // conv0 row of one channel: cols -1..63
 constexpr int kC0Row = kC * kC0S;  // one conv0 row of all kC channels
 constexpr int kSubSmem = (kTm * kMelS + kT1 * kC0Row) * 4;
 
-__global__ void __launch_bounds__(256, 2) k_sub_conv0_dw1(SubParams p, int w0) {
+// Persistent: CTA b walks work items w0 + b, w0 + b + gridDim.x, ... up to
+// w1.  Items are (utterance, t2 row block, channel group) with the group
+// fastest and a multiple of 8 items per utterance, and the grid is a
+// multiple of 8, so a CTA keeps one channel group: its conv0 and conv1 taps
+// stay in registers for the whole launch, and the next item's mel rows are
+// loaded into registers while the current item computes.
+__global__ void __launch_bounds__(256, 2) k_sub_conv0_dw1(SubParams p, int w0, int w1) {
     extern __shared__ float sub_smem[];
     float* mel = sub_smem;                 // [kTm][kMelS]
     float* c0 = sub_smem + kTm * kMelS;    // [kT1][kC][kC0S]
-    const int4 wk = p.work[w0 + blockIdx.x];   // (utterance, t2_0, channel group)
-    const int u = wk.x, t2_0 = wk.y, cg = wk.z * kC;
-    const int F = p.mel_off[u + 1] - p.mel_off[u];
-    const int F1 = conv_len_d(F), F2 = conv_len_d(F1);
-    const int nvalid = p.n_valid[u];
-    const int v1 = conv_len_d(nvalid > 1 ? nvalid : 1);
-    const int v2 = conv_len_d(v1);
-    const float* melu = p.mel + static_cast<size_t>(p.mel_off[u]) * kMel;
-    const int t1_0 = 2 * t2_0 - 1;      // first conv0 row
-    const int tm_0 = 2 * t1_0 - 1;      // first mel row
-    // 16-byte loads of mel columns 4 c .. 4 c + 3: the even pair goes to even
-    // slots 2 c, 2 c + 1 and the odd pair to odd slots 66 + 2 c, 67 + 2 c
-    for (int i = threadIdx.x; i < kTm * (kMel / 4); i += blockDim.x) {
-        const int r = i >> 5, c = i & 31;
-        const int tm = tm_0 + r;
-        const float4 v = (tm >= 0 && tm < F)
-                             ? __ldg(reinterpret_cast<const float4*>(melu + static_cast<size_t>(tm) * kMel) + c)
-                             : make_float4(0.f, 0.f, 0.f, 0.f);
-        *reinterpret_cast<float2*>(mel + r * kMelS + 2 * c) = make_float2(v.x, v.z);
-        *reinterpret_cast<float2*>(mel + r * kMelS + 66 + 2 * c) = make_float2(v.y, v.w);
-    }
-    if (threadIdx.x < kTm) {
-        mel[threadIdx.x * kMelS + 64] = 0.f;   // even col 128 (never read)
-        mel[threadIdx.x * kMelS + 65] = 0.f;   // col -1
-    }
-    for (int i = threadIdx.x; i < kT1 * kC; i += blockDim.x) c0[i * kC0S] = 0.f;  // col -1
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    {
-        // conv0: warp w owns channels 8 (w & 3) .. +8 as 4 channel pairs (one
-        // packed f32x2 FMA per pair and tap) over columns 32 (w >> 2) + lane
-        const int cq = (warp & 3) * 8;
-        const int j = (warp >> 2) * 32 + lane;
-        float2 w[4][9], bias[4];
+    int e = w0 + blockIdx.x;
+    if (e >= w1) return;
+    const int cg = p.work[e].z * kC;
+    // conv0 taps: warp w owns channels 8 (w & 3) .. +8 as 4 channel pairs (one
+    // packed f32x2 FMA per pair and tap) over columns 32 (w >> 2) + lane
+    const int cq = (warp & 3) * 8;
+    const int j = (warp >> 2) * 32 + lane;
+    float2 w[4][9], bias[4];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            bias[q] = make_float2(__ldg(p.b0 + cg + cq + 2 * q), __ldg(p.b0 + cg + cq + 2 * q + 1));
+    for (int q = 0; q < 4; ++q) {
+        bias[q] = make_float2(__ldg(p.b0 + cg + cq + 2 * q), __ldg(p.b0 + cg + cq + 2 * q + 1));
 #pragma unroll
-            for (int t = 0; t < 9; ++t)
-                w[q][t] = make_float2(__ldg(p.w0 + (cg + cq + 2 * q) * 9 + t), __ldg(p.w0 + (cg + cq + 2 * q + 1) * 9 + t));
+        for (int t = 0; t < 9; ++t)
+            w[q][t] = make_float2(__ldg(p.w0 + (cg + cq + 2 * q) * 9 + t), __ldg(p.w0 + (cg + cq + 2 * q + 1) * 9 + t));
+    }
+    // conv1 taps: a lane per channel
+    float wd[9];
+#pragma unroll
+    for (int t = 0; t < 9; ++t) wd[t] = __ldg(p.w2 + (cg + lane) * 9 + t);
+    const float bias2 = __ldg(p.b2 + cg + lane);
+    // padding that no item overwrites: mel column slots 64 (even col 128,
+    // never read) and 65 (col -1); conv0 column -1
+    if (threadIdx.x < kTm) {
+        mel[threadIdx.x * kMelS + 64] = 0.f;
+        mel[threadIdx.x * kMelS + 65] = 0.f;
+    }
+    for (int i = threadIdx.x; i < kT1 * kC; i += blockDim.x) c0[i * kC0S] = 0.f;
+    // an item's mel rows, 16-byte loads of columns 4 c .. 4 c + 3 (three per thread)
+    constexpr int kLoads = (kTm * (kMel / 4) + 255) / 256;
+    float4 pre[kLoads];
+    auto fetch = [&](int item) {
+        const int4 wk = p.work[item];
+        const int F = p.mel_off[wk.x + 1] - p.mel_off[wk.x];
+        const int tm_0 = 2 * (2 * wk.y - 1) - 1;
+        const float* melu = p.mel + static_cast<size_t>(p.mel_off[wk.x]) * kMel;
+#pragma unroll
+        for (int k = 0; k < kLoads; ++k) {
+            const int i = threadIdx.x + 256 * k;
+            const int r = i >> 5, c = i & 31;
+            const int tm = tm_0 + r;
+            pre[k] = (i < kTm * (kMel / 4) && tm >= 0 && tm < F)
+                         ? __ldg(reinterpret_cast<const float4*>(melu + static_cast<size_t>(tm) * kMel) + c)
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
         }
-        __syncthreads();
+    };
+    // the even pair of a load goes to even slots 2 c, 2 c + 1, the odd pair
+    // to odd slots 66 + 2 c, 67 + 2 c
+    auto park = [&]() {
+#pragma unroll
+        for (int k = 0; k < kLoads; ++k) {
+            const int i = threadIdx.x + 256 * k;
+            if (i < kTm * (kMel / 4)) {
+                const int r = i >> 5, c = i & 31;
+                *reinterpret_cast<float2*>(mel + r * kMelS + 2 * c) = make_float2(pre[k].x, pre[k].z);
+                *reinterpret_cast<float2*>(mel + r * kMelS + 66 + 2 * c) = make_float2(pre[k].y, pre[k].w);
+            }
+        }
+    };
+    fetch(e);
+    park();
+    for (; e < w1; e += gridDim.x) {
+        const int4 wk = p.work[e];   // (utterance, t2_0, channel group)
+        const int u = wk.x, t2_0 = wk.y;
+        const int F = p.mel_off[u + 1] - p.mel_off[u];
+        const int F1 = conv_len_d(F), F2 = conv_len_d(F1);
+        const int nvalid = p.n_valid[u];
+        const int v1 = conv_len_d(nvalid > 1 ? nvalid : 1);
+        const int v2 = conv_len_d(v1);
+        const int t1_0 = 2 * t2_0 - 1;      // first conv0 row
+        __syncthreads();                     // this item's mel rows are parked
+        const int next = e + static_cast<int>(gridDim.x);
+        if (next < w1) fetch(next);          // lands while this item computes
         for (int r = 0; r < kT1; ++r) {
             const int t1 = t1_0 + r;
             const bool live = t1 >= 0 && t1 < F1 && t1 < v1;
@@ -291,42 +329,40 @@ __global__ void __launch_bounds__(256, 2) k_sub_conv0_dw1(SubParams p, int w0) {
                 out[(2 * q + 1) * kC0S] = live ? fmaxf(acc[q].y, 0.f) : 0.f;
             }
         }
-    }
-    __syncthreads();
-    {
-        // depthwise conv: a lane per channel, warps walk (row, 16-column run)
-        // two output columns at a time as one packed f32x2 FMA per tap
-        const int c = lane;
-        float w[9];
+        __syncthreads();
+        {
+            // depthwise conv: a lane per channel, warps walk (row, 16-column run)
+            // two output columns at a time as one packed f32x2 FMA per tap
+            const int r2 = warp >> 1, jb = (warp & 1) * 16;
+            const int t2 = t2_0 + r2;
+            if (t2 < F2) {
+                const bool live = t2 < v2;
+                // conv0 local rows 2 r2 + ki hold t1 = 2 t2 - 1 + ki; index 1 + col
+                const float* base = c0 + (2 * r2 * kC + lane) * kC0S;
+                __half* out = p.x2 + static_cast<size_t>(p.x2_off[u] + t2) * 32 * 256 + cg + lane;
+                float prev[3];
 #pragma unroll
-        for (int t = 0; t < 9; ++t) w[t] = __ldg(p.w2 + (cg + c) * 9 + t);
-        const float bias = __ldg(p.b2 + cg + c);
-        const int r2 = warp >> 1, jb = (warp & 1) * 16;
-        const int t2 = t2_0 + r2;
-        if (t2 >= F2) return;
-        const bool live = t2 < v2;
-        // conv0 local rows 2 r2 + ki hold t1 = 2 t2 - 1 + ki; index 1 + col
-        const float* base = c0 + (2 * r2 * kC + c) * kC0S;
-        __half* out = p.x2 + static_cast<size_t>(p.x2_off[u] + t2) * 32 * 256 + cg + c;
-        float prev[3];
-#pragma unroll
-        for (int ki = 0; ki < 3; ++ki) prev[ki] = base[ki * kC0Row + 2 * jb];   // col 2 jb - 1
+                for (int ki = 0; ki < 3; ++ki) prev[ki] = base[ki * kC0Row + 2 * jb];   // col 2 jb - 1
 #pragma unroll 2
-        for (int jj = 0; jj < 16; jj += 2) {
-            const int j2 = jb + jj;   // outputs j2 (cols 2j2-1..2j2+1) and j2+1 (cols 2j2+1..2j2+3)
-            float2 s = make_float2(bias, bias);
+                for (int jj = 0; jj < 16; jj += 2) {
+                    const int j2 = jb + jj;   // outputs j2 (cols 2j2-1..2j2+1) and j2+1 (cols 2j2+1..2j2+3)
+                    float2 s = make_float2(bias2, bias2);
 #pragma unroll
-            for (int ki = 0; ki < 3; ++ki) {
-                const float* row = base + ki * kC0Row;
-                const float x0 = row[2 * j2 + 1], x1 = row[2 * j2 + 2], x2 = row[2 * j2 + 3], x3 = row[2 * j2 + 4];
-                s = __ffma2_rn(make_float2(w[ki * 3], w[ki * 3]), make_float2(prev[ki], x1), s);
-                s = __ffma2_rn(make_float2(w[ki * 3 + 1], w[ki * 3 + 1]), make_float2(x0, x2), s);
-                s = __ffma2_rn(make_float2(w[ki * 3 + 2], w[ki * 3 + 2]), make_float2(x1, x3), s);
-                prev[ki] = x3;
+                    for (int ki = 0; ki < 3; ++ki) {
+                        const float* row = base + ki * kC0Row;
+                        const float x0 = row[2 * j2 + 1], x1 = row[2 * j2 + 2], x2 = row[2 * j2 + 3], x3 = row[2 * j2 + 4];
+                        s = __ffma2_rn(make_float2(wd[ki * 3], wd[ki * 3]), make_float2(prev[ki], x1), s);
+                        s = __ffma2_rn(make_float2(wd[ki * 3 + 1], wd[ki * 3 + 1]), make_float2(x0, x2), s);
+                        s = __ffma2_rn(make_float2(wd[ki * 3 + 2], wd[ki * 3 + 2]), make_float2(x1, x3), s);
+                        prev[ki] = x3;
+                    }
+                    out[j2 * 256] = __float2half_rn(live ? s.x : 0.f);
+                    out[(j2 + 1) * 256] = __float2half_rn(live ? s.y : 0.f);
+                }
             }
-            out[j2 * 256] = __float2half_rn(live ? s.x : 0.f);
-            out[(j2 + 1) * 256] = __float2half_rn(live ? s.y : 0.f);
         }
+        __syncthreads();                     // every read of this item's mel rows and conv0 tile done
+        if (next < w1) park();
     }
 }
 
@@ -452,7 +488,10 @@ int launch_sub_conv0_dw1(const SubParams& p, int w0, int w1, cudaStream_t st) {
     static PerDeviceOnce attr;
     const int rc = set_smem_limit_once(attr, k_sub_conv0_dw1, kSubSmem, "cudaFuncSetAttribute(k_sub_conv0_dw1)");
     if (rc) return rc;
-    k_sub_conv0_dw1<<<n_work, 256, kSubSmem, st>>>(p, w0);
+    // persistent: two CTAs per SM, a multiple of 8 so each keeps one channel group
+    const int per_sm = 2 * device_sms() / 8 * 8;
+    const int grid = n_work < per_sm ? n_work : per_sm;
+    k_sub_conv0_dw1<<<grid, 256, kSubSmem, st>>>(p, w0, w1);
     return check_launch("k_sub_conv0_dw1");
 }
 
