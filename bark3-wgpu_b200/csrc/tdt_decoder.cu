@@ -716,6 +716,15 @@ constexpr uint32_t kWsTmemCols = 256;
 
 enum { kWsHead = 0, kWsL0 = 1, kWsL1hh = 2, kWsL1ih = 3, kWsProj = 4 };
 
+// Gate functions of the weight-stationary kernel's cell.  The cell runs on six
+// warps and is bound by the instructions they issue, so the logistic function
+// uses the exponential intrinsic and the approximate divide (relative error a
+// few ulp for the gate range), and tanh follows from the identity
+// tanh(x) = 2 sigma(2x) - 1 (absolute error ~1e-7).  Against the precise
+// functions this takes ~0.4-1.0 us off each cell phase.
+__device__ __forceinline__ float ws_sigm(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+__device__ __forceinline__ float ws_tanh(float x) { return 2.0f * ws_sigm(2.0f * x) - 1.0f; }
+
 __device__ __forceinline__ unsigned long long ws_key(float v, int idx) {
     uint32_t u = __float_as_uint(v);
     u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);   // order-preserving map of f32 onto u32
@@ -995,11 +1004,11 @@ __global__ void __launch_bounds__(kWsThreads, 1)
             float gate[4];
 #pragma unroll
             for (int g = 0; g < 4; ++g) gate[g] = xc[(g * nt + col) * 32 + ch] + e[i][g];
-            const float in = sigm(gate[0]);
-            const float fg = sigm(gate[1]);
-            const float cand = tanhf(gate[2]);
+            const float in = ws_sigm(gate[0]);
+            const float fg = ws_sigm(gate[1]);
+            const float cand = ws_tanh(gate[2]);
             const float cn = fg * cold[i] + in * cand;
-            const float h = sigm(gate[3]) * tanhf(cn);
+            const float h = ws_sigm(gate[3]) * ws_tanh(cn);
             p.c[(static_cast<size_t>(n) * 2 + layer) * 640 + 32 * t + ch] = cn;
             __half* a = layer == 0 ? p.act0 : p.act1;
             split_store(ws_panel(a, p.bpad, 32 * t + ch, n, 0), ws_panel(a, p.bpad, 32 * t + ch, n, 1), h);
