@@ -235,13 +235,29 @@ __global__ void __launch_bounds__(kDwThreads, 1) k3_dwconv_bn_silu(const __half*
     asm volatile("cp.async.wait_group 0;" ::: "memory");
 }
 
+// f32 -> f16 (round to nearest even).  A thread converts kCvtUnroll float4s
+// per pass with all their loads issued first (streaming: the f32 source is
+// read once, while the f16 result should stay in L2 for the GEMM behind it).
+constexpr int kCvtUnroll = 4;
 __global__ void k_f32_to_f16(const float4* __restrict__ src, uint2* __restrict__ dst, int64_t n4) {
-    for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
-         i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-        const float4 v = src[i];
-        __half2 a = __floats2half2_rn(v.x, v.y);
-        __half2 b = __floats2half2_rn(v.z, v.w);
-        dst[i] = make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+    for (int64_t i0 = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i0 < n4;
+         i0 += stride * kCvtUnroll) {
+        float4 v[kCvtUnroll];
+#pragma unroll
+        for (int u = 0; u < kCvtUnroll; ++u) {
+            const int64_t i = i0 + u * stride;
+            v[u] = i < n4 ? __ldcs(src + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < kCvtUnroll; ++u) {
+            const int64_t i = i0 + u * stride;
+            if (i < n4) {
+                __half2 a = __floats2half2_rn(v[u].x, v[u].y);
+                __half2 b = __floats2half2_rn(v[u].z, v[u].w);
+                dst[i] = make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+            }
+        }
     }
 }
 
@@ -285,9 +301,9 @@ int launch_f32_to_f16(const float* src, __half* dst, int64_t n, cudaStream_t st)
     if (n <= 0) return 0;
     if (n % 4) return set_error(B3_EINVAL, "f32->f16 length %lld not a multiple of 4", (long long)n);
     const int64_t n4 = n / 4;
-    int blocks = static_cast<int>((n4 + 255) / 256);
-    if (blocks > 148 * 16) blocks = 148 * 16;
-    k_f32_to_f16<<<blocks, 256, 0, st>>>(reinterpret_cast<const float4*>(src), reinterpret_cast<uint2*>(dst), n4);
+    int64_t blocks = (n4 + 256 * kCvtUnroll - 1) / (256 * kCvtUnroll);
+    if (blocks > 8 * device_sms()) blocks = 8 * device_sms();   // one wave of 8 CTAs per SM
+    k_f32_to_f16<<<static_cast<int>(blocks), 256, 0, st>>>(reinterpret_cast<const float4*>(src), reinterpret_cast<uint2*>(dst), n4);
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? 0 : set_cuda_error("k_f32_to_f16", e);
 }

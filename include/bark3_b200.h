@@ -79,7 +79,7 @@ void* b3_stream(b3_ctx* ctx);
 int b3_set_wait_limit(b3_ctx* ctx, int64_t grid_barrier_ns);
 
 /* Which greedy-decoder kernel decodes a batch.  B3_DECODER_AUTO (the
- * default): batches of up to 256 utterances run on the weight-stationary
+ * default): batches of up to 128 utterances run on the weight-stationary
  * kernel (every CTA keeps one 128-row weight tile in shared memory for the
  * whole decode; four grid barriers per lock step), larger ones on the
  * split-K kernel.  B3_DECODER_SPLIT_K: every batch on the split-K kernel
