@@ -163,7 +163,8 @@ struct SubParams {
     const float* mel;         // [frames][128]
     const int* mel_off;       // [n_utt + 1]
     const int* n_valid;       // [n_utt] valid mel frames
-    const int4* work;         // (utterance, first t2 row, channel group, 0) per CTA
+    const int4* work;         // per item: (first mel row, mel frames, valid frames, first t2 row),
+                              // (first x2 row, channel group, 0, 0)
     const float *w0, *b0, *w2, *b2, *w5, *b5;  // conv0 and the two depthwise convs, [256][9] + [256]
     __half* x2;               // [sum F2][32][256]  after depthwise 1
     const __half* x3;         // [sum F2][32][256]  after pointwise 1

@@ -1281,9 +1281,15 @@ void fe_shape_from_frames(FeShape& s, const std::vector<int32_t>& frames, const 
         s.foff[u + 1] = s.foff[u] + frames[u];
         s.x2off[u + 1] = s.x2off[u] + f2;
         s.x4off[u + 1] = s.x4off[u] + t;
+        // two int4 per item: (first mel row, mel frames, valid frames, first
+        // t2 row), (first x2 row, channel group, 0, 0): every table value the
+        // item needs, so the kernel's per-item reads have no dependent chain
         for (int t2 = 0; t2 < f2; t2 += rows)
-            for (int g = 0; g < groups; ++g) s.work.push_back(make_int4(u, t2, g, 0));
-        s.woff[u + 1] = static_cast<int32_t>(s.work.size());
+            for (int g = 0; g < groups; ++g) {
+                s.work.push_back(make_int4(s.foff[u], frames[u], nvalid[u], t2));
+                s.work.push_back(make_int4(s.x2off[u], g, 0, 0));
+            }
+        s.woff[u + 1] = static_cast<int32_t>(s.work.size() / 2);
     }
 }
 

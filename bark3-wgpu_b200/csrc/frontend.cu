@@ -223,7 +223,10 @@ constexpr int kSubSmem = (kTm * kMelS + kT1 * kC0Row) * 4;
 // fastest and a multiple of 8 items per utterance, and the grid is a
 // multiple of 8, so a CTA keeps one channel group: its conv0 and conv1 taps
 // stay in registers for the whole launch, and the next item's mel rows are
-// loaded into registers while the current item computes.
+// loaded into registers while the current item computes.  An item's work
+// entry holds every table value it needs (no dependent reads); the entry of
+// the item after next is read while the current one computes, so the next
+// item's mel addresses are known without waiting.
 __global__ void __launch_bounds__(256, 2) k_sub_conv0_dw1(SubParams p, int w0, int w1) {
     extern __shared__ float sub_smem[];
     float* mel = sub_smem;                 // [kTm][kMelS]
@@ -231,7 +234,7 @@ __global__ void __launch_bounds__(256, 2) k_sub_conv0_dw1(SubParams p, int w0, i
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int e = w0 + blockIdx.x;
     if (e >= w1) return;
-    const int cg = p.work[e].z * kC;
+    const int cg = p.work[2 * e + 1].y * kC;
     // conv0 taps: warp w owns channels 8 (w & 3) .. +8 as 4 channel pairs (one
     // packed f32x2 FMA per pair and tap) over columns 32 (w >> 2) + lane
     const int cq = (warp & 3) * 8;
@@ -259,11 +262,12 @@ __global__ void __launch_bounds__(256, 2) k_sub_conv0_dw1(SubParams p, int w0, i
     // an item's mel rows, 16-byte loads of columns 4 c .. 4 c + 3 (three per thread)
     constexpr int kLoads = (kTm * (kMel / 4) + 255) / 256;
     float4 pre[kLoads];
-    auto fetch = [&](int item) {
-        const int4 wk = p.work[item];
-        const int F = p.mel_off[wk.x + 1] - p.mel_off[wk.x];
-        const int tm_0 = 2 * (2 * wk.y - 1) - 1;
-        const float* melu = p.mel + static_cast<size_t>(p.mel_off[wk.x]) * kMel;
+    // an item's entry: a = (first mel row, mel frames, valid frames, first
+    // t2 row), b = (first x2 row, channel group, 0, 0)
+    auto fetch = [&](const int4& a) {
+        const int F = a.y;
+        const int tm_0 = 2 * (2 * a.w - 1) - 1;
+        const float* melu = p.mel + static_cast<size_t>(a.x) * kMel;
 #pragma unroll
         for (int k = 0; k < kLoads; ++k) {
             const int i = threadIdx.x + 256 * k;
@@ -287,20 +291,27 @@ __global__ void __launch_bounds__(256, 2) k_sub_conv0_dw1(SubParams p, int w0, i
             }
         }
     };
-    fetch(e);
+    const int G = static_cast<int>(gridDim.x);
+    const int4 zero4 = make_int4(0, 0, 0, 0);
+    int4 ca = __ldg(p.work + 2 * e);                            // this item
+    int4 na = e + G < w1 ? __ldg(p.work + 2 * (e + G)) : zero4;  // the next
+    fetch(ca);
     park();
-    for (; e < w1; e += gridDim.x) {
-        const int4 wk = p.work[e];   // (utterance, t2_0, channel group)
-        const int u = wk.x, t2_0 = wk.y;
-        const int F = p.mel_off[u + 1] - p.mel_off[u];
+    for (; e < w1; e += G) {
+        const int t2_0 = ca.w;
+        const int F = ca.y;
         const int F1 = conv_len_d(F), F2 = conv_len_d(F1);
-        const int nvalid = p.n_valid[u];
+        const int nvalid = ca.z;
         const int v1 = conv_len_d(nvalid > 1 ? nvalid : 1);
         const int v2 = conv_len_d(v1);
         const int t1_0 = 2 * t2_0 - 1;      // first conv0 row
         __syncthreads();                     // this item's mel rows are parked
-        const int next = e + static_cast<int>(gridDim.x);
-        if (next < w1) fetch(next);          // lands while this item computes
+        const int next = e + G;
+        if (next < w1) fetch(na);            // lands while this item computes
+        // the item after next: its entry lands meanwhile; this item's x2
+        // row is needed only by the depthwise conv, after conv0
+        const int4 fa = next + G < w1 ? __ldg(p.work + 2 * (next + G)) : zero4;
+        const int x2row = __ldg(&p.work[2 * e + 1].x);
         for (int r = 0; r < kT1; ++r) {
             const int t1 = t1_0 + r;
             const bool live = t1 >= 0 && t1 < F1 && t1 < v1;
@@ -339,7 +350,7 @@ __global__ void __launch_bounds__(256, 2) k_sub_conv0_dw1(SubParams p, int w0, i
                 const bool live = t2 < v2;
                 // conv0 local rows 2 r2 + ki hold t1 = 2 t2 - 1 + ki; index 1 + col
                 const float* base = c0 + (2 * r2 * kC + lane) * kC0S;
-                __half* out = p.x2 + static_cast<size_t>(p.x2_off[u] + t2) * 32 * 256 + cg + lane;
+                __half* out = p.x2 + static_cast<size_t>(x2row + t2) * 32 * 256 + cg + lane;
                 float prev[3];
 #pragma unroll
                 for (int ki = 0; ki < 3; ++ki) prev[ki] = base[ki * kC0Row + 2 * jb];   // col 2 jb - 1
@@ -363,6 +374,8 @@ __global__ void __launch_bounds__(256, 2) k_sub_conv0_dw1(SubParams p, int w0, i
         }
         __syncthreads();                     // every read of this item's mel rows and conv0 tile done
         if (next < w1) park();
+        ca = na;
+        na = fa;
     }
 }
 
