@@ -214,16 +214,27 @@ def job_config(args, world, syn):
 
 
 class ClockSampler:
-    """nvidia-smi samples of the SM clock and throttle reasons while running."""
+    """nvidia-smi samples (every 100 ms) of the SM clock and throttle reasons.
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    Started before the warm-up steps, so that nvidia-smi is already sampling
+    when the timed region begins; `mark(t0, t1)` records the timed region's
+    wall-clock window, and the summary keeps the samples inside it. A region
+    too short to hold a sample (a few fast steps on many GPUs) falls back to
+    the loaded samples of the warm-up and timed steps, and says so."""
+
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu_index):
         self.gpu = gpu_index
         self.proc = None
+        self.window = None
         self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+
+    def mark(self, t0, t1):
+        """The timed region ran from wall-clock t0 to t1 (time.time())."""
+        self.window = (t0, t1)
 
     def __enter__(self):
         try:
@@ -244,23 +255,43 @@ class ClockSampler:
 
     def summary(self):
         self.f.flush()
-        rows = []
-        for line in pathlib.Path(self.f.name).read_text().splitlines():
-            parts = [p.strip() for p in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[5:9]))
-            except ValueError:
-                continue
+        text = pathlib.Path(self.f.name).read_text()
         os.unlink(self.f.name)
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        loaded = [r for r in rows if r[2] > 300.0] or rows
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in loaded for i, v in enumerate(r[3]) if v.lower() == "active"})
-        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": max(r[1] for r in rows),
-                "reasons": reasons, "samples": len(loaded)}
+        return summarize_clocks(text, self.window)
+
+
+def summarize_clocks(text, window):
+    """Median SM clock and the throttle reasons seen, from nvidia-smi CSV rows
+    (timestamp, index, clocks.sm, clocks.max.sm, power.draw, reasons.active,
+    hw_slowdown, hw_thermal_slowdown, sw_thermal_slowdown, sw_power_cap)."""
+    import datetime
+
+    rows = []
+    for line in text.splitlines():
+        parts = [p.strip() for p in line.split(",")]
+        if len(parts) < 10:
+            continue
+        try:
+            ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+            rows.append((ts, float(parts[2]), float(parts[3]), float(parts[4]), parts[6:10]))
+        except ValueError:
+            continue
+    if not rows:
+        return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+    span = "timed steps"
+    chosen = rows
+    if window is not None:
+        inside = [r for r in rows if window[0] <= r[0] <= window[1]]
+        if inside:
+            chosen = inside
+        else:
+            chosen = [r for r in rows if r[3] > 300.0] or rows
+            span = "warm-up and timed steps (no sample fell inside the timed steps)"
+    loaded = [r for r in chosen if r[3] > 300.0] or chosen
+    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    reasons = sorted({names[i] for r in loaded for i, v in enumerate(r[4]) if v.lower() == "active"})
+    return {"sm_mhz": statistics.median(r[1] for r in loaded), "sm_max_mhz": max(r[2] for r in rows),
+            "reasons": reasons, "samples": len(loaded), "span": span}
 
 
 def make_cpu_pipeline(oracle, syn, pkg, weights, workload):
@@ -465,6 +496,7 @@ def main():
         return float(t.item())
 
     # ── value: device-resident inputs ──
+    clk = ClockSampler(local).__enter__()   # already sampling when the timed steps start
     for _ in range(args.warmup):
         step_device()
     enc.sync()
@@ -474,13 +506,15 @@ def main():
     enc.sync()
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:
-        ev0.record(stream)
-        for _ in range(args.steps):
-            step_device()
-        ev1.record(stream)
-        enc.sync()
+    t_wall0 = time.time()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step_device()
+    ev1.record(stream)
+    enc.sync()
     torch.cuda.synchronize()
+    clk.mark(t_wall0, time.time())
+    clk.__exit__(None, None, None)
     ms = ev0.elapsed_time(ev1)
     clocks = clk.summary()
     prof = {}
