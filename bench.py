@@ -496,25 +496,24 @@ def main():
         return float(t.item())
 
     # ── value: device-resident inputs ──
-    clk = ClockSampler(local).__enter__()   # already sampling when the timed steps start
-    for _ in range(args.warmup):
-        step_device()
-    enc.sync()
-    L.b3_profile(enc.ctx, 1)
-    barrier()
-    torch.cuda.synchronize()
-    enc.sync()
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
-    t_wall0 = time.time()
-    ev0.record(stream)
-    for _ in range(args.steps):
-        step_device()
-    ev1.record(stream)
-    enc.sync()
-    torch.cuda.synchronize()
-    clk.mark(t_wall0, time.time())
-    clk.__exit__(None, None, None)
+    with ClockSampler(local) as clk:   # already sampling when the timed steps start
+        for _ in range(args.warmup):
+            step_device()
+        enc.sync()
+        L.b3_profile(enc.ctx, 1)
+        barrier()
+        torch.cuda.synchronize()
+        enc.sync()
+        t_wall0 = time.time()
+        ev0.record(stream)
+        for _ in range(args.steps):
+            step_device()
+        ev1.record(stream)
+        enc.sync()
+        torch.cuda.synchronize()
+        clk.mark(t_wall0, time.time())
     ms = ev0.elapsed_time(ev1)
     clocks = clk.summary()
     prof = {}
