@@ -171,6 +171,8 @@ struct SubParams {
     __half* x4;               // [sum T][16][256]   after depthwise 2
     const int* x2_off;        // [n_utt + 1] row offsets of x2 / x3
     const int* x4_off;        // [n_utt + 1] row offsets of x4 (= encoder frames)
+    const int4* rows3;        // per x4 row: (first x2 row of its utterance, depthwise-1 rows,
+                              // valid x4 rows, row within the utterance)
 };
 
 // The front-end kernels over a range of the batch: mel frames [f0, f1) and

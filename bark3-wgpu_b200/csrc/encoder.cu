@@ -165,6 +165,7 @@ struct FeShape {
     std::vector<int32_t> foff, nvalid, x2off, x4off;
     std::vector<int32_t> woff;   // first conv work item of each utterance (n + 1)
     std::vector<int4> work;
+    std::vector<int4> rows3;     // per encoder frame: (first x2 row, depthwise-1 rows, valid frames, frame)
 };
 
 // Per-kernel-class CUDA-event timing (the analogue of the reference's
@@ -255,7 +256,7 @@ struct b3_ctx {
         Linear pw1, pw2;      // pointwise convs, f16 [256][256]
         DevBuf pw_bias;       // [2][256] f32
         Linear sub_w_perm;    // encoder subsampling linear, input columns in (freq, channel) order
-        DevBuf wave, wave_off, frame_off, mel, x2, x3, x4, ints, work;
+        DevBuf wave, wave_off, frame_off, mel, x2, x3, x4, ints, work, rows3;
         std::vector<int32_t> sub_key;   // batch shape whose tables are on the device
         std::vector<int64_t> mel_key;   // padded wave offsets of the cached shape
         FeShape mel_shape;
@@ -275,7 +276,7 @@ struct b3_ctx {
         }
         if (fe.copy_st) cudaStreamSynchronize(fe.copy_st);
         for (DevBuf* b : {&fe.tables, &fe.conv, &fe.pw_bias, &fe.wave, &fe.wave_off, &fe.frame_off, &fe.mel, &fe.x2,
-                          &fe.x3, &fe.x4, &fe.ints, &fe.work})
+                          &fe.x3, &fe.x4, &fe.ints, &fe.work, &fe.rows3})
             b->release();
         for (cudaEvent_t e : fe.chunk_ev) cudaEventDestroy(e);
         if (fe.wave_free) cudaEventDestroy(fe.wave_free);
@@ -1273,6 +1274,7 @@ void fe_shape_from_frames(FeShape& s, const std::vector<int32_t>& frames, const 
     s.x4off.assign(n + 1, 0);
     s.nvalid = nvalid;
     s.work.clear();
+    s.rows3.clear();
     s.woff.assign(n + 1, 0);
     const int rows = sub_work_rows(), groups = 256 / sub_work_channels();
     for (int u = 0; u < n; ++u) {
@@ -1290,6 +1292,9 @@ void fe_shape_from_frames(FeShape& s, const std::vector<int32_t>& frames, const 
                 s.work.push_back(make_int4(s.x2off[u], g, 0, 0));
             }
         s.woff[u + 1] = static_cast<int32_t>(s.work.size() / 2);
+        // the second depthwise conv's rows: every table value a row needs
+        const int v3 = conv_len_h(conv_len_h(conv_len_h(nvalid[u] > 1 ? nvalid[u] : 1)));
+        for (int t3 = 0; t3 < t; ++t3) s.rows3.push_back(make_int4(s.x2off[u], f2, v3, t3));
     }
 }
 
@@ -1312,11 +1317,14 @@ int fe_sub_setup(b3_ctx* c, const FeShape& s, SubParams& sp) {
     if (key != F.sub_key) {
         B3_TRY(F.ints.ensure((3 * n + 2) * sizeof(int32_t)));
         B3_TRY(F.work.ensure(s.work.size() * sizeof(int4) + 16));
+        B3_TRY(F.rows3.ensure(s.rows3.size() * sizeof(int4) + 16));
         ints = F.ints.as<int32_t>();
         B3_CUDA(cudaMemcpyAsync(ints, s.nvalid.data(), n * 4, cudaMemcpyHostToDevice, c->stream));
         B3_CUDA(cudaMemcpyAsync(ints + n, s.x2off.data(), (n + 1) * 4, cudaMemcpyHostToDevice, c->stream));
         B3_CUDA(cudaMemcpyAsync(ints + 2 * n + 1, s.x4off.data(), (n + 1) * 4, cudaMemcpyHostToDevice, c->stream));
         B3_CUDA(cudaMemcpyAsync(F.work.p, s.work.data(), s.work.size() * sizeof(int4), cudaMemcpyHostToDevice, c->stream));
+        B3_CUDA(cudaMemcpyAsync(F.rows3.p, s.rows3.data(), s.rows3.size() * sizeof(int4), cudaMemcpyHostToDevice,
+                                c->stream));
         F.sub_key = key;
     }
     ints = F.ints.as<int32_t>();
@@ -1325,6 +1333,7 @@ int fe_sub_setup(b3_ctx* c, const FeShape& s, SubParams& sp) {
     sp.mel_off = F.frame_off.as<int>();
     sp.n_valid = ints;
     sp.work = F.work.as<int4>();
+    sp.rows3 = F.rows3.as<int4>();
     const float* cv = F.conv.as<float>();
     sp.w0 = cv;
     sp.b0 = cv + 2304;

@@ -380,96 +380,89 @@ __global__ void __launch_bounds__(256, 2) k_sub_conv0_dw1(SubParams p, int w0, i
 }
 
 // Second depthwise conv (+ bias, + mask): x3 [t2][32][256] -> x4 [t3][16][256].
-// 64 threads per t3 row (4 rows per CTA), a thread owns 4 channels: it walks
-// the 16 output columns left to right, loading each input column (3 rows x
-// 4 channels, 8-byte loads) once and carrying the shared column to the next
-// output.  Every output keeps the scalar accumulation order (bias, then taps
-// row by row, left to right).
+// Persistent: 64 threads per x4 row, 4 rows per CTA pass.  A thread owns 4
+// channels, whose taps and bias stay in registers for the whole launch, and
+// walks the row's 16 output columns left to right, loading each input column
+// (3 rows x 4 channels, 8-byte loads) once and carrying the shared column to
+// the next output; two channels per packed f32x2 FMA.  A row's table values
+// (first x2 row of its utterance, depthwise-1 rows, valid x4 rows, row within
+// the utterance) are one int4, read a pass ahead.  Every output keeps the
+// scalar accumulation order (bias, then taps row by row, left to right).
 constexpr int kDw2Rows = 4;
 __global__ void __launch_bounds__(64 * kDw2Rows) k_sub_dw2(SubParams p, int r0, int r1) {
-    const int row = r0 + blockIdx.x * kDw2Rows + (threadIdx.x >> 6);  // global t3 row
-    if (row >= r1) return;
-    int lo = 0, hi = p.n_utt;
-    while (hi - lo > 1) {
-        const int mid = (lo + hi) >> 1;
-        if (p.x4_off[mid] <= row) lo = mid; else hi = mid;
-    }
-    const int u = lo;
-    const int t3 = row - p.x4_off[u];
-    const int F = p.mel_off[u + 1] - p.mel_off[u];
-    const int F2 = conv_len_d(conv_len_d(F));
-    const int nvalid = p.n_valid[u];
-    const int v3 = conv_len_d(conv_len_d(conv_len_d(nvalid > 1 ? nvalid : 1)));
-    const __half* x3 = p.x3 + static_cast<size_t>(p.x2_off[u]) * 32 * 256;
     const int c0 = (threadIdx.x & 63) * 4;
-    float w[9][4], bias[4];
+    float2 w[9][2], bias[2];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) {
-        bias[e] = __ldg(p.b5 + c0 + e);
+    for (int q = 0; q < 2; ++q) {
+        const int ca = c0 + 2 * q;
+        bias[q] = make_float2(__ldg(p.b5 + ca), __ldg(p.b5 + ca + 1));
 #pragma unroll
-        for (int t = 0; t < 9; ++t) w[t][e] = __ldg(p.w5 + (c0 + e) * 9 + t);
+        for (int t = 0; t < 9; ++t) w[t][q] = make_float2(__ldg(p.w5 + ca * 9 + t), __ldg(p.w5 + (ca + 1) * 9 + t));
     }
-    const bool live = t3 < v3;
-    bool rok[3];
-#pragma unroll
-    for (int ki = 0; ki < 3; ++ki) {
-        const int t2 = 2 * t3 + ki - 1;
-        rok[ki] = t2 >= 0 && t2 < F2;
-    }
-    // column j2 of the 3 input rows, 4 channels
-    auto col = [&](int j2, float (&v)[3][4]) {
+    const int stride = static_cast<int>(gridDim.x) * kDw2Rows;
+    const int4 zero4 = make_int4(0, 0, 0, 0);
+    int row = r0 + static_cast<int>(blockIdx.x) * kDw2Rows + (threadIdx.x >> 6);   // global x4 row
+    int4 nm = row < r1 ? __ldg(p.rows3 + row) : zero4;
+    for (; row < r1; row += stride) {
+        const int4 m = nm;
+        if (row + stride < r1) nm = __ldg(p.rows3 + row + stride);   // lands while this row computes
+        const int F2 = m.y, t3 = m.w;
+        const bool live = t3 < m.z;
+        const __half* x3 = p.x3 + static_cast<size_t>(m.x) * 32 * 256;
+        bool rok[3];
 #pragma unroll
         for (int ki = 0; ki < 3; ++ki) {
-            uint2 raw = make_uint2(0u, 0u);
-            if (rok[ki]) {
-                const int t2 = 2 * t3 + ki - 1;
-                raw = __ldg(reinterpret_cast<const uint2*>(x3 + (static_cast<size_t>(t2) * 32 + j2) * 256 + c0));
-            }
-            const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
-            const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
-            v[ki][0] = a.x;
-            v[ki][1] = a.y;
-            v[ki][2] = b.x;
-            v[ki][3] = b.y;
+            const int t2 = 2 * t3 + ki - 1;
+            rok[ki] = t2 >= 0 && t2 < F2;
         }
-    };
-    float cl[3][4];   // column 2 j3 - 1 (the previous output's right column)
+        // column j2 of the 3 input rows: channels (c0, c0 + 1) and (c0 + 2, c0 + 3)
+        auto col = [&](int j2, float2 (&v)[3][2]) {
 #pragma unroll
-    for (int ki = 0; ki < 3; ++ki)
+            for (int ki = 0; ki < 3; ++ki) {
+                uint2 raw = make_uint2(0u, 0u);
+                if (rok[ki]) {
+                    const int t2 = 2 * t3 + ki - 1;
+                    raw = __ldg(reinterpret_cast<const uint2*>(x3 + (static_cast<size_t>(t2) * 32 + j2) * 256 + c0));
+                }
+                v[ki][0] = __half22float2(*reinterpret_cast<const __half2*>(&raw.x));
+                v[ki][1] = __half22float2(*reinterpret_cast<const __half2*>(&raw.y));
+            }
+        };
+        float2 cl[3][2];   // column 2 j3 - 1 (the previous output's right column)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) cl[ki][e] = 0.f;
-    __half* out = p.x4 + static_cast<size_t>(row) * 16 * 256 + c0;
+        for (int ki = 0; ki < 3; ++ki) cl[ki][0] = cl[ki][1] = make_float2(0.f, 0.f);
+        __half* out = p.x4 + static_cast<size_t>(row) * 16 * 256 + c0;
 #pragma unroll 2
-    for (int j3 = 0; j3 < 16; ++j3) {
-        float cm[3][4], cr[3][4];
-        col(2 * j3, cm);
-        col(2 * j3 + 1, cr);
-        float s[4] = {0.f, 0.f, 0.f, 0.f};
-        if (live) {
+        for (int j3 = 0; j3 < 16; ++j3) {
+            float2 cm[3][2], cr[3][2];
+            col(2 * j3, cm);
+            col(2 * j3 + 1, cr);
+            float2 s[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+            if (live) {
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                s[e] = bias[e];
+                for (int q = 0; q < 2; ++q) {
+                    s[q] = bias[q];
 #pragma unroll
-                for (int ki = 0; ki < 3; ++ki) {
-                    if (!rok[ki]) continue;
-                    if (j3 > 0) s[e] += w[ki * 3][e] * cl[ki][e];   // column 2 j3 - 1 exists
-                    s[e] += w[ki * 3 + 1][e] * cm[ki][e];
-                    s[e] += w[ki * 3 + 2][e] * cr[ki][e];
+                    for (int ki = 0; ki < 3; ++ki) {
+                        if (!rok[ki]) continue;
+                        if (j3 > 0) s[q] = __ffma2_rn(w[ki * 3][q], cl[ki][q], s[q]);   // column 2 j3 - 1 exists
+                        s[q] = __ffma2_rn(w[ki * 3 + 1][q], cm[ki][q], s[q]);
+                        s[q] = __ffma2_rn(w[ki * 3 + 2][q], cr[ki][q], s[q]);
+                    }
                 }
             }
+            __half2 h0 = __floats2half2_rn(s[0].x, s[0].y), h1 = __floats2half2_rn(s[1].x, s[1].y);
+            *reinterpret_cast<uint2*>(out + j3 * 256) =
+                make_uint2(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1));
+#pragma unroll
+            for (int ki = 0; ki < 3; ++ki) {
+                cl[ki][0] = cr[ki][0];
+                cl[ki][1] = cr[ki][1];
+            }
         }
-        __half2 h0 = __floats2half2_rn(s[0], s[1]), h1 = __floats2half2_rn(s[2], s[3]);
-        *reinterpret_cast<uint2*>(out + j3 * 256) =
-            make_uint2(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1));
-#pragma unroll
-        for (int ki = 0; ki < 3; ++ki)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) cl[ki][e] = cr[ki][e];
     }
 }
 
-// [T][16][256] f16 (freq, channel) -> [T][4096] f32 in the reference's
-// (channel, freq) order, for the subsampling parity entry point.
 __global__ void k_sub_to_ref(const __half* src, float* dst, int rows) {
     const int t = blockIdx.x;
     if (t >= rows) return;
@@ -510,7 +503,13 @@ int launch_sub_conv0_dw1(const SubParams& p, int w0, int w1, cudaStream_t st) {
 
 int launch_sub_dw2(const SubParams& p, int r0, int r1, cudaStream_t st) {
     if (r1 <= r0) return 0;
-    k_sub_dw2<<<(r1 - r0 + kDw2Rows - 1) / kDw2Rows, 64 * kDw2Rows, 0, st>>>(p, r0, r1);
+    // persistent: as many CTAs as are resident at once
+    int per_sm = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_sub_dw2, 64 * kDw2Rows, 0) != cudaSuccess || per_sm < 1)
+        per_sm = 1;
+    const int passes = (r1 - r0 + kDw2Rows - 1) / kDw2Rows;
+    const int grid = passes < per_sm * device_sms() ? passes : per_sm * device_sms();
+    k_sub_dw2<<<grid, 64 * kDw2Rows, 0, st>>>(p, r0, r1);
     return check_launch("k_sub_dw2");
 }
 
