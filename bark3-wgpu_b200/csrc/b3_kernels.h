@@ -154,6 +154,9 @@ struct MelParams {
     const float* fb;          // [128][257] slaney filterbank
     const int* fb_lo;         // [128] first nonzero bin of each filter
     const int* fb_hi;         // [128] one past the last
+    const int* fb_off;        // [129] start of filter m's span in fb_pack
+    const float* fb_pack;     // the filters' nonzero spans, packed end to end
+    int fb_total;             // fb_off[128]
     float* mel;               // [frames][128]
 };
 

@@ -257,6 +257,7 @@ struct b3_ctx {
         DevBuf pw_bias;       // [2][256] f32
         Linear sub_w_perm;    // encoder subsampling linear, input columns in (freq, channel) order
         DevBuf wave, wave_off, frame_off, mel, x2, x3, x4, ints, work, rows3;
+        int fb_packed = 0;    // weights in the packed filterbank spans
         std::vector<int32_t> sub_key;   // batch shape whose tables are on the device
         std::vector<int64_t> mel_key;   // padded wave offsets of the cached shape
         FeShape mel_shape;
@@ -1182,15 +1183,9 @@ void slaney_filterbank(std::vector<float>& fb) {
 int build_fe_tables(b3_ctx* c) {
     std::vector<float> fb;
     slaney_filterbank(fb);
-    std::vector<float> t(512 + 512 + fb.size() + 256, 0.f);
-    for (int i = 0; i < 400; ++i)  // symmetric Hann(400) centred in 512 (src/mel.rs:27-36)
-        t[56 + i] = 0.5f * (1.0f - cosf(6.2831855f * static_cast<float>(i) / 399.0f));
-    for (int k = 0; k < 256; ++k) {
-        t[512 + 2 * k] = static_cast<float>(std::cos(-2.0 * M_PI * k / 512.0));
-        t[512 + 2 * k + 1] = static_cast<float>(std::sin(-2.0 * M_PI * k / 512.0));
-    }
-    memcpy(&t[1024], fb.data(), fb.size() * 4);
-    int32_t* lohi = reinterpret_cast<int32_t*>(&t[1024 + fb.size()]);
+    // each filter's nonzero span [lo, hi), and the spans packed end to end
+    // (fb_off: start of filter m in the packed weights)
+    std::vector<int32_t> lo_hi(256, 0), off(129, 0);
     for (int m = 0; m < 128; ++m) {
         int lo = 257, hi = 0;
         for (int k = 0; k < 257; ++k)
@@ -1198,9 +1193,26 @@ int build_fe_tables(b3_ctx* c) {
                 lo = std::min(lo, k);
                 hi = k + 1;
             }
-        lohi[m] = lo < hi ? lo : 0;
-        lohi[128 + m] = lo < hi ? hi : 0;
+        lo_hi[m] = lo < hi ? lo : 0;
+        lo_hi[128 + m] = lo < hi ? hi : 0;
+        off[m + 1] = off[m] + (lo_hi[128 + m] - lo_hi[m]);
     }
+    // window [512] | twiddle [256][2] | fb [128][257] | fb_lo [128] | fb_hi [128] | fb_off [129]
+    // (+ 3 pad) | packed weights [fb_off[128]]
+    const size_t pack0 = 1024 + fb.size() + 256 + 132;
+    std::vector<float> t(pack0 + off[128], 0.f);
+    for (int i = 0; i < 400; ++i)  // symmetric Hann(400) centred in 512 (src/mel.rs:27-36)
+        t[56 + i] = 0.5f * (1.0f - cosf(6.2831855f * static_cast<float>(i) / 399.0f));
+    for (int k = 0; k < 256; ++k) {
+        t[512 + 2 * k] = static_cast<float>(std::cos(-2.0 * M_PI * k / 512.0));
+        t[512 + 2 * k + 1] = static_cast<float>(std::sin(-2.0 * M_PI * k / 512.0));
+    }
+    memcpy(&t[1024], fb.data(), fb.size() * 4);
+    memcpy(&t[1024 + fb.size()], lo_hi.data(), 256 * 4);
+    memcpy(&t[1024 + fb.size() + 256], off.data(), 129 * 4);
+    for (int m = 0; m < 128; ++m)
+        for (int k = lo_hi[m]; k < lo_hi[128 + m]; ++k) t[pack0 + off[m] + (k - lo_hi[m])] = fb[m * 257 + k];
+    c->fe.fb_packed = off[128];
     B3_TRY(upload(c->fe.tables, t.data(), t.size() * 4, c->stream));
     B3_CUDA(cudaStreamSynchronize(c->stream));
     return 0;
@@ -1417,6 +1429,9 @@ int fe_mel_setup(b3_ctx* c, const float* wave, const std::vector<int64_t>& woff,
     mp.fb = t + 1024;
     mp.fb_lo = reinterpret_cast<const int*>(t + 1024 + 128 * 257);
     mp.fb_hi = mp.fb_lo + 128;
+    mp.fb_off = mp.fb_hi + 128;
+    mp.fb_pack = t + 1024 + 128 * 257 + 256 + 132;
+    mp.fb_total = F.fb_packed;
     mp.mel = F.mel.as<float>();
     return 0;
 }

@@ -42,6 +42,18 @@ __device__ __forceinline__ int conv_len_d(int l) { return (l - 1) / 2 + 1; }
 //   X[k] = (Z[k] + conj Z[256-k]) / 2 + W512^k (Z[k] - conj Z[256-k]) / 2i.
 constexpr int kMelWarps = 8;
 
+// Shared-memory slot of FFT point i (an injective map of 0..255 into
+// 0..256): with it the bit-reversed scatter, every butterfly stage pair and
+// the forward half of the real-input split touch 32 distinct banks per warp
+// access (the split's mirrored half 2-way), where plain indices gave up to
+// 8-way conflicts (the scatter) and 4-way (the first two stage pairs).
+__device__ __forceinline__ int fft_slot(int i) { return (i ^ ((i >> 2) & 31)) + (i >> 7); }
+
+// The filters' packed nonzero spans are staged in shared memory when they
+// fit (504 weights for the 128-filter slaney bank); otherwise each lane
+// reads its span from the packed global copy.
+constexpr int kMelFbSmem = 1024;
+
 // Sample s of an utterance whose first `lead` samples are zeros (the leading
 // silence, never stored) followed by x[0 .. len - lead): pre-emphasised and
 // windowed.
@@ -52,10 +64,14 @@ __device__ __forceinline__ float mel_sample(const float* x, int64_t len, int lea
     return (s == 0 ? cur : cur - 0.97f * prev) * w;
 }
 
-__global__ void __launch_bounds__(256) k_mel_frames(MelParams p, int f0, int f1) {
-    __shared__ float zre[kMelWarps][256], zim[kMelWarps][256], pwr[kMelWarps][260];
+__global__ void __launch_bounds__(256, 7) k_mel_frames(MelParams p, int f0, int f1) {
+    __shared__ float zre[kMelWarps][257], zim[kMelWarps][257], pwr[kMelWarps][260];
     __shared__ float2 tw[256];
+    __shared__ float fbs[kMelFbSmem];
     tw[threadIdx.x] = p.twiddle[threadIdx.x];
+    const bool fb_smem = p.fb_total <= kMelFbSmem;
+    if (fb_smem)
+        for (int i = threadIdx.x; i < p.fb_total; i += blockDim.x) fbs[i] = __ldg(p.fb_pack + i);
     __syncthreads();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int f = f0 + blockIdx.x * kMelWarps + warp;
@@ -76,8 +92,8 @@ __global__ void __launch_bounds__(256) k_mel_frames(MelParams p, int f0, int f1)
     for (int q = 0; q < 8; ++q) {
         const int m = lane + 32 * q;
         const int r = __brev(m) >> 24;  // 8-bit reversal
-        re[r] = mel_sample(x, len, p.lead, start + 2 * m, __ldg(p.window + 2 * m));
-        im[r] = mel_sample(x, len, p.lead, start + 2 * m + 1, __ldg(p.window + 2 * m + 1));
+        re[fft_slot(r)] = mel_sample(x, len, p.lead, start + 2 * m, __ldg(p.window + 2 * m));
+        im[fft_slot(r)] = mel_sample(x, len, p.lead, start + 2 * m + 1, __ldg(p.window + 2 * m + 1));
     }
     __syncwarp();
     // radix-2 stages taken two at a time: the 4 points i0 + {0, h, 2h, 3h}
@@ -100,7 +116,8 @@ __global__ void __launch_bounds__(256) k_mel_frames(MelParams p, int f0, int f1)
         for (int q = 0; q < 2; ++q) {
             const int b = lane + 32 * q;   // group-of-4 index, 0..63
             const int k = b & (h - 1);
-            const int i0 = ((b - k) << 2) + k, i1 = i0 + h, i2 = i0 + 2 * h, i3 = i0 + 3 * h;
+            const int j0 = ((b - k) << 2) + k;
+            const int i0 = fft_slot(j0), i1 = fft_slot(j0 + h), i2 = fft_slot(j0 + 2 * h), i3 = fft_slot(j0 + 3 * h);
             float r0 = re[i0], m0 = im[i0], r1 = re[i1], m1 = im[i1];
             float r2 = re[i2], m2 = im[i2], r3 = re[i3], m3 = im[i3];
             const float2 wa = tw[k << (8 - lh)];   // W256^(k * 128 / h) = W512^(k * 256 / h)
@@ -125,7 +142,8 @@ __global__ void __launch_bounds__(256) k_mel_frames(MelParams p, int f0, int f1)
         const int k = lane + 32 * q;
         if (k <= 256) {
             const int ka = k & 255, kb = (256 - k) & 255;
-            const float ar = re[ka], ai = im[ka], br = re[kb], bi = -im[kb];
+            const int sa = fft_slot(ka), sb = fft_slot(kb);
+            const float ar = re[sa], ai = im[sa], br = re[sb], bi = -im[sb];
             const float er = 0.5f * (ar + br), ei = 0.5f * (ai + bi);
             const float orr = 0.5f * (ai - bi), oi = -0.5f * (ar - br);
             const float2 w = k < 256 ? tw[k] : make_float2(-1.f, 0.f);
@@ -139,9 +157,15 @@ __global__ void __launch_bounds__(256) k_mel_frames(MelParams p, int f0, int f1)
     for (int q = 0; q < 4; ++q) {
         const int m = lane + 32 * q;
         const int k0 = __ldg(p.fb_lo + m), k1 = __ldg(p.fb_hi + m);
-        const float* fb = p.fb + m * 257;
+        const int o = __ldg(p.fb_off + m);
         float s = 0.f;
-        for (int k = k0; k < k1; ++k) s += __ldg(fb + k) * pw[k];
+        if (fb_smem) {
+            const float* wv = fbs + o - k0;
+            for (int k = k0; k < k1; ++k) s += wv[k] * pw[k];
+        } else {
+            const float* wv = p.fb_pack + o - k0;
+            for (int k = k0; k < k1; ++k) s += __ldg(wv + k) * pw[k];
+        }
         p.mel[static_cast<size_t>(f) * kMel + m] = logf(s + 5.9604645e-08f);
     }
 }
