@@ -323,7 +323,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int i = q * 32 + lane;                   // query row / TMEM lane
         const uint32_t lrow = static_cast<uint32_t>(q * 32) << 16;
         float* sh = sSh + i * kShStride;               // this query's parked row (all four warps of the quad)
-        float* xslot = sh + 96;                        // exchange slots [4 warps][2 parities]
+        // exchange slots [4 warps][2 parities], one word further on for rows
+        // 16..31 of each quarter: with the row stride of 2 mod 32 words, lane
+        // l and lane l + 16 would otherwise hit the same bank
+        float* xslot = sh + 96 + ((i >> 4) & 1);
         // the four warps of the quad meet: every slot of parity `par` written
         auto quad_sum = [&](int par) {
             return ((xslot[par] + xslot[2 + par]) + xslot[4 + par]) + xslot[6 + par];
