@@ -74,7 +74,7 @@ constexpr uint32_t kVOff = kKOff + 32768;        // V: same
 constexpr uint32_t kROff = kVOff + 32768;        // R chunks: same (64 R rows per chunk)
 constexpr uint32_t kShOff = kROff + 32768;       // parked band rows 128 x 130 f32
 constexpr uint32_t kBarOff = kShOff + kShRows * kShStride * 4;
-constexpr uint32_t kBarBytes = 208;                   // 25 mbarriers + the TMEM address
+constexpr uint32_t kBarBytes = 176;                   // 21 mbarriers + the TMEM address
 constexpr uint32_t kSmemMax = 232448;
 constexpr uint32_t kSmem = kSmemMax;
 constexpr uint32_t kAlignSlack = kSmemMax - kBarOff - kBarBytes;   // room to align the base to 1024 B
@@ -93,13 +93,22 @@ __device__ __forceinline__ uint32_t h2u(float a, float b) {
     return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// The four softmax warps of a lane quarter meet on their mbarrier (one
-// arrival per warp; a bounded wait, so a warp that left early ends the
-// others' wait with an error instead of a hang).
-__device__ __forceinline__ bool pair_exchange(uint64_t* bar, int lane, uint32_t parity, unsigned int site) {
-    __syncwarp();
-    if (lane == 0) mbar_arrive(smem_u32(bar));
-    return mbar_wait(smem_u32(bar), parity, site);
+// The four softmax warps of lane quarter q meet on named barrier q + 1 (128
+// threads) and AND their flags.  Every warp of the quad takes every one of
+// these barriers in the same order: a failed bounded wait only clears the
+// warp's flag, and the AND makes all four leave the item loop together at
+// the next meeting, so no warp is left waiting on one that has gone.
+__device__ __forceinline__ bool quad_sync_and(int q, bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, t;\n\t"
+        "setp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.and.pred t, %2, 128, p;\n\t"
+        "selp.u32 %0, 1, 0, t;\n\t}"
+        : "=r"(r)
+        : "r"(static_cast<uint32_t>(v)), "r"(q + 1)
+        : "memory");
+    return r != 0;
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -140,9 +149,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t* p_ready = bars + 17;   // [2] a block's P is in TMEM
     uint64_t* o_ready = bars + 19;   // every P.V (waited only when O is rescaled)
     uint64_t* o_final = bars + 20;   // the last P.V of an item
-    uint64_t* xchg = bars + 21;      // [4] softmax warp quads (one per lane quarter)
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 25);
-    static_assert(25 * 8 + 4 <= kBarBytes, "barrier area");
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 21);
+    static_assert(21 * 8 + 4 <= kBarBytes, "barrier area");
 
     const int warp = threadIdx.x >> 5;
     const int lane = threadIdx.x & 31;
@@ -165,7 +173,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(smem_u32(qld), 1);
         mbar_init(smem_u32(o_ready), 1);
         mbar_init(smem_u32(o_final), 1);
-        for (int c = 0; c < 4; ++c) mbar_init(smem_u32(&xchg[c]), 4);
         fence_mbar_init();
     }
     if (warp == 1) {
@@ -334,7 +341,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         auto quad_max = [&](int par) {
             return fmaxf(fmaxf(xslot[par], xslot[2 + par]), fmaxf(xslot[4 + par], xslot[6 + par]));
         };
-        bool ok = true;
+        bool ok = true;     // uniform across the quad: set only from quad_sync_and
+        bool fine = true;   // this warp's bounded waits all succeeded
         int g0 = 0, n = 0, x = 0, cbase = 0;
         for (int ii = blockIdx.x; ii < n_items && ok; ii += gridDim.x, ++n) {
             const Item it = item(ii);
@@ -347,10 +355,10 @@ __global__ void __launch_bounds__(kThreads, 1)
             float m_use = -INFINITY, l_part = 0.f;
             for (int kb = 0; kb < it.nkb && ok; ++kb) {
                 const int g = g0 + kb, st = g & 1;
-                if (!(ok = mbar_wait(smem_u32(&sg_full[g & 1]), (g >> 1) & 1, 0x28))) break;
-                tc_fence_after();
+                const bool got = __all_sync(0xffffffffu, mbar_wait(smem_u32(&sg_full[g & 1]), (g >> 1) & 1, 0x28));
                 float s[16];
-                {
+                if (got) {
+                    tc_fence_after();
                     // S columns [16 ks, 16 ks + 16); the quad's band window is band
                     // columns [96 - 32q, 192 - 32q) (chunks kb .. kb + 2), of which this
                     // warp loads [24 ks, 24 ks + 24); band column w sits in ring column
@@ -375,7 +383,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int e = 0; e < 24; e += 2) *reinterpret_cast<uint2*>(wp + e) = make_uint2(gr[e], gr[e + 1]);
                 }
                 // the other warps' parts of the window are parked too
-                if (!(ok = pair_exchange(&xchg[q], lane, x & 1, 0x27))) break;
+                fine = fine && got;
+                if (!(ok = quad_sync_and(q, fine))) break;
                 ++x;
                 // row i, key 16 ks + j: band column 127 - i + 16 ks + j = window column
                 // 16 ks + 31 - lane + j; across a warp the word index moves by 129 per
@@ -399,7 +408,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int j = 0; j < 16; ++j) mx[j & 3] = fmaxf(mx[j & 3], s[j]);
                 const float mloc = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
                 xslot[2 * ks + (x & 1)] = mloc;
-                if (!(ok = pair_exchange(&xchg[q], lane, x & 1, 0x2B))) break;
+                quad_sync_and(q, true);
                 const float m_blk = quad_max(x & 1);
                 ++x;
                 const bool grow = m_blk > m_use + kRescale;
@@ -412,14 +421,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                         // O columns [32 ks, 32 ks + 32) (after P_{g-1} V) *= corr.
                         // Passing sg_full(g) implies P_{g-2} V is done and P_g V is not
                         // issued yet, so o_ready is at phase g-1 or g: the parity is exact.
-                        if (!(ok = mbar_wait(smem_u32(o_ready), (g - 1) & 1, 0x29))) break;
-                        tc_fence_after();
-                        uint32_t o0[32];
-                        tmem_ld_32x32b_x32(tmem + lrow + kTO + 32 * ks, o0);
-                        tmem_wait_ld();
+                        const bool ordy = __all_sync(0xffffffffu, mbar_wait(smem_u32(o_ready), (g - 1) & 1, 0x29));
+                        fine = fine && ordy;
+                        if (ordy) {
+                            tc_fence_after();
+                            uint32_t o0[32];
+                            tmem_ld_32x32b_x32(tmem + lrow + kTO + 32 * ks, o0);
+                            tmem_wait_ld();
 #pragma unroll
-                        for (int e = 0; e < 32; ++e) o0[e] = __float_as_uint(__uint_as_float(o0[e]) * corr);
-                        tmem_st_32x32b_x32(tmem + lrow + kTO + 32 * ks, o0);
+                            for (int e = 0; e < 32; ++e) o0[e] = __float_as_uint(__uint_as_float(o0[e]) * corr);
+                            tmem_st_32x32b_x32(tmem + lrow + kTO + 32 * ks, o0);
+                        }
                     }
                 }
                 float2 ls[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
@@ -440,11 +452,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (lane == 0) mbar_arrive(smem_u32(&p_ready[g & 1]));
             }
             // ── O / l -> f16 row, columns [32 ks, 32 ks + 32) ──
-            if (ok && mbar_wait(smem_u32(o_final), n & 1, 0x2A)) {
-                tc_fence_after();
-                xslot[2 * ks + (x & 1)] = l_part;
-                const bool xok = pair_exchange(&xchg[q], lane, x & 1, 0x2C);
-                const float inv = 1.0f / quad_sum(x & 1);
+            if (ok) {   // uniform: every warp of the quad takes this meeting
+                const bool fin = __all_sync(0xffffffffu, mbar_wait(smem_u32(o_final), n & 1, 0x2A));
+                if (fin) {
+                    tc_fence_after();
+                    xslot[2 * ks + (x & 1)] = l_part;
+                }
+                const bool xok = quad_sync_and(q, fine && fin);
+                const float inv = xok ? 1.0f / quad_sum(x & 1) : 0.f;
                 ++x;
                 const bool store = xok && it.q0 + i < it.T;
                 __half* dst = p.out + static_cast<size_t>(it.seg0 + it.q0 + i) * 1024 + it.head * 128 + 32 * ks;
@@ -463,8 +478,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 tc_fence_before();
                 ok = xok;
-            } else {
-                ok = false;
             }
             g0 += it.nkb;
             cbase += it.nkb + 2;
