@@ -24,6 +24,7 @@ the product's.
 from __future__ import annotations
 
 import argparse
+import atexit
 import json
 import os
 import pathlib
@@ -216,11 +217,13 @@ def job_config(args, world, syn):
 class ClockSampler:
     """nvidia-smi samples (every 100 ms) of the SM clock and throttle reasons.
 
-    Started before the warm-up steps, so that nvidia-smi is already sampling
-    when the timed region begins; `mark(t0, t1)` records the timed region's
+    Started before the warm-up steps and stopped after the end-to-end steps
+    that follow the timed ones, so that nvidia-smi is already sampling when
+    the timed region begins; `mark(t0, t1)` records the timed region's
     wall-clock window, and the summary keeps the samples inside it. A region
     too short to hold a sample (a few fast steps on many GPUs) falls back to
-    the loaded samples of the warm-up and timed steps, and says so."""
+    the loaded samples around it (warm-up and end-to-end steps), and says
+    so."""
 
     FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -252,6 +255,7 @@ class ClockSampler:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+            self.proc = None
 
     def summary(self):
         self.f.flush()
@@ -286,7 +290,7 @@ def summarize_clocks(text, window):
             chosen = inside
         else:
             chosen = [r for r in rows if r[3] > 300.0] or rows
-            span = "warm-up and timed steps (no sample fell inside the timed steps)"
+            span = "loaded samples around the timed steps (warm-up, end-to-end); none fell inside them"
     loaded = [r for r in chosen if r[3] > 300.0] or chosen
     names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
     reasons = sorted({names[i] for r in loaded for i, v in enumerate(r[4]) if v.lower() == "active"})
@@ -498,24 +502,24 @@ def main():
     # ── value: device-resident inputs ──
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clk:   # already sampling when the timed steps start
-        for _ in range(args.warmup):
-            step_device()
-        enc.sync()
-        L.b3_profile(enc.ctx, 1)
-        barrier()
-        torch.cuda.synchronize()
-        enc.sync()
-        t_wall0 = time.time()
-        ev0.record(stream)
-        for _ in range(args.steps):
-            step_device()
-        ev1.record(stream)
-        enc.sync()
-        torch.cuda.synchronize()
-        clk.mark(t_wall0, time.time())
+    clk = ClockSampler(local).__enter__()   # already sampling when the timed steps start
+    atexit.register(clk.__exit__, None, None, None)   # stopped on any exit path
+    for _ in range(args.warmup):
+        step_device()
+    enc.sync()
+    L.b3_profile(enc.ctx, 1)
+    barrier()
+    torch.cuda.synchronize()
+    enc.sync()
+    t_wall0 = time.time()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step_device()
+    ev1.record(stream)
+    enc.sync()
+    torch.cuda.synchronize()
+    clk.mark(t_wall0, time.time())
     ms = ev0.elapsed_time(ev1)
-    clocks = clk.summary()
     prof = {}
     import ctypes
     for kind, name in enumerate(KINDS):
@@ -531,18 +535,6 @@ def main():
         dist.all_reduce(tot)
     job_audio = float(tot.item())
     value = job_audio * args.steps / (ms_max / 1000.0)
-    # per-rank attribution: step time, clocks and the per-kind split of every rank
-    mine = {"rank": rank, "utterances": n_utt, "frames": M, "audio_s": round(audio, 1),
-            "longest_frames": int(max(frames)) if frames else 0,
-            "ms_per_step": round(ms / args.steps, 3), "sm_mhz": clocks.get("sm_mhz"),
-            "reasons": clocks.get("reasons"),
-            "kernels_ms_per_step": {k: round(v["ms"] / args.steps, 3) for k, v in prof.items() if v["launches"]}}
-    ranks = [None] * world
-    if world > 1:
-        dist.all_gather_object(ranks, mine)
-    else:
-        ranks = [mine]
-
     # ── e2e: host buffers through the host-pointer ABI call ──
     barrier()
     hin, hout = host_in.numpy(), host_out.numpy()
@@ -557,6 +549,20 @@ def main():
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1))
     e2e_value = job_audio * args.steps / (e2e_ms / 1000.0)
+    clk.__exit__(None, None, None)
+    clocks = clk.summary()
+
+    # per-rank attribution: step time, clocks and the per-kind split of every rank
+    mine = {"rank": rank, "utterances": n_utt, "frames": M, "audio_s": round(audio, 1),
+            "longest_frames": int(max(frames)) if frames else 0,
+            "ms_per_step": round(ms / args.steps, 3), "sm_mhz": clocks.get("sm_mhz"),
+            "reasons": clocks.get("reasons"),
+            "kernels_ms_per_step": {k: round(v["ms"] / args.steps, 3) for k, v in prof.items() if v["launches"]}}
+    ranks = [None] * world
+    if world > 1:
+        dist.all_gather_object(ranks, mine)
+    else:
+        ranks = [mine]
 
     pk, pk_kind = peaks()
     g = prof["gemm_lut4"]

@@ -40,7 +40,7 @@ def test_short_window_falls_back_to_loaded_samples():
     text = "\n".join([row(0.0, 1965, 100), row(0.1, 1800, 900), row(0.2, 1700, 950)])
     c = bench.summarize_clocks(text, (at(0.12), at(0.18)))
     assert c["sm_mhz"] == 1750.0 and c["samples"] == 2
-    assert c["span"].startswith("warm-up and timed steps")
+    assert c["span"].startswith("loaded samples around the timed steps")
 
 
 def test_no_samples_is_unsampled():
