@@ -88,6 +88,16 @@ constexpr uint32_t kTO = 384;     // O, 128
 constexpr uint32_t kIdescS = idesc_f16_f32_b<128, 64, 0>();
 constexpr uint32_t kIdescPV = idesc_f16_f32_b<128, 128, 1>();
 
+// 2^x by the special-function unit's approximation (relative error below
+// 2^-22, far inside the f16 rounding the probabilities get; results below
+// 2^-126 flush to zero, where a probability is negligible beside the row's
+// maximum of 1 and its f16 copy is zero anyway).
+__device__ __forceinline__ float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 __device__ __forceinline__ uint32_t h2u(float a, float b) {
     __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<uint32_t*>(&h);
@@ -440,7 +450,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int j = 0; j < 16; j += 2) {
                     const float2 xv = __fadd2_rn(make_float2(s[j], s[j + 1]), mneg);
-                    const float2 e = make_float2(exp2f(xv.x), exp2f(xv.y));
+                    const float2 e = make_float2(ex2_approx(xv.x), ex2_approx(xv.y));
                     ls[(j >> 1) & 1] = __fadd2_rn(ls[(j >> 1) & 1], e);
                     pk[j >> 1] = h2u(e.x, e.y);
                 }
