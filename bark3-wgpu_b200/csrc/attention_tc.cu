@@ -200,11 +200,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     auto item = [&](int i) {
         Item it;
-        const int2 wk = p.work[i >> 3];
+        const int4 wk = __ldg(p.work + (i >> 3));   // one load: no dependent reads at an item's start
         it.head = i & 7;
-        it.seg0 = p.cu[wk.x];
-        it.T = p.cu[wk.x + 1] - it.seg0;
-        it.q0 = wk.y;
+        it.seg0 = wk.x;
+        it.T = wk.y;
+        it.q0 = wk.z;
         it.nkb = (it.T + kBK - 1) / kBK;
         // band of key block kb: R rows [r_lo0 + 64 kb, r_lo0 + 64 kb + 191], the
         // band chunks kb, kb + 1 and kb + 2 of 64 rows (chunk c = R rows

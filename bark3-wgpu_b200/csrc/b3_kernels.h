@@ -27,8 +27,7 @@ struct AttnParams {
     const __half* R;     // [r_rows][1024] relative-position keys
     int r_center;        // row of R holding offset 0; row r_center - d holds offset d
     int r_rows;
-    const int* cu;       // device cu_seqlens [n_utt + 1]
-    const int2* work;    // device (utterance, first query) per CTA
+    const int4* work;    // device (first row of the utterance, its frames, first query, 0) per work entry
     __half* out;         // [M][1024]
     float scale_log2;    // log2(e) / sqrt(128)
 };

@@ -549,7 +549,7 @@ int ensure_arena(b3_ctx* c, int M) {
     B3_TRY(c->g16.ensure(m * kHidden * 2));
     B3_TRY(c->sub16.ensure(m * kSubIn * 2));
     B3_TRY(c->seg_d.ensure(m * sizeof(int2)));
-    B3_TRY(c->work_d.ensure((m / 64 + 1024) * sizeof(int2)));
+    B3_TRY(c->work_d.ensure((m / 64 + 1024) * sizeof(int4)));
     c->mcap = mcap;
     return 0;
 }
@@ -584,20 +584,20 @@ int make_plan(b3_ctx* c, const int32_t* cu, int n_utt) {
     B3_TRY(ensure_arena(c, M));
     B3_TRY(ensure_pos(c, tmax));
     const int bq = attention_tc_block_rows();
-    std::vector<int2> work;
+    // attention work entries: (first row of the utterance, its frames, first
+    // query, 0), every value an item needs in one load
+    std::vector<int4> work;
     std::vector<int2> seg(M);
     for (int i = 0; i < n_utt; ++i) {
-        for (int q = 0; q < cu[i + 1] - cu[i]; q += bq) work.push_back(make_int2(i, q));
+        for (int q = 0; q < cu[i + 1] - cu[i]; q += bq) work.push_back(make_int4(cu[i], cu[i + 1] - cu[i], q, 0));
         for (int r = cu[i]; r < cu[i + 1]; ++r) seg[r] = make_int2(cu[i], cu[i + 1]);
     }
     // attention CTAs of the longest utterances first (their key loops are
     // longest), so the last wave is made of short ones
-    std::stable_sort(work.begin(), work.end(), [&](const int2& a, const int2& b) {
-        return cu[a.x + 1] - cu[a.x] > cu[b.x + 1] - cu[b.x];
-    });
-    B3_TRY(c->work_d.ensure(work.size() * sizeof(int2)));
+    std::stable_sort(work.begin(), work.end(), [](const int4& a, const int4& b) { return a.y > b.y; });
+    B3_TRY(c->work_d.ensure(work.size() * sizeof(int4)));
     B3_TRY(c->cu_d.ensure(key.size() * sizeof(int32_t)));
-    B3_CUDA(cudaMemcpyAsync(c->work_d.p, work.data(), work.size() * sizeof(int2), cudaMemcpyHostToDevice, c->stream));
+    B3_CUDA(cudaMemcpyAsync(c->work_d.p, work.data(), work.size() * sizeof(int4), cudaMemcpyHostToDevice, c->stream));
     B3_CUDA(cudaMemcpyAsync(c->seg_d.p, seg.data(), seg.size() * sizeof(int2), cudaMemcpyHostToDevice, c->stream));
     B3_CUDA(cudaMemcpyAsync(c->cu_d.p, key.data(), key.size() * sizeof(int32_t), cudaMemcpyHostToDevice, c->stream));
     B3_CUDA(cudaStreamSynchronize(c->stream));
@@ -631,8 +631,7 @@ int attention_section(b3_ctx* c, const Layer& L, int M) {
     ap.R = c->R16.as<__half>();
     ap.r_center = tmax - 1;
     ap.r_rows = prows;
-    ap.cu = c->cu_d.as<int>();
-    ap.work = c->work_d.as<int2>();
+    ap.work = c->work_d.as<int4>();
     ap.out = a16;
     ap.scale_log2 = 1.4426950408889634f / std::sqrt(128.0f);
     {
