@@ -174,7 +174,10 @@ __global__ void __launch_bounds__(256, 7) k_mel_frames(MelParams p, int f0, int 
 // one CTA per (utterance, 32 mel bins); kNormLanes frame lanes per bin
 // (1024 threads, so a CTA keeps 32 rows of loads in flight per pass),
 // reduced in shared memory; two passes (mean, then squared deviations) as
-// the reference.
+// the reference.  The frame loops are unrolled 16 deep so each thread keeps
+// 16 loads in flight (a launch lasts as long as its longest utterance's CTA,
+// which walks thousands of frames); each running sum still adds in frame
+// order.
 constexpr int kNormLanes = 32;
 __global__ void __launch_bounds__(32 * kNormLanes) k_mel_norm(MelParams p, int u0) {
     __shared__ float red[kNormLanes][33];
@@ -188,7 +191,7 @@ __global__ void __launch_bounds__(32 * kNormLanes) k_mel_norm(MelParams p, int u
     const int nv = nvalid > 1 ? nvalid : 1;
     float* mel = p.mel + static_cast<size_t>(f0) * kMel + m;
     float s = 0.f;
-#pragma unroll 4
+#pragma unroll 16
     for (int t = fl; t < nvalid; t += kNormLanes) s += mel[static_cast<size_t>(t) * kMel];
     red[fl][b] = s;
     __syncthreads();
@@ -201,7 +204,7 @@ __global__ void __launch_bounds__(32 * kNormLanes) k_mel_norm(MelParams p, int u
     __syncthreads();
     const float mean = stat[b];
     float q = 0.f;
-#pragma unroll 4
+#pragma unroll 16
     for (int t = fl; t < nvalid; t += kNormLanes) {
         const float d = mel[static_cast<size_t>(t) * kMel] - mean;
         q += d * d;
@@ -216,6 +219,7 @@ __global__ void __launch_bounds__(32 * kNormLanes) k_mel_norm(MelParams p, int u
     }
     __syncthreads();
     const float den = stat[b];
+#pragma unroll 16
     for (int t = fl; t < nf; t += kNormLanes) {
         float& v = mel[static_cast<size_t>(t) * kMel];
         v = t < nvalid ? (v - mean) / den : 0.f;
